@@ -1,0 +1,68 @@
+// Python bindings of the nano_gpic_b200 CUDA extension (module nano_gpic_b200._C).
+#include <torch/extension.h>
+
+#include "status.h"
+
+namespace ng {
+void gemm_torch(const at::Tensor& A, bool a_mn, int64_t lda, int64_t a_bs, const at::Tensor& B, bool b_mn, int64_t ldb,
+                int64_t b_bs, int64_t b_rows, const at::Tensor& out, int64_t ldo, int64_t out_bs, int64_t epi, int64_t M,
+                int64_t N, int64_t K, int64_t batch, const c10::optional<at::Tensor>& out2, int64_t ldo2,
+                const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& res, int64_t ldr,
+                int64_t res_bs, const c10::optional<at::Tensor>& gate, int64_t ldg, int64_t rows_per_group,
+                const c10::optional<at::Tensor>& aux, int64_t ld_aux, int64_t half_n, double alpha, double beta,
+                bool accumulate);
+void rms_mod_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& shift,
+                 const c10::optional<at::Tensor>& scale, const at::Tensor& h, const at::Tensor& rstd, int64_t rpg,
+                 double eps);
+void rms_mod_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& rstd, const at::Tensor& w,
+                 const c10::optional<at::Tensor>& scale, const c10::optional<at::Tensor>& dres, const at::Tensor& dx,
+                 const c10::optional<at::Tensor>& dw, const c10::optional<at::Tensor>& dshift,
+                 const c10::optional<at::Tensor>& dscale, int64_t rpg);
+void layernorm_fwd(const at::Tensor& x, const at::Tensor& h, const at::Tensor& mu, const at::Tensor& rstd, double eps);
+void layernorm_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& mu, const at::Tensor& rstd,
+                   const at::Tensor& dx);
+void qk_norm_fwd(const at::Tensor& src, const at::Tensor& w, const c10::optional<at::Tensor>& cosT,
+                 const c10::optional<at::Tensor>& sinT, const at::Tensor& out, const at::Tensor& rstd, int64_t L,
+                 double eps);
+void qk_norm_bwd(const at::Tensor& dout, const at::Tensor& src, const at::Tensor& rstd, const at::Tensor& w,
+                 const c10::optional<at::Tensor>& cosT, const c10::optional<at::Tensor>& sinT, const at::Tensor& dsrc,
+                 const c10::optional<at::Tensor>& dw, int64_t L);
+void attn_fwd(const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0, const c10::optional<at::Tensor>& k1,
+              const c10::optional<at::Tensor>& v1, const at::Tensor& n0, const at::Tensor& n1, const at::Tensor& o,
+              const at::Tensor& lse, int64_t Lq, int64_t L0, int64_t L1, double scale);
+void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0,
+              const c10::optional<at::Tensor>& k1, const c10::optional<at::Tensor>& v1, const at::Tensor& n0,
+              const at::Tensor& n1, const at::Tensor& o, const at::Tensor& lse, const at::Tensor& dq,
+              const at::Tensor& dk0, const at::Tensor& dv0, const c10::optional<at::Tensor>& dk1,
+              const c10::optional<at::Tensor>& dv1, int64_t Lq, int64_t L0, int64_t L1, double scale);
+void gate_bwd(const at::Tensor& dout, const at::Tensor& y, const at::Tensor& gate, const at::Tensor& dy,
+              const c10::optional<at::Tensor>& dgate, const c10::optional<at::Tensor>& dbias, int64_t rpg);
+void fm_prep(const at::Tensor& x, const at::Tensor& noise, const at::Tensor& t, const at::Tensor& xt_tok, int64_t p);
+void fm_loss(const at::Tensor& pred, const at::Tensor& x, const at::Tensor& noise, const at::Tensor& t,
+             const c10::optional<at::Tensor>& dpred, const at::Tensor& per_sample, int64_t p, double t_eps,
+             double grad_scale);
+void patchify(const at::Tensor& img, const at::Tensor& tok, int64_t p);
+void unpatchify(const at::Tensor& tok, const at::Tensor& img, int64_t p);
+void add_rows(const at::Tensor& a, const at::Tensor& table, const at::Tensor& out, int64_t period);
+}  // namespace ng
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "nano_gpic_b200 sm_100a kernels";
+  m.def("gemm", &ng::gemm_torch, "tcgen05 GEMM with fused epilogues");
+  m.def("rms_mod_fwd", &ng::rms_mod_fwd);
+  m.def("rms_mod_bwd", &ng::rms_mod_bwd);
+  m.def("layernorm_fwd", &ng::layernorm_fwd);
+  m.def("layernorm_bwd", &ng::layernorm_bwd);
+  m.def("qk_norm_fwd", &ng::qk_norm_fwd);
+  m.def("qk_norm_bwd", &ng::qk_norm_bwd);
+  m.def("attn_fwd", &ng::attn_fwd);
+  m.def("attn_bwd", &ng::attn_bwd);
+  m.def("gate_bwd", &ng::gate_bwd);
+  m.def("fm_prep", &ng::fm_prep);
+  m.def("fm_loss", &ng::fm_loss);
+  m.def("patchify", &ng::patchify);
+  m.def("unpatchify", &ng::unpatchify);
+  m.def("add_rows", &ng::add_rows);
+  m.def("status_read", &ng::status_read, "read the device error word (synchronizes the current stream)");
+  m.def("status_clear", &ng::status_clear, "clear the device error word");
+}

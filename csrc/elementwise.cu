@@ -1,0 +1,321 @@
+// Memory-bound kernels around the GEMMs, for sm_100a:
+//   gate_bwd      backward of out = res + gate[g] * y: dy = gate * dout, d_gate[g] = sum_rows dout * y,
+//                 d_bias = sum_rows dy (deterministic chunk partials, fixed-order reduce)
+//   fm_prep       flow-matching input: x_t = t x + (1 - t) eps, patchified to bf16 tokens [B*N, 3*p*p]
+//   fm_loss       per-sample sum of (out - v)^2 with out = (pred - x_t)/d, v = (x - x_t)/d, d = max(1 - t, t_eps),
+//                 and the gradient w.r.t. the bf16 prediction tokens in the same pass
+//   patchify / unpatchify, add_rows (bf16(a + table[row % period]))
+// Reference: the gated residuals of JiT_T2I.py:201-210, JiTTrainer._impl_trainstep
+// (baselines/PixelGen/src/diffusion/flow_matching/training_JiT.py:36-64) and patchify (JiT_T2I.py:42-52).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace ng {
+
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ void u8(const uint4& u, float (&f)[8]) {
+  f[0] = bf16_bits_lo(u.x);
+  f[1] = bf16_bits_hi(u.x);
+  f[2] = bf16_bits_lo(u.y);
+  f[3] = bf16_bits_hi(u.y);
+  f[4] = bf16_bits_lo(u.z);
+  f[5] = bf16_bits_hi(u.z);
+  f[6] = bf16_bits_lo(u.w);
+  f[7] = bf16_bits_hi(u.w);
+}
+__device__ __forceinline__ uint4 p8(const float (&f)[8]) {
+  uint4 u;
+  u.x = pack_bf16(f[0], f[1]);
+  u.y = pack_bf16(f[2], f[3]);
+  u.z = pack_bf16(f[4], f[5]);
+  u.w = pack_bf16(f[6], f[7]);
+  return u;
+}
+
+// ---------------------------------------------------------------------------------------------------- gate backward
+constexpr int GB_ROWS = 64;
+
+__global__ void __launch_bounds__(256) gate_bwd_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ y,
+                                                       const bf16* __restrict__ gate, int64_t ldg,
+                                                       bf16* __restrict__ dy, float* __restrict__ part, int M, int C,
+                                                       int rpg) {
+  const int g = blockIdx.y, chunk = blockIdx.x;
+  const int r0 = g * rpg + chunk * GB_ROWS;
+  const int r1 = min(min(g * rpg + rpg, r0 + GB_ROWS), M);
+  const int v = threadIdx.x, nv = C >> 3;
+  const int cid = g * gridDim.x + chunk;
+  for (int vv = v; vv < nv; vv += blockDim.x) {
+    const int c0 = vv * 8;
+    float gv[8], pg[8], pb[8];
+    u8(*reinterpret_cast<const uint4*>(gate + (int64_t)g * ldg + c0), gv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) pg[j] = pb[j] = 0.f;
+    for (int row = r0; row < r1; ++row) {
+      float d[8], yy[8], o[8];
+      u8(*reinterpret_cast<const uint4*>(dout + (int64_t)row * C + c0), d);
+      u8(*reinterpret_cast<const uint4*>(y + (int64_t)row * C + c0), yy);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        pg[j] += d[j] * yy[j];
+        o[j] = gv[j] * d[j];
+      }
+      const uint4 packed = p8(o);
+      *reinterpret_cast<uint4*>(dy + (int64_t)row * C + c0) = packed;
+      float ob[8];
+      u8(packed, ob);  // the bias sees the rounded dy that the GEMMs consume
+#pragma unroll
+      for (int j = 0; j < 8; ++j) pb[j] += ob[j];
+    }
+    float* pp = part + (int64_t)cid * 2 * C;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      pp[c0 + j] = pg[j];
+      pp[C + c0 + j] = pb[j];
+    }
+  }
+}
+
+__global__ void gate_bwd_reduce(const float* __restrict__ part, int G, int chunks, int C, float* dgate, int64_t ld_dg,
+                                float* dbias) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  float tb = 0.f;
+  for (int g = 0; g < G; ++g) {
+    float a = 0.f;
+    for (int k = 0; k < chunks; ++k) {
+      const float* pp = part + (int64_t)(g * chunks + k) * 2 * C;
+      a += pp[c];
+      tb += pp[C + c];
+    }
+    if (dgate != nullptr) dgate[(int64_t)g * ld_dg + c] = a;
+  }
+  if (dbias != nullptr) dbias[c] += tb;
+}
+
+// ---------------------------------------------------------------------------------------------- flow matching
+// token n of sample b, element e = c*p*p + py*p + px  <->  pixel (b, c, (n / gw)*p + py, (n % gw)*p + px)
+// each thread handles 8 consecutive elements (same c, py; px in [8k, 8k+8)): needs p % 8 == 0
+__global__ void fm_prep_kernel(const float* __restrict__ x, const float* __restrict__ noise,
+                               const float* __restrict__ t, bf16* __restrict__ xt_tok, int B, int Cin, int H, int W,
+                               int p) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // index of an 8-element group
+  const int D = Cin * p * p, gw = W / p, N = (H / p) * gw;
+  const int64_t total = (int64_t)B * N * D / 8;
+  if (i >= total) return;
+  const int64_t e0 = i * 8;
+  const int64_t tok = e0 / D;
+  const int e = (int)(e0 - tok * D);
+  const int b = (int)(tok / N), n = (int)(tok - (int64_t)b * N);
+  const int c = e / (p * p), py = (e / p) % p, px = e % p;
+  const int yy = (n / gw) * p + py, xx = (n % gw) * p + px;
+  const int64_t pix = (((int64_t)b * Cin + c) * H + yy) * W + xx;
+  const float tb = t[b];
+  const float4 xa = *reinterpret_cast<const float4*>(x + pix), xb = *reinterpret_cast<const float4*>(x + pix + 4);
+  const float4 na = *reinterpret_cast<const float4*>(noise + pix), nb = *reinterpret_cast<const float4*>(noise + pix + 4);
+  const float s = 1.f - tb;
+  float o[8] = {tb * xa.x + na.x * s, tb * xa.y + na.y * s, tb * xa.z + na.z * s, tb * xa.w + na.w * s,
+                tb * xb.x + nb.x * s, tb * xb.y + nb.y * s, tb * xb.z + nb.z * s, tb * xb.w + nb.w * s};
+  *reinterpret_cast<uint4*>(xt_tok + e0) = p8(o);
+}
+
+// per-(sample, block) partial sums; grid.x = blocks per sample, grid.y = B
+__global__ void __launch_bounds__(256) fm_loss_kernel(const bf16* __restrict__ pred, const float* __restrict__ x,
+                                                      const float* __restrict__ noise, const float* __restrict__ t,
+                                                      bf16* __restrict__ dpred, float* __restrict__ part, int Cin,
+                                                      int H, int W, int p, float t_eps, float grad_scale) {
+  __shared__ float red[8];
+  const int b = blockIdx.y;
+  const int D = Cin * p * p, gw = W / p, N = (H / p) * gw;
+  const int64_t per_sample = (int64_t)N * D / 8;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  float acc = 0.f;
+  if (i < per_sample) {
+    const int64_t e0 = i * 8;
+    const int n = (int)(e0 / D);
+    const int e = (int)(e0 - (int64_t)n * D);
+    const int c = e / (p * p), py = (e / p) % p, px = e % p;
+    const int yy = (n / gw) * p + py, xx = (n % gw) * p + px;
+    const int64_t pix = (((int64_t)b * Cin + c) * H + yy) * W + xx;
+    const float tb = t[b];
+    const float den = fmaxf(1.f - tb, t_eps);
+    float xv[8], nv[8], pv[8], g[8];
+    *reinterpret_cast<float4*>(xv) = *reinterpret_cast<const float4*>(x + pix);
+    *reinterpret_cast<float4*>(xv + 4) = *reinterpret_cast<const float4*>(x + pix + 4);
+    *reinterpret_cast<float4*>(nv) = *reinterpret_cast<const float4*>(noise + pix);
+    *reinterpret_cast<float4*>(nv + 4) = *reinterpret_cast<const float4*>(noise + pix + 4);
+    const int64_t tokoff = ((int64_t)b * N + n) * D + e;
+    u8(*reinterpret_cast<const uint4*>(pred + tokoff), pv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float xt = tb * xv[j] + nv[j] * (1.f - tb);
+      const float out = (pv[j] - xt) / den;
+      const float v = (xv[j] - xt) / den;
+      const float d = out - v;
+      acc += d * d;
+      g[j] = grad_scale * 2.f * d / den;
+    }
+    if (dpred != nullptr) *reinterpret_cast<uint4*>(dpred + tokoff) = p8(g);
+  }
+  acc = warp_sum(acc);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float s = 0.f;
+    for (int k = 0; k < 8; ++k) s += red[k];
+    part[(int64_t)b * gridDim.x + blockIdx.x] = s;
+  }
+}
+
+__global__ void fm_loss_reduce(const float* __restrict__ part, int nblk, float* __restrict__ per_sample, float inv_d) {
+  const int b = blockIdx.x;
+  if (threadIdx.x == 0) {
+    float s = 0.f;
+    for (int k = 0; k < nblk; ++k) s += part[(int64_t)b * nblk + k];
+    per_sample[b] = s * inv_d;
+  }
+}
+
+// tokens [B*N, Cin*p*p] (bf16) <-> image [B, Cin, H, W] (fp32 or bf16 out)
+template <typename Tin, typename Tout, bool TO_TOKENS>
+__global__ void patch_kernel(const Tin* __restrict__ src, Tout* __restrict__ dst, int B, int Cin, int H, int W, int p) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int D = Cin * p * p, gw = W / p, N = (H / p) * gw;
+  const int64_t total = (int64_t)B * N * D;
+  if (i >= total) return;
+  const int64_t tok = i / D;
+  const int e = (int)(i - tok * D);
+  const int b = (int)(tok / N), n = (int)(tok - (int64_t)b * N);
+  const int c = e / (p * p), py = (e / p) % p, px = e % p;
+  const int64_t pix = (((int64_t)b * Cin + c) * H + (n / gw) * p + py) * W + (n % gw) * p + px;
+  if (TO_TOKENS)
+    dst[i] = (Tout)(float)src[pix];
+  else
+    dst[pix] = (Tout)(float)src[i];
+}
+
+// out[row] = bf16(a[row] + table[row % period]) (fp32 or bf16 table [period, C])
+template <typename TT>
+__global__ void add_rows_kernel(const bf16* __restrict__ a, const TT* __restrict__ table, bf16* __restrict__ out,
+                                int64_t rows, int C, int period) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int nv = C / 8;
+  if (i >= rows * nv) return;
+  const int64_t row = i / nv;
+  const int c0 = (int)(i - row * nv) * 8;
+  float f[8];
+  u8(*reinterpret_cast<const uint4*>(a + row * C + c0), f);
+  const TT* tr = table + (int64_t)(row % period) * C + c0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) f[j] += (float)tr[j];
+  *reinterpret_cast<uint4*>(out + row * C + c0) = p8(f);
+}
+
+// ====================================================================================================== torch glue
+void gate_bwd(const at::Tensor& dout, const at::Tensor& y, const at::Tensor& gate, const at::Tensor& dy,
+              const c10::optional<at::Tensor>& dgate, const c10::optional<at::Tensor>& dbias, int64_t rpg) {
+  TORCH_CHECK(dout.is_contiguous() && y.is_contiguous() && dy.is_contiguous() && gate.stride(1) == 1,
+              "gate_bwd: layouts");
+  const at::cuda::CUDAGuard guard(dout.device());
+  const int M = dout.size(0), C = dout.size(1);
+  TORCH_CHECK(C % 8 == 0, "gate_bwd: C % 8");
+  const int G = (M + (int)rpg - 1) / (int)rpg;
+  const int chunks = ((int)rpg + GB_ROWS - 1) / GB_ROWS;
+  auto s = at::cuda::getCurrentCUDAStream();
+  at::Tensor part = at::empty({(int64_t)G * chunks * 2 * C}, dout.options().dtype(at::kFloat));
+  gate_bwd_kernel<<<dim3(chunks, G), 256, 0, s>>>(
+      reinterpret_cast<const bf16*>(dout.data_ptr()), reinterpret_cast<const bf16*>(y.data_ptr()),
+      reinterpret_cast<const bf16*>(gate.data_ptr()), gate.stride(0), reinterpret_cast<bf16*>(dy.data_ptr()),
+      part.data_ptr<float>(), M, C, (int)rpg);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  float* dg = (dgate.has_value() && dgate->defined()) ? dgate->data_ptr<float>() : nullptr;
+  float* db = (dbias.has_value() && dbias->defined()) ? dbias->data_ptr<float>() : nullptr;
+  gate_bwd_reduce<<<(C + 255) / 256, 256, 0, s>>>(part.data_ptr<float>(), G, chunks, C, dg,
+                                                   dg ? dgate->stride(0) : 0, db);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void fm_prep(const at::Tensor& x, const at::Tensor& noise, const at::Tensor& t, const at::Tensor& xt_tok, int64_t p) {
+  TORCH_CHECK(x.is_contiguous() && noise.is_contiguous() && x.scalar_type() == at::kFloat, "fm_prep: fp32 images");
+  TORCH_CHECK(p % 8 == 0, "fm_prep: patch size must be a multiple of 8");
+  const at::cuda::CUDAGuard guard(x.device());
+  const int B = x.size(0), Cin = x.size(1), H = x.size(2), W = x.size(3);
+  const int64_t groups = x.numel() / 8;
+  fm_prep_kernel<<<(unsigned)((groups + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      x.data_ptr<float>(), noise.data_ptr<float>(), t.data_ptr<float>(), reinterpret_cast<bf16*>(xt_tok.data_ptr()),
+      B, Cin, H, W, (int)p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void fm_loss(const at::Tensor& pred, const at::Tensor& x, const at::Tensor& noise, const at::Tensor& t,
+             const c10::optional<at::Tensor>& dpred, const at::Tensor& per_sample, int64_t p, double t_eps,
+             double grad_scale) {
+  const at::cuda::CUDAGuard guard(x.device());
+  const int B = x.size(0), Cin = x.size(1), H = x.size(2), W = x.size(3);
+  const int64_t per = x.numel() / B / 8;
+  const int nblk = (int)((per + 255) / 256);
+  auto s = at::cuda::getCurrentCUDAStream();
+  at::Tensor part = at::empty({(int64_t)B * nblk}, x.options());
+  bf16* dp = (dpred.has_value() && dpred->defined()) ? reinterpret_cast<bf16*>(dpred->data_ptr()) : nullptr;
+  fm_loss_kernel<<<dim3(nblk, B), 256, 0, s>>>(reinterpret_cast<const bf16*>(pred.data_ptr()), x.data_ptr<float>(),
+                                               noise.data_ptr<float>(), t.data_ptr<float>(), dp,
+                                               part.data_ptr<float>(), Cin, H, W, (int)p, (float)t_eps,
+                                               (float)grad_scale);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  fm_loss_reduce<<<B, 32, 0, s>>>(part.data_ptr<float>(), nblk, per_sample.data_ptr<float>(),
+                                  1.f / (float)(x.numel() / B));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void patchify(const at::Tensor& img, const at::Tensor& tok, int64_t p) {
+  const at::cuda::CUDAGuard guard(img.device());
+  const int B = img.size(0), Cin = img.size(1), H = img.size(2), W = img.size(3);
+  const int64_t n = img.numel();
+  auto s = at::cuda::getCurrentCUDAStream();
+  TORCH_CHECK(tok.scalar_type() == at::kBFloat16, "patchify: bf16 tokens");
+  if (img.scalar_type() == at::kFloat)
+    patch_kernel<float, bf16, true><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+        img.data_ptr<float>(), reinterpret_cast<bf16*>(tok.data_ptr()), B, Cin, H, W, (int)p);
+  else
+    patch_kernel<bf16, bf16, true><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+        reinterpret_cast<const bf16*>(img.data_ptr()), reinterpret_cast<bf16*>(tok.data_ptr()), B, Cin, H, W, (int)p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void unpatchify(const at::Tensor& tok, const at::Tensor& img, int64_t p) {
+  const at::cuda::CUDAGuard guard(img.device());
+  const int B = img.size(0), Cin = img.size(1), H = img.size(2), W = img.size(3);
+  const int64_t n = img.numel();
+  auto s = at::cuda::getCurrentCUDAStream();
+  if (img.scalar_type() == at::kFloat)
+    patch_kernel<bf16, float, false><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+        reinterpret_cast<const bf16*>(tok.data_ptr()), img.data_ptr<float>(), B, Cin, H, W, (int)p);
+  else
+    patch_kernel<bf16, bf16, false><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+        reinterpret_cast<const bf16*>(tok.data_ptr()), reinterpret_cast<bf16*>(img.data_ptr()), B, Cin, H, W, (int)p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void add_rows(const at::Tensor& a, const at::Tensor& table, const at::Tensor& out, int64_t period) {
+  TORCH_CHECK(a.is_contiguous() && table.is_contiguous() && out.is_contiguous(), "add_rows: contiguous");
+  const at::cuda::CUDAGuard guard(a.device());
+  const int64_t rows = a.size(0);
+  const int C = a.size(1);
+  TORCH_CHECK(C % 8 == 0, "add_rows: C % 8");
+  const int64_t n = rows * (C / 8);
+  auto s = at::cuda::getCurrentCUDAStream();
+  if (table.scalar_type() == at::kFloat)
+    add_rows_kernel<float><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+        reinterpret_cast<const bf16*>(a.data_ptr()), table.data_ptr<float>(), reinterpret_cast<bf16*>(out.data_ptr()),
+        rows, C, (int)period);
+  else
+    add_rows_kernel<bf16><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+        reinterpret_cast<const bf16*>(a.data_ptr()), reinterpret_cast<const bf16*>(table.data_ptr()),
+        reinterpret_cast<bf16*>(out.data_ptr()), rows, C, (int)period);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace ng

@@ -1,0 +1,616 @@
+// Persistent tcgen05 GEMM for sm_100a: D[M, N] = A[M, K] * B[N, K]^T in bf16 with an fp32 accumulator in TMEM.
+//
+// Replaces every nn.Linear of the reference's JiT-T2I (cuBLAS under autocast, reference
+// baselines/PixelGen/src/models/transformer/JiT_T2I.py:114-311) in its three forms:
+//   forward  Y  = X  W^T     A K-major ([M, K] row-major), B K-major ([N, K] row-major)
+//   dgrad    dX = dY W       A K-major, B MN-major ([K, N] row-major)
+//   wgrad    dW = dY^T X     A MN-major ([K, M] row-major), B MN-major
+// and the Newton-Schulz GEMM chain of Muon (reference baselines/PixelGen/src/optim/muon.py:64-86) through the
+// batched alpha/beta epilogue.
+//
+// Structure (one CTA per SM, persistent over output tiles of 128 x 256):
+//   warp 0      TMA producer: 4-stage ring of (A 128x64, B 256x64) bf16 tiles, 128-byte swizzle, no multicast
+//   warp 1      TMEM owner and MMA issuer: tcgen05.mma M=128 N=256 K=16, one elected thread
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (double-buffered in TMEM, 2 x 256 columns), fused
+//               elementwise work, vector stores to global memory
+// The epilogue of tile i overlaps the MMAs of tile i+1.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "gemm.h"
+
+namespace ng {
+
+namespace gemm_cfg {
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KiB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KiB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
+}  // namespace gemm_cfg
+
+struct EpiParams {
+  int M, N, K, batch;
+  int half_n;  // SwiGLU: column offset of the second (x2) half in the pre-activation / the W12 rows
+  void* out;
+  int64_t ldo, out_bs;
+  void* out2;
+  int64_t ldo2;
+  const float* bias;
+  const __nv_bfloat16* res;
+  int64_t ldr, res_bs;
+  const __nv_bfloat16* gate;
+  int64_t ldg;
+  int rows_per_group;
+  const __nv_bfloat16* aux;
+  int64_t ld_aux;
+  float alpha, beta;
+  int accumulate;
+  int* err;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& b, int& mb, int& nb) {
+  const int per_batch = num_m * num_n;
+  b = t / per_batch;
+  int r = t - b * per_batch;
+  constexpr int GROUP_M = 8;
+  const int per_group = GROUP_M * num_n;
+  const int g = r / per_group;
+  const int first_m = g * GROUP_M;
+  const int gsize = min(num_m - first_m, GROUP_M);
+  const int rr = r - g * per_group;
+  mb = first_m + rr % gsize;
+  nb = rr / gsize;
+}
+
+template <int EPI>
+__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const float (&v)[32], int col0, int N) {
+  if (col0 + 32 <= N) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 w;
+      w.x = pack_bf16(v[8 * j + 0], v[8 * j + 1]);
+      w.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
+      w.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
+      w.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
+      d4[j] = w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < N) dst[j] = __float2bfloat16_rn(v[j]);
+  }
+}
+
+__device__ __forceinline__ void load_row_bf16(const __nv_bfloat16* src, float (&v)[32], int col0, int N) {
+  if (col0 + 32 <= N) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 w = s4[j];
+      v[8 * j + 0] = bf16_bits_lo(w.x);
+      v[8 * j + 1] = bf16_bits_hi(w.x);
+      v[8 * j + 2] = bf16_bits_lo(w.y);
+      v[8 * j + 3] = bf16_bits_hi(w.y);
+      v[8 * j + 4] = bf16_bits_lo(w.z);
+      v[8 * j + 5] = bf16_bits_hi(w.z);
+      v[8 * j + 6] = bf16_bits_lo(w.w);
+      v[8 * j + 7] = bf16_bits_hi(w.w);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = (col0 + j < N) ? __bfloat162float(src[j]) : 0.0f;
+  }
+}
+
+__device__ __forceinline__ void load_bias(const float* bias, float (&bv)[32], int col0, int N) {
+  if (bias == nullptr) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) bv[j] = 0.f;
+    return;
+  }
+  if (col0 + 32 <= N) {
+    const float4* b4 = reinterpret_cast<const float4*>(bias + col0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float4 w = __ldg(b4 + j);
+      bv[4 * j] = w.x;
+      bv[4 * j + 1] = w.y;
+      bv[4 * j + 2] = w.z;
+      bv[4 * j + 3] = w.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) bv[j] = (col0 + j < N) ? bias[col0 + j] : 0.f;
+  }
+}
+
+template <int AMN, int BMN, int EPI>
+__global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const EpiParams p) {
+  using namespace gemm_cfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // SwiGLU tiles cover 128 output columns of each half: the MMA's N extent is still 256
+  const int num_m = (p.M + BM - 1) / BM;
+  const int num_n = (EPI == EPI_SWIGLU) ? (p.half_n + 127) / 128 : (p.N + BN - 1) / BN;
+  const int num_k = (p.K + BK - 1) / BK;
+  const int total = p.batch * num_m * num_n;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&tmA);
+    tma_prefetch_map(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;  // stages filled since the start (for draining on abort)
+      for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+        int b, mb, nb;
+        tile_coords(t, num_m, num_n, b, mb, nb);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
+          uint8_t* sA = smem + stage * STAGE_BYTES;
+          uint8_t* sB = sA + A_BYTES;
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          const int k0 = kb * BK;
+          if (AMN == 0) {
+            tma_load_3d(&tmA, &full[stage], sA, k0, mb * BM, b);
+          } else {
+            tma_load_3d(&tmA, &full[stage], sA, mb * BM, k0, b);
+            tma_load_3d(&tmA, &full[stage], sA + 8192, mb * BM + 64, k0, b);
+          }
+          if (BMN == 0) {
+            int r0, r1;
+            if (EPI == EPI_SWIGLU) {
+              r0 = nb * 128;
+              r1 = p.half_n + nb * 128;
+            } else {
+              r0 = nb * BN;
+              r1 = nb * BN + 128;
+            }
+            tma_load_3d(&tmB, &full[stage], sB, k0, r0, b);
+            tma_load_3d(&tmB, &full[stage], sB + 16384, k0, r1, b);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) tma_load_3d(&tmB, &full[stage], sB + j * 8192, nb * BN + 64 * j, k0, b);
+          }
+          ++issued;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (*abort_flag) {
+        // unwinding: let the copies already issued land before the CTA's shared memory goes away
+        const uint64_t t0 = globaltimer_ns();
+        int s = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < min(issued, STAGES); ++i) {
+          if (--s < 0) {
+            s = STAGES - 1;
+            ph ^= 1;
+          }
+          while (!mbar_try_wait(&full[s], ph)) {
+            if (globaltimer_ns() - t0 > NG_WAIT_BUDGET_NS) {
+              raise_error(p.err, kErrWaitDrain);
+              break;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, AMN, BMN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool issued_any = false;
+      for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, ++it) {
+        const int a = it & 1;
+        const uint32_t aph = (it >> 1) & 1;
+        if (!mbar_wait(&acc_empty[a], aph ^ 1, abort_flag, p.err, kErrWaitAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + a * BN;
+        bool ok = true;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t da = AMN == 0 ? smem_desc_sw128(sa + k * 32, 16, 1024)
+                                         : smem_desc_sw128(sa + k * 2048, 8192, 1024);
+            const uint64_t db = BMN == 0 ? smem_desc_sw128(sb + k * 32, 16, 1024)
+                                         : smem_desc_sw128(sb + k * 2048, 8192, 1024);
+            umma_f16(d_tmem, da, db, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[a]);
+      }
+      if (*abort_flag && issued_any) {
+        // unwinding: wait for the MMAs in flight before TMEM is released
+        umma_commit(drain);
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(drain, 0)) {
+          if (globaltimer_ns() - t0 > NG_WAIT_BUDGET_NS) {
+            raise_error(p.err, kErrWaitDrain);
+            break;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int r_in_tile = q * 32 + lane;
+    int it = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
+      const int a = it & 1;
+      const uint32_t aph = (it >> 1) & 1;
+      const bool got = mbar_wait(&acc_full[a], aph, abort_flag, p.err, kErrWaitAccFull);
+      __syncwarp();
+      if (!got) break;
+      tc_fence_after();
+      int b, mb, nb;
+      tile_coords(t, num_m, num_n, b, mb, nb);
+      const int row = mb * BM + r_in_tile;
+      const bool row_ok = row < p.M;
+      const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + a * BN;
+      if (EPI == EPI_SWIGLU) {
+        // columns [0,128) of the accumulator are x1 = gate half, [128,256) are x2 = up half
+        __nv_bfloat16* pre = reinterpret_cast<__nv_bfloat16*>(p.out2) + (int64_t)row * p.ldo2;
+        __nv_bfloat16* act = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r1[32], r2[32];
+          __syncwarp();
+          tmem_ld32(tb + c * 32, r1);
+          tmem_ld32(tb + 128 + c * 32, r2);
+          tmem_wait_ld();
+          const int col = nb * 128 + c * 32;
+          if (row_ok) {
+            float x1[32], x2[32], h[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              x1[j] = round_bf16(__uint_as_float(r1[j]));
+              x2[j] = round_bf16(__uint_as_float(r2[j]));
+              h[j] = round_bf16(x1[j] * sigmoidf_(x1[j])) * x2[j];
+            }
+            store_row_bf16<EPI>(pre + col, x1, col, p.half_n);
+            store_row_bf16<EPI>(pre + p.half_n + col, x2, col, p.half_n);
+            store_row_bf16<EPI>(act + col, h, col, p.half_n);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld32(tb + c * 32, r);
+          tmem_wait_ld();
+          const int col = nb * BN + c * 32;
+          if (!row_ok || col >= p.N) continue;  // the next TMEM load re-converges the warp first
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          if (EPI == EPI_BF16) {
+            float bv[32];
+            load_bias(p.bias, bv, col, p.N);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] += bv[j];
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + b * p.out_bs + (int64_t)row * p.ldo + col;
+            store_row_bf16<EPI>(o, v, col, p.N);
+          } else if (EPI == EPI_F32) {
+            float* o = reinterpret_cast<float*>(p.out) + b * p.out_bs + (int64_t)row * p.ldo + col;
+            if (col + 32 <= p.N) {
+              float4* o4 = reinterpret_cast<float4*>(o);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                float4 w = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                if (p.accumulate) {
+                  float4 u = o4[j];
+                  w.x += u.x;
+                  w.y += u.y;
+                  w.z += u.z;
+                  w.w += u.w;
+                }
+                o4[j] = w;
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col + j < p.N) o[j] = p.accumulate ? o[j] + v[j] : v[j];
+            }
+          } else if (EPI == EPI_AXPBY) {
+            float cv[32];
+            if (p.beta != 0.f) {
+              load_row_bf16(p.res + b * p.res_bs + (int64_t)row * p.ldr + col, cv, col, p.N);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) cv[j] = 0.f;
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = p.alpha * v[j] + p.beta * cv[j];
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + b * p.out_bs + (int64_t)row * p.ldo + col;
+            store_row_bf16<EPI>(o, v, col, p.N);
+          } else if (EPI == EPI_GATED) {
+            // y = acc + bias (kept for the backward); out = res + gate[sample] * y
+            float bv[32], rv[32], gv[32];
+            load_bias(p.bias, bv, col, p.N);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = round_bf16(v[j] + bv[j]);
+            store_row_bf16<EPI>(reinterpret_cast<__nv_bfloat16*>(p.out2) + (int64_t)row * p.ldo2 + col, v, col, p.N);
+            load_row_bf16(p.res + (int64_t)row * p.ldr + col, rv, col, p.N);
+            load_row_bf16(p.gate + (int64_t)(row / p.rows_per_group) * p.ldg + col, gv, col, p.N);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = rv[j] + gv[j] * v[j];
+            store_row_bf16<EPI>(reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo + col, v, col, p.N);
+          } else if (EPI == EPI_SWIGLU_BWD) {
+            // v = d(act) for act columns [col, col+32); aux = the saved pre-activation [x1 | x2]
+            float x1[32], x2[32], d1[32], d2[32];
+            const __nv_bfloat16* pre = p.aux + (int64_t)row * p.ld_aux;
+            load_row_bf16(pre + col, x1, col, p.N);
+            load_row_bf16(pre + p.half_n + col, x2, col, p.N);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float s = sigmoidf_(x1[j]);
+              const float si = x1[j] * s;
+              d2[j] = v[j] * si;
+              d1[j] = v[j] * x2[j] * (s * (1.0f + x1[j] * (1.0f - s)));
+            }
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo;
+            store_row_bf16<EPI>(o + col, d1, col, p.N);
+            store_row_bf16<EPI>(o + p.half_n + col, d2, col, p.N);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[a]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+// ============================================================================================================== host
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && ptr != nullptr,
+                "nano_gpic_b200: cuTensorMapEncodeTiled is unavailable");
+    fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// A 3-D bf16 tensor map (inner, outer, batch) with a 128-byte swizzle; inner is contiguous.
+CUtensorMap make_tmap_bf16(const void* ptr, int64_t inner, int64_t outer, int64_t batch, int64_t ld, int64_t bstride,
+                           int box_inner, int box_outer) {
+  CUtensorMap m;
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)(batch > 1 ? bstride : ld * outer) * 2};
+  cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base address must be 16-byte aligned");
+  TORCH_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes, got ld=", ld);
+  TORCH_CHECK(batch == 1 || (bstride * 2) % 16 == 0, "TMA batch stride must be a multiple of 16 bytes");
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
+  return m;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int AMN, int BMN, int EPI>
+static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& p, int grid, cudaStream_t s) {
+  auto kern = gemm_tcgen05_kernel<AMN, BMN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_cfg::SMEM_BYTES);
+    attr_set = true;
+  }
+  kern<<<grid, gemm_cfg::THREADS, gemm_cfg::SMEM_BYTES, s>>>(ta, tb, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+template <int AMN, int BMN>
+static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& p, int grid,
+                         cudaStream_t s) {
+  switch (epi) {
+    case EPI_BF16: return launch_t<AMN, BMN, EPI_BF16>(ta, tb, p, grid, s);
+    case EPI_F32: return launch_t<AMN, BMN, EPI_F32>(ta, tb, p, grid, s);
+    case EPI_AXPBY: return launch_t<AMN, BMN, EPI_AXPBY>(ta, tb, p, grid, s);
+    case EPI_GATED: return launch_t<AMN, BMN, EPI_GATED>(ta, tb, p, grid, s);
+    case EPI_SWIGLU: return launch_t<AMN, BMN, EPI_SWIGLU>(ta, tb, p, grid, s);
+    case EPI_SWIGLU_BWD: return launch_t<AMN, BMN, EPI_SWIGLU_BWD>(ta, tb, p, grid, s);
+    default: TORCH_CHECK(false, "unknown GEMM epilogue ", epi);
+  }
+}
+
+void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
+  using namespace gemm_cfg;
+  TORCH_CHECK(g.M > 0 && g.N > 0 && g.K > 0 && g.batch > 0, "empty GEMM");
+  // operand tensor maps: K-major [rows, K] boxes of 64 x 128; MN-major [K, rows] boxes of 64 x 64
+  CUtensorMap ta = g.a_mn ? make_tmap_bf16(g.A, g.M, g.K, g.batch, g.lda, g.a_bs, 64, 64)
+                          : make_tmap_bf16(g.A, g.K, g.M, g.batch, g.lda, g.a_bs, 64, 128);
+  const int64_t b_rows = g.b_rows > 0 ? g.b_rows : g.N;
+  CUtensorMap tb = g.b_mn ? make_tmap_bf16(g.B, b_rows, g.K, g.batch, g.ldb, g.b_bs, 64, 64)
+                          : make_tmap_bf16(g.B, g.K, b_rows, g.batch, g.ldb, g.b_bs, 64, 128);
+  EpiParams p;
+  p.M = g.M;
+  p.N = g.N;
+  p.K = g.K;
+  p.batch = g.batch;
+  p.half_n = g.half_n;
+  p.out = g.out;
+  p.ldo = g.ldo;
+  p.out_bs = g.out_bs;
+  p.out2 = g.out2;
+  p.ldo2 = g.ldo2;
+  p.bias = g.bias;
+  p.res = g.res;
+  p.ldr = g.ldr;
+  p.res_bs = g.res_bs;
+  p.gate = g.gate;
+  p.ldg = g.ldg;
+  p.rows_per_group = g.rows_per_group > 0 ? g.rows_per_group : 1;
+  p.aux = g.aux;
+  p.ld_aux = g.ld_aux;
+  p.alpha = g.alpha;
+  p.beta = g.beta;
+  p.accumulate = g.accumulate;
+  p.err = g.err;
+  const int num_m = (g.M + BM - 1) / BM;
+  const int num_n = g.epi == EPI_SWIGLU ? (g.half_n + 127) / 128 : (g.N + BN - 1) / BN;
+  const int64_t tiles = (int64_t)g.batch * num_m * num_n;
+  const int grid = (int)std::min<int64_t>(tiles, num_sms());
+  if (!g.a_mn && !g.b_mn)
+    dispatch_epi<0, 0>(g.epi, ta, tb, p, grid, stream);
+  else if (!g.a_mn && g.b_mn)
+    dispatch_epi<0, 1>(g.epi, ta, tb, p, grid, stream);
+  else if (g.a_mn && g.b_mn)
+    dispatch_epi<1, 1>(g.epi, ta, tb, p, grid, stream);
+  else
+    dispatch_epi<1, 0>(g.epi, ta, tb, p, grid, stream);
+}
+
+}  // namespace ng
+
+// ======================================================================================================= torch glue
+#include "status.h"
+
+namespace ng {
+
+static const void* ptr_or_null(const c10::optional<at::Tensor>& t) {
+  return (t.has_value() && t->defined()) ? t->data_ptr() : nullptr;
+}
+
+// All strides are in elements; every tensor is addressed from its data_ptr (storage offset included).
+void gemm_torch(const at::Tensor& A, bool a_mn, int64_t lda, int64_t a_bs, const at::Tensor& B, bool b_mn, int64_t ldb,
+                int64_t b_bs, int64_t b_rows, const at::Tensor& out, int64_t ldo, int64_t out_bs, int64_t epi, int64_t M,
+                int64_t N, int64_t K, int64_t batch, const c10::optional<at::Tensor>& out2, int64_t ldo2,
+                const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& res, int64_t ldr,
+                int64_t res_bs, const c10::optional<at::Tensor>& gate, int64_t ldg, int64_t rows_per_group,
+                const c10::optional<at::Tensor>& aux, int64_t ld_aux, int64_t half_n, double alpha, double beta,
+                bool accumulate) {
+  TORCH_CHECK(A.is_cuda() && B.is_cuda() && out.is_cuda(), "gemm: CUDA tensors expected");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: bf16 operands expected");
+  if (bias.has_value() && bias->defined()) TORCH_CHECK(bias->scalar_type() == at::kFloat, "gemm: fp32 bias expected");
+  const at::cuda::CUDAGuard guard(A.device());
+  GemmArgs g;
+  g.M = (int)M;
+  g.N = (int)N;
+  g.K = (int)K;
+  g.batch = (int)batch;
+  g.A = A.data_ptr();
+  g.lda = lda;
+  g.a_bs = a_bs;
+  g.a_mn = a_mn;
+  g.B = B.data_ptr();
+  g.ldb = ldb;
+  g.b_bs = b_bs;
+  g.b_mn = b_mn;
+  g.b_rows = b_rows;
+  g.epi = (int)epi;
+  g.out = out.data_ptr();
+  g.ldo = ldo;
+  g.out_bs = out_bs;
+  g.out2 = const_cast<void*>(ptr_or_null(out2));
+  g.ldo2 = ldo2;
+  g.bias = static_cast<const float*>(ptr_or_null(bias));
+  g.res = static_cast<const __nv_bfloat16*>(ptr_or_null(res));
+  g.ldr = ldr;
+  g.res_bs = res_bs;
+  g.gate = static_cast<const __nv_bfloat16*>(ptr_or_null(gate));
+  g.ldg = ldg;
+  g.rows_per_group = (int)rows_per_group;
+  g.aux = static_cast<const __nv_bfloat16*>(ptr_or_null(aux));
+  g.ld_aux = ld_aux;
+  g.half_n = (int)half_n;
+  g.alpha = (float)alpha;
+  g.beta = (float)beta;
+  g.accumulate = accumulate ? 1 : 0;
+  g.err = status_word();
+  gemm_launch(g, at::cuda::getCurrentCUDAStream());
+}
+
+}  // namespace ng

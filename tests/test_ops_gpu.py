@@ -1,0 +1,113 @@
+"""CUDA kernels of the norm, q/k-prep and attention ops against the same ops' fp32 PyTorch paths (run on CPU copies)."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _close(a, b, rtol=2e-2, atol=2e-2, what=""):
+    a, b = a.float().cpu(), b.float().cpu()
+    err = (a - b).abs().max().item()
+    ref = b.abs().max().item() + 1e-6
+    assert err <= atol + rtol * ref, f"{what}: max err {err} vs ref max {ref}"
+
+
+def _cpu(*ts):
+    return [t.cpu() if isinstance(t, torch.Tensor) else t for t in ts]
+
+
+@pytest.mark.parametrize("mod", [True, False])
+@pytest.mark.parametrize("M,C,rpg", [(512, 1024, 256), (520, 768, 40), (96, 64, 96)])
+def test_rms_mod(mod, M, C, rpg):
+    from nano_gpic_b200.ops import norm
+    G = (M + rpg - 1) // rpg
+    x = torch.randn(M, C, device="cuda").bfloat16()
+    w = torch.rand(C, device="cuda") + 0.5
+    m = (torch.randn(G, 6 * C, device="cuda") * 0.3).bfloat16()
+    sh, sc = (m[:, :C], m[:, C:2 * C]) if mod else (None, None)
+    h, r = norm.rms_mod_fwd(x, w, sh, sc, rpg)
+    hc, rc = norm.rms_mod_fwd(*_cpu(x, w, sh, sc), rpg)
+    _close(h, hc, what="h")
+    _close(r, rc, rtol=1e-3, atol=1e-3, what="rstd")
+    dh = torch.randn(M, C, device="cuda").bfloat16()
+    dres = torch.randn(M, C, device="cuda").bfloat16()
+    dw = torch.zeros(C, device="cuda")
+    dmod = torch.zeros(G, 6 * C, device="cuda")
+    dx = norm.rms_mod_bwd(dh, x, r, w, sc, rpg, dres=dres, dw_acc=dw,
+                          dshift=dmod[:, :C] if mod else None, dscale=dmod[:, C:2 * C] if mod else None)
+    dwc = torch.zeros(C)
+    dmodc = torch.zeros(G, 6 * C)
+    dxc = norm.rms_mod_bwd(*_cpu(dh, x, rc, w, sc), rpg, dres=dres.cpu(), dw_acc=dwc,
+                           dshift=dmodc[:, :C] if mod else None, dscale=dmodc[:, C:2 * C] if mod else None)
+    _close(dx, dxc, what="dx")
+    _close(dw, dwc, rtol=1e-2, atol=1e-2, what="dw")
+    _close(dmod, dmodc, rtol=1e-2, atol=1e-2, what="dmod")
+
+
+def test_layernorm():
+    from nano_gpic_b200.ops import norm
+    x = (torch.randn(700, 1024, device="cuda") * 3 + 1).bfloat16()
+    h, mu, r = norm.layernorm_fwd(x)
+    hc, muc, rc = norm.layernorm_fwd(x.cpu())
+    _close(h, hc, what="h")
+    dh = torch.randn_like(x)
+    _close(norm.layernorm_bwd(dh, x, mu, r), norm.layernorm_bwd(dh.cpu(), x.cpu(), muc, rc), what="dx")
+
+
+@pytest.mark.parametrize("rope", [True, False])
+def test_qk_norm(rope):
+    from nano_gpic_b200.ops import qk
+    from nano_gpic_b200.models.layers import rope_tables
+    B, L, H = 3, 256, 4
+    qkv = torch.randn(B * L, 3 * H * 64, device="cuda").bfloat16()
+    src = qkv[:, H * 64:2 * H * 64]
+    w = torch.rand(64, device="cuda") + 0.5
+    cos, sin = rope_tables(64, 16, 16, device="cuda") if rope else (None, None)
+    out, r = qk.qk_norm_fwd(src, w, cos, sin, L)
+    outc, rc = qk.qk_norm_fwd(*_cpu(src, w, cos, sin), L)
+    _close(out, outc, what="out")
+    d = torch.randn_like(out)
+    dsrc = torch.zeros_like(qkv)
+    dw = torch.zeros(64, device="cuda")
+    qk.qk_norm_bwd(d, src, r, w, cos, sin, L, dsrc=dsrc[:, H * 64:2 * H * 64], dw_acc=dw)
+    dwc = torch.zeros(64)
+    dxc = qk.qk_norm_bwd(*_cpu(d, src, rc, w, cos, sin), L, dw_acc=dwc)
+    _close(dsrc[:, H * 64:2 * H * 64], dxc, what="dx")
+    assert dsrc[:, :H * 64].abs().max() == 0
+    _close(dw, dwc, rtol=1e-2, atol=1e-2, what="dw")
+
+
+@pytest.mark.parametrize("joint", [True, False])
+def test_attention(joint):
+    from nano_gpic_b200.ops import attention as A
+    torch.manual_seed(0)
+    B, H = 3, 2
+    C = H * 64
+    if joint:
+        Lq, L0, L1 = 256, 256, 72
+        n0 = 256
+        n1 = torch.tensor([72, 5, 40], dtype=torch.int32, device="cuda")
+    else:
+        Lq, L0, L1 = 72, 72, 0
+        n0 = torch.tensor([72, 9, 33], dtype=torch.int32, device="cuda")
+        n1 = None
+    qkv = torch.randn(B * Lq, 3 * C, device="cuda").bfloat16()
+    q, k0, v0 = qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:]
+    if joint:
+        kv = torch.randn(B * L1, 2 * C, device="cuda").bfloat16()
+        k1, v1 = kv[:, :C], kv[:, C:]
+    else:
+        k1 = v1 = None
+    o, lse = A.attn_fwd(q, Lq, k0, v0, L0, n0, k1, v1, L1, n1)
+    oc, lsec = A.attn_fwd(*_cpu(q), Lq, *_cpu(k0, v0), L0, n0 if isinstance(n0, int) else n0.cpu(),
+                          *_cpu(k1, v1), L1, n1.cpu() if n1 is not None else None)
+    _close(o, oc, what="o")
+    _close(lse, lsec, rtol=1e-3, atol=1e-3, what="lse")
+    do = torch.randn_like(o)
+    g = A.attn_bwd(do, q, Lq, k0, v0, L0, n0, o, lse, k1, v1, L1, n1)
+    gc = A.attn_bwd(*_cpu(do, q), Lq, *_cpu(k0, v0), L0, n0 if isinstance(n0, int) else n0.cpu(), *_cpu(oc, lsec, k1, v1),
+                    L1, n1.cpu() if n1 is not None else None)
+    for name, a, b in zip(["dq", "dk0", "dv0", "dk1", "dv1"], g, gc):
+        if a is None:
+            continue
+        _close(a, b, what=name)
