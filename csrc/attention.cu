@@ -16,6 +16,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "status.h"
 
 namespace ng {
 
@@ -581,7 +582,7 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0, c
   const int B = (int)(q.size(0) / Lq);
   dim3 grid((unsigned)((Lq + 63) / 64), (unsigned)(B * p.H));
   attn_fwd_kernel<<<grid, 128, 0, at::cuda::getCurrentCUDAStream()>>>(p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
 }
 
 void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0,
@@ -618,7 +619,7 @@ void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k0,
   const int64_t n = q.size(0) * (int64_t)p.H;
   attn_delta_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(p.dout, p.lddo, p.o, p.ldo, delta.data_ptr<float>(),
                                                                  (int)q.size(0), (int)Lq, p.H);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
   constexpr int kDkdvSmem = 49152 + 4 * 128 * 4;
   static bool attr = false;
   if (!attr) {
@@ -627,10 +628,10 @@ void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k0,
   }
   dim3 g1((unsigned)((p.L0 + p.L1 + 63) / 64), (unsigned)(B * p.H));
   attn_bwd_dkdv_kernel<<<g1, 128, kDkdvSmem, s>>>(p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
   dim3 g2((unsigned)((Lq + 63) / 64), (unsigned)(B * p.H));
   attn_bwd_dq_kernel<<<g2, 128, 0, s>>>(p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
 }
 
 }  // namespace ng

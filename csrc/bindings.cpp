@@ -64,5 +64,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("unpatchify", &ng::unpatchify);
   m.def("add_rows", &ng::add_rows);
   m.def("status_read", &ng::status_read, "read the device error word (synchronizes the current stream)");
+  m.def("launch_count", &ng::launch_count, "kernel launches issued by this extension so far (host count)");
   m.def("status_clear", &ng::status_clear, "clear the device error word");
 }

@@ -12,6 +12,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "status.h"
 
 namespace ng {
 
@@ -179,6 +180,15 @@ __global__ void fm_loss_reduce(const float* __restrict__ part, int nblk, float* 
   }
 }
 
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(bf16 v) { return __bfloat162float(v); }
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ bf16 from_f<bf16>(float v) { return __float2bfloat16_rn(v); }
+
 // tokens [B*N, Cin*p*p] (bf16) <-> image [B, Cin, H, W] (fp32 or bf16 out)
 template <typename Tin, typename Tout, bool TO_TOKENS>
 __global__ void patch_kernel(const Tin* __restrict__ src, Tout* __restrict__ dst, int B, int Cin, int H, int W, int p) {
@@ -192,9 +202,9 @@ __global__ void patch_kernel(const Tin* __restrict__ src, Tout* __restrict__ dst
   const int c = e / (p * p), py = (e / p) % p, px = e % p;
   const int64_t pix = (((int64_t)b * Cin + c) * H + (n / gw) * p + py) * W + (n % gw) * p + px;
   if (TO_TOKENS)
-    dst[i] = (Tout)(float)src[pix];
+    dst[i] = from_f<Tout>(to_f(src[pix]));
   else
-    dst[pix] = (Tout)(float)src[i];
+    dst[pix] = from_f<Tout>(to_f(src[i]));
 }
 
 // out[row] = bf16(a[row] + table[row % period]) (fp32 or bf16 table [period, C])
@@ -210,7 +220,7 @@ __global__ void add_rows_kernel(const bf16* __restrict__ a, const TT* __restrict
   u8(*reinterpret_cast<const uint4*>(a + row * C + c0), f);
   const TT* tr = table + (int64_t)(row % period) * C + c0;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) f[j] += (float)tr[j];
+  for (int j = 0; j < 8; ++j) f[j] += to_f(tr[j]);
   *reinterpret_cast<uint4*>(out + row * C + c0) = p8(f);
 }
 
@@ -230,12 +240,12 @@ void gate_bwd(const at::Tensor& dout, const at::Tensor& y, const at::Tensor& gat
       reinterpret_cast<const bf16*>(dout.data_ptr()), reinterpret_cast<const bf16*>(y.data_ptr()),
       reinterpret_cast<const bf16*>(gate.data_ptr()), gate.stride(0), reinterpret_cast<bf16*>(dy.data_ptr()),
       part.data_ptr<float>(), M, C, (int)rpg);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
   float* dg = (dgate.has_value() && dgate->defined()) ? dgate->data_ptr<float>() : nullptr;
   float* db = (dbias.has_value() && dbias->defined()) ? dbias->data_ptr<float>() : nullptr;
   gate_bwd_reduce<<<(C + 255) / 256, 256, 0, s>>>(part.data_ptr<float>(), G, chunks, C, dg,
                                                    dg ? dgate->stride(0) : 0, db);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
 }
 
 void fm_prep(const at::Tensor& x, const at::Tensor& noise, const at::Tensor& t, const at::Tensor& xt_tok, int64_t p) {
@@ -247,7 +257,7 @@ void fm_prep(const at::Tensor& x, const at::Tensor& noise, const at::Tensor& t, 
   fm_prep_kernel<<<(unsigned)((groups + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       x.data_ptr<float>(), noise.data_ptr<float>(), t.data_ptr<float>(), reinterpret_cast<bf16*>(xt_tok.data_ptr()),
       B, Cin, H, W, (int)p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
 }
 
 void fm_loss(const at::Tensor& pred, const at::Tensor& x, const at::Tensor& noise, const at::Tensor& t,
@@ -264,10 +274,10 @@ void fm_loss(const at::Tensor& pred, const at::Tensor& x, const at::Tensor& nois
                                                noise.data_ptr<float>(), t.data_ptr<float>(), dp,
                                                part.data_ptr<float>(), Cin, H, W, (int)p, (float)t_eps,
                                                (float)grad_scale);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
   fm_loss_reduce<<<B, 32, 0, s>>>(part.data_ptr<float>(), nblk, per_sample.data_ptr<float>(),
                                   1.f / (float)(x.numel() / B));
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
 }
 
 void patchify(const at::Tensor& img, const at::Tensor& tok, int64_t p) {
@@ -282,7 +292,7 @@ void patchify(const at::Tensor& img, const at::Tensor& tok, int64_t p) {
   else
     patch_kernel<bf16, bf16, true><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
         reinterpret_cast<const bf16*>(img.data_ptr()), reinterpret_cast<bf16*>(tok.data_ptr()), B, Cin, H, W, (int)p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
 }
 
 void unpatchify(const at::Tensor& tok, const at::Tensor& img, int64_t p) {
@@ -296,7 +306,7 @@ void unpatchify(const at::Tensor& tok, const at::Tensor& img, int64_t p) {
   else
     patch_kernel<bf16, bf16, false><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
         reinterpret_cast<const bf16*>(tok.data_ptr()), reinterpret_cast<bf16*>(img.data_ptr()), B, Cin, H, W, (int)p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
 }
 
 void add_rows(const at::Tensor& a, const at::Tensor& table, const at::Tensor& out, int64_t period) {
@@ -315,7 +325,7 @@ void add_rows(const at::Tensor& a, const at::Tensor& table, const at::Tensor& ou
     add_rows_kernel<bf16><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
         reinterpret_cast<const bf16*>(a.data_ptr()), reinterpret_cast<const bf16*>(table.data_ptr()),
         reinterpret_cast<bf16*>(out.data_ptr()), rows, C, (int)period);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
 }
 
 }  // namespace ng

@@ -22,6 +22,7 @@
 
 #include "common.cuh"
 #include "gemm.h"
+#include "status.h"
 
 namespace ng {
 
@@ -52,6 +53,8 @@ struct EpiParams {
   int64_t ld_aux;
   float alpha, beta;
   int accumulate;
+  int k_splits;      // >1: split-K, each split writes its own fp32 slice out + split * out_bs
+  int kb_per_split;  // k-blocks (of BK) per split
   int* err;
 };
 
@@ -152,7 +155,9 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
   const int num_m = (p.M + BM - 1) / BM;
   const int num_n = (EPI == EPI_SWIGLU) ? (p.half_n + 127) / 128 : (p.N + BN - 1) / BN;
   const int num_k = (p.K + BK - 1) / BK;
-  const int total = p.batch * num_m * num_n;
+  const int splits = p.k_splits > 1 ? p.k_splits : 1;
+  const int kps = splits > 1 ? p.kb_per_split : num_k;
+  const int total = p.batch * splits * num_m * num_n;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -187,9 +192,11 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
       uint32_t phase = 0;
       int issued = 0;  // stages filled since the start (for draining on abort)
       for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
-        int b, mb, nb;
-        tile_coords(t, num_m, num_n, b, mb, nb);
-        for (int kb = 0; kb < num_k; ++kb) {
+        int bs, mb, nb;
+        tile_coords(t, num_m, num_n, bs, mb, nb);
+        const int b = bs / splits, sp = bs - b * splits;
+        const int kb0 = sp * kps, kb1 = min(num_k, kb0 + kps);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
           uint8_t* sA = smem + stage * STAGE_BYTES;
           uint8_t* sB = sA + A_BYTES;
@@ -257,7 +264,9 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + a * BN;
         bool ok = true;
-        for (int kb = 0; kb < num_k; ++kb) {
+        const int sp = (t / (num_m * num_n)) % splits;
+        const int kb0 = sp * kps, kb1 = min(num_k, kb0 + kps);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.err, kErrWaitFull)) {
             ok = false;
             break;
@@ -271,7 +280,7 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
                                          : smem_desc_sw128(sa + k * 2048, 8192, 1024);
             const uint64_t db = BMN == 0 ? smem_desc_sw128(sb + k * 32, 16, 1024)
                                          : smem_desc_sw128(sb + k * 2048, 8192, 1024);
-            umma_f16(d_tmem, da, db, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16(d_tmem, da, db, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           issued_any = true;
           umma_commit(&empty[stage]);
@@ -452,6 +461,35 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
+static bool trace_on() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("NG_TRACE");
+    v = (e != nullptr && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+#define NG_TRACE(...)                   \
+  do {                                  \
+    if (trace_on()) {                   \
+      fprintf(stderr, __VA_ARGS__);     \
+      fflush(stderr);                   \
+    }                                   \
+  } while (0)
+
+// cuTensorMapEncodeTiled is a driver-API call and needs a current context in the calling thread. A fresh autograd
+// worker thread whose first CUDA work is this call has none (torch's device guard skips cudaSetDevice when the index
+// already matches), and the driver then crashes; so make the primary context current once per thread.
+static void ensure_context() {
+  thread_local bool ready = false;
+  if (ready) return;
+  int dev = 0;
+  TORCH_CHECK(cudaGetDevice(&dev) == cudaSuccess, "cudaGetDevice failed");
+  TORCH_CHECK(cudaSetDevice(dev) == cudaSuccess, "cudaSetDevice failed");
+  TORCH_CHECK(cudaFree(nullptr) == cudaSuccess, "CUDA context initialisation failed");
+  ready = true;
+}
+
 // A 3-D bf16 tensor map (inner, outer, batch) with a 128-byte swizzle; inner is contiguous.
 CUtensorMap make_tmap_bf16(const void* ptr, int64_t inner, int64_t outer, int64_t batch, int64_t ld, int64_t bstride,
                            int box_inner, int box_outer) {
@@ -463,9 +501,13 @@ CUtensorMap make_tmap_bf16(const void* ptr, int64_t inner, int64_t outer, int64_
   TORCH_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base address must be 16-byte aligned");
   TORCH_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes, got ld=", ld);
   TORCH_CHECK(batch == 1 || (bstride * 2) % 16 == 0, "TMA batch stride must be a multiple of 16 bytes");
+  ensure_context();
+  NG_TRACE("[tmap] ptr=%p inner=%lld outer=%lld batch=%lld ld=%lld box=%dx%d m@%p\n", ptr, (long long)inner,
+           (long long)outer, (long long)batch, (long long)ld, box_inner, box_outer, (void*)&m);
   CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  NG_TRACE("[tmap]   encode -> %d\n", (int)r);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
   return m;
 }
@@ -489,7 +531,7 @@ static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const EpiPara
     attr_set = true;
   }
   kern<<<grid, gemm_cfg::THREADS, gemm_cfg::SMEM_BYTES, s>>>(ta, tb, p);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
 }
 
 template <int AMN, int BMN>
@@ -509,6 +551,9 @@ static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, 
 void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   using namespace gemm_cfg;
   TORCH_CHECK(g.M > 0 && g.N > 0 && g.K > 0 && g.batch > 0, "empty GEMM");
+  NG_TRACE("[gemm] M=%d N=%d K=%d batch=%d a_mn=%d b_mn=%d epi=%d lda=%lld ldb=%lld ldo=%lld splits=%d A=%p B=%p out=%p\n",
+           g.M, g.N, g.K, g.batch, g.a_mn, g.b_mn, g.epi, (long long)g.lda, (long long)g.ldb, (long long)g.ldo,
+           g.k_splits, g.A, g.B, g.out);
   // operand tensor maps: K-major [rows, K] boxes of 64 x 128; MN-major [K, rows] boxes of 64 x 64
   CUtensorMap ta = g.a_mn ? make_tmap_bf16(g.A, g.M, g.K, g.batch, g.lda, g.a_bs, 64, 64)
                           : make_tmap_bf16(g.A, g.K, g.M, g.batch, g.lda, g.a_bs, 64, 128);
@@ -538,11 +583,14 @@ void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   p.alpha = g.alpha;
   p.beta = g.beta;
   p.accumulate = g.accumulate;
+  p.k_splits = g.k_splits > 1 ? g.k_splits : 1;
+  p.kb_per_split = g.kb_per_split;
   p.err = g.err;
   const int num_m = (g.M + BM - 1) / BM;
   const int num_n = g.epi == EPI_SWIGLU ? (g.half_n + 127) / 128 : (g.N + BN - 1) / BN;
-  const int64_t tiles = (int64_t)g.batch * num_m * num_n;
+  const int64_t tiles = (int64_t)g.batch * (g.k_splits > 1 ? g.k_splits : 1) * num_m * num_n;
   const int grid = (int)std::min<int64_t>(tiles, num_sms());
+  NG_TRACE("[gemm]   maps ok, grid=%d tiles=%lld\n", grid, (long long)tiles);
   if (!g.a_mn && !g.b_mn)
     dispatch_epi<0, 0>(g.epi, ta, tb, p, grid, stream);
   else if (!g.a_mn && g.b_mn)
@@ -551,6 +599,7 @@ void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     dispatch_epi<1, 1>(g.epi, ta, tb, p, grid, stream);
   else
     dispatch_epi<1, 0>(g.epi, ta, tb, p, grid, stream);
+  NG_TRACE("[gemm]   launched\n");
 }
 
 }  // namespace ng
@@ -559,6 +608,30 @@ void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
 #include "status.h"
 
 namespace ng {
+
+// out[i] (+)= sum_s ws[s * n + i], splits summed in order (deterministic)
+__global__ void splitk_reduce_kernel(const float4* __restrict__ ws, int splits, int64_t n4, float4* __restrict__ out,
+                                     int accumulate) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n4) return;
+  float4 a = accumulate ? out[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < splits; ++s) {
+    const float4 v = ws[s * n4 + i];
+    a.x += v.x;
+    a.y += v.y;
+    a.z += v.z;
+    a.w += v.w;
+  }
+  out[i] = a;
+}
+
+static void splitk_reduce(const float* ws, int splits, int64_t n, float* out, bool accumulate, cudaStream_t s) {
+  TORCH_CHECK(n % 4 == 0, "split-K reduce needs a multiple of 4 elements");
+  const int64_t n4 = n / 4;
+  splitk_reduce_kernel<<<(unsigned)((n4 + 255) / 256), 256, 0, s>>>(reinterpret_cast<const float4*>(ws), splits, n4,
+                                                                   reinterpret_cast<float4*>(out), accumulate ? 1 : 0);
+  NG_LAUNCH_CHECK();
+}
 
 static const void* ptr_or_null(const c10::optional<at::Tensor>& t) {
   return (t.has_value() && t->defined()) ? t->data_ptr() : nullptr;
@@ -576,6 +649,11 @@ void gemm_torch(const at::Tensor& A, bool a_mn, int64_t lda, int64_t a_bs, const
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: bf16 operands expected");
   if (bias.has_value() && bias->defined()) TORCH_CHECK(bias->scalar_type() == at::kFloat, "gemm: fp32 bias expected");
   const at::cuda::CUDAGuard guard(A.device());
+  NG_TRACE("[gemm_torch] enter epi=%lld M=%lld N=%lld K=%lld\n", (long long)epi, (long long)M, (long long)N, (long long)K);
+  if (trace_on()) {
+    const cudaError_t pre = cudaDeviceSynchronize();
+    NG_TRACE("[gemm_torch]   device state before: %s\n", cudaGetErrorString(pre));
+  }
   GemmArgs g;
   g.M = (int)M;
   g.N = (int)N;
@@ -610,7 +688,31 @@ void gemm_torch(const at::Tensor& A, bool a_mn, int64_t lda, int64_t a_bs, const
   g.beta = (float)beta;
   g.accumulate = accumulate ? 1 : 0;
   g.err = status_word();
-  gemm_launch(g, at::cuda::getCurrentCUDAStream());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  // Weight gradients with few output tiles (e.g. a 1024 x 1024 dW is 32 tiles for 148 SMs) but a long reduction
+  // (all tokens): split K over CTAs, each split writes an fp32 slice, then one ordered reduction adds the slices.
+  const int64_t tiles = (int64_t)((M + 127) / 128) * ((N + 255) / 256);
+  const int64_t nkb = (K + 63) / 64;
+  if (epi == EPI_F32 && batch == 1 && tiles * 2 <= num_sms() && nkb >= 16 && ldo == N) {
+    int splits = (int)std::min<int64_t>(num_sms() / tiles, nkb / 8);
+    const int kps = (int)((nkb + splits - 1) / splits);
+    splits = (int)((nkb + kps - 1) / kps);
+    if (splits > 1) {
+      at::Tensor ws = at::empty({(int64_t)splits * M * N}, out.options().dtype(at::kFloat));
+      g.out = ws.data_ptr();
+      g.ldo = N;
+      g.out_bs = M * N;
+      g.accumulate = 0;
+      g.k_splits = splits;
+      g.kb_per_split = kps;
+      gemm_launch(g, stream);
+      NG_TRACE("[gemm]   split-K reduce splits=%d n=%lld\n", splits, (long long)(M * N));
+      splitk_reduce(ws.data_ptr<float>(), splits, M * N, out.data_ptr<float>(), accumulate, stream);
+      NG_TRACE("[gemm]   reduce launched\n");
+      return;
+    }
+  }
+  gemm_launch(g, stream);
 }
 
 }  // namespace ng

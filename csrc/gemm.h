@@ -44,6 +44,7 @@ struct GemmArgs {
   int half_n = 0;
   float alpha = 1.f, beta = 0.f;
   int accumulate = 0;
+  int k_splits = 1, kb_per_split = 0;
   int* err = nullptr;
 };
 

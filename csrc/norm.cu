@@ -11,6 +11,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "status.h"
 
 namespace ng {
 
@@ -346,7 +347,7 @@ void rms_mod_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<a
     rms_mod_fwd_kernel<false><<<grid, 256, 0, s>>>(reinterpret_cast<const bf16*>(x.data_ptr()), w.data_ptr<float>(),
                                                    nullptr, 0, nullptr, 0, reinterpret_cast<bf16*>(h.data_ptr()),
                                                    rstd.data_ptr<float>(), M, C, (int)rpg, (float)eps);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
 }
 
 void rms_mod_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& rstd, const at::Tensor& w,
@@ -374,13 +375,13 @@ void rms_mod_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& rs
         reinterpret_cast<const bf16*>(dh.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),
         rstd.data_ptr<float>(), w.data_ptr<float>(), nullptr, 0, bptr(dres), reinterpret_cast<bf16*>(dx.data_ptr()),
         part.data_ptr<float>(), M, C, rows_per_group);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
   float* dsh = (dshift.has_value() && dshift->defined()) ? dshift->data_ptr<float>() : nullptr;
   float* dsc = (dscale.has_value() && dscale->defined()) ? dscale->data_ptr<float>() : nullptr;
   float* dwp = (dw.has_value() && dw->defined()) ? dw->data_ptr<float>() : nullptr;
   rms_mod_bwd_reduce<<<(C + 255) / 256, 256, 0, s>>>(part.data_ptr<float>(), G, chunks, C, mod ? dsh : nullptr,
                                                       ld_of(dshift), mod ? dsc : nullptr, ld_of(dscale), dwp);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
 }
 
 void layernorm_fwd(const at::Tensor& x, const at::Tensor& h, const at::Tensor& mu, const at::Tensor& rstd, double eps) {
@@ -390,7 +391,7 @@ void layernorm_fwd(const at::Tensor& x, const at::Tensor& h, const at::Tensor& m
   layernorm_fwd_kernel<<<(M + 7) / 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const bf16*>(x.data_ptr()), reinterpret_cast<bf16*>(h.data_ptr()), mu.data_ptr<float>(),
       rstd.data_ptr<float>(), M, C, (float)eps);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
 }
 
 void layernorm_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& mu, const at::Tensor& rstd,
@@ -401,7 +402,7 @@ void layernorm_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& 
   layernorm_bwd_kernel<<<(M + 7) / 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const bf16*>(dh.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()), mu.data_ptr<float>(),
       rstd.data_ptr<float>(), reinterpret_cast<bf16*>(dx.data_ptr()), M, C);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
 }
 
 }  // namespace ng

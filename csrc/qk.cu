@@ -8,6 +8,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "status.h"
 
 namespace ng {
 
@@ -162,7 +163,7 @@ void qk_norm_fwd(const at::Tensor& src, const at::Tensor& w, const c10::optional
   else
     qk_norm_fwd_kernel<false><<<grid, 256, 0, s>>>(sp, src.stride(0), w.data_ptr<float>(), nullptr, nullptr, op,
                                                    rstd.data_ptr<float>(), rows, H, (int)L, (float)eps);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
 }
 
 void qk_norm_bwd(const at::Tensor& dout, const at::Tensor& src, const at::Tensor& rstd, const at::Tensor& w,
@@ -186,10 +187,10 @@ void qk_norm_bwd(const at::Tensor& dout, const at::Tensor& src, const at::Tensor
     qk_norm_bwd_kernel<false><<<grid, 256, 0, s>>>(dp, sp, src.stride(0), rstd.data_ptr<float>(), w.data_ptr<float>(),
                                                    nullptr, nullptr, op, dsrc.stride(0), part.data_ptr<float>(), rows,
                                                    H, (int)L);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  NG_LAUNCH_CHECK();
   if (dw.has_value() && dw->defined()) {
     reduce_cols_kernel<<<1, 64, 0, s>>>(part.data_ptr<float>(), grid, 64, dw->data_ptr<float>());
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    NG_LAUNCH_CHECK();
   }
 }
 

@@ -4,6 +4,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <torch/extension.h>
 
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -35,6 +36,10 @@ int64_t status_read() {
   TORCH_CHECK(cudaStreamSynchronize(stream) == cudaSuccess);
   return v;
 }
+
+static std::atomic<int64_t> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+int64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
 void status_clear() {
   auto stream = at::cuda::getCurrentCUDAStream();

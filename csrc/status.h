@@ -6,4 +6,17 @@ namespace ng {
 int* status_word();
 int64_t status_read();
 void status_clear();
+// Host-side count of kernel launches issued by this extension (the benchmark's launch claim).
+void note_launch();
+int64_t launch_count();
+}  // namespace ng
+
+#include <c10/cuda/CUDAException.h>
+// Checks the launch just issued and counts it.
+#define NG_LAUNCH_CHECK()            \
+  do {                               \
+    C10_CUDA_KERNEL_LAUNCH_CHECK();  \
+    ::ng::note_launch();             \
+  } while (0)
+namespace ng {
 }  // namespace ng

@@ -62,7 +62,7 @@ def fm_prep(x, noise, t, p):
         return patchify(tt * x + noise * (1 - tt), p)
     B, Cin, H, W = x.shape
     tok = torch.empty(B * (H // p) * (W // p), Cin * p * p, device=x.device, dtype=torch.bfloat16)
-    ext().fm_prep(x, noise, t.float().contiguous(), tok, p)
+    ext().fm_prep(x.float().contiguous(), noise.float().contiguous(), t.float().contiguous(), tok, p)
     return tok
 
 
@@ -84,7 +84,8 @@ def fm_loss(pred_tok, x, noise, t, p, t_eps=0.05, grad_scale=None, need_grad=Tru
         return per, g
     per = torch.empty(B, device=x.device, dtype=torch.float32)
     g = torch.empty_like(pred_tok) if need_grad else None
-    ext().fm_loss(pred_tok, x, noise, t.float().contiguous(), g, per, p, t_eps, grad_scale)
+    ext().fm_loss(pred_tok.contiguous(), x.float().contiguous(), noise.float().contiguous(), t.float().contiguous(), g,
+                  per, p, t_eps, grad_scale)
     return per, g
 
 

@@ -1,0 +1,221 @@
+"""Muon for the hidden matrices of the transformer blocks, AdamW for every other parameter.
+
+Same constructor, param groups, state names (momentum_buffer; step/exp_avg/exp_avg_sq) and update rules as the
+reference's MuonAdamW (baselines/PixelGen/src/optim/muon.py:102-254), so optimizer checkpoints are interchangeable:
+    m <- beta m + (1 - beta) g                  (beta = 0.95)
+    u <- (1 - beta) g + beta m                  (Nesterov)
+    O <- msign(u)                               5 quintic Newton-Schulz steps in bf16, coefficients (3.4445, -4.7750,
+                                                2.0315), Frobenius normalisation + 1e-7, transposed when tall
+    W <- (1 - lr wd) W - lr * coef * O          coef = sqrt(rows / cols) ("mup") or 0.2 sqrt(max) ("moonlight")
+With split=True each fused matrix is cut along d_out into its parts (q,k,v; k,v; gate,up; the six adaLN vectors) and
+each part ("unit") is orthogonalised on its own (tag_muon_params, reference muon.py:43-61).
+
+Newton-Schulz runs on the tcgen05 GEMM (nano_gpic_b200.ops.gemm.bmm_axpby), batched per unit shape, each step three
+GEMMs with the scalings fused in the epilogue: A = X X^T, B = b A + c A A, X = a X + B X (the reference's lever NS,
+muon.py:64-86). Units are owned by ranks with the reference's longest-processing-time plan (muon.py:150-175); with one
+rank every unit is local. The distributed exchange lives in nano_gpic_b200.parallel.muon_dist.
+"""
+import math
+
+import torch
+import torch.distributed as dist
+
+from ..ops import gemm as G
+
+NS_COEFFS = (3.4445, -4.7750, 2.0315)
+FUSED_PARTS = {"attn.qkv_x.weight": 3, "attn.qkv.weight": 3, "attn.kv_y.weight": 2, "mlp.w12.weight": 2,
+               "adaLN_modulation.0.weight": 6}
+
+
+def tag_muon_params(model, prefixes=("blocks.", "text_refine_blocks.")):
+    """Mark the 2-D weights inside the transformer blocks for Muon (p._muon_parts = fused parts along d_out).
+    Returns (n_tagged, numel_tagged)."""
+    n = numel = 0
+    for name, p in model.named_parameters():
+        if p.ndim != 2 or not p.requires_grad or not name.startswith(prefixes):
+            continue
+        parts = next((k for suffix, k in FUSED_PARTS.items() if name.endswith(suffix)), 1)
+        assert p.shape[0] % parts == 0, (name, tuple(p.shape), parts)
+        p._muon_parts = parts
+        p._muon_name = name
+        n += 1
+        numel += p.numel()
+    return n, numel
+
+
+@torch.no_grad()
+def msign(Gm, steps=5, dtype=torch.bfloat16, fused=True):
+    """Orthogonalise each matrix of Gm [..., a, b] with the quintic Newton-Schulz iteration. bf16 CUDA inputs run on
+    the tcgen05 GEMM with fused alpha/beta epilogues; other dtypes/devices use torch (the fp32 path is the exact
+    reference for tests)."""
+    a, b, c = NS_COEFFS
+    X = Gm.to(dtype)
+    tall = Gm.size(-2) > Gm.size(-1)
+    if tall:
+        X = X.mT
+    X = X / (X.norm(dim=(-2, -1), keepdim=True) + 1e-7)
+    if X.is_cuda and dtype == torch.bfloat16 and fused:
+        squeeze = X.dim() == 2
+        X = (X.unsqueeze(0) if squeeze else X).contiguous()
+        for _ in range(steps):
+            A = G.bmm_axpby(X, X, False)                       # X X^T
+            B = G.bmm_axpby(A, A, False, alpha=c, beta=b, C=A)  # b A + c A A  (A symmetric)
+            X = G.bmm_axpby(B, X, True, alpha=1.0, beta=a, C=X)  # a X + B X
+        X = X[0] if squeeze else X
+        return X.mT if tall else X
+    for _ in range(steps):
+        A = X @ X.mT
+        B = b * A + c * (A @ A)
+        X = a * X + B @ X
+    return X.mT if tall else X
+
+
+class MuonAdamW(torch.optim.Optimizer):
+    def __init__(self, params, lr=1e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, muon_lr=None,
+                 muon_weight_decay=None, muon_momentum=0.95, muon_nesterov=True, ns_steps=5, split=False,
+                 fused_adamw=True, ns_dtype="bfloat16", update_scale="mup"):
+        assert update_scale in ("mup", "moonlight"), update_scale
+        groups = list(params)
+        if groups and not isinstance(groups[0], dict):
+            groups = [{"params": groups}]
+        adam_groups, muon_params = [], []
+        for g in groups:
+            ps = list(g["params"])
+            muon_params += [p for p in ps if hasattr(p, "_muon_parts")]
+            rest = [p for p in ps if not hasattr(p, "_muon_parts")]
+            if rest:
+                adam_groups.append({**g, "params": rest, "use_muon": False, "fused": fused_adamw})
+        all_groups = adam_groups
+        if muon_params:
+            all_groups = all_groups + [{
+                "params": muon_params, "use_muon": True,
+                "lr": muon_lr if muon_lr is not None else lr,
+                "weight_decay": muon_weight_decay if muon_weight_decay is not None else weight_decay,
+                "momentum": muon_momentum, "nesterov": muon_nesterov, "ns_steps": ns_steps, "split": split,
+                "update_scale": update_scale}]
+        defaults = dict(lr=lr, betas=tuple(betas), eps=eps, weight_decay=weight_decay, use_muon=False)
+        super().__init__(all_groups, defaults)
+        self.fused_adamw = fused_adamw
+        self.ns_dtype = getattr(torch, ns_dtype)
+        self._plan = None
+        self.exchange = None  # set by nano_gpic_b200.parallel.muon_dist for multi-rank runs
+
+    @staticmethod
+    def update_coef(group, shape):
+        rows, cols = shape
+        if group.get("update_scale", "moonlight") == "mup":
+            return math.sqrt(rows / cols)
+        return 0.2 * math.sqrt(max(rows, cols))
+
+    def _build_plan(self, group):
+        """Units (matrix parts), their owner ranks (longest processing time first, cost rows*cols*min) and offsets in
+        each owner's flat slot. Deterministic on every rank."""
+        world = dist.get_world_size() if dist.is_initialized() else 1
+        units = []
+        for i, p in enumerate(group["params"]):
+            parts = p._muon_parts if group["split"] else 1
+            rows = p.shape[0] // parts
+            for k in range(parts):
+                units.append({"p": i, "r0": k * rows, "r1": (k + 1) * rows, "shape": (rows, p.shape[1])})
+        load = [0.0] * world
+        order = sorted(range(len(units)), key=lambda j: (-math.prod(units[j]["shape"]) * min(units[j]["shape"]), j))
+        for j in order:
+            r = min(range(world), key=lambda q: (load[q], q))
+            units[j]["owner"] = r
+            load[r] += math.prod(units[j]["shape"]) * min(units[j]["shape"])
+        offsets = [0] * world
+        for u in units:
+            u["off"] = offsets[u["owner"]]
+            offsets[u["owner"]] += math.prod(u["shape"])
+        shard = max(offsets) if offsets else 0
+        rank = dist.get_rank() if dist.is_initialized() else 0
+        mine = {}
+        for u in units:
+            if u["owner"] == rank:
+                mine.setdefault(u["shape"], []).append(u)
+        return {"world": world, "rank": rank, "units": units, "shard": shard, "mine": mine}
+
+    @torch.no_grad()
+    def _muon_step(self, group):
+        params = group["params"]
+        grads, bufs = [], []
+        for p in params:
+            g = p.grad if p.grad is not None else torch.zeros_like(p)
+            st = self.state[p]
+            if "momentum_buffer" not in st:
+                st["momentum_buffer"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+            grads.append(g)
+            bufs.append(st["momentum_buffer"])
+        beta, lr, wd = group["momentum"], group["lr"], group["weight_decay"]
+        torch._foreach_lerp_(bufs, grads, 1 - beta)
+        if self._plan is None:
+            self._plan = self._build_plan(group)
+        plan = self._plan
+        dev = params[0].device
+        shard = torch.zeros(plan["shard"], dtype=self.ns_dtype, device=dev)
+        for shape, us in plan["mine"].items():
+            ins = []
+            for u in us:
+                g, m = grads[u["p"]][u["r0"]:u["r1"]], bufs[u["p"]][u["r0"]:u["r1"]]
+                ins.append(g.lerp(m, beta) if group["nesterov"] else m)
+            O = msign(torch.stack(ins), steps=group["ns_steps"], dtype=self.ns_dtype)
+            for u, o in zip(us, O):
+                shard[u["off"]:u["off"] + o.numel()].copy_(o.reshape(-1))
+        if plan["world"] > 1:
+            full = self.exchange(shard, plan) if self.exchange is not None else self._all_gather(shard, plan)
+        else:
+            full = shard
+        if wd:
+            torch._foreach_mul_(params, 1 - lr * wd)
+        for u in plan["units"]:
+            o0 = u["owner"] * plan["shard"] + u["off"]
+            src = full[o0:o0 + math.prod(u["shape"])].view(u["shape"])
+            params[u["p"]][u["r0"]:u["r1"]].add_(src, alpha=-lr * self.update_coef(group, u["shape"]))
+
+    @staticmethod
+    def _all_gather(shard, plan):
+        full = torch.empty(plan["world"] * plan["shard"], dtype=shard.dtype, device=shard.device)
+        dist.all_gather_into_tensor(full, shard)
+        return full
+
+    @torch.no_grad()
+    def _adamw_step(self, group):
+        from torch.optim.adam import adam as _adam_fn
+        params, grads, m1, m2, steps = [], [], [], [], []
+        for p in group["params"]:
+            if p.grad is None:
+                continue
+            st = self.state[p]
+            if not st:
+                st["step"] = (torch.zeros((), dtype=torch.float32, device=p.device) if self.fused_adamw
+                              else torch.tensor(0.0, dtype=torch.float32))
+                st["exp_avg"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+                st["exp_avg_sq"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+            if self.fused_adamw and st["step"].device != p.device:
+                st["step"] = st["step"].to(p.device, torch.float32)
+            params.append(p)
+            grads.append(p.grad)
+            m1.append(st["exp_avg"])
+            m2.append(st["exp_avg_sq"])
+            steps.append(st["step"])
+        if not params:
+            return
+        b1, b2 = group["betas"]
+        fused = self.fused_adamw and params[0].is_cuda
+        _adam_fn(params, grads, m1, m2, [], steps, foreach=None if fused else True, capturable=False,
+                 differentiable=False, fused=fused or None, grad_scale=None, found_inf=None, has_complex=False,
+                 decoupled_weight_decay=True, amsgrad=False, beta1=b1, beta2=b2, lr=group["lr"],
+                 weight_decay=group["weight_decay"], eps=group["eps"], maximize=False)
+
+    @torch.no_grad()
+    def step(self, closure=None):
+        loss = None
+        if closure is not None:
+            with torch.enable_grad():
+                loss = closure()
+        for group in self.param_groups:
+            if group.get("use_muon"):
+                self._muon_step(group)
+            else:
+                self._adamw_step(group)
+        return loss

@@ -1,0 +1,119 @@
+"""The training step: gradient accumulation over micro-batches, data-parallel gradient reduction, global-norm clip,
+Muon/AdamW update, LR schedule and the bf16 weight refresh, with no host synchronisation inside a step.
+
+This is the part of the reference's Lightning loop that runs per optimizer step
+(baselines/PixelGen/src/lightning_model_gpic.py:147-174 clip, :287-350 training_step; Lightning's automatic
+optimisation with accumulate_grad_batches and DDP/FSDP2 strategies), as one plain Python object.
+
+    tr = Trainer.for_ladder("d12", world=dist_world, rank=rank)      # model, optimizer, schedule of the ladder size
+    loss = tr.train_step(images_u8, captions, caption_mask)          # one optimizer step over this rank's images
+"""
+import math
+
+import torch
+import torch.distributed as dist
+
+from ..config.ladder import GLOBAL_BATCH, SIZES
+from ..diffusion.flow_matching import JiTTrainer
+from ..models.jit_t2i import JiT_T2I
+from ..optim.lr_scheduler import WarmupFlatCooldown
+from ..optim.muon import MuonAdamW, tag_muon_params
+from ..parallel.flat import FlatParams
+
+
+def uint8_to_float(img):
+    """uint8 HWC [B, H, W, 3] -> fp32 CHW in [-1, 1]: ToTensor then Normalize(0.5, 0.5), as the reference's lever D
+    (baselines/PixelGen/src/data/dataset/gpic_dataset.py:869-881)."""
+    return (((img.permute(0, 3, 1, 2).float() / 255.0) - 0.5) / 0.5).contiguous()
+
+
+class Trainer:
+    def __init__(self, model, optimizer, scheduler=None, objective=None, accum=1, clip=1.0, flat=None, dp=None):
+        self.model = model
+        self.opt = optimizer
+        self.sched = scheduler
+        self.obj = objective or JiTTrainer()
+        self.accum = accum
+        self.clip = clip
+        self.flat = flat
+        self.dp = dp  # a nano_gpic_b200.parallel data-parallel reducer, or None
+        self.global_step = 0
+        self.copy_stream = None
+
+    # --------------------------------------------------------------------------------------------- construction
+    @classmethod
+    def for_ladder(cls, size="d12", device="cuda", world=1, rank=0, micro_batch=None, global_batch=GLOBAL_BATCH,
+                   max_steps=None, dp="nccl", seed=0, model_kwargs=None):
+        s = SIZES[size]
+        torch.manual_seed(seed)
+        kw = s.model_kwargs()
+        kw.update(model_kwargs or {})
+        model = JiT_T2I(**kw).to(device)
+        tag_muon_params(model)
+        flat = FlatParams(model, device=device)
+        mb = micro_batch or s.micro_batch
+        per_rank = global_batch // world
+        assert per_rank % mb == 0, (global_batch, world, mb)
+        opt = MuonAdamW([{"params": [p for p in model.parameters() if p.requires_grad]}], lr=s.adamw_lr,
+                        betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, muon_lr=s.muon_lr, muon_weight_decay=s.muon_wd,
+                        muon_momentum=0.95, muon_nesterov=True, ns_steps=5, split=True, fused_adamw=True,
+                        ns_dtype="bfloat16", update_scale="mup")
+        steps = max_steps or s.steps
+        wu, cd = s.schedule()
+        sched = WarmupFlatCooldown(wu, cd, steps, min_lr=3e-5)(opt)
+        reducer = None
+        if world > 1:
+            from ..parallel.ddp import GradReducer
+            reducer = GradReducer(flat, mode=dp)
+            reducer.broadcast_params(0)
+        return cls(model, opt, sched, JiTTrainer(), accum=per_rank // mb, clip=1.0, flat=flat, dp=reducer)
+
+    # --------------------------------------------------------------------------------------------------- step
+    def _to_device(self, t, dev):
+        if t.device == dev:
+            return t
+        return t.to(dev, non_blocking=True)
+
+    def train_step(self, images, captions, caption_mask=None, t=None, noise=None):
+        """One optimizer step over this rank's batch, split into `accum` micro-batches.
+        images: uint8 [B, H, W, 3] or float [B, 3, H, W] in [-1, 1] (host pinned or device);
+        captions [B, T, D] (bf16); caption_mask [B, T] bool or None. Returns the batch-mean loss (device scalar)."""
+        dev = self.flat.data.device if self.flat is not None else next(self.model.parameters()).device
+        B = images.shape[0]
+        assert B % self.accum == 0
+        mb = B // self.accum
+        if self.flat is not None:
+            self.flat.zero_grad()
+        losses = []
+        for i in range(self.accum):
+            sl = slice(i * mb, (i + 1) * mb)
+            x = self._to_device(images[sl], dev)
+            x = uint8_to_float(x) if x.dtype == torch.uint8 else x.float()
+            y = self._to_device(captions[sl], dev).to(torch.bfloat16)
+            m = self._to_device(caption_mask[sl], dev) if caption_mask is not None else None
+            ti = t[sl].to(dev) if t is not None else None
+            ni = noise[sl].to(dev) if noise is not None else None
+            per = self.obj.train_step(self.model, x, y, m, t=ti, noise=ni,
+                                      grad_scale=1.0 / (x.numel() * self.accum))
+            losses.append(per)
+        if self.dp is not None:
+            self.dp.reduce()
+        self.clip_grad()
+        self.opt.step()
+        if self.sched is not None:
+            self.sched.step()
+        if self.flat is not None:
+            self.flat.sync_bf16()
+        self.global_step += 1
+        return torch.cat(losses).mean()
+
+    @torch.no_grad()
+    def clip_grad(self):
+        """Global 2-norm clip (max_norm = self.clip), on the device: coef = min(1, max / (norm + 1e-6))."""
+        if not self.clip:
+            return None
+        if self.flat is not None:
+            norm = self.flat.grad.norm()
+            self.flat.grad.mul_((self.clip / (norm + 1e-6)).clamp(max=1.0))
+            return norm
+        return torch.nn.utils.clip_grad_norm_([p for p in self.model.parameters() if p.grad is not None], self.clip)
