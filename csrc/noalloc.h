@@ -1,0 +1,55 @@
+// No-allocation entry point of the fused RMSNorm + adaLN-modulation backward.
+//
+// This entry point has no counterpart in the reference (wenhaochai/nano-gpic); it is an addition of this library.
+//
+// Who needs it: callers that cannot allocate device memory at the moment they call. For example: code running inside
+// a CUDA stream capture, where cudaMalloc is not allowed; embedders with their own fixed memory pool that forbid any
+// allocation behind their back; and hosts that call from a plain C runtime with no PyTorch caching allocator. The
+// regular entry point (rms_mod_bwd in csrc/norm.cu) gets its scratch from PyTorch's allocator. This one takes the same
+// inputs and outputs but keeps its scratch, the per-chunk partial column sums, in a fixed device array inside the
+// library, so it calls no cudaMalloc, cudaFree or any other allocating routine.
+//
+// The scratch array is NG_NOALLOC_RMS_SCRATCH_FLOATS fp32 values (8 MiB). Every GPU that loads the library holds it
+// until the process exits. A call needs ceil(rows_per_group / 64) * groups * 3 * C values of it. For example, 128
+// samples x 256 tokens at C = 1024 need 1.57M values. Larger calls are rejected with NG_NOALLOC_ERR_TOO_LARGE and
+// nothing is launched.
+//
+// Set-up: the first call on each device looks up the array's device address (cudaGetSymbolAddress) with that device
+// current. Make that first call outside any stream capture. Later calls do no set-up.
+//
+// Sharing: every call on a device uses the same array, and the array keeps the last call's contents. Each call
+// overwrites every value it reads, so nothing has to start at zero. Calls that overlap on the GPU (on different
+// streams without ordering, or from several threads at once) race on the array and give wrong results. Order them on
+// one stream, or serialise them.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define NG_NOALLOC_RMS_SCRATCH_FLOATS (2 * 1024 * 1024)
+
+#define NG_NOALLOC_OK 0
+#define NG_NOALLOC_ERR_TOO_LARGE 1  // the call needs more scratch than NG_NOALLOC_RMS_SCRATCH_FLOATS
+#define NG_NOALLOC_ERR_ARGS 2       // a null pointer, C % 8 != 0, C > 2048, or a non-positive size
+#define NG_NOALLOC_ERR_SETUP 3      // cudaGetSymbolAddress failed (no device, or the library's module did not load)
+#define NG_NOALLOC_ERR_LAUNCH 4     // a kernel launch failed (cudaGetLastError after the launch)
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// Backward of h = bf16(w * x * rstd * (1 + scale[g]) + shift[g]), g = row / rows_per_group (see csrc/norm.cu).
+//   dh, x, dres, dx: bf16 [M, C] contiguous (dres may be null); rstd: fp32 [M]; w: fp32 [C].
+//   scale: bf16 rows of `ld_scale` elements (a column slice of the adaLN output), or null for a plain RMSNorm.
+//   dw: fp32 [C], the weight gradient is ADDED into it (may be null).
+//   dshift / dscale: fp32 rows of ld_dshift / ld_dscale elements, overwritten (ignored when scale is null; may be null).
+// Launches two kernels on `stream` and returns at once. Returns NG_NOALLOC_OK or one of the error codes above.
+int ng_rms_mod_bwd_noalloc(const void* dh, const void* x, const float* rstd, const float* w, const void* scale,
+                           int64_t ld_scale, const void* dres, void* dx, float* dw, float* dshift, int64_t ld_dshift,
+                           float* dscale, int64_t ld_dscale, int M, int C, int rows_per_group, cudaStream_t stream);
+
+// Human-readable text of an error code of ng_rms_mod_bwd_noalloc.
+const char* ng_noalloc_error_string(int code);
+
+#ifdef __cplusplus
+}
+#endif

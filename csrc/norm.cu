@@ -406,3 +406,88 @@ void layernorm_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& 
 }
 
 }  // namespace ng
+
+// =============================================================================================== no-allocation entry
+// ng_rms_mod_bwd_noalloc (declared and documented in csrc/noalloc.h): the same two kernels as rms_mod_bwd, with the
+// chunk partials in a fixed device array instead of a PyTorch allocation. This block adds a path; it changes none.
+#include <mutex>
+
+#include "noalloc.h"
+
+namespace ng {
+namespace {
+// The scratch: fp32 partial column sums, [chunks * groups][3][C]. Host code must not use this name as an address.
+static __device__ __align__(256) float g_noalloc_rms_scratch[NG_NOALLOC_RMS_SCRATCH_FLOATS];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_addr[kMaxDevices] = {nullptr};
+
+// Device address of the scratch array for the current device, looked up once per device.
+float* noalloc_scratch(int* err) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    *err = NG_NOALLOC_ERR_SETUP;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_rms_scratch) != cudaSuccess || p == nullptr) {
+      *err = NG_NOALLOC_ERR_SETUP;
+      return nullptr;
+    }
+    g_noalloc_addr[dev] = static_cast<float*>(p);
+  }
+  return g_noalloc_addr[dev];
+}
+}  // namespace
+}  // namespace ng
+
+extern "C" __attribute__((visibility("default"))) int ng_rms_mod_bwd_noalloc(
+    const void* dh, const void* x, const float* rstd, const float* w, const void* scale, int64_t ld_scale,
+    const void* dres, void* dx, float* dw, float* dshift, int64_t ld_dshift, float* dscale, int64_t ld_dscale, int M,
+    int C, int rows_per_group, cudaStream_t stream) {
+  using namespace ng;
+  if (dh == nullptr || x == nullptr || rstd == nullptr || w == nullptr || dx == nullptr || M <= 0 || C <= 0 ||
+      C % 8 != 0 || C > 2048 || (scale != nullptr && rows_per_group <= 0))
+    return NG_NOALLOC_ERR_ARGS;
+  const bool mod = scale != nullptr;
+  const int rpg = mod ? rows_per_group : M;
+  const int G = mod ? (M + rpg - 1) / rpg : 1;
+  const int chunks = (rpg + BWD_ROWS - 1) / BWD_ROWS;
+  const int64_t need = (int64_t)G * chunks * 3 * C;
+  if (need > (int64_t)NG_NOALLOC_RMS_SCRATCH_FLOATS) return NG_NOALLOC_ERR_TOO_LARGE;
+  int err = NG_NOALLOC_OK;
+  float* part = noalloc_scratch(&err);
+  if (part == nullptr) return err;
+  cudaGetLastError();  // a launch error from earlier work is not this call's
+  const dim3 grid(chunks, G);
+  const bf16* sc = static_cast<const bf16*>(scale);
+  if (mod)
+    rms_mod_bwd_kernel<true><<<grid, 256, 0, stream>>>(static_cast<const bf16*>(dh), static_cast<const bf16*>(x), rstd,
+                                                       w, sc, ld_scale, static_cast<const bf16*>(dres),
+                                                       static_cast<bf16*>(dx), part, M, C, rpg);
+  else
+    rms_mod_bwd_kernel<false><<<grid, 256, 0, stream>>>(static_cast<const bf16*>(dh), static_cast<const bf16*>(x),
+                                                        rstd, w, nullptr, 0, static_cast<const bf16*>(dres),
+                                                        static_cast<bf16*>(dx), part, M, C, rpg);
+  if (cudaGetLastError() != cudaSuccess) return NG_NOALLOC_ERR_LAUNCH;
+  rms_mod_bwd_reduce<<<(C + 255) / 256, 256, 0, stream>>>(part, G, chunks, C, mod ? dshift : nullptr, ld_dshift,
+                                                           mod ? dscale : nullptr, ld_dscale, dw);
+  if (cudaGetLastError() != cudaSuccess) return NG_NOALLOC_ERR_LAUNCH;
+  return NG_NOALLOC_OK;
+}
+
+extern "C" __attribute__((visibility("default"))) const char* ng_noalloc_error_string(int code) {
+  switch (code) {
+    case NG_NOALLOC_OK: return "ok";
+    case NG_NOALLOC_ERR_TOO_LARGE:
+      return "ng_rms_mod_bwd_noalloc: the call needs more than NG_NOALLOC_RMS_SCRATCH_FLOATS (2097152) fp32 scratch "
+             "values (ceil(rows_per_group / 64) * groups * 3 * C); use the allocating entry point for it";
+    case NG_NOALLOC_ERR_ARGS: return "ng_rms_mod_bwd_noalloc: bad arguments (null pointer, C % 8 != 0, C > 2048 or a size <= 0)";
+    case NG_NOALLOC_ERR_SETUP: return "ng_rms_mod_bwd_noalloc: could not resolve the scratch array on this device";
+    case NG_NOALLOC_ERR_LAUNCH: return "ng_rms_mod_bwd_noalloc: kernel launch failed";
+    default: return "ng_rms_mod_bwd_noalloc: unknown error code";
+  }
+}
