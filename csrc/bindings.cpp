@@ -43,6 +43,7 @@ void fm_loss(const at::Tensor& pred, const at::Tensor& x, const at::Tensor& nois
              double grad_scale);
 void patchify(const at::Tensor& img, const at::Tensor& tok, int64_t p);
 void unpatchify(const at::Tensor& tok, const at::Tensor& img, int64_t p);
+void colsum(const at::Tensor& src, const at::Tensor& out, bool accumulate);
 void add_rows(const at::Tensor& a, const at::Tensor& table, const at::Tensor& out, int64_t period);
 }  // namespace ng
 
@@ -63,6 +64,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("patchify", &ng::patchify);
   m.def("unpatchify", &ng::unpatchify);
   m.def("add_rows", &ng::add_rows);
+  m.def("colsum", &ng::colsum, "deterministic column sums (fp32/bf16 source) into an fp32 vector");
   m.def("status_read", &ng::status_read, "read the device error word (synchronizes the current stream)");
   m.def("launch_count", &ng::launch_count, "kernel launches issued by this extension so far (host count)");
   m.def("status_clear", &ng::status_clear, "clear the device error word");

@@ -12,6 +12,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "reduce.h"
 #include "status.h"
 
 namespace ng {
@@ -243,9 +244,9 @@ void gate_bwd(const at::Tensor& dout, const at::Tensor& y, const at::Tensor& gat
   NG_LAUNCH_CHECK();
   float* dg = (dgate.has_value() && dgate->defined()) ? dgate->data_ptr<float>() : nullptr;
   float* db = (dbias.has_value() && dbias->defined()) ? dbias->data_ptr<float>() : nullptr;
-  gate_bwd_reduce<<<(C + 255) / 256, 256, 0, s>>>(part.data_ptr<float>(), G, chunks, C, dg,
-                                                   dg ? dgate->stride(0) : 0, db);
-  NG_LAUNCH_CHECK();
+  const float* pp = part.data_ptr<float>();
+  group_sum_launch(pp, G, chunks, C, 2 * C, dg, dg ? dgate->stride(0) : 0, s);
+  if (db != nullptr) colsum_launch(pp + C, false, (int64_t)G * chunks, C, 2 * C, db, true, s);
 }
 
 void fm_prep(const at::Tensor& x, const at::Tensor& noise, const at::Tensor& t, const at::Tensor& xt_tok, int64_t p) {

@@ -27,14 +27,33 @@
 namespace ng {
 
 namespace gemm_cfg {
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int BM = 128, BN = 256, BK = 64;
 constexpr int A_BYTES = BM * BK * 2;  // 16 KiB
 constexpr int B_BYTES = BN * BK * 2;  // 32 KiB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int THREADS = 192;
+constexpr int THREADS = 320;  // producer, MMA, 8 epilogue warps (two per TMEM lane quarter)
 constexpr int TMEM_COLS = 512;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align slack*/ + 256 /*barriers*/;
 }  // namespace gemm_cfg
+
+// Per-epilogue shared-memory plan. Epilogues that read inputs or write several outputs per tile (SwiGLU forward and
+// backward, the gated residual) trade one mainloop stage (48 KiB) for a deeper epilogue pipeline: a ring of IN_RING
+// prefetched input tiles and two output slots, so neither input latency nor store drain sits on the critical path.
+template <int EPI>
+struct EpiCfg {
+  static constexpr bool HEAVY = EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_BWD || EPI == EPI_GATED;
+  static constexpr int STAGES = HEAVY ? 3 : 4;
+  // one output slot holds every 32x32 output tile of a chunk (bf16 2 KiB, fp32 4 KiB)
+  static constexpr int OUT_SLOT = EPI == EPI_SWIGLU ? 6144
+                                  : (EPI == EPI_F32 || EPI == EPI_GATED || EPI == EPI_SWIGLU_BWD) ? 4096
+                                                                                                  : 2048;
+  static constexpr int OUT_SLOTS = (EPI == EPI_BF16) ? 2 : 1;
+  static constexpr int IN_SLOT = EPI == EPI_SWIGLU_BWD ? 4096 : (EPI == EPI_GATED || EPI == EPI_AXPBY) ? 2048 : 0;
+  static constexpr int IN_RING = IN_SLOT == 0 ? 0 : (EPI == EPI_GATED ? 2 : 1);
+  static constexpr int WARP_BYTES = (OUT_SLOTS * OUT_SLOT + IN_RING * IN_SLOT + 1023) / 1024 * 1024;
+  static constexpr int EPI_BYTES = 8 * WARP_BYTES;
+  static constexpr int SMEM = STAGES * gemm_cfg::STAGE_BYTES + EPI_BYTES + 1024 /*align slack*/ + 512 /*barriers*/;
+  static_assert(SMEM <= 232448, "shared memory budget of one sm_100 CTA");
+};
 
 struct EpiParams {
   int M, N, K, batch;
@@ -135,19 +154,61 @@ __device__ __forceinline__ void load_bias(const float* bias, float (&bv)[32], in
   }
 }
 
+// Epilogue tiles are 32 rows x 32 columns. bf16: 64-byte rows with the 64-byte TMA swizzle (16-byte chunk j of row r
+// at chunk j ^ ((r >> 1) & 3)); fp32: 128-byte rows with the 128-byte swizzle (chunk j at j ^ (r & 7)). A thread owns
+// one row, so a warp's 16-byte accesses hit 8 distinct bank groups per quarter-warp (conflict-free).
+__device__ __forceinline__ uint32_t sw64(int r, int j) { return r * 64 + ((j ^ ((r >> 1) & 3)) << 4); }
+__device__ __forceinline__ uint32_t sw128(int r, int j) { return r * 128 + ((j ^ (r & 7)) << 4); }
+
+__device__ __forceinline__ void st_tile_bf16(uint8_t* buf, int r, const float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 w;
+    w.x = pack_bf16(v[8 * j + 0], v[8 * j + 1]);
+    w.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
+    w.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
+    w.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
+    *reinterpret_cast<uint4*>(buf + sw64(r, j)) = w;
+  }
+}
+__device__ __forceinline__ void ld_tile_bf16(const uint8_t* buf, int r, float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint4 w = *reinterpret_cast<const uint4*>(buf + sw64(r, j));
+    v[8 * j + 0] = bf16_bits_lo(w.x);
+    v[8 * j + 1] = bf16_bits_hi(w.x);
+    v[8 * j + 2] = bf16_bits_lo(w.y);
+    v[8 * j + 3] = bf16_bits_hi(w.y);
+    v[8 * j + 4] = bf16_bits_lo(w.z);
+    v[8 * j + 5] = bf16_bits_hi(w.z);
+    v[8 * j + 6] = bf16_bits_lo(w.w);
+    v[8 * j + 7] = bf16_bits_hi(w.w);
+  }
+}
+__device__ __forceinline__ void st_tile_f32(uint8_t* buf, int r, const float (&v)[32]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+    *reinterpret_cast<float4*>(buf + sw128(r, j)) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+}
+
 template <int AMN, int BMN, int EPI>
 __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmOut2,
+                        const __grid_constant__ CUtensorMap tmRes, const __grid_constant__ CUtensorMap tmAux,
                         const EpiParams p) {
   using namespace gemm_cfg;
+  using Cfg = EpiCfg<EPI>;
+  constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + Cfg::EPI_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* in_bar = drain + 1;  // [8 epilogue warps][2]: input ring slots
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(in_bar + 16);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -166,15 +227,22 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 4);
+      mbar_init(&acc_empty[a], 8);
     }
     mbar_init(drain, 1);
+    for (int e = 0; e < 16; ++e) mbar_init(&in_bar[e], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_map(&tmA);
     tma_prefetch_map(&tmB);
+  }
+  if (warp >= 2 && lane == 0) {
+    tma_prefetch_map(&tmOut);
+    if (EPI == EPI_GATED || EPI == EPI_SWIGLU) tma_prefetch_map(&tmOut2);
+    if (EPI == EPI_GATED || EPI == EPI_AXPBY) tma_prefetch_map(&tmRes);
+    if (EPI == EPI_SWIGLU_BWD) tma_prefetch_map(&tmAux);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -306,132 +374,197 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
     }
   } else {
     // ------------------------------------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int r_in_tile = q * 32 + lane;
-    int it = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x, ++it) {
+    // Warp e = warp - 2 may read TMEM lanes [32q, 32q+32), q = warp % 4: rows row0 .. row0+31 of each tile. A 32-column
+    // chunk goes TMEM -> registers -> a swizzled smem tile -> one TMA store per output; inputs (the residual, C, or
+    // the saved SwiGLU pre-activation) arrive by TMA loads into a ring of IN_RING slots that runs ahead of the chunk
+    // being processed (across tiles), and outputs alternate between two slots, so neither the input latency nor the
+    // drain of the previous stores is waited for. TMA clips rows/columns outside the tensors.
+    // Two warps share each TMEM lane quarter and take alternate 32-column chunks of a tile (h = 0: even chunks).
+    constexpr int NCH = (EPI == EPI_SWIGLU) ? 4 : BN / 32;
+    constexpr int NCW = NCH / 2;  // chunks per warp per tile
+    constexpr int R = Cfg::IN_RING;
+    const int q = warp & 3, e = warp - 2, h = e >> 2;
+    uint8_t* wbase = smem + STAGES * STAGE_BYTES + e * Cfg::WARP_BYTES;
+    uint8_t* ibase = wbase + Cfg::OUT_SLOTS * Cfg::OUT_SLOT;
+    uint64_t* ibar = &in_bar[e * 2];
+    const bool has_in = R > 0 && (EPI != EPI_AXPBY || p.beta != 0.f);
+    const int my_tiles = blockIdx.x < total ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int n_chunks = my_tiles * NCW;  // this warp's chunk sequence, in processing order
+    // issue the input loads of chunk L (linear index over this warp's chunks) into ring slot L % R
+    auto issue_in = [&](int L) {
+      if (!has_in || L >= n_chunks) return;
+      const int i = L / NCW, c = h + 2 * (L - (L / NCW) * NCW);
+      int bs, mb, nb;
+      tile_coords(blockIdx.x + i * gridDim.x, num_m, num_n, bs, mb, nb);
+      const int row0 = mb * BM + q * 32;
+      const int col = (EPI == EPI_SWIGLU ? nb * 128 : nb * BN) + c * 32;
+      uint64_t* bar = &ibar[L % R];
+      uint8_t* dst = ibase + (L % R) * Cfg::IN_SLOT;
+      if (EPI == EPI_SWIGLU_BWD) {
+        mbar_arrive_expect_tx(bar, 4096);
+        tma_load_3d(&tmAux, bar, dst, col, row0, 0);
+        tma_load_3d(&tmAux, bar, dst + 2048, p.half_n + col, row0, 0);
+      } else {
+        mbar_arrive_expect_tx(bar, 2048);
+        tma_load_3d(&tmRes, bar, dst, col, row0, bs);
+      }
+    };
+    if (lane == 0)
+      for (int L = 0; L < R; ++L) issue_in(L);
+    int it = 0, L = 0, oslot = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
       const int a = it & 1;
       const uint32_t aph = (it >> 1) & 1;
       const bool got = mbar_wait(&acc_full[a], aph, abort_flag, p.err, kErrWaitAccFull);
       __syncwarp();
       if (!got) break;
       tc_fence_after();
-      int b, mb, nb;
-      tile_coords(t, num_m, num_n, b, mb, nb);
-      const int row = mb * BM + r_in_tile;
-      const bool row_ok = row < p.M;
+      int bs, mb, nb;
+      tile_coords(t, num_m, num_n, bs, mb, nb);
+      const int row0 = mb * BM + q * 32;
+      const int row = row0 + lane;
       const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + a * BN;
-      if (EPI == EPI_SWIGLU) {
-        // columns [0,128) of the accumulator are x1 = gate half, [128,256) are x2 = up half
-        __nv_bfloat16* pre = reinterpret_cast<__nv_bfloat16*>(p.out2) + (int64_t)row * p.ldo2;
-        __nv_bfloat16* act = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t r1[32], r2[32];
+      for (int c = h; c < NCH; c += 2, ++L) {
+        const int col = (EPI == EPI_SWIGLU ? nb * 128 : nb * BN) + c * 32;
+        const bool live = col < ((EPI == EPI_SWIGLU) ? p.half_n : p.N);  // warp-uniform
+        uint32_t r1[32], r2[32];
+        __syncwarp();
+        tmem_ld32(tb + c * 32, r1);
+        if (EPI == EPI_SWIGLU) tmem_ld32(tb + 128 + c * 32, r2);
+        tmem_wait_ld();
+        // per-sample gate / bias values (global, shared by the warp's lanes) before waiting for the inputs
+        float gv[32], bv[32];
+        if (live && (EPI == EPI_GATED || EPI == EPI_BF16)) load_bias(p.bias, bv, col, p.N);
+        if (live && EPI == EPI_GATED) {
+          const int grow = min(row, p.M - 1) / p.rows_per_group;
+          load_row_bf16(p.gate + (int64_t)grow * p.ldg + col, gv, col, p.N);
+        }
+        const uint8_t* ibuf = ibase + (L % (R > 0 ? R : 1)) * Cfg::IN_SLOT;
+        if (has_in) {
+          const bool arrived = mbar_wait(&ibar[L % R], (L / R) & 1, abort_flag, p.err, kErrWaitFull);
           __syncwarp();
-          tmem_ld32(tb + c * 32, r1);
-          tmem_ld32(tb + 128 + c * 32, r2);
-          tmem_wait_ld();
-          const int col = nb * 128 + c * 32;
-          if (row_ok) {
-            float x1[32], x2[32], h[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              x1[j] = round_bf16(__uint_as_float(r1[j]));
-              x2[j] = round_bf16(__uint_as_float(r2[j]));
-              h[j] = round_bf16(x1[j] * sigmoidf_(x1[j])) * x2[j];
-            }
-            store_row_bf16<EPI>(pre + col, x1, col, p.half_n);
-            store_row_bf16<EPI>(pre + p.half_n + col, x2, col, p.half_n);
-            store_row_bf16<EPI>(act + col, h, col, p.half_n);
+          if (!arrived) {
+            ok = false;
+            break;
           }
         }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          __syncwarp();
-          tmem_ld32(tb + c * 32, r);
-          tmem_wait_ld();
-          const int col = nb * BN + c * 32;
-          if (!row_ok || col >= p.N) continue;  // the next TMEM load re-converges the warp first
+        // output slot: the stores last issued from it must have read it
+        uint8_t* obuf = wbase + oslot * Cfg::OUT_SLOT;
+        if (lane == 0) {
+          if (Cfg::OUT_SLOTS == 2)
+            asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          else
+            bulk_wait_read0();
+        }
+        __syncwarp();
+        if (live) {
           float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r1[j]);
           if (EPI == EPI_BF16) {
-            float bv[32];
-            load_bias(p.bias, bv, col, p.N);
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] += bv[j];
-            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + b * p.out_bs + (int64_t)row * p.ldo + col;
-            store_row_bf16<EPI>(o, v, col, p.N);
+            st_tile_bf16(obuf, lane, v);
           } else if (EPI == EPI_F32) {
-            float* o = reinterpret_cast<float*>(p.out) + b * p.out_bs + (int64_t)row * p.ldo + col;
-            if (col + 32 <= p.N) {
-              float4* o4 = reinterpret_cast<float4*>(o);
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                float4 w = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
-                if (p.accumulate) {
-                  float4 u = o4[j];
-                  w.x += u.x;
-                  w.y += u.y;
-                  w.z += u.z;
-                  w.w += u.w;
-                }
-                o4[j] = w;
-              }
-            } else {
-              for (int j = 0; j < 32; ++j)
-                if (col + j < p.N) o[j] = p.accumulate ? o[j] + v[j] : v[j];
-            }
+            st_tile_f32(obuf, lane, v);
           } else if (EPI == EPI_AXPBY) {
-            float cv[32];
-            if (p.beta != 0.f) {
-              load_row_bf16(p.res + b * p.res_bs + (int64_t)row * p.ldr + col, cv, col, p.N);
+            if (has_in) {
+              float cv[32];
+              ld_tile_bf16(ibuf, lane, cv);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = p.alpha * v[j] + p.beta * cv[j];
             } else {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) cv[j] = 0.f;
+              for (int j = 0; j < 32; ++j) v[j] = p.alpha * v[j];
             }
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = p.alpha * v[j] + p.beta * cv[j];
-            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + b * p.out_bs + (int64_t)row * p.ldo + col;
-            store_row_bf16<EPI>(o, v, col, p.N);
+            st_tile_bf16(obuf, lane, v);
           } else if (EPI == EPI_GATED) {
             // y = acc + bias (kept for the backward); out = res + gate[sample] * y
-            float bv[32], rv[32], gv[32];
-            load_bias(p.bias, bv, col, p.N);
+            float rv[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = round_bf16(v[j] + bv[j]);
-            store_row_bf16<EPI>(reinterpret_cast<__nv_bfloat16*>(p.out2) + (int64_t)row * p.ldo2 + col, v, col, p.N);
-            load_row_bf16(p.res + (int64_t)row * p.ldr + col, rv, col, p.N);
-            load_row_bf16(p.gate + (int64_t)(row / p.rows_per_group) * p.ldg + col, gv, col, p.N);
+            st_tile_bf16(obuf + 2048, lane, v);
+            ld_tile_bf16(ibuf, lane, rv);
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = rv[j] + gv[j] * v[j];
-            store_row_bf16<EPI>(reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo + col, v, col, p.N);
-          } else if (EPI == EPI_SWIGLU_BWD) {
-            // v = d(act) for act columns [col, col+32); aux = the saved pre-activation [x1 | x2]
-            float x1[32], x2[32], d1[32], d2[32];
-            const __nv_bfloat16* pre = p.aux + (int64_t)row * p.ld_aux;
-            load_row_bf16(pre + col, x1, col, p.N);
-            load_row_bf16(pre + p.half_n + col, x2, col, p.N);
+            st_tile_bf16(obuf, lane, v);
+          } else if (EPI == EPI_SWIGLU) {
+            // accumulator columns [0,128) are x1 (gate half), [128,256) are x2 (up half)
+            float x2[32], h[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
-              const float s = sigmoidf_(x1[j]);
-              const float si = x1[j] * s;
-              d2[j] = v[j] * si;
-              d1[j] = v[j] * x2[j] * (s * (1.0f + x1[j] * (1.0f - s)));
+              v[j] = round_bf16(v[j]);
+              x2[j] = round_bf16(__uint_as_float(r2[j]));
+              h[j] = round_bf16(v[j] * sigmoidf_(v[j])) * x2[j];
             }
-            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo;
-            store_row_bf16<EPI>(o + col, d1, col, p.N);
-            store_row_bf16<EPI>(o + p.half_n + col, d2, col, p.N);
+            st_tile_bf16(obuf, lane, v);
+            st_tile_bf16(obuf + 2048, lane, x2);
+            st_tile_bf16(obuf + 4096, lane, h);
+          } else if (EPI == EPI_SWIGLU_BWD) {
+            // v = d(act) for act columns [col, col+32); ibuf = the saved pre-activation tiles [x1 | x2]
+            float x1[32], x2[32], d2[32];
+            ld_tile_bf16(ibuf, lane, x1);
+            ld_tile_bf16(ibuf + 2048, lane, x2);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float sg = sigmoidf_(x1[j]);
+              d2[j] = v[j] * x1[j] * sg;
+              v[j] = v[j] * x2[j] * (sg * (1.0f + x1[j] * (1.0f - sg)));
+            }
+            st_tile_bf16(obuf, lane, v);
+            st_tile_bf16(obuf + 2048, lane, d2);
           }
+          fence_proxy_async_smem();
         }
+        __syncwarp();
+        if (lane == 0) {
+          if (live) {
+            if (EPI == EPI_BF16 || EPI == EPI_AXPBY) {
+              tma_store_3d(&tmOut, obuf, col, row0, bs);
+            } else if (EPI == EPI_F32) {
+              if (p.accumulate)
+                tma_reduce_add_3d(&tmOut, obuf, col, row0, bs);
+              else
+                tma_store_3d(&tmOut, obuf, col, row0, bs);
+            } else if (EPI == EPI_GATED) {
+              tma_store_3d(&tmOut2, obuf + 2048, col, row0, 0);
+              tma_store_3d(&tmOut, obuf, col, row0, 0);
+            } else if (EPI == EPI_SWIGLU) {
+              tma_store_3d(&tmOut2, obuf, col, row0, 0);
+              tma_store_3d(&tmOut2, obuf + 2048, p.half_n + col, row0, 0);
+              tma_store_3d(&tmOut, obuf + 4096, col, row0, 0);
+            } else if (EPI == EPI_SWIGLU_BWD) {
+              tma_store_3d(&tmOut, obuf, col, row0, 0);
+              tma_store_3d(&tmOut, obuf + 2048, p.half_n + col, row0, 0);
+            }
+          }
+          bulk_commit();  // (an empty group keeps the two-slot accounting uniform)
+          // this chunk's input slot has been read by every lane: refill it with the chunk R ahead
+          if (R > 0) issue_in(L + R);
+        }
+        if (Cfg::OUT_SLOTS == 2) oslot ^= 1;
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[a]);
     }
+    // every store has finished before the CTA (and its shared memory) goes away; on an abort, the input loads still
+    // in flight land first (bounded wait)
+    if (lane == 0) {
+      bulk_wait0();
+      if (has_in && !ok) {
+        const uint64_t t0 = globaltimer_ns();
+        for (int k = L; k < min(L + R, n_chunks); ++k)
+          while (!mbar_try_wait(&ibar[k % R], (k / R) & 1))
+            if (globaltimer_ns() - t0 > NG_WAIT_BUDGET_NS) {
+              raise_error(p.err, kErrWaitDrain);
+              break;
+            }
+      }
+    }
+    __syncwarp();
   }
 
   tc_fence_before();
@@ -490,26 +623,44 @@ static void ensure_context() {
   ready = true;
 }
 
-// A 3-D bf16 tensor map (inner, outer, batch) with a 128-byte swizzle; inner is contiguous.
-CUtensorMap make_tmap_bf16(const void* ptr, int64_t inner, int64_t outer, int64_t batch, int64_t ld, int64_t bstride,
-                           int box_inner, int box_outer) {
+// A 3-D tensor map (inner, outer, batch); inner is contiguous. ld / bstride in elements.
+static CUtensorMap make_tmap(const void* ptr, CUtensorMapDataType dt, int esize, int64_t inner, int64_t outer,
+                             int64_t batch, int64_t ld, int64_t bstride, int box_inner, int box_outer,
+                             CUtensorMapSwizzle sw) {
+  ensure_context();
   CUtensorMap m;
   cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)outer, (cuuint64_t)batch};
-  cuuint64_t strides[2] = {(cuuint64_t)ld * 2, (cuuint64_t)(batch > 1 ? bstride : ld * outer) * 2};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * esize), (cuuint64_t)((batch > 1 ? bstride : ld * outer) * esize)};
   cuuint32_t box[3] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer, 1};
   cuuint32_t estr[3] = {1, 1, 1};
+  TORCH_CHECK(ptr != nullptr, "TMA operand is null");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(ptr) & 15) == 0, "TMA base address must be 16-byte aligned");
-  TORCH_CHECK((ld * 2) % 16 == 0, "TMA row stride must be a multiple of 16 bytes, got ld=", ld);
-  TORCH_CHECK(batch == 1 || (bstride * 2) % 16 == 0, "TMA batch stride must be a multiple of 16 bytes");
-  ensure_context();
-  NG_TRACE("[tmap] ptr=%p inner=%lld outer=%lld batch=%lld ld=%lld box=%dx%d m@%p\n", ptr, (long long)inner,
-           (long long)outer, (long long)batch, (long long)ld, box_inner, box_outer, (void*)&m);
-  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box,
-                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  NG_TRACE("[tmap]   encode -> %d\n", (int)r);
+  TORCH_CHECK((ld * esize) % 16 == 0, "TMA row stride must be a multiple of 16 bytes, got ld=", ld);
+  TORCH_CHECK(batch == 1 || (bstride * esize) % 16 == 0, "TMA batch stride must be a multiple of 16 bytes");
+  NG_TRACE("[tmap] ptr=%p inner=%lld outer=%lld batch=%lld ld=%lld box=%dx%d\n", ptr, (long long)inner,
+           (long long)outer, (long long)batch, (long long)ld, box_inner, box_outer);
+  CUresult r = get_encode_fn()(&m, dt, 3, const_cast<void*>(ptr), dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", (int)r);
   return m;
+}
+
+// bf16 operand map with the 128-byte swizzle (the GEMM's A/B tiles).
+CUtensorMap make_tmap_bf16(const void* ptr, int64_t inner, int64_t outer, int64_t batch, int64_t ld, int64_t bstride,
+                           int box_inner, int box_outer) {
+  return make_tmap(ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, inner, outer, batch, ld, bstride, box_inner, box_outer,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// 32 x 32 epilogue tile maps: bf16 with the 64-byte swizzle, fp32 with the 128-byte swizzle.
+static CUtensorMap epi_map_bf16(const void* ptr, int64_t cols, int64_t rows, int64_t batch, int64_t ld, int64_t bs) {
+  return make_tmap(ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, batch, ld, bs, 32, 32,
+                   CU_TENSOR_MAP_SWIZZLE_64B);
+}
+static CUtensorMap epi_map_f32(const void* ptr, int64_t cols, int64_t rows, int64_t batch, int64_t ld, int64_t bs) {
+  return make_tmap(ptr, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, cols, rows, batch, ld, bs, 32, 32,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 static int num_sms() {
@@ -522,28 +673,33 @@ static int num_sms() {
   return n;
 }
 
+struct EpiMaps {
+  CUtensorMap out, out2, res, aux;
+};
+
 template <int AMN, int BMN, int EPI>
-static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& p, int grid, cudaStream_t s) {
+static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps& em, const EpiParams& p, int grid,
+                     cudaStream_t s) {
   auto kern = gemm_tcgen05_kernel<AMN, BMN, EPI>;
   static bool attr_set = false;
   if (!attr_set) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_cfg::SMEM_BYTES);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, EpiCfg<EPI>::SMEM);
     attr_set = true;
   }
-  kern<<<grid, gemm_cfg::THREADS, gemm_cfg::SMEM_BYTES, s>>>(ta, tb, p);
+  kern<<<grid, gemm_cfg::THREADS, EpiCfg<EPI>::SMEM, s>>>(ta, tb, em.out, em.out2, em.res, em.aux, p);
   NG_LAUNCH_CHECK();
 }
 
 template <int AMN, int BMN>
-static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const EpiParams& p, int grid,
-                         cudaStream_t s) {
+static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps& em, const EpiParams& p,
+                         int grid, cudaStream_t s) {
   switch (epi) {
-    case EPI_BF16: return launch_t<AMN, BMN, EPI_BF16>(ta, tb, p, grid, s);
-    case EPI_F32: return launch_t<AMN, BMN, EPI_F32>(ta, tb, p, grid, s);
-    case EPI_AXPBY: return launch_t<AMN, BMN, EPI_AXPBY>(ta, tb, p, grid, s);
-    case EPI_GATED: return launch_t<AMN, BMN, EPI_GATED>(ta, tb, p, grid, s);
-    case EPI_SWIGLU: return launch_t<AMN, BMN, EPI_SWIGLU>(ta, tb, p, grid, s);
-    case EPI_SWIGLU_BWD: return launch_t<AMN, BMN, EPI_SWIGLU_BWD>(ta, tb, p, grid, s);
+    case EPI_BF16: return launch_t<AMN, BMN, EPI_BF16>(ta, tb, em, p, grid, s);
+    case EPI_F32: return launch_t<AMN, BMN, EPI_F32>(ta, tb, em, p, grid, s);
+    case EPI_AXPBY: return launch_t<AMN, BMN, EPI_AXPBY>(ta, tb, em, p, grid, s);
+    case EPI_GATED: return launch_t<AMN, BMN, EPI_GATED>(ta, tb, em, p, grid, s);
+    case EPI_SWIGLU: return launch_t<AMN, BMN, EPI_SWIGLU>(ta, tb, em, p, grid, s);
+    case EPI_SWIGLU_BWD: return launch_t<AMN, BMN, EPI_SWIGLU_BWD>(ta, tb, em, p, grid, s);
     default: TORCH_CHECK(false, "unknown GEMM epilogue ", epi);
   }
 }
@@ -581,7 +737,7 @@ void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   p.aux = g.aux;
   p.ld_aux = g.ld_aux;
   p.alpha = g.alpha;
-  p.beta = g.beta;
+  p.beta = (g.res != nullptr) ? g.beta : 0.f;
   p.accumulate = g.accumulate;
   p.k_splits = g.k_splits > 1 ? g.k_splits : 1;
   p.kb_per_split = g.kb_per_split;
@@ -590,15 +746,30 @@ void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   const int num_n = g.epi == EPI_SWIGLU ? (g.half_n + 127) / 128 : (g.N + BN - 1) / BN;
   const int64_t tiles = (int64_t)g.batch * (g.k_splits > 1 ? g.k_splits : 1) * num_m * num_n;
   const int grid = (int)std::min<int64_t>(tiles, num_sms());
+  // epilogue maps: the output(s) and the input tiles the epilogue reads
+  const int zb = g.k_splits > 1 ? g.k_splits : g.batch;
+  EpiMaps em;
+  if (g.epi == EPI_F32) {
+    em.out = epi_map_f32(g.out, g.N, g.M, zb, g.ldo, g.out_bs);
+  } else {
+    const int64_t ocols = g.epi == EPI_SWIGLU ? g.half_n : (g.epi == EPI_SWIGLU_BWD ? 2 * (int64_t)g.half_n : g.N);
+    em.out = epi_map_bf16(g.out, ocols, g.M, zb, g.ldo, g.out_bs);
+  }
+  em.out2 = em.res = em.aux = em.out;
+  if (g.epi == EPI_GATED) em.out2 = epi_map_bf16(g.out2, g.N, g.M, 1, g.ldo2, 0);
+  if (g.epi == EPI_SWIGLU) em.out2 = epi_map_bf16(g.out2, 2 * (int64_t)g.half_n, g.M, 1, g.ldo2, 0);
+  if (g.epi == EPI_GATED || (g.epi == EPI_AXPBY && g.beta != 0.f && g.res != nullptr))
+    em.res = epi_map_bf16(g.res, g.N, g.M, g.batch, g.ldr, g.res_bs);
+  if (g.epi == EPI_SWIGLU_BWD) em.aux = epi_map_bf16(g.aux, 2 * (int64_t)g.half_n, g.M, 1, g.ld_aux, 0);
   NG_TRACE("[gemm]   maps ok, grid=%d tiles=%lld\n", grid, (long long)tiles);
   if (!g.a_mn && !g.b_mn)
-    dispatch_epi<0, 0>(g.epi, ta, tb, p, grid, stream);
+    dispatch_epi<0, 0>(g.epi, ta, tb, em, p, grid, stream);
   else if (!g.a_mn && g.b_mn)
-    dispatch_epi<0, 1>(g.epi, ta, tb, p, grid, stream);
+    dispatch_epi<0, 1>(g.epi, ta, tb, em, p, grid, stream);
   else if (g.a_mn && g.b_mn)
-    dispatch_epi<1, 1>(g.epi, ta, tb, p, grid, stream);
+    dispatch_epi<1, 1>(g.epi, ta, tb, em, p, grid, stream);
   else
-    dispatch_epi<1, 0>(g.epi, ta, tb, p, grid, stream);
+    dispatch_epi<1, 0>(g.epi, ta, tb, em, p, grid, stream);
   NG_TRACE("[gemm]   launched\n");
 }
 

@@ -11,6 +11,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "reduce.h"
 #include "status.h"
 
 namespace ng {
@@ -379,9 +380,12 @@ void rms_mod_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& rs
   float* dsh = (dshift.has_value() && dshift->defined()) ? dshift->data_ptr<float>() : nullptr;
   float* dsc = (dscale.has_value() && dscale->defined()) ? dscale->data_ptr<float>() : nullptr;
   float* dwp = (dw.has_value() && dw->defined()) ? dw->data_ptr<float>() : nullptr;
-  rms_mod_bwd_reduce<<<(C + 255) / 256, 256, 0, s>>>(part.data_ptr<float>(), G, chunks, C, mod ? dsh : nullptr,
-                                                      ld_of(dshift), mod ? dsc : nullptr, ld_of(dscale), dwp);
-  NG_LAUNCH_CHECK();
+  const float* pp = part.data_ptr<float>();
+  if (mod) {
+    group_sum_launch(pp, G, chunks, C, 3 * C, dsh, ld_of(dshift), s);
+    group_sum_launch(pp + C, G, chunks, C, 3 * C, dsc, ld_of(dscale), s);
+  }
+  if (dwp != nullptr) colsum_launch(pp + 2 * C, false, (int64_t)G * chunks, C, 3 * C, dwp, true, s);
 }
 
 void layernorm_fwd(const at::Tensor& x, const at::Tensor& h, const at::Tensor& mu, const at::Tensor& rstd, double eps) {

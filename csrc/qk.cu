@@ -8,6 +8,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "reduce.h"
 #include "status.h"
 
 namespace ng {
@@ -83,12 +84,12 @@ __global__ void __launch_bounds__(256) qk_norm_bwd_kernel(const bf16* __restrict
                                                           int64_t ld_dsrc, float* __restrict__ part, int rows, int H,
                                                           int L) {
   __shared__ float s_part[8][64];
-  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float dw[64];
 #pragma unroll
   for (int i = 0; i < 64; ++i) dw[i] = 0.f;
-  if (t < (int64_t)rows * H) {
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < (int64_t)rows * H;
+       t += (int64_t)gridDim.x * blockDim.x) {
     const int row = (int)(t / H), h = (int)(t - (int64_t)row * H);
     float d[64], x[64];
     ld64(dout + (int64_t)row * H * 64 + h * 64, d);
@@ -108,7 +109,7 @@ __global__ void __launch_bounds__(256) qk_norm_bwd_kernel(const bf16* __restrict
 #pragma unroll
     for (int i = 0; i < 64; ++i) {
       const float xh = x[i] * r;
-      dw[i] = d[i] * xh;
+      dw[i] += d[i] * xh;
       d[i] = d[i] * __ldg(w + i);  // d(xhat)
       dot += d[i] * xh;
     }
@@ -173,7 +174,9 @@ void qk_norm_bwd(const at::Tensor& dout, const at::Tensor& src, const at::Tensor
   const at::cuda::CUDAGuard guard(src.device());
   const int rows = src.size(0), H = src.size(1) / 64;
   const int64_t n = (int64_t)rows * H;
-  const int grid = (int)((n + 255) / 256);
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, src.get_device());
+  const int grid = (int)std::min<int64_t>((n + 255) / 256, 4 * (int64_t)sms);
   auto s = at::cuda::getCurrentCUDAStream();
   at::Tensor part = at::empty({(int64_t)grid * 64}, src.options().dtype(at::kFloat));
   const auto* dp = reinterpret_cast<const bf16*>(dout.data_ptr());
@@ -188,10 +191,7 @@ void qk_norm_bwd(const at::Tensor& dout, const at::Tensor& src, const at::Tensor
                                                    nullptr, nullptr, op, dsrc.stride(0), part.data_ptr<float>(), rows,
                                                    H, (int)L);
   NG_LAUNCH_CHECK();
-  if (dw.has_value() && dw->defined()) {
-    reduce_cols_kernel<<<1, 64, 0, s>>>(part.data_ptr<float>(), grid, 64, dw->data_ptr<float>());
-    NG_LAUNCH_CHECK();
-  }
+  if (dw.has_value() && dw->defined()) colsum_launch(part.data_ptr<float>(), false, grid, 64, 64, dw->data_ptr<float>(), true, s);
 }
 
 }  // namespace ng

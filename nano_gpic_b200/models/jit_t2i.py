@@ -59,7 +59,7 @@ def _wgrad(dy, x, p):
 
 
 def _bias_grad(dy, p):
-    grad_of(p).add_(dy.float().sum(0))
+    E.colsum(dy, grad_of(p), accumulate=True)
 
 
 # ------------------------------------------------------------------------------------------------------ modules
@@ -333,7 +333,8 @@ class _AddRowsFn(torch.autograd.Function):
         if ctx.param is not None:
             P = ctx.period
             g = grad_of(ctx.param)
-            g.view(-1, g.shape[-1])[:P].add_(d.float().view(-1, P, d.shape[-1]).sum(0))
+            Cd = d.shape[-1]
+            E.colsum(d.reshape(-1, P * Cd), g.view(-1)[:P * Cd], accumulate=True)
         return d, None, None, None, None
 
 

@@ -89,6 +89,15 @@ def fm_loss(pred_tok, x, noise, t, p, t_eps=0.05, grad_scale=None, need_grad=Tru
     return per, g
 
 
+def colsum(src, out, accumulate=True):
+    """out (+)= column sums of src [rows, C] (fp32 or bf16), deterministic, fp32 accumulation."""
+    if not src.is_cuda:
+        t = src.float().sum(0)
+        return out.add_(t) if accumulate else out.copy_(t)
+    ext().colsum(src, out, accumulate)
+    return out
+
+
 def add_rows(a, table, period):
     """bf16(a[row] + table[row % period]): a [rows, C] bf16, table [period, C] fp32 or bf16."""
     if not a.is_cuda:

@@ -63,6 +63,28 @@ def bench_gemm(d, batch, rows):
         del x, w, dy
 
 
+def bench_fused(d, batch, rows):
+    """Fused-epilogue GEMMs against the plain GEMM of the same shape (the epilogue's cost is the difference)."""
+    from nano_gpic_b200.ops import gemm
+    M = batch * 256
+    pk, _, src = peaks()
+    r = lambda *s: (torch.randn(*s, device="cuda") * 0.5).bfloat16()
+    x, w12, w3, pre, dy = r(M, d), r(8 * d, d), r(d, 4 * d), r(M, 8 * d), r(M, d)
+    wp, res, mod = r(d, d), r(M, d), r(batch, 6 * d)
+    bias = torch.zeros(d, device="cuda")
+    cases = [("swiglu_fwd", lambda: gemm.swiglu_linear(x, w12), lambda: gemm.linear(x, w12), 2.0 * M * 8 * d * d),
+             ("swiglu_bwd", lambda: gemm.swiglu_dgrad(dy, w3, pre), lambda: gemm.linear_dgrad(dy, w3), 2.0 * M * 4 * d * d),
+             ("gated_proj", lambda: gemm.linear_gated_residual(x, wp, bias, res, mod[:, 2 * d:3 * d], 256),
+              lambda: gemm.linear(x, wp), 2.0 * M * d * d)]
+    for name, fused, plain, fl in cases:
+        tf, tp = time_fn(fused), time_fn(plain)
+        row = {"kernel": "gemm_fused", "name": name, "M": M, "d": d, "fused_us": round(tf * 1e6, 1),
+               "plain_us": round(tp * 1e6, 1), "fused_tflops": round(fl / tf / 1e12, 1),
+               "plain_tflops": round(fl / tp / 1e12, 1), "fused_frac_of_" + src: round(fl / tf / 1e12 / pk, 3)}
+        rows.append(row)
+        print(json.dumps(row), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm")
@@ -74,6 +96,8 @@ def main():
     only = set(a.only.split(","))
     if "gemm" in only:
         bench_gemm(a.d, a.batch, rows)
+    if "fused" in only:
+        bench_fused(a.d, a.batch, rows)
     if a.json:
         with open(a.json, "w") as f:
             json.dump(rows, f, indent=1)

@@ -1,0 +1,65 @@
+"""Runs one kernel on one shape a few times: the target of ncu captures (small cases that end by themselves).
+
+    python -m nano_gpic_b200.tools.kernel_case --case swiglu_fwd --m 8192 --d 1024 [--reps 3]
+cases: linear_fwd, linear_dgrad, linear_wgrad, swiglu_fwd, swiglu_bwd, gated, attn_fwd, attn_bwd, rms_bwd
+"""
+import argparse
+
+import torch
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", required=True)
+    ap.add_argument("--m", type=int, default=8192, help="token rows (multiple of 256 for attention cases)")
+    ap.add_argument("--d", type=int, default=1024)
+    ap.add_argument("--t", type=int, default=128, help="caption length (attention cases)")
+    ap.add_argument("--reps", type=int, default=3)
+    a = ap.parse_args()
+    from nano_gpic_b200.ops import attention as A, gemm as G, norm as NR, status
+    torch.manual_seed(0)
+    M, d = a.m, a.d
+    r = lambda *s: (torch.randn(*s, device="cuda") * 0.5).bfloat16()
+    if a.case in ("linear_fwd", "linear_dgrad", "linear_wgrad"):
+        x, w, dy = r(M, d), r(3 * d, d), r(M, 3 * d)
+        fn = {"linear_fwd": lambda: G.linear(x, w), "linear_dgrad": lambda: G.linear_dgrad(dy, w),
+              "linear_wgrad": lambda: G.linear_wgrad(dy, x)}[a.case]
+    elif a.case == "swiglu_fwd":
+        x, w12 = r(M, d), r(8 * d, d)
+        fn = lambda: G.swiglu_linear(x, w12)
+    elif a.case == "swiglu_bwd":
+        dy, w3, pre = r(M, d), r(d, 4 * d), r(M, 8 * d)
+        fn = lambda: G.swiglu_dgrad(dy, w3, pre)
+    elif a.case == "gated":
+        x, w, res, mod = r(M, d), r(d, d), r(M, d), r(M // 256, 6 * d)
+        b = torch.zeros(d, device="cuda")
+        fn = lambda: G.linear_gated_residual(x, w, b, res, mod[:, 2 * d:3 * d], 256)
+    elif a.case in ("attn_fwd", "attn_bwd"):
+        B, L, T = M // 256, 256, a.t
+        qkv, kv = r(M, 3 * d), r(B * T, 2 * d)
+        lens = torch.randint(1, T + 1, (B,), device="cuda", dtype=torch.int32)
+        o, lse = A.attn_fwd(qkv[:, :d], L, qkv[:, d:2 * d], qkv[:, 2 * d:], L, L, kv[:, :d], kv[:, d:], T, lens)
+        do = r(M, d)
+        if a.case == "attn_fwd":
+            fn = lambda: A.attn_fwd(qkv[:, :d], L, qkv[:, d:2 * d], qkv[:, 2 * d:], L, L, kv[:, :d], kv[:, d:], T, lens)
+        else:
+            fn = lambda: A.attn_bwd(do, qkv[:, :d], L, qkv[:, d:2 * d], qkv[:, 2 * d:], L, L, o, lse, kv[:, :d],
+                                    kv[:, d:], T, lens)
+    elif a.case == "rms_bwd":
+        x, dh = r(M, d), r(M, d)
+        w = torch.ones(d, device="cuda")
+        mod = r(M // 256, 6 * d)
+        h, rstd = NR.rms_mod_fwd(x, w, mod[:, :d], mod[:, d:2 * d], 256)
+        dw = torch.zeros(d, device="cuda")
+        fn = lambda: NR.rms_mod_bwd(dh, x, rstd, w, mod[:, d:2 * d], 256, dres=dh, dw_acc=dw)
+    else:
+        raise SystemExit(f"unknown case {a.case}")
+    for _ in range(a.reps):
+        fn()
+    torch.cuda.synchronize()
+    status.check()
+    print(f"{a.case} ok", flush=True)
+
+
+if __name__ == "__main__":
+    main()
