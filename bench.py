@@ -184,6 +184,9 @@ def run_reference(a, rank, world, dev):
     torch.set_float32_matmul_precision("medium")  # reference patch_bugs.py:5
     torch.manual_seed(0)
     net = JiT_T2I(**s.model_kwargs()).to(dev)
+    # the reference caches its RoPE tables on first use; building them eagerly keeps that CPU work out of the compiled
+    # graph (as its own compile warm-up does), so Inductor emits GPU kernels only
+    net.fetch_pos(256 // 16, 256 // 16, dev)
     tag_muon_params(net)
     params = [p for p in net.parameters() if p.requires_grad]
     opt = MuonAdamW([{"params": params}], lr=s.adamw_lr, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0,

@@ -1,0 +1,63 @@
+"""Exponential moving average of the weights (reference baselines/PixelGen/src/callbacks/simple_ema.py:12-111).
+
+ema <- decay * ema + (1 - decay) * w once per optimizer step, as one lerp over the flat fp32 parameter buffer on a side
+stream, joined before the next optimizer step and before any checkpoint. With off=True (the ladder: GPIC_MFU_NO_EMA=1)
+nothing is updated and checkpoints mirror the raw weights into the EMA slot.
+"""
+import os
+
+import torch
+
+
+class SimpleEMA:
+    def __init__(self, flat, decay=0.9999, every_n_steps=1, off=None):
+        self.flat = flat
+        self.decay, self.every_n_steps = decay, every_n_steps
+        self.off = (os.environ.get("GPIC_MFU_NO_EMA") == "1") if off is None else off
+        self.buf = None if self.off else flat.data.clone()
+        self._stream = None
+        self.previous_step = 0
+
+    def step(self, global_step):
+        """Call after the optimizer step; updates once per new step."""
+        if self.off or global_step == self.previous_step:
+            return
+        self.previous_step = global_step
+        if global_step % self.every_n_steps:
+            return
+        if self.buf.is_cuda:
+            if self._stream is None:
+                self._stream = torch.cuda.Stream(device=self.buf.device)
+            self._stream.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(self._stream):
+                self.buf.lerp_(self.flat.data, 1.0 - self.decay)
+        else:
+            self.buf.lerp_(self.flat.data, 1.0 - self.decay)
+
+    def join(self):
+        if self._stream is not None:
+            torch.cuda.current_stream().wait_stream(self._stream)
+
+    def state_tensors(self, prefix):
+        """The EMA weights under the denoiser's parameter names (non-trainable buffers/params as the model has them)."""
+        self.join()
+        model = self.flat.module
+        out = {}
+        ema_of = {id(p): self.flat.view(self.buf, i) for i, p in enumerate(self.flat.params)}
+        for k, v in model.state_dict(keep_vars=True).items():
+            out[prefix + k] = ema_of.get(id(v), v).detach()
+        return out
+
+    def load_tensors(self, sd):
+        if self.off:
+            return
+        names = dict(zip(self.flat.names, range(len(self.flat.params))))
+        for k, v in sd.items():
+            if k in names:
+                self.flat.view(self.buf, names[k]).copy_(v)
+
+    def state_dict(self):
+        return {"decay": self.decay, "every_n_steps": self.every_n_steps}
+
+    def load_state_dict(self, sd):
+        self.decay, self.every_n_steps = sd["decay"], sd["every_n_steps"]
