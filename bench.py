@@ -163,10 +163,9 @@ def run_ours(a, rank, world, dev):
 
 
 # ------------------------------------------------------------------------------------------------- reference arm
-def run_reference(a, rank, world, dev):
+def reference_step_fn(a, rank, world, dev):
+    """The reference's training step (one optimizer step over this rank's batch), built from its own classes."""
     pg = os.path.join(ROOT, "baseline", "_ref", "baselines", "PixelGen")
-    if not os.path.isdir(os.path.join(pg, "src")):
-        return None, "baseline/_ref is missing: copy the reference tree there (see DESIGN.md)"
     # the reference's final-ladder levers for a DDP size (jobs/final_ladder.sh:30-35), minus FA3 (Hopper-only binary)
     os.environ.setdefault("GPIC_MFU_ATTN", "sdpa")
     os.environ.setdefault("GPIC_MFU_FUSED_NORM", "1")
@@ -231,6 +230,15 @@ def run_reference(a, rank, world, dev):
         opt.zero_grad(set_to_none=True)
         return torch.stack(losses).mean()
 
+    return step
+
+
+def run_reference(a, rank, world, dev):
+    pg = os.path.join(ROOT, "baseline", "_ref", "baselines", "PixelGen")
+    if not os.path.isdir(os.path.join(pg, "src")):
+        return None, "baseline/_ref is missing: copy the reference tree there (see DESIGN.md)"
+    step = reference_step_fn(a, rank, world, dev)
+    B = a.global_batch // world
     dev_batch = synthetic_batch(B, a.caption_len, 2048, seed=1000 + rank, device=dev)
     host_batches = [synthetic_batch(B, a.caption_len, 2048, seed=2000 + 10 * rank + i, pin=True) for i in range(2)]
     for _ in range(a.warmup):

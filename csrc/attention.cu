@@ -585,6 +585,13 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0, c
   NG_LAUNCH_CHECK();
 }
 
+void attn_delta(const bf16* dout, int64_t lddo, const bf16* o, int64_t ldo, float* delta, int rows, int Lq, int H,
+                cudaStream_t s) {
+  const int64_t n = (int64_t)rows * H;
+  attn_delta_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(dout, lddo, o, ldo, delta, rows, Lq, H);
+  NG_LAUNCH_CHECK();
+}
+
 void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0,
               const c10::optional<at::Tensor>& k1, const c10::optional<at::Tensor>& v1, const at::Tensor& n0,
               const at::Tensor& n1, const at::Tensor& o, const at::Tensor& lse, const at::Tensor& dq,

@@ -1,0 +1,726 @@
+// Masked multi-head attention forward on the 5th-generation tensor cores (tcgen05 + TMEM), head dim 64, for sm_100a.
+//
+// One CTA per (128 queries, sample, head). Keys are visited in 128-key tiles of the storage order (rows [0, L0) of
+// source 0, then rows [0, L1) of source 1; the key-validity rule is that of csrc/attention.cu); tiles without a valid
+// key are skipped. Per tile j:
+//   MMA warp      S_j = Q K_j^T        (M=128 queries, N=128 keys, K=64) into TMEM buffer j % 2
+//                 O  += P_{j-1} V_{j-1}  (M=128, N=64, K=128; P from shared memory, V as an MN-major operand)
+//   softmax warps (a thread per query row) read S_j from TMEM, mask, online-softmax update (running max m, sum l),
+//                 rescale O in TMEM by exp(m_old - m_new), write P_j (bf16, 128-byte swizzle) to shared memory
+//   TMA warp      K_j, V_j (one 3-D box each: rows past a sample's length are zero-filled, never the next sample's)
+// S_{j+1} is computed while the softmax works on S_j. The epilogue divides O by l, stores it and the log-sum-exp.
+// Reference: the joint image/caption attention of baselines/PixelGen/src/models/transformer/JiT_T2I.py:114-187.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "gemm.h"
+#include "status.h"
+
+namespace ng {
+
+using bf16 = __nv_bfloat16;
+
+namespace atc {
+constexpr int BQ = 128, BKV = 128, D = 64;
+constexpr int THREADS = 192;  // warp 0 TMA, warp 1 MMA, warps 2..5 softmax
+constexpr int Q_BYTES = BQ * D * 2;        // 16 KiB
+constexpr int KV_BYTES = BKV * D * 2;      // 16 KiB each of K and V
+constexpr int P_BYTES = BQ * BKV * 2;      // 32 KiB (two 64-key swizzle atoms)
+constexpr int SMEM = Q_BYTES + 2 * 2 * KV_BYTES + 2 * P_BYTES + 1024 + 256;
+constexpr uint32_t TMEM_COLS = 512;        // S0 [0,128), S1 [128,256), O [256,320)
+constexpr uint32_t O_COL = 256;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+}  // namespace atc
+
+struct AttnTcParams {
+  const int *n0, *n1;
+  int Lq, L0, L1, H;
+  int nt0, nt1;  // 128-key tiles of each source
+  float scale_log2;
+  bf16* o;
+  int64_t ldo;
+  float* lse;
+  int* err;
+};
+
+__device__ __forceinline__ bool atc_tile_live(int j, const AttnTcParams& p, int n0b, int n1b) {
+  return j < p.nt0 ? (j * atc::BKV < n0b) : ((j - p.nt0) * atc::BKV < n1b);
+}
+__device__ __forceinline__ bool atc_key_valid(int j, int c, const AttnTcParams& p, int n0b, int n1b) {
+  if (j < p.nt0) {
+    const int s = j * atc::BKV + c;
+    return s < n0b && s < p.L0;
+  }
+  const int s = (j - p.nt0) * atc::BKV + c;
+  return s < n1b && s < p.L1;
+}
+
+__global__ void __launch_bounds__(atc::THREADS, 1)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK0,
+                       const __grid_constant__ CUtensorMap tmV0, const __grid_constant__ CUtensorMap tmK1,
+                       const __grid_constant__ CUtensorMap tmV1, const AttnTcParams p) {
+  using namespace atc;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + Q_BYTES;                 // stage s: K at s * 2 * KV_BYTES, V after it
+  uint8_t* sP = sKV + 4 * KV_BYTES;            // buffer b at b * P_BYTES
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * P_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;   // [2]
+  uint64_t* kv_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* p_full = bars + 7;    // [2]
+  uint64_t* o_done = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const int q0 = blockIdx.x * BQ;
+  const int n0b = p.n0[b], n1b = p.n1 ? p.n1[b] : 0;
+  const int nt = p.nt0 + p.nt1;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+    }
+    mbar_init(o_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // --------------------------------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, Q_BYTES);
+      tma_load_3d(&tmQ, q_full, sQ, h * D, q0, b);
+      int it = 0;
+      for (int j = 0; j < nt; ++j) {
+        if (!atc_tile_live(j, p, n0b, n1b)) continue;
+        const int st = it & 1;
+        if (!mbar_wait(&kv_empty[st], ((it >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
+        uint8_t* k = sKV + st * 2 * KV_BYTES;
+        mbar_arrive_expect_tx(&kv_full[st], 2 * KV_BYTES);
+        if (j < p.nt0) {
+          tma_load_3d(&tmK0, &kv_full[st], k, h * D, j * BKV, b);
+          tma_load_3d(&tmV0, &kv_full[st], k + KV_BYTES, h * D, j * BKV, b);
+        } else {
+          tma_load_3d(&tmK1, &kv_full[st], k, h * D, (j - p.nt0) * BKV, b);
+          tma_load_3d(&tmV1, &kv_full[st], k + KV_BYTES, h * D, (j - p.nt0) * BKV, b);
+        }
+        ++it;
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_f32(BQ, BKV, 0, 0);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(BQ, D, 0, 1);
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.err, kErrWaitFull);
+      const uint32_t aq = smem_u32(sQ);
+      int it = 0;
+      // issue S for live tile `it` (its K/V are in stage it % 2)
+      auto issue_s = [&](int i) {
+        const int st = i & 1;
+        if (!mbar_wait(&kv_full[st], (i >> 1) & 1, abort_flag, p.err, kErrWaitFull)) return false;
+        tc_fence_after();
+        const uint32_t kb = smem_u32(sKV + st * 2 * KV_BYTES);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k)
+          umma_f16(tmem + st * BKV, smem_desc_sw128(aq + k * 32, 16, 1024), smem_desc_sw128(kb + k * 32, 16, 1024),
+                   idesc_s, k != 0 ? 1u : 0u);
+        umma_commit(&s_full[st]);
+        return true;
+      };
+      auto issue_pv = [&](int i) {
+        const int st = i & 1;
+        if (!mbar_wait(&p_full[st], (i >> 1) & 1, abort_flag, p.err, kErrWaitFull)) return false;
+        tc_fence_after();
+        const uint32_t pa = smem_u32(sP + st * P_BYTES);
+        const uint32_t vb = smem_u32(sKV + st * 2 * KV_BYTES + KV_BYTES);
+#pragma unroll
+        for (int k = 0; k < BKV / 16; ++k)
+          umma_f16(tmem + O_COL, smem_desc_sw128(pa + (k >> 2) * (P_BYTES / 2) + (k & 3) * 32, 16, 1024),
+                   smem_desc_sw128(vb + k * 2048, 8192, 1024), idesc_o, (i != 0 || k != 0) ? 1u : 0u);
+        umma_commit(o_done);
+        umma_commit(&kv_empty[st]);
+        return true;
+      };
+      int nlive = 0;
+      for (int j = 0; j < nt; ++j) nlive += atc_tile_live(j, p, n0b, n1b) ? 1 : 0;
+      for (it = 0; ok && it < nlive; ++it) {
+        if (!issue_s(it)) break;
+        if (it >= 1 && !issue_pv(it - 1)) break;
+      }
+      if (ok && it == nlive && nlive > 0) issue_pv(nlive - 1);
+    }
+  } else {
+    // --------------------------------------------------------------------------------------- softmax / epilogue
+    const int q = warp & 3;
+    const int row = q * 32 + lane;  // query row within the tile
+    const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+    float m = -INFINITY, l = 0.f;
+    int it = 0;
+    bool ok = true;
+    for (int j = 0; j < nt && ok; ++j) {
+      if (!atc_tile_live(j, p, n0b, n1b)) continue;
+      const int st = it & 1;
+      const bool got = __all_sync(0xffffffffu, mbar_wait(&s_full[st], (it >> 1) & 1, abort_flag, p.err, kErrWaitAccFull));
+      if (!got) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[BKV];
+#pragma unroll
+      for (int c = 0; c < BKV / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(trow + st * BKV + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int k = 0; k < 32; ++k) s[c * 32 + k] = __uint_as_float(r[k]);
+      }
+      float mt = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < BKV; ++c) {
+        s[c] = atc_key_valid(j, c, p, n0b, n1b) ? s[c] * p.scale_log2 : -INFINITY;
+        mt = fmaxf(mt, s[c]);
+      }
+      const float mn = fmaxf(m, mt);
+      const float corr = exp2f(m - mn);  // 0 on the first tile (m = -inf)
+      float ps = 0.f;
+#pragma unroll
+      for (int c = 0; c < BKV; ++c) {
+        s[c] = exp2f(s[c] - mn);
+        ps += s[c];
+      }
+      l = l * corr + ps;
+      m = mn;
+      // O (TMEM) and the P buffer are free once the previous P V product has completed
+      if (it >= 1) {
+        const bool done = __all_sync(0xffffffffu, mbar_wait(o_done, (it - 1) & 1, abort_flag, p.err, kErrWaitAccFull));
+        if (!done) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld16(trow + O_COL + c * 16, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int k = 0; k < 16; ++k) r[k] = __float_as_uint(__uint_as_float(r[k]) * corr);
+          tmem_st16(trow + O_COL + c * 16, r);
+        }
+        tmem_wait_st();
+      }
+      // P_j: row `row` of a [128 x 128] bf16 K-major tile, two 64-key atoms with the 128-byte swizzle
+      uint8_t* pb = sP + st * P_BYTES;
+#pragma unroll
+      for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          const int c0 = a * 64 + ch * 8;
+          uint4 w;
+          w.x = pack_bf16(s[c0 + 0], s[c0 + 1]);
+          w.y = pack_bf16(s[c0 + 2], s[c0 + 3]);
+          w.z = pack_bf16(s[c0 + 4], s[c0 + 5]);
+          w.w = pack_bf16(s[c0 + 6], s[c0 + 7]);
+          *reinterpret_cast<uint4*>(pb + a * (P_BYTES / 2) + row * 128 + ((ch ^ (row & 7)) << 4)) = w;
+        }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[st]);
+      ++it;
+    }
+    // epilogue: O / l and the log-sum-exp (natural log)
+    if (ok && it > 0) {
+      const bool done = __all_sync(0xffffffffu, mbar_wait(o_done, (it - 1) & 1, abort_flag, p.err, kErrWaitAccFull));
+      if (done) {
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const int qrow = q0 + row;
+        float o[D];
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(trow + O_COL + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int k = 0; k < 32; ++k) o[c * 32 + k] = __uint_as_float(r[k]) * inv;
+        }
+        if (qrow < p.Lq) {
+          uint4* dst = reinterpret_cast<uint4*>(p.o + ((int64_t)b * p.Lq + qrow) * p.ldo + h * D);
+#pragma unroll
+          for (int k = 0; k < D / 8; ++k) {
+            uint4 w;
+            w.x = pack_bf16(o[8 * k + 0], o[8 * k + 1]);
+            w.y = pack_bf16(o[8 * k + 2], o[8 * k + 3]);
+            w.z = pack_bf16(o[8 * k + 4], o[8 * k + 5]);
+            w.w = pack_bf16(o[8 * k + 6], o[8 * k + 7]);
+            dst[k] = w;
+          }
+          p.lse[((int64_t)b * p.H + h) * p.Lq + qrow] = (m + log2f(l)) * kLn2;
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ====================================================================================================== torch glue
+// 3-D map over a token-major view [B * L rows, C] with row stride ld: dims (C, L, B), box (64, 128, 1).
+static CUtensorMap seq_map(const at::Tensor& t, int64_t L) {
+  const int64_t B = t.size(0) / L;
+  return make_tmap_bf16(t.data_ptr(), t.size(1), L, B, t.stride(0), t.stride(0) * L, atc::D, atc::BKV);
+}
+
+void attn_fwd_tc(const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0, const c10::optional<at::Tensor>& k1,
+                 const c10::optional<at::Tensor>& v1, const at::Tensor& n0, const at::Tensor& n1, const at::Tensor& o,
+                 const at::Tensor& lse, int64_t Lq, int64_t L0, int64_t L1, double scale) {
+  TORCH_CHECK(q.is_cuda() && q.size(1) % 64 == 0, "attn_fwd_tc: head dim 64");
+  TORCH_CHECK(n0.scalar_type() == at::kInt && n1.scalar_type() == at::kInt, "int32 key counts expected");
+  const at::cuda::CUDAGuard guard(q.device());
+  const bool has1 = k1.has_value() && k1->defined() && L1 > 0;
+  AttnTcParams p{};
+  p.n0 = n0.data_ptr<int>();
+  p.n1 = n1.data_ptr<int>();
+  p.Lq = (int)Lq;
+  p.L0 = (int)L0;
+  p.L1 = has1 ? (int)L1 : 0;
+  p.H = (int)(q.size(1) / 64);
+  p.nt0 = (int)((L0 + atc::BKV - 1) / atc::BKV);
+  p.nt1 = has1 ? (int)((L1 + atc::BKV - 1) / atc::BKV) : 0;
+  p.scale_log2 = (float)scale * atc::kLog2e;
+  p.o = reinterpret_cast<bf16*>(o.data_ptr());
+  p.ldo = o.stride(0);
+  p.lse = lse.data_ptr<float>();
+  p.err = status_word();
+  CUtensorMap mq = make_tmap_bf16(q.data_ptr(), q.size(1), Lq, q.size(0) / Lq, q.stride(0), q.stride(0) * Lq, atc::D,
+                                  atc::BQ);
+  CUtensorMap mk0 = seq_map(k0, L0), mv0 = seq_map(v0, L0);
+  CUtensorMap mk1 = has1 ? seq_map(*k1, L1) : mk0, mv1 = has1 ? seq_map(*v1, L1) : mv0;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, atc::SMEM);
+    attr = true;
+  }
+  const int B = (int)(q.size(0) / Lq);
+  dim3 grid((unsigned)((Lq + atc::BQ - 1) / atc::BQ), (unsigned)(B * p.H));
+  attn_fwd_tc_kernel<<<grid, atc::THREADS, atc::SMEM, at::cuda::getCurrentCUDAStream()>>>(mq, mk0, mv0, mk1, mv1, p);
+  NG_LAUNCH_CHECK();
+}
+
+
+// ====================================================================================================== backward
+// One CTA per (128-key tile, sample, head); loops over 128-query tiles i:
+//   MMA warp       S^T  = K Q_i^T, dP^T = V dO_i^T          (M = 128 keys, N = 128 queries, K = 64) into TMEM
+//   compute warps  (a thread per key row) P^T = exp(S^T * scale - lse), dS^T = P^T (dP^T - delta), both bf16 into
+//                  shared memory (K-major over queries: two 64-query swizzle atoms)
+//   MMA warp       dV += P^T dO_i, dK += dS^T Q_i           (M = 128 keys, N = 64, K = 128 queries; dO_i, Q_i as
+//                                                            MN-major operands)
+//                  dQ_i = dS K                               (M = 128 queries: dS^T read as an MN-major A operand)
+//   compute warps  (a thread per query row) scale * dQ_i -> fp32 tiles -> TMA reduce-add into an fp32 dQ buffer
+// dV and dK stay in TMEM across the query tiles and are written once (keys without validity get zeros).
+namespace atb {
+constexpr int BQ = 128, BK = 128, D = 64;
+constexpr int THREADS = 192;
+constexpr int T16 = BK * D * 2;        // 16 KiB: a [128 x 64] bf16 tile
+constexpr int PT = BK * BQ * 2;        // 32 KiB: P^T or dS^T [128 keys x 128 queries]
+constexpr int OFF_K = 0, OFF_V = T16, OFF_Q = 2 * T16, OFF_DO = 4 * T16, OFF_P = 6 * T16, OFF_DS = OFF_P + PT;
+constexpr int OFF_DQ = OFF_DS + PT;    // per compute warp: 2 x [32 rows x 32 fp32] = 8 KiB; 4 warps = 32 KiB
+constexpr int OFF_LSE = OFF_DQ + 32768;
+constexpr int SMEM = OFF_LSE + 4 * 2 * BQ * 4 + 1024 + 256;  // + per compute warp lse/delta, barriers
+constexpr uint32_t TMEM_COLS = 512;    // S^T [0,128), dP^T [128,256), dV [256,320), dK [320,384), dQ [384,448)
+constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320, C_DQ = 384;
+}  // namespace atb
+
+struct AttnTcBwdParams {
+  const int *n0, *n1;
+  int Lq, L0, L1, H;
+  int nt0, nt1, nq;
+  float scale, scale_log2;
+  const float* lse;
+  const float* delta;
+  bf16 *dk0, *dv0, *dk1, *dv1;
+  int64_t lddk0, lddv0, lddk1, lddv1;
+  int* err;
+};
+
+__global__ void __launch_bounds__(atb::THREADS, 1)
+    attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                       const __grid_constant__ CUtensorMap tmK0, const __grid_constant__ CUtensorMap tmV0,
+                       const __grid_constant__ CUtensorMap tmK1, const __grid_constant__ CUtensorMap tmV1,
+                       const __grid_constant__ CUtensorMap tmDQ, const AttnTcBwdParams p) {
+  using namespace atb;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* sLse = reinterpret_cast<float*>(smem + OFF_LSE);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_LSE + 4 * 2 * BQ * 4);
+  uint64_t* kv_full = bars;
+  uint64_t* qd_full = bars + 1;   // [2]
+  uint64_t* qd_empty = bars + 3;  // [2]
+  uint64_t* st_full = bars + 5;
+  uint64_t* ps_full = bars + 6;
+  uint64_t* dq_full = bars + 7;
+  uint64_t* dq_empty = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int j = blockIdx.x, bh = blockIdx.y, b = bh / p.H, h = bh - b * p.H;
+  const int n0b = p.n0[b], n1b = p.n1 ? p.n1[b] : 0;
+  const bool src1 = j >= p.nt0;
+  const int kt0 = (src1 ? j - p.nt0 : j) * BK;  // first row of this tile in its source
+  const int Lsrc = src1 ? p.L1 : p.L0;
+  const int nvalid = src1 ? n1b : n0b;
+  const bool live = kt0 < nvalid && kt0 < Lsrc;
+
+  bf16* dk_base = src1 ? p.dk1 : p.dk0;
+  bf16* dv_base = src1 ? p.dv1 : p.dv0;
+  const int64_t lddk = src1 ? p.lddk1 : p.lddk0, lddv = src1 ? p.lddv1 : p.lddv0;
+
+  if (!live) {
+    // no valid key in this tile: zero gradients for its existing rows
+    for (int idx = threadIdx.x; idx < BK * 8; idx += blockDim.x) {
+      const int r = idx >> 3, ch = idx & 7;
+      const int s = kt0 + r;
+      if (s >= Lsrc) continue;
+      const int64_t row = (int64_t)b * Lsrc + s;
+      *reinterpret_cast<uint4*>(dk_base + row * lddk + h * D + ch * 8) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(dv_base + row * lddv + h * D + ch * 8) = make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+    }
+    mbar_init(st_full, 1);
+    mbar_init(ps_full, 4);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 4);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // --------------------------------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * T16);
+      tma_load_3d(src1 ? &tmK1 : &tmK0, kv_full, smem + OFF_K, h * D, kt0, b);
+      tma_load_3d(src1 ? &tmV1 : &tmV0, kv_full, smem + OFF_V, h * D, kt0, b);
+      for (int i = 0; i < p.nq; ++i) {
+        const int st = i & 1;
+        if (!mbar_wait(&qd_empty[st], ((i >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&qd_full[st], 2 * T16);
+        tma_load_3d(&tmQ, &qd_full[st], smem + OFF_Q + st * T16, h * D, i * BQ, b);
+        tma_load_3d(&tmDO, &qd_full[st], smem + OFF_DO + st * T16, h * D, i * BQ, b);
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_bf16_f32(BK, BQ, 0, 0);  // M keys, N queries, both K-major over d
+      constexpr uint32_t id_kv = idesc_bf16_f32(BK, D, 0, 1);  // M keys, N = d (MN-major), K = queries
+      constexpr uint32_t id_q = idesc_bf16_f32(BQ, D, 1, 1);   // M queries (dS^T as MN-major A), N = d, K = keys
+      const uint32_t aK = smem_u32(smem + OFF_K), aV = smem_u32(smem + OFF_V);
+      const uint32_t aP = smem_u32(smem + OFF_P), aDS = smem_u32(smem + OFF_DS);
+      bool ok = mbar_wait(kv_full, 0, abort_flag, p.err, kErrWaitFull);
+      for (int i = 0; ok && i < p.nq; ++i) {
+        const int st = i & 1;
+        if (!mbar_wait(&qd_full[st], (i >> 1) & 1, abort_flag, p.err, kErrWaitFull)) break;
+        tc_fence_after();
+        const uint32_t aQ = smem_u32(smem + OFF_Q + st * T16), aDO = smem_u32(smem + OFF_DO + st * T16);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          umma_f16(tmem + C_S, smem_desc_sw128(aK + k * 32, 16, 1024), smem_desc_sw128(aQ + k * 32, 16, 1024), id_s,
+                   k != 0 ? 1u : 0u);
+          umma_f16(tmem + C_DP, smem_desc_sw128(aV + k * 32, 16, 1024), smem_desc_sw128(aDO + k * 32, 16, 1024),
+                   id_s, k != 0 ? 1u : 0u);
+        }
+        umma_commit(st_full);
+        if (!mbar_wait(ps_full, i & 1, abort_flag, p.err, kErrWaitFull)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < BQ / 16; ++k) {
+          const uint32_t ka = (k >> 2) * (PT / 2) + (k & 3) * 32;  // K-major over queries: atom, then 32 B steps
+          umma_f16(tmem + C_DV, smem_desc_sw128(aP + ka, 16, 1024), smem_desc_sw128(aDO + k * 2048, 8192, 1024),
+                   id_kv, (i != 0 || k != 0) ? 1u : 0u);
+          umma_f16(tmem + C_DK, smem_desc_sw128(aDS + ka, 16, 1024), smem_desc_sw128(aQ + k * 2048, 8192, 1024),
+                   id_kv, (i != 0 || k != 0) ? 1u : 0u);
+        }
+        if (i >= 1 && !mbar_wait(dq_empty, (i - 1) & 1, abort_flag, p.err, kErrWaitAccEmpty)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k)  // A = dS (queries x keys): dS^T rows are keys -> MN-major, 16 keys per step
+          umma_f16(tmem + C_DQ, smem_desc_sw128(aDS + k * 2048, PT / 2, 1024),
+                   smem_desc_sw128(aK + k * 2048, 8192, 1024), id_q, k != 0 ? 1u : 0u);
+        umma_commit(dq_full);
+        umma_commit(&qd_empty[st]);
+      }
+    }
+  } else {
+    // --------------------------------------------------------------------------------------- compute warps
+    const int qq = warp & 3;
+    const int r = qq * 32 + lane;                        // key row (P/dS phase) or query row (dQ phase)
+    const uint32_t trow = tmem + ((uint32_t)(qq * 32) << 16);
+    const bool key_ok = (kt0 + r) < nvalid && (kt0 + r) < Lsrc;
+    uint8_t* dq_st = smem + OFF_DQ + (warp - 2) * 8192;  // this warp's two [32 x 32] fp32 tiles
+    const float* lse_bh = p.lse + ((int64_t)b * p.H + h) * p.Lq;
+    const float* del_bh = p.delta + ((int64_t)b * p.H + h) * p.Lq;
+    float* wLse = sLse + (warp - 2) * 2 * BQ;  // this warp's copy of the query tile's lse (log2 units) and delta
+    float* wDel = wLse + BQ;
+    bool ok = true;
+    for (int i = 0; i < p.nq && ok; ++i) {
+      __syncwarp();
+#pragma unroll
+      for (int k = 0; k < BQ / 32; ++k) {
+        const int qg = i * BQ + k * 32 + lane;
+        wLse[k * 32 + lane] = qg < p.Lq ? lse_bh[qg] * atc::kLog2e : INFINITY;
+        wDel[k * 32 + lane] = qg < p.Lq ? del_bh[qg] : 0.f;
+      }
+      __syncwarp();
+      const bool got = __all_sync(0xffffffffu, mbar_wait(st_full, i & 1, abort_flag, p.err, kErrWaitAccFull));
+      if (!got) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint8_t* sP = smem + OFF_P;
+      uint8_t* sDS = smem + OFF_DS;
+#pragma unroll 1
+      for (int c = 0; c < BQ / 32; ++c) {
+        uint32_t rs[32], rd[32];
+        tmem_ld32(trow + C_S + c * 32, rs);
+        tmem_ld32(trow + C_DP + c * 32, rd);
+        tmem_wait_ld();
+        float pv[32], dv[32];
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+          const int qc = c * 32 + k;
+          const float pk = key_ok ? exp2f(__uint_as_float(rs[k]) * p.scale_log2 - wLse[qc]) : 0.f;
+          pv[k] = pk;
+          dv[k] = pk * (__uint_as_float(rd[k]) - wDel[qc]);
+        }
+        // 32 queries = half of a 64-query atom: atom c / 2, chunks 4 * (c % 2) .. +3
+        const int atom = c >> 1;
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          const int cc = (c & 1) * 4 + ch;
+          const uint32_t off = atom * (PT / 2) + r * 128 + ((cc ^ (r & 7)) << 4);
+          uint4 w;
+          w.x = pack_bf16(pv[8 * ch + 0], pv[8 * ch + 1]);
+          w.y = pack_bf16(pv[8 * ch + 2], pv[8 * ch + 3]);
+          w.z = pack_bf16(pv[8 * ch + 4], pv[8 * ch + 5]);
+          w.w = pack_bf16(pv[8 * ch + 6], pv[8 * ch + 7]);
+          *reinterpret_cast<uint4*>(sP + off) = w;
+          w.x = pack_bf16(dv[8 * ch + 0], dv[8 * ch + 1]);
+          w.y = pack_bf16(dv[8 * ch + 2], dv[8 * ch + 3]);
+          w.z = pack_bf16(dv[8 * ch + 4], dv[8 * ch + 5]);
+          w.w = pack_bf16(dv[8 * ch + 6], dv[8 * ch + 7]);
+          *reinterpret_cast<uint4*>(sDS + off) = w;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ps_full);
+      // dQ_i: rows are queries now
+      const bool dq = __all_sync(0xffffffffu, mbar_wait(dq_full, i & 1, abort_flag, p.err, kErrWaitAccFull));
+      if (!dq) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (lane == 0) bulk_wait_read0();  // the previous tile's dQ stores have read the staging tiles
+      __syncwarp();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t rq[32];
+        tmem_ld32(trow + C_DQ + c * 32, rq);
+        tmem_wait_ld();
+        uint8_t* t = dq_st + c * 4096;
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch)
+          *reinterpret_cast<float4*>(t + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
+              make_float4(__uint_as_float(rq[4 * ch]) * p.scale, __uint_as_float(rq[4 * ch + 1]) * p.scale,
+                          __uint_as_float(rq[4 * ch + 2]) * p.scale, __uint_as_float(rq[4 * ch + 3]) * p.scale);
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(dq_empty);
+        tma_reduce_add_3d(&tmDQ, dq_st, h * D, i * BQ + qq * 32, b);
+        tma_reduce_add_3d(&tmDQ, dq_st + 4096, h * D + 32, i * BQ + qq * 32, b);
+        bulk_commit();
+      }
+    }
+    // dV, dK (complete once the last dq_full arrived: their MMAs were committed before it). The TMEM loads are
+    // warp-collective (.sync.aligned): every lane issues them; only the stores depend on the row existing.
+    if (ok) {
+      tc_fence_after();
+      const int s = kt0 + r;
+      const int64_t row = (int64_t)b * Lsrc + s;
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {
+        float v[D];
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t rr[32];
+          tmem_ld32(trow + (which ? C_DK : C_DV) + c * 32, rr);
+          tmem_wait_ld();
+#pragma unroll
+          for (int k = 0; k < 32; ++k) v[c * 32 + k] = __uint_as_float(rr[k]) * (which ? p.scale : 1.f);
+        }
+        if (s < Lsrc) {
+          bf16* dst = which ? dk_base + row * lddk + h * D : dv_base + row * lddv + h * D;
+#pragma unroll
+          for (int k = 0; k < D / 8; ++k) {
+            uint4 w;
+            w.x = pack_bf16(v[8 * k + 0], v[8 * k + 1]);
+            w.y = pack_bf16(v[8 * k + 2], v[8 * k + 3]);
+            w.z = pack_bf16(v[8 * k + 4], v[8 * k + 5]);
+            w.w = pack_bf16(v[8 * k + 6], v[8 * k + 7]);
+            reinterpret_cast<uint4*>(dst)[k] = w;
+          }
+        }
+      }
+    }
+    if (lane == 0) bulk_wait0();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// dq_acc[row, c] (fp32, TMA reduce-add target) -> dq (bf16, strided view)
+__global__ void dq_store_kernel(const float* __restrict__ acc, bf16* __restrict__ dq, int64_t lddq, int64_t rows,
+                                int C) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t n8 = rows * (C / 8);
+  if (t >= n8) return;
+  const int64_t row = t / (C / 8);
+  const int c8 = (int)(t - row * (C / 8));
+  const float4 a = reinterpret_cast<const float4*>(acc + row * C)[2 * c8];
+  const float4 b = reinterpret_cast<const float4*>(acc + row * C)[2 * c8 + 1];
+  uint4 w;
+  w.x = pack_bf16(a.x, a.y);
+  w.y = pack_bf16(a.z, a.w);
+  w.z = pack_bf16(b.x, b.y);
+  w.w = pack_bf16(b.z, b.w);
+  *reinterpret_cast<uint4*>(dq + row * lddq + c8 * 8) = w;
+}
+
+void attn_delta(const bf16* dout, int64_t lddo, const bf16* o, int64_t ldo, float* delta, int rows, int Lq, int H,
+                cudaStream_t s);
+
+// Same contract as attn_bwd (csrc/attention.cu): delta = rowsum(dO * O), then the tcgen05 kernel, whose dQ partials
+// (one per key tile) are summed by TMA reduce-adds into a zeroed fp32 buffer and stored as bf16 at the end.
+void attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0,
+                 const c10::optional<at::Tensor>& k1, const c10::optional<at::Tensor>& v1, const at::Tensor& n0,
+                 const at::Tensor& n1, const at::Tensor& o, const at::Tensor& lse, const at::Tensor& dq,
+                 const at::Tensor& dk0, const at::Tensor& dv0, const c10::optional<at::Tensor>& dk1,
+                 const c10::optional<at::Tensor>& dv1, int64_t Lq, int64_t L0, int64_t L1, double scale) {
+  TORCH_CHECK(q.is_cuda() && q.size(1) % 64 == 0, "attn_bwd_tc: head dim 64");
+  TORCH_CHECK(n0.scalar_type() == at::kInt && n1.scalar_type() == at::kInt, "int32 key counts expected");
+  for (const at::Tensor* t : {&dout, &o, &dq, &dk0, &dv0})
+    TORCH_CHECK(t->dim() == 2 && t->stride(1) == 1 && t->stride(0) % 8 == 0 && t->scalar_type() == at::kBFloat16,
+                "attn_bwd_tc: bf16 row-major views with 16-byte row strides expected");
+  const at::cuda::CUDAGuard guard(q.device());
+  const bool has1 = k1.has_value() && k1->defined() && L1 > 0;
+  const int64_t B = q.size(0) / Lq, C = q.size(1);
+  AttnTcBwdParams p{};
+  p.n0 = n0.data_ptr<int>();
+  p.n1 = n1.data_ptr<int>();
+  p.Lq = (int)Lq;
+  p.L0 = (int)L0;
+  p.L1 = has1 ? (int)L1 : 0;
+  p.H = (int)(C / 64);
+  p.nt0 = (int)((L0 + atb::BK - 1) / atb::BK);
+  p.nt1 = has1 ? (int)((L1 + atb::BK - 1) / atb::BK) : 0;
+  p.nq = (int)((Lq + atb::BQ - 1) / atb::BQ);
+  p.scale = (float)scale;
+  p.scale_log2 = (float)scale * atc::kLog2e;
+  p.lse = lse.data_ptr<float>();
+  p.dk0 = reinterpret_cast<bf16*>(dk0.data_ptr());
+  p.dv0 = reinterpret_cast<bf16*>(dv0.data_ptr());
+  p.lddk0 = dk0.stride(0);
+  p.lddv0 = dv0.stride(0);
+  if (has1) {
+    TORCH_CHECK(dk1.has_value() && dv1.has_value(), "attn_bwd_tc: dk1/dv1 required with a second key source");
+    p.dk1 = reinterpret_cast<bf16*>(dk1->data_ptr());
+    p.dv1 = reinterpret_cast<bf16*>(dv1->data_ptr());
+    p.lddk1 = dk1->stride(0);
+    p.lddv1 = dv1->stride(0);
+  }
+  p.err = status_word();
+  auto s = at::cuda::getCurrentCUDAStream();
+  at::Tensor delta = at::empty({B, (int64_t)p.H, Lq}, q.options().dtype(at::kFloat));
+  attn_delta(reinterpret_cast<const bf16*>(dout.data_ptr()), dout.stride(0), reinterpret_cast<const bf16*>(o.data_ptr()),
+             o.stride(0), delta.data_ptr<float>(), (int)q.size(0), (int)Lq, p.H, s);
+  p.delta = delta.data_ptr<float>();
+  at::Tensor acc = at::empty({q.size(0), C}, q.options().dtype(at::kFloat));
+  cudaMemsetAsync(acc.data_ptr(), 0, acc.numel() * sizeof(float), s);
+  CUtensorMap mq = make_tmap_bf16(q.data_ptr(), C, Lq, B, q.stride(0), q.stride(0) * Lq, 64, 128);
+  CUtensorMap mdo = make_tmap_bf16(dout.data_ptr(), C, Lq, B, dout.stride(0), dout.stride(0) * Lq, 64, 128);
+  CUtensorMap mk0 = seq_map(k0, L0), mv0 = seq_map(v0, L0);
+  CUtensorMap mk1 = has1 ? seq_map(*k1, L1) : mk0, mv1 = has1 ? seq_map(*v1, L1) : mv0;
+  CUtensorMap mdq = make_tmap_f32_box(acc.data_ptr(), C, Lq, B, C, C * Lq, 32, 32);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, atb::SMEM);
+    attr = true;
+  }
+  dim3 grid((unsigned)(p.nt0 + p.nt1), (unsigned)(B * p.H));
+  attn_bwd_tc_kernel<<<grid, atb::THREADS, atb::SMEM, s>>>(mq, mdo, mk0, mv0, mk1, mv1, mdq, p);
+  NG_LAUNCH_CHECK();
+  const int64_t n8 = q.size(0) * (C / 8);
+  dq_store_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(acc.data_ptr<float>(),
+                                                               reinterpret_cast<bf16*>(dq.data_ptr()), dq.stride(0),
+                                                               q.size(0), (int)C);
+  NG_LAUNCH_CHECK();
+}
+
+}  // namespace ng

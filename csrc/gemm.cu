@@ -653,6 +653,13 @@ CUtensorMap make_tmap_bf16(const void* ptr, int64_t inner, int64_t outer, int64_
                    CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// fp32 map with the 128-byte swizzle and a given box (inner box of 32 fp32 = 128 bytes).
+CUtensorMap make_tmap_f32_box(const void* ptr, int64_t inner, int64_t outer, int64_t batch, int64_t ld,
+                              int64_t bstride, int box_inner, int box_outer) {
+  return make_tmap(ptr, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, inner, outer, batch, ld, bstride, box_inner, box_outer,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 // 32 x 32 epilogue tile maps: bf16 with the 64-byte swizzle, fp32 with the 128-byte swizzle.
 static CUtensorMap epi_map_bf16(const void* ptr, int64_t cols, int64_t rows, int64_t batch, int64_t ld, int64_t bs) {
   return make_tmap(ptr, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, cols, rows, batch, ld, bs, 32, 32,

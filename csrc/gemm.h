@@ -50,6 +50,8 @@ struct GemmArgs {
 
 void gemm_launch(const GemmArgs& g, cudaStream_t stream);
 
+CUtensorMap make_tmap_f32_box(const void* ptr, int64_t inner, int64_t outer, int64_t batch, int64_t ld,
+                              int64_t bstride, int box_inner, int box_outer);
 CUtensorMap make_tmap_bf16(const void* ptr, int64_t inner, int64_t outer, int64_t batch, int64_t ld, int64_t bstride,
                            int box_inner, int box_outer);
 

@@ -40,9 +40,10 @@ def _keys_cpu(k0, v0, L0, n0, k1, v1, L1, n1, B, H):
     return torch.stack(ks), torch.stack(vs), torch.stack(masks)
 
 
-def attn_fwd(q, Lq, k0, v0, L0, n0, k1=None, v1=None, L1=0, n1=None, scale=0.125):
+def attn_fwd(q, Lq, k0, v0, L0, n0, k1=None, v1=None, L1=0, n1=None, scale=0.125, impl="tc"):
     """q [B*Lq, H*64]; k0/v0 [B*L0, H*64]; k1/v1 [B*L1, H*64] or None; n0/n1: int or int32 [B] valid-key counts.
-    Returns (o [B*Lq, H*64] bf16, lse [B, H, Lq] fp32)."""
+    Returns (o [B*Lq, H*64] bf16, lse [B, H, Lq] fp32). On CUDA the forward runs on tcgen05/TMEM
+    (csrc/attn_tc.cu); impl="mma" selects the warp-level mma.sync kernel (csrc/attention.cu), kept as a test oracle."""
     rows, C = q.shape
     B, H = rows // Lq, C // HEAD
     n0 = _lens(n0, B, q.device)
@@ -58,14 +59,18 @@ def attn_fwd(q, Lq, k0, v0, L0, n0, k1=None, v1=None, L1=0, n1=None, scale=0.125
         return o.to(torch.bfloat16), lse
     o = torch.empty(rows, C, device=q.device, dtype=torch.bfloat16)
     lse = torch.empty(B, H, Lq, device=q.device, dtype=torch.float32)
-    ext().attn_fwd(q, k0, v0, k1, v1, n0, n1, o, lse, Lq, L0, L1, scale)
+    if impl == "tc":
+        ext().attn_fwd_tc(q, k0, v0, k1, v1, n0, n1, o, lse, Lq, L0, L1, scale)
+    else:
+        ext().attn_fwd(q, k0, v0, k1, v1, n0, n1, o, lse, Lq, L0, L1, scale)
     return o, lse
 
 
 def attn_bwd(do, q, Lq, k0, v0, L0, n0, o, lse, k1=None, v1=None, L1=0, n1=None, scale=0.125,
-             dq=None, dk0=None, dv0=None, dk1=None, dv1=None):
+             dq=None, dk0=None, dv0=None, dk1=None, dv1=None, impl="tc"):
     """Gradients of attn_fwd. dq/dk*/dv* may be given as (strided) views to write into; missing ones are allocated.
-    Returns (dq, dk0, dv0, dk1, dv1)."""
+    Returns (dq, dk0, dv0, dk1, dv1). On CUDA the backward runs on tcgen05/TMEM (csrc/attn_tc.cu: CTA per key tile,
+    dK/dV accumulated in TMEM, dQ summed over key tiles by TMA reduce-adds); impl="mma" selects the mma.sync kernels."""
     rows, C = q.shape
     B, H = rows // Lq, C // HEAD
     n0 = _lens(n0, B, q.device)
@@ -112,5 +117,6 @@ def attn_bwd(do, q, Lq, k0, v0, L0, n0, o, lse, k1=None, v1=None, L1=0, n1=None,
     if k1 is not None:
         dk1 = alloc(dk1, B * L1)
         dv1 = alloc(dv1, B * L1)
-    ext().attn_bwd(do, q, k0, v0, k1, v1, n0, n1, o, lse, dq, dk0, dv0, dk1, dv1, Lq, L0, L1, scale)
+    fn = ext().attn_bwd_tc if impl == "tc" else ext().attn_bwd
+    fn(do, q, k0, v0, k1, v1, n0, n1, o, lse, dq, dk0, dv0, dk1, dv1, Lq, L0, L1, scale)
     return dq, dk0, dv0, dk1, dv1

@@ -85,6 +85,44 @@ def bench_fused(d, batch, rows):
         print(json.dumps(row), flush=True)
 
 
+def bench_attn(d, batch, rows, T=128):
+    """Image joint attention (256 queries, 256 image + T caption keys with random valid lengths): tcgen05 and
+    mma.sync forward/backward, and torch SDPA with a boolean key mask (the reference's call) on the same problem."""
+    from nano_gpic_b200.ops import attention as A
+    H, L = d // 64, 256
+    M = batch * L
+    r = lambda *s: (torch.randn(*s, device="cuda")).bfloat16()
+    qkv, kv = r(M, 3 * d), r(batch * T, 2 * d)
+    lens = torch.randint(1, T + 1, (batch,), device="cuda", dtype=torch.int32)
+    q, k0, v0, k1, v1 = qkv[:, :d], qkv[:, d:2 * d], qkv[:, 2 * d:], kv[:, :d], kv[:, d:]
+    o, lse = A.attn_fwd(q, L, k0, v0, L, L, k1, v1, T, lens)
+    do = r(M, d)
+    # FLOPs of the work that must be done: valid keys only
+    keys = (L + lens.float()).sum().item()
+    fl_fwd = 4.0 * L * keys * 64 * H
+    res = {"tc_fwd": time_fn(lambda: A.attn_fwd(q, L, k0, v0, L, L, k1, v1, T, lens, impl="tc")),
+           "mma_fwd": time_fn(lambda: A.attn_fwd(q, L, k0, v0, L, L, k1, v1, T, lens, impl="mma")),
+           "tc_bwd": time_fn(lambda: A.attn_bwd(do, q, L, k0, v0, L, L, o, lse, k1, v1, T, lens, impl="tc")),
+           "mma_bwd": time_fn(lambda: A.attn_bwd(do, q, L, k0, v0, L, L, o, lse, k1, v1, T, lens, impl="mma"))}
+    Q = q.view(batch, L, H, 64).transpose(1, 2)
+    K = torch.cat([k0.reshape(batch, L, H, 64), k1.reshape(batch, T, H, 64)], 1).transpose(1, 2)
+    V = torch.cat([v0.reshape(batch, L, H, 64), v1.reshape(batch, T, H, 64)], 1).transpose(1, 2)
+    mask = torch.cat([torch.ones(batch, L, dtype=torch.bool, device="cuda"),
+                      torch.arange(T, device="cuda")[None] < lens[:, None]], 1)[:, None, None, :]
+    sdpa = torch.nn.functional.scaled_dot_product_attention
+    res["sdpa_fwd"] = time_fn(lambda: sdpa(Q, K, V, attn_mask=mask))
+    Qg, Kg, Vg = (t.detach().clone().requires_grad_(True) for t in (Q, K, V))
+    out = sdpa(Qg, Kg, Vg, attn_mask=mask)
+    g = torch.randn_like(out)
+    res["sdpa_bwd"] = time_fn(lambda: torch.autograd.grad(out, (Qg, Kg, Vg), g, retain_graph=True))
+    row = {"kernel": "attention", "B": batch, "H": H, "Lq": L, "T": T}
+    for k, v in res.items():
+        row[k + "_us"] = round(v * 1e6, 1)
+        row[k + "_tflops"] = round((fl_fwd if "fwd" in k else 2.5 * fl_fwd) / v / 1e12, 1)
+    rows.append(row)
+    print(json.dumps(row), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm")
@@ -98,6 +136,8 @@ def main():
         bench_gemm(a.d, a.batch, rows)
     if "fused" in only:
         bench_fused(a.d, a.batch, rows)
+    if "attn" in only:
+        bench_attn(a.d, a.batch, rows)
     if a.json:
         with open(a.json, "w") as f:
             json.dump(rows, f, indent=1)

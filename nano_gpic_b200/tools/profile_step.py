@@ -17,6 +17,7 @@ def main():
     ap.add_argument("--caption-len", type=int, default=128)
     ap.add_argument("--out", default=None)
     ap.add_argument("--rows", type=int, default=40)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     a = ap.parse_args()
     import sys, os
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
@@ -24,14 +25,23 @@ def main():
     from nano_gpic_b200.train.trainer import Trainer
     dev = torch.device("cuda", 0)
     gb = a.micro_batch * a.accum
-    tr = Trainer.for_ladder(a.size, device=dev, micro_batch=a.micro_batch, global_batch=gb)
     batch = synthetic_batch(gb, a.caption_len, 2048, seed=0, device=dev)
+    if a.impl == "reference":  # the reference arm of bench.py, one step
+        import types
+        import bench
+        ns = types.SimpleNamespace(size=a.size, micro_batch=a.micro_batch, global_batch=gb, caption_len=a.caption_len,
+                                   warmup=3, steps=1, no_e2e=True)
+        step = bench.reference_step_fn(ns, 0, 1, dev)
+        run = lambda: step(*batch)
+    else:
+        tr = Trainer.for_ladder(a.size, device=dev, micro_batch=a.micro_batch, global_batch=gb)
+        run = lambda: tr.train_step(*batch)
     for _ in range(3):
-        tr.train_step(*batch)
+        run()
     torch.cuda.synchronize()
     from torch.profiler import ProfilerActivity, profile
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        tr.train_step(*batch)
+        run()
         torch.cuda.synchronize()
     table = prof.key_averages().table(sort_by="cuda_time_total", row_limit=a.rows, max_name_column_width=90)
     print(table)

@@ -111,3 +111,76 @@ def test_attention(joint):
         if a is None:
             continue
         _close(a, b, what=name)
+
+
+@pytest.mark.parametrize("case", ["joint", "text", "joint_long"])
+def test_attention_tc_forward(case):
+    """tcgen05 forward against the fp32 reference and the mma.sync kernel (partial tiles, skipped tiles, T > 128)."""
+    from nano_gpic_b200.ops import attention as A
+    torch.manual_seed(1)
+    B, H = 3, 4
+    C = H * 64
+    if case == "joint":
+        Lq, L0, L1, n0, n1 = 256, 256, 72, 256, torch.tensor([72, 5, 40], dtype=torch.int32, device="cuda")
+    elif case == "joint_long":
+        Lq, L0, L1, n0, n1 = 256, 256, 200, 256, torch.tensor([200, 129, 3], dtype=torch.int32, device="cuda")
+    else:
+        Lq, L0, L1, n0, n1 = 72, 72, 0, torch.tensor([72, 9, 33], dtype=torch.int32, device="cuda"), None
+    qkv = torch.randn(B * Lq, 3 * C, device="cuda").bfloat16()
+    q, k0, v0 = qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:]
+    if L1:
+        kv = torch.randn(B * L1, 2 * C, device="cuda").bfloat16()
+        k1, v1 = kv[:, :C], kv[:, C:]
+    else:
+        k1 = v1 = None
+    o, lse = A.attn_fwd(q, Lq, k0, v0, L0, n0, k1, v1, L1, n1, impl="tc")
+    om, lsem = A.attn_fwd(q, Lq, k0, v0, L0, n0, k1, v1, L1, n1, impl="mma")
+    oc, lsec = A.attn_fwd(*_cpu(q), Lq, *_cpu(k0, v0), L0, n0 if isinstance(n0, int) else n0.cpu(),
+                          *_cpu(k1, v1), L1, n1.cpu() if n1 is not None else None)
+    _close(o, oc, what="o vs fp32")
+    _close(lse, lsec, rtol=1e-3, atol=2e-3, what="lse vs fp32")
+    _close(o, om, what="o vs mma")
+    from nano_gpic_b200.ops import status
+    assert status.read() == 0
+
+
+@pytest.mark.parametrize("case", ["joint", "text", "joint_long", "odd"])
+def test_attention_tc_backward(case):
+    """tcgen05 backward against the fp32 autograd reference and the mma.sync kernels; dK/dV of padded keys are zero."""
+    from nano_gpic_b200.ops import attention as A
+    torch.manual_seed(2)
+    B, H = 3, 4
+    C = H * 64
+    if case == "joint":
+        Lq, L0, L1, n0, n1 = 256, 256, 72, 256, torch.tensor([72, 5, 40], dtype=torch.int32, device="cuda")
+    elif case == "joint_long":
+        Lq, L0, L1, n0, n1 = 256, 256, 200, 256, torch.tensor([200, 129, 3], dtype=torch.int32, device="cuda")
+    elif case == "odd":
+        Lq, L0, L1, n0, n1 = 200, 200, 40, torch.tensor([200, 150, 7], dtype=torch.int32, device="cuda"), \
+            torch.tensor([40, 0, 17], dtype=torch.int32, device="cuda")
+    else:
+        Lq, L0, L1, n0, n1 = 72, 72, 0, torch.tensor([72, 9, 33], dtype=torch.int32, device="cuda"), None
+    qkv = torch.randn(B * Lq, 3 * C, device="cuda").bfloat16()
+    q, k0, v0 = qkv[:, :C], qkv[:, C:2 * C], qkv[:, 2 * C:]
+    if L1:
+        kv = torch.randn(B * L1, 2 * C, device="cuda").bfloat16()
+        k1, v1 = kv[:, :C], kv[:, C:]
+    else:
+        k1 = v1 = None
+    o, lse = A.attn_fwd(q, Lq, k0, v0, L0, n0, k1, v1, L1, n1)
+    do = torch.randn_like(o)
+    dqkv = torch.full_like(qkv, 7.0)  # strided destinations, like the fused qkv gradient
+    dkv = torch.full((B * L1, 2 * C), 7.0, device="cuda", dtype=torch.bfloat16) if L1 else None
+    g = A.attn_bwd(do, q, Lq, k0, v0, L0, n0, o, lse, k1, v1, L1, n1, dq=dqkv[:, :C], dk0=dqkv[:, C:2 * C],
+                   dv0=dqkv[:, 2 * C:], dk1=dkv[:, :C] if L1 else None, dv1=dkv[:, C:] if L1 else None, impl="tc")
+    gm = A.attn_bwd(do, q, Lq, k0, v0, L0, n0, o, lse, k1, v1, L1, n1, impl="mma")
+    n0c = n0 if isinstance(n0, int) else n0.cpu()
+    gc = A.attn_bwd(*_cpu(do, q), Lq, *_cpu(k0, v0), L0, n0c, *_cpu(o, lse, k1, v1), L1,
+                    n1.cpu() if n1 is not None else None)
+    for name, a, m, c in zip(["dq", "dk0", "dv0", "dk1", "dv1"], g, gm, gc):
+        if a is None:
+            continue
+        _close(a, c, what=name + " vs fp32")
+        _close(a, m, what=name + " vs mma")
+    from nano_gpic_b200.ops import status
+    assert status.read() == 0
