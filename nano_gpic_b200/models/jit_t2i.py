@@ -171,9 +171,16 @@ class FinalLayer(nn.Module):
 
 
 # ------------------------------------------------------------------------------------------- block functions
+def _stage_hook(hook):
+    """hook = (model, n): at the start of a block's backward the first n backward stages (final layer, image blocks
+    from the last, text blocks from the last) hold final gradients; tell the data-parallel layer, if it listens."""
+    if hook is not None and hook[0]._bwd_hook is not None:
+        hook[0]._bwd_hook(hook[1])
+
+
 class _TextBlockFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, y, mod, anchor, blk, lens, T):
+    def forward(ctx, y, mod, anchor, blk, lens, T, hook=None):
         C = y.shape[1]
         a = blk.attn
         n1, n2 = blk.norm1, blk.norm2
@@ -186,7 +193,7 @@ class _TextBlockFn(torch.autograd.Function):
         h2, r2 = NR.rms_mod_fwd(y2, f32(n2.weight), mod[:, 3 * C:4 * C], mod[:, 4 * C:5 * C], T, n2.variance_epsilon)
         act, pre = G.swiglu_linear(h2, w16(blk.mlp.w12))
         y3, ym = G.linear_gated_residual(act, w16(blk.mlp.w3), None, y2, mod[:, 5 * C:6 * C], T)
-        ctx.blk, ctx.T = blk, T
+        ctx.blk, ctx.T, ctx.hook = blk, T, hook
         ctx.save_for_backward(y, mod, lens, h1, r1, qkv, q, rq, k, rk, o, lse, y2, ya, h2, r2, act, pre, ym)
         return y3
 
@@ -194,6 +201,7 @@ class _TextBlockFn(torch.autograd.Function):
     def backward(ctx, dy3):
         (y, mod, lens, h1, r1, qkv, q, rq, k, rk, o, lse, y2, ya, h2, r2, act, pre, ym) = ctx.saved_tensors
         blk, T = ctx.blk, ctx.T
+        _stage_hook(ctx.hook)
         a = blk.attn
         C = y.shape[1]
         dy3 = dy3.contiguous()
@@ -220,12 +228,12 @@ class _TextBlockFn(torch.autograd.Function):
         _wgrad(dqkv, h1, a.qkv.weight)
         dy = NR.rms_mod_bwd(dh1, y, r1, f32(blk.norm1.weight), mod[:, C:2 * C], T, dres=dy2,
                             dw_acc=grad_of(blk.norm1.weight), dshift=dmod[:, 0:C], dscale=dmod[:, C:2 * C])
-        return dy, dmod.to(BF16), None, None, None, None
+        return dy, dmod.to(BF16), None, None, None, None, None
 
 
 class _ImageBlockFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, yt, mod, anchor, blk, lens, L, T, cos, sin):
+    def forward(ctx, x, yt, mod, anchor, blk, lens, L, T, cos, sin, hook=None):
         C = x.shape[1]
         a = blk.attn
         n1, n2 = blk.norm1, blk.norm2
@@ -240,7 +248,7 @@ class _ImageBlockFn(torch.autograd.Function):
         h2, r2 = NR.rms_mod_fwd(x2, f32(n2.weight), mod[:, 3 * C:4 * C], mod[:, 4 * C:5 * C], L, n2.variance_epsilon)
         act, pre = G.swiglu_linear(h2, w16(blk.mlp.w12))
         x3, ym = G.linear_gated_residual(act, w16(blk.mlp.w3), None, x2, mod[:, 5 * C:6 * C], L)
-        ctx.blk, ctx.L, ctx.T = blk, L, T
+        ctx.blk, ctx.L, ctx.T, ctx.hook = blk, L, T, hook
         ctx.save_for_backward(x, yt, mod, lens, cos, sin, h1, r1, qkv, kvy, q, rq, kx, rkx, ky, rky, o, lse, x2, ya,
                               h2, r2, act, pre, ym)
         return x3
@@ -250,6 +258,7 @@ class _ImageBlockFn(torch.autograd.Function):
         (x, yt, mod, lens, cos, sin, h1, r1, qkv, kvy, q, rq, kx, rkx, ky, rky, o, lse, x2, ya, h2, r2, act, pre,
          ym) = ctx.saved_tensors
         blk, L, T = ctx.blk, ctx.L, ctx.T
+        _stage_hook(ctx.hook)
         a = blk.attn
         C = x.shape[1]
         dx3 = dx3.contiguous()
@@ -280,7 +289,27 @@ class _ImageBlockFn(torch.autograd.Function):
         _wgrad(dkvy, yt, a.kv_y.weight)
         dx = NR.rms_mod_bwd(dh1, x, r1, f32(blk.norm1.weight), mod[:, C:2 * C], L, dres=dx2,
                             dw_acc=grad_of(blk.norm1.weight), dshift=dmod[:, 0:C], dscale=dmod[:, C:2 * C])
-        return dx, dyt, dmod.to(BF16), None, None, None, None, None, None, None
+        return dx, dyt, dmod.to(BF16), None, None, None, None, None, None, None, None
+
+
+class _ModFn(torch.autograd.Function):
+    """adaLN modulation mod = c W^T + b from the bf16 weight shadow (the reference's autocast Linear(C, 6C));
+    W and b gradients into the fp32 .grad buffers, dc = dmod W."""
+
+    @staticmethod
+    def forward(ctx, c16, anchor, lin):
+        ctx.lin = lin
+        ctx.save_for_backward(c16)
+        return F.linear(c16, w16(lin), w16(lin.bias))
+
+    @staticmethod
+    def backward(ctx, dmod):
+        (c16,) = ctx.saved_tensors
+        lin = ctx.lin
+        dmod = dmod.to(BF16).contiguous()
+        _wgrad(dmod, c16, lin.weight)
+        _bias_grad(dmod, lin.bias)
+        return G.linear_dgrad(dmod, w16(lin)), None, None
 
 
 class _LinearFn(torch.autograd.Function):
@@ -387,7 +416,10 @@ class JiT_T2I(nn.Module):
                                                  for _ in range(num_text_blocks)])
         self.final_layer = FinalLayer(hidden_size, patch_dim)
         self.initialize_weights()
+        for p in self.t_embedder.parameters():  # read in fp32 by the forward: replicated under sharding
+            p._replicate = True
         self._rope = {}
+        self._bwd_hook = None  # set by the data-parallel layer around the last micro-batch's backward
 
     # ------------------------------------------------------------------------------------------------- init
     def initialize_weights(self):
@@ -437,20 +469,21 @@ class JiT_T2I(nn.Module):
         yt = y.reshape(B * T, -1).to(BF16)
         yt = _LinearFn.apply(yt, self.y_embedder.proj.weight, self.y_embedder.proj, False)
         yt = _RMSFn.apply(yt, self.y_embedder.norm.weight, self.y_embedder.norm)
-        yt = _AddRowsFn.apply(yt, self.y_pos_embedding, self.y_pos_embedding.detach()[0, :T].to(BF16), T,
-                              self.y_pos_embedding)
-        for blk in self.text_refine_blocks:
+        yt = _AddRowsFn.apply(yt, self.y_pos_embedding, w16(self.y_pos_embedding)[0, :T], T, self.y_pos_embedding)
+        nb, nt = len(self.blocks), len(self.text_refine_blocks)
+        c = c.to(BF16)
+        for j, blk in enumerate(self.text_refine_blocks):
             lin = blk.adaLN_modulation.lin
-            mod = F.linear(c, lin.weight.to(BF16), lin.bias.to(BF16))
-            yt = _TextBlockFn.apply(yt, mod, blk.norm1.weight, blk, lens, T)
+            mod = _ModFn.apply(c, lin.weight, lin)
+            yt = _TextBlockFn.apply(yt, mod, blk.norm1.weight, blk, lens, T, (self, 1 + nb + (nt - 1 - j)))
         # image tokens: Linear(Linear(patch)) + pos_embed
         h = _LinearFn.apply(x_tok, self.x_embedder.proj1.weight, self.x_embedder.proj1, False)
         h = _LinearFn.apply(h, self.x_embedder.proj2.weight, self.x_embedder.proj2, True)
         x = _AddRowsFn.apply(h, None, self.pos_embed.detach()[0], N, None)
-        for blk in self.blocks:
+        for i, blk in enumerate(self.blocks):
             lin = blk.adaLN_modulation.lin
-            mod = F.linear(c, lin.weight.to(BF16), lin.bias.to(BF16))
-            x = _ImageBlockFn.apply(x, yt, mod, blk.norm1.weight, blk, lens, N, T, cos, sin)
+            mod = _ModFn.apply(c, lin.weight, lin)
+            x = _ImageBlockFn.apply(x, yt, mod, blk.norm1.weight, blk, lens, N, T, cos, sin, (self, nb - i))
         x = _LayerNormFn.apply(x, 1e-6)
         return _LinearFn.apply(x, self.final_layer.linear.weight, self.final_layer.linear, True)
 

@@ -98,7 +98,10 @@ class MuonAdamW(torch.optim.Optimizer):
         self.fused_adamw = fused_adamw
         self.ns_dtype = getattr(torch, ns_dtype)
         self._plan = None
-        self.exchange = None  # set by nano_gpic_b200.parallel.muon_dist for multi-rank runs
+        self.exchange = None  # optional replacement of the bf16 all-gather of Muon updates (ddp mode)
+        # zero mode (nano_gpic_b200.parallel.ddp): ids of the parameters this rank owns; the step touches only those,
+        # Muon orthogonalises all their units locally (their reduced gradients are whole on this rank)
+        self.owned = None
 
     @staticmethod
     def update_coef(group, shape):
@@ -136,7 +139,41 @@ class MuonAdamW(torch.optim.Optimizer):
         return {"world": world, "rank": rank, "units": units, "shard": shard, "mine": mine}
 
     @torch.no_grad()
+    def _muon_step_owned(self, group):
+        params = [p for p in group["params"] if id(p) in self.owned]
+        if not params:
+            return
+        grads, bufs = [], []
+        for p in params:
+            st = self.state[p]
+            if "momentum_buffer" not in st:
+                st["momentum_buffer"] = torch.zeros_like(p, memory_format=torch.preserve_format)
+            grads.append(p.grad)
+            bufs.append(st["momentum_buffer"])
+        beta, lr, wd = group["momentum"], group["lr"], group["weight_decay"]
+        torch._foreach_lerp_(bufs, grads, 1 - beta)
+        by_shape = {}
+        for i, p in enumerate(params):
+            parts = p._muon_parts if group["split"] else 1
+            rows = p.shape[0] // parts
+            for k in range(parts):
+                by_shape.setdefault((rows, p.shape[1]), []).append((i, k * rows, (k + 1) * rows))
+        outs = []
+        for shape, us in by_shape.items():
+            ins = [grads[i][r0:r1].lerp(bufs[i][r0:r1], beta) if group["nesterov"] else bufs[i][r0:r1]
+                   for i, r0, r1 in us]
+            outs.append((shape, us, msign(torch.stack(ins), steps=group["ns_steps"], dtype=self.ns_dtype)))
+        if wd:
+            torch._foreach_mul_(params, 1 - lr * wd)
+        for shape, us, O in outs:
+            coef = -lr * self.update_coef(group, shape)
+            for (i, r0, r1), o in zip(us, O):
+                params[i][r0:r1].add_(o, alpha=coef)
+
+    @torch.no_grad()
     def _muon_step(self, group):
+        if self.owned is not None:
+            return self._muon_step_owned(group)
         params = group["params"]
         grads, bufs = [], []
         for p in params:
@@ -183,7 +220,7 @@ class MuonAdamW(torch.optim.Optimizer):
         from torch.optim.adam import adam as _adam_fn
         params, grads, m1, m2, steps = [], [], [], [], []
         for p in group["params"]:
-            if p.grad is None:
+            if p.grad is None or (self.owned is not None and id(p) not in self.owned):
                 continue
             st = self.state[p]
             if not st:

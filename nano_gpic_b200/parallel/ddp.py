@@ -1,29 +1,334 @@
-"""Data-parallel gradient reduction over the flat gradient buffer.
+"""Data parallelism over the flat parameter / gradient buffers: the flat layout (buckets in the order the backward
+finishes gradients, owners inside each bucket), gradient collectives overlapped with the backward, and two modes.
 
-mode "nccl" (the baseline, as the reference's DDP: fp32 all-reduce of all gradients, averaged; reference
-baselines/PixelGen/configs_h100/lite_ladder.yaml:7-12): one torch.distributed all-reduce per bucket of the flat buffer
-(buckets on parameter boundaries, default 1000 MB like the reference's bucket_cap_mb).
+  ddp   The reference's DDP (Lightning DDPStrategy with bucket_cap_mb=1000, baselines/PixelGen/configs_h100/
+        lite_ladder.yaml:7-12; `gradient_as_bucket_view`): one fp32 all-reduce per bucket. Gradients are pre-scaled by
+        1/world in the loss, so the sum is the mean. Every rank holds the full averaged gradient; Muon units are
+        orthogonalised by their longest-processing-time owner and the bf16 results all-gathered (MuonAdamW; reference
+        baselines/PixelGen/src/optim/muon.py:150-216); AdamW runs replicated.
+
+  zero  Sharded optimizer, the role of the reference's FSDP2 + ShardMuonAdamW (baselines/PixelGen/src/utils/
+        fsdp_setup.py:116-148, src/optim/muon_fsdp.py:41-188), laid out for one B200's 180 GB: inside each bucket the
+        parameters are placed owner-major. Owners are chosen by longest-processing-time on the Muon cost
+        (rows * cols * min(rows, cols)), or numel for AdamW parameters. Each owner's segment is padded to a common
+        size, so ONE fp32 reduce-scatter per bucket leaves every owner the summed gradient of WHOLE parameters and
+        Muon needs no all-to-all (the reference sends rows to owners and back with two all_to_all_single). The owner
+        clips (global norm from one scalar all-reduce), runs Muon / AdamW on its parameters with its own optimizer
+        state, writes them in bf16, and ONE bf16 all-gather per bucket refreshes every rank's compute weights.
+        Other owners' fp32 masters and optimizer state are gathered only when a checkpoint needs them.
+        Per optimizer step and rank this moves (world-1)/world of the fp32 gradients once (reduce-scatter) and of the
+        bf16 weights once (all-gather): less than DDP's all-reduce + Muon all-gather, and less than FSDP2 + two
+        all-to-alls.
+
+Overlap: the model calls `hook(n)` at the start of each block's backward on the LAST micro-batch, meaning the first n
+backward stages (final layer, image blocks from the last, text blocks from the last) hold final gradients; every
+bucket made only of finished stages is reduced at once on a side CUDA stream, under the rest of the backward.
 """
 import torch
 import torch.distributed as dist
 
+from .flat import FlatParams, _round
 
-class GradReducer:
-    def __init__(self, flat, mode="nccl", bucket_mb=1000, group=None):
-        self.flat = flat
-        self.mode = mode
-        self.group = group
+
+# ------------------------------------------------------------------------------------------------------- layout
+def backward_stages(model):
+    """Lists of trainable parameters in the order the backward finishes their gradients. For JiT_T2I: final layer,
+    image blocks last to first, text blocks last to first, then everything else (embedders, time MLP, caption
+    table). Other modules: one stage."""
+    seen, stages = set(), []
+
+    def add(mod_or_params):
+        ps = [p for p in (mod_or_params.parameters() if hasattr(mod_or_params, "parameters") else mod_or_params)
+              if p.requires_grad and id(p) not in seen]
+        seen.update(id(p) for p in ps)
+        stages.append(ps)
+
+    if hasattr(model, "blocks") and hasattr(model, "final_layer"):
+        add(model.final_layer)
+        for blk in reversed(model.blocks):
+            add(blk)
+        for blk in reversed(getattr(model, "text_refine_blocks", [])):
+            add(blk)
+    add([p for p in model.parameters()])
+    return stages
+
+
+class Bucket:
+    def __init__(self, start, end, seg, last_stage, params, replicated=False):
+        self.start, self.end, self.seg = start, end, seg  # [start, end) of the flat buffers; owner segment size
+        self.last_stage = last_stage  # ready once stages [0, last_stage] are finished
+        self.params = params
+        self.replicated = replicated  # all-reduced and updated on every rank (ddp mode, zero mode's fp32 consumers)
+
+
+def replicated_in_zero(p):
+    """Parameters the forward reads in fp32 (vectors: norm weights, biases; and those marked `_replicate`) stay
+    replicated in zero mode, as the reference's FSDP2 keeps RMSNorm weights replicated (fsdp_setup.py:21-26,
+    271-280): their gradients are all-reduced and every rank updates them."""
+    return p.ndim < 2 or getattr(p, "_replicate", False)
+
+
+class Layout:
+    """Flat order, offsets and buckets for `world` ranks. mode "ddp": parameters in backward order; "zero": owner-major
+    inside each bucket with equal (padded) owner segments."""
+
+    def __init__(self, model, world, mode="ddp", bucket_numel=250_000_000):
+        assert mode in ("ddp", "zero"), mode
+        self.world, self.mode = world, mode
+        stages = backward_stages(model)
+        self.params, self.offsets, self.buckets, self.owner = [], [], [], {}
+        groups, cur, cur_n = [], [], 0
+        for si, ps in enumerate(stages):
+            cur += [(si, p) for p in ps]
+            cur_n += sum(p.numel() for p in ps)
+            if cur_n >= bucket_numel:
+                groups.append(cur)
+                cur, cur_n = [], 0
+        if cur:
+            groups.append(cur)
+        off = 0
+        rep = []
+        for g in groups:
+            last = max(si for si, _ in g)
+            ps = [p for _, p in g]
+            if mode == "zero" and world > 1:
+                rep += [p for p in ps if replicated_in_zero(p)]
+                ps = [p for p in ps if not replicated_in_zero(p)]
+                if not ps:
+                    continue
+            start = off
+            if mode == "ddp" or world == 1:
+                for p in ps:
+                    self.params.append(p)
+                    self.offsets.append(off)
+                    self.owner[id(p)] = None
+                    off = _round(off + p.numel())
+                seg = off - start
+            else:
+                load = [0] * world
+                mine = [[] for _ in range(world)]
+                order = sorted(range(len(ps)), key=lambda i: (-self.cost(ps[i]), i))
+                for i in order:
+                    r = min(range(world), key=lambda q: (load[q], q))
+                    mine[r].append(i)
+                    load[r] += _round(ps[i].numel())
+                seg = _round(max(load))
+                for r in range(world):
+                    o = start + r * seg
+                    for p in (ps[i] for i in sorted(mine[r])):
+                        self.params.append(p)
+                        self.offsets.append(o)
+                        self.owner[id(p)] = r
+                        o = _round(o + p.numel())
+                off = start + world * seg
+            self.buckets.append(Bucket(start, off, seg, last, ps))
+        if rep:
+            start = off
+            for p in rep:
+                self.params.append(p)
+                self.offsets.append(off)
+                self.owner[id(p)] = None
+                off = _round(off + p.numel())
+            self.buckets.append(Bucket(start, off, off - start, len(stages) - 1, rep, replicated=True))
+        self.numel = off
+
+    @staticmethod
+    def cost(p):
+        if getattr(p, "_muon_parts", None):
+            rows, cols = p.shape[0] // p._muon_parts, p.shape[1]
+            return p._muon_parts * rows * cols * min(rows, cols)
+        return p.numel()
+
+    def flat(self, model, device=None):
+        return FlatParams(model, device=device, params=self.params, offsets=self.offsets, numel=self.numel)
+
+    def padding(self):
+        used = sum(_round(p.numel()) for p in self.params)
+        return 1.0 - used / max(self.numel, 1)
+
+
+# ---------------------------------------------------------------------------------------------- collectives
+def _gloo(group):
+    return dist.get_backend(group) == "gloo"
+
+
+def _reduce_scatter_inplace(buf, seg, rank, group):
+    """Sum over ranks; rank r's segment [r*seg, (r+1)*seg) receives its sums (NCCL in-place reduce-scatter)."""
+    if _gloo(group):  # gloo has no reduce-scatter: the same sums through an all-reduce
+        dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
+    else:
+        dist.reduce_scatter_tensor(buf[rank * seg:(rank + 1) * seg], buf, op=dist.ReduceOp.SUM, group=group)
+
+
+def _all_gather_inplace(buf, seg, rank, world, group):
+    """Every rank's segment r of buf from rank r (NCCL in-place all-gather)."""
+    if _gloo(group):
+        parts = list(buf.view(world, seg).unbind(0))
+        dist.all_gather(parts, buf[rank * seg:(rank + 1) * seg].clone(), group=group)
+    else:
+        dist.all_gather_into_tensor(buf, buf[rank * seg:(rank + 1) * seg], group=group)
+
+
+class DataParallel:
+    """The gradient / weight synchronisation of one data-parallel group over a Layout's flat buffers."""
+
+    def __init__(self, model, layout, flat, group=None, overlap=True):
+        self.model, self.layout, self.flat, self.group = model, layout, flat, group
+        self.mode = layout.mode
         self.world = dist.get_world_size(group)
-        self.buckets = flat.ranges(bucket_mb * 1024 * 1024 // 4)
+        self.rank = dist.get_rank(group)
+        assert self.world == layout.world
+        self.overlap = overlap
+        self.cuda = flat.grad.is_cuda
+        self.comm = torch.cuda.Stream(device=flat.grad.device) if self.cuda else None
+        self._launched = set()
+        self.early = 0  # buckets launched under the backward in the last step (overlap statistics)
+        # zero mode: the parameters this rank updates (its own and the replicated ones)
+        self.owned = None if self.mode == "ddp" else {id(p) for p in layout.params
+                                                      if layout.owner[id(p)] in (self.rank, None)}
+
+    # ----------------------------------------------------------------------------------------- gradients
+    def arm(self):
+        """Before the backward of the last micro-batch: reduce buckets as their stages finish."""
+        self._launched = set()
+        if self.overlap:
+            self.model._bwd_hook = self._stages_done
+
+    def _stages_done(self, n):
+        for i, b in enumerate(self.layout.buckets):
+            if i not in self._launched and b.last_stage < n:
+                self._launch(i)
+
+    def _launch(self, i):
+        self._launched.add(i)
+        b = self.layout.buckets[i]
+        g = self.flat.grad[b.start:b.end]
+        if self.cuda:
+            self.comm.wait_stream(torch.cuda.current_stream(g.device))
+            with torch.cuda.stream(self.comm):
+                self._reduce(g, b)
+        else:
+            self._reduce(g, b)
+
+    def _reduce(self, g, b):
+        if self.mode == "ddp" or b.replicated:
+            dist.all_reduce(g, op=dist.ReduceOp.SUM, group=self.group)
+        else:
+            _reduce_scatter_inplace(g, b.seg, self.rank, self.group)
+
+    def finish_grads(self):
+        """After the backward: reduce what is left and make the compute stream wait for every collective."""
+        self.model._bwd_hook = None
+        self.early = len(self._launched)
+        for i in range(len(self.layout.buckets)):
+            if i not in self._launched:
+                self._launch(i)
+        if self.cuda:
+            torch.cuda.current_stream(self.flat.grad.device).wait_stream(self.comm)
+
+    def _sharded(self):
+        return [b for b in self.layout.buckets if not b.replicated]
+
+    def own_slices(self, buf):
+        """The parts of a flat buffer this rank is responsible for: all of it in ddp mode; its owner segments (and
+        the replicated bucket, which every rank holds) in zero mode."""
+        if self.mode == "ddp":
+            return [buf]
+        return ([buf[b.start + self.rank * b.seg:b.start + (self.rank + 1) * b.seg] for b in self._sharded()] +
+                [buf[b.start:b.end] for b in self.layout.buckets if b.replicated])
 
     @torch.no_grad()
-    def reduce(self):
+    def grad_norm(self):
+        """Global 2-norm of the (reduced) gradient: local sum of squares of the owned segments, one scalar
+        all-reduce, plus the replicated part (identical on every rank, counted once)."""
+        if self.mode == "ddp":
+            return self.flat.grad.norm()
         g = self.flat.grad
-        for a, b in self.buckets:
-            dist.all_reduce(g[a:b], op=dist.ReduceOp.SUM, group=self.group)
-        g.mul_(1.0 / self.world)
+        z = torch.zeros((), device=g.device)
+        sq = sum((s.pow(2).sum() for s in (g[b.start + self.rank * b.seg:b.start + (self.rank + 1) * b.seg]
+                                           for b in self._sharded())), z)
+        dist.all_reduce(sq, op=dist.ReduceOp.SUM, group=self.group)
+        sq = sq + sum((g[b.start:b.end].pow(2).sum() for b in self.layout.buckets if b.replicated), z)
+        return sq.sqrt()
+
+    @torch.no_grad()
+    def scale_grads(self, coef):
+        for s in self.own_slices(self.flat.grad):
+            s.mul_(coef)
+
+    # ------------------------------------------------------------------------------------------- weights
+    @torch.no_grad()
+    def refresh_weights(self):
+        """After the optimizer step: the bf16 compute weights of every rank from the owners' fp32 masters."""
+        if self.mode == "ddp":
+            self.flat.sync_bf16()
+            return
+        for b in self.layout.buckets:
+            if b.replicated:
+                self.flat.data16[b.start:b.end].copy_(self.flat.data[b.start:b.end])
+                continue
+            lo = b.start + self.rank * b.seg
+            self.flat.data16[lo:lo + b.seg].copy_(self.flat.data[lo:lo + b.seg])
+            _all_gather_inplace(self.flat.data16[b.start:b.end], b.seg, self.rank, self.world, self.group)
+
+    @torch.no_grad()
+    def gather_master(self):
+        """zero mode: every rank's fp32 masters from their owners (for checkpoints)."""
+        if self.mode == "ddp":
+            return
+        for b in self._sharded():
+            _all_gather_inplace(self.flat.data[b.start:b.end], b.seg, self.rank, self.world, self.group)
+
+    @torch.no_grad()
+    def gather_optimizer_state(self, opt):
+        """zero mode: every rank's optimizer state for every parameter from its owner, through flat buffers of the
+        layout (one all-gather per bucket and state kind). Afterwards opt.state_dict() is the full state."""
+        if self.mode == "ddp":
+            return
+        dev = self.flat.data.device
+        kinds = {}
+        index = {id(p): i for i, p in enumerate(self.flat.params)}
+        for grp in opt.param_groups:
+            for p in grp["params"]:
+                if id(p) not in index:  # frozen parameters have no state
+                    continue
+                keys = ("momentum_buffer",) if grp.get("use_muon") else ("exp_avg", "exp_avg_sq")
+                for k in keys:
+                    kinds.setdefault(k, []).append(p)
+        for k, ps in kinds.items():
+            buf = torch.zeros(self.flat.numel, dtype=torch.float32, device=dev)
+            for p in ps:
+                st = opt.state.get(p, {})
+                if id(p) in self.owned and k in st:
+                    o = self.flat.offsets[index[id(p)]]
+                    buf[o:o + p.numel()].copy_(st[k].reshape(-1))
+            for b in self._sharded():
+                _all_gather_inplace(buf[b.start:b.end], b.seg, self.rank, self.world, self.group)
+            for p in ps:
+                o = self.flat.offsets[index[id(p)]]
+                opt.state[p][k] = buf[o:o + p.numel()].view(p.shape).clone()
+        steps = [opt.state[p]["step"] for p in kinds.get("exp_avg", []) if "step" in opt.state[p]
+                 and id(p) in self.owned]
+        s = torch.tensor(float(steps[0]) if steps else 0.0, device=dev)
+        dist.all_reduce(s, op=dist.ReduceOp.MAX, group=self.group)
+        for p in kinds.get("exp_avg", []):
+            old = opt.state[p].get("step")
+            opt.state[p]["step"] = s.clone().to(old.device if old is not None else dev)
 
     @torch.no_grad()
     def broadcast_params(self, src=0):
         dist.broadcast(self.flat.data, src, group=self.group)
         self.flat.sync_bf16()
+
+
+def make_data_parallel(model, world, mode="ddp", bucket_mb=1000, device=None, group=None, overlap=True):
+    """Layout + flat buffers + DataParallel for `model` (Muon tags must already be set). bucket_mb counts fp32
+    gradient bytes, as the reference's bucket_cap_mb."""
+    layout = Layout(model, world, mode, bucket_numel=bucket_mb * 1024 * 1024 // 4)
+    flat = layout.flat(model, device=device)
+    dp = DataParallel(model, layout, flat, group=group, overlap=overlap) if world > 1 else None
+    return layout, flat, dp
+
+
+# the name the trainer used before the layout existed
+GradReducer = DataParallel

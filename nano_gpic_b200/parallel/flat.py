@@ -19,17 +19,26 @@ def _round(n, a=ALIGN):
 
 
 class FlatParams:
-    def __init__(self, module, device=None, params=None):
+    """params/offsets/numel: an explicit layout (e.g. the data-parallel planner's bucket and owner order, with padding);
+    by default the module's trainable parameters back to back."""
+
+    def __init__(self, module, device=None, params=None, offsets=None, numel=None):
         self.module = module
         self.params = list(params) if params is not None else [p for p in module.parameters() if p.requires_grad]
         names = {id(p): n for n, p in module.named_parameters()}
         self.names = [names.get(id(p), f"param{i}") for i, p in enumerate(self.params)]
         device = device or self.params[0].device
-        self.offsets = []
-        off = 0
-        for p in self.params:
-            self.offsets.append(off)
-            off = _round(off + p.numel())
+        if offsets is None:
+            self.offsets = []
+            off = 0
+            for p in self.params:
+                self.offsets.append(off)
+                off = _round(off + p.numel())
+        else:
+            assert len(offsets) == len(self.params) and all(o % ALIGN == 0 for o in offsets)
+            self.offsets = list(offsets)
+            off = numel
+            assert all(o + p.numel() <= off for o, p in zip(self.offsets, self.params))
         self.numel = off
         self.data = torch.zeros(off, dtype=torch.float32, device=device)
         self.grad = torch.zeros(off, dtype=torch.float32, device=device)

@@ -18,7 +18,6 @@ from ..diffusion.flow_matching import JiTTrainer
 from ..models.jit_t2i import JiT_T2I
 from ..optim.lr_scheduler import WarmupFlatCooldown
 from ..optim.muon import MuonAdamW, tag_muon_params
-from ..parallel.flat import FlatParams
 
 
 def uint8_to_float(img):
@@ -36,21 +35,28 @@ class Trainer:
         self.accum = accum
         self.clip = clip
         self.flat = flat
-        self.dp = dp  # a nano_gpic_b200.parallel data-parallel reducer, or None
+        self.dp = dp  # nano_gpic_b200.parallel.ddp.DataParallel (ddp or zero mode), or None
+        self.world = dp.world if dp is not None else 1
+        if dp is not None and dp.owned is not None:
+            optimizer.owned = dp.owned
         self.global_step = 0
         self.copy_stream = None
 
     # --------------------------------------------------------------------------------------------- construction
     @classmethod
     def for_ladder(cls, size="d12", device="cuda", world=1, rank=0, micro_batch=None, global_batch=GLOBAL_BATCH,
-                   max_steps=None, dp="nccl", seed=0, model_kwargs=None):
+                   max_steps=None, dp="ddp", seed=0, model_kwargs=None, bucket_mb=1000, overlap=True):
+        """dp: "ddp" (all-reduce, as the reference's DDP sizes) or "zero" (reduce-scatter to owners, sharded
+        optimizer state; the role of the reference's FSDP2 sizes)."""
         s = SIZES[size]
         torch.manual_seed(seed)
         kw = s.model_kwargs()
         kw.update(model_kwargs or {})
         model = JiT_T2I(**kw).to(device)
         tag_muon_params(model)
-        flat = FlatParams(model, device=device)
+        from ..parallel.ddp import make_data_parallel
+        _, flat, reducer = make_data_parallel(model, world, mode="ddp" if dp == "nccl" else dp, bucket_mb=bucket_mb,
+                                              device=device, overlap=overlap)
         mb = micro_batch or s.micro_batch
         per_rank = global_batch // world
         assert per_rank % mb == 0, (global_batch, world, mb)
@@ -61,10 +67,7 @@ class Trainer:
         steps = max_steps or s.steps
         wu, cd = s.schedule()
         sched = WarmupFlatCooldown(wu, cd, steps, min_lr=3e-5)(opt)
-        reducer = None
-        if world > 1:
-            from ..parallel.ddp import GradReducer
-            reducer = GradReducer(flat, mode=dp)
+        if reducer is not None:
             reducer.broadcast_params(0)
         return cls(model, opt, sched, JiTTrainer(), accum=per_rank // mb, clip=1.0, flat=flat, dp=reducer)
 
@@ -86,6 +89,8 @@ class Trainer:
             self.flat.zero_grad()
         losses = []
         for i in range(self.accum):
+            if self.dp is not None and i == self.accum - 1:
+                self.dp.arm()
             sl = slice(i * mb, (i + 1) * mb)
             x = self._to_device(images[sl], dev)
             x = uint8_to_float(x) if x.dtype == torch.uint8 else x.float()
@@ -93,16 +98,19 @@ class Trainer:
             m = self._to_device(caption_mask[sl], dev) if caption_mask is not None else None
             ti = t[sl].to(dev) if t is not None else None
             ni = noise[sl].to(dev) if noise is not None else None
+            # mean over this rank's images and over ranks (the collectives sum)
             per = self.obj.train_step(self.model, x, y, m, t=ti, noise=ni,
-                                      grad_scale=1.0 / (x.numel() * self.accum))
+                                      grad_scale=1.0 / (x.numel() * self.accum * self.world))
             losses.append(per)
         if self.dp is not None:
-            self.dp.reduce()
+            self.dp.finish_grads()
         self.clip_grad()
         self.opt.step()
         if self.sched is not None:
             self.sched.step()
-        if self.flat is not None:
+        if self.dp is not None:
+            self.dp.refresh_weights()
+        elif self.flat is not None:
             self.flat.sync_bf16()
         self.global_step += 1
         return torch.cat(losses).mean()
@@ -112,6 +120,10 @@ class Trainer:
         """Global 2-norm clip (max_norm = self.clip), on the device: coef = min(1, max / (norm + 1e-6))."""
         if not self.clip:
             return None
+        if self.dp is not None:
+            norm = self.dp.grad_norm()
+            self.dp.scale_grads((self.clip / (norm + 1e-6)).clamp(max=1.0))
+            return norm
         if self.flat is not None:
             norm = self.flat.grad.norm()
             self.flat.grad.mul_((self.clip / (norm + 1e-6)).clamp(max=1.0))
