@@ -179,20 +179,70 @@ class GPICDataset(IterableDataset):
 
 class SyntheticGPIC:
     """Synthetic batches of the benchmark's shape: uint8 images uniform (x uniform in [-1, 1]), N(0, 1) caption
-    features, left-aligned masks with lengths uniform in [1, T]."""
+    features, left-aligned masks with lengths uniform in [1, T]. Batch i is drawn from a generator seeded
+    (seed * 1000003 + i), so a loader started at `start` (a resume) yields the batches an uninterrupted run would."""
 
-    def __init__(self, batch, T=128, D=2048, image_size=256, seed=0):
+    def __init__(self, batch, T=128, D=2048, image_size=256, seed=0, start=0):
         self.batch, self.T, self.D, self.size = batch, T, D, image_size
-        self.g = torch.Generator().manual_seed(seed)
+        self.seed, self.index = seed, start
 
     def __iter__(self):
         return self
 
     def __next__(self):
-        g, B, T = self.g, self.batch, self.T
+        g = torch.Generator().manual_seed(self.seed * 1000003 + self.index)
+        self.index += 1
+        B, T = self.batch, self.T
         img = torch.randint(0, 256, (B, self.size, self.size, 3), dtype=torch.uint8, generator=g)
         cap = torch.randn(B, T, self.D, generator=g).to(torch.bfloat16)
         lens = torch.randint(1, T + 1, (B,), generator=g)
         lens[0] = T
         mask = torch.arange(T)[None] < lens[:, None]
         return img, [""] * B, {"caption_type": ["synthetic"] * B, "text_emb": cap, "text_mask": mask}
+
+
+class GPICWebDataset(GPICDataset):
+    """GPICDataset under the reference's constructor (baselines/PixelGen/src/data/dataset/gpic_dataset.py:402-440
+    init args), so its YAML `data.train_dataset` nodes build this loader: tar_dir + tar_pattern, the text-cache
+    directory, length grouping (group_text_len, group_window) or shared buckets, caption padding. Arguments that only
+    select the reference's alternative paths (shuffle_buffer, corrupted_csv, output_fields, is_val) are accepted."""
+
+    def __init__(self, tar_dir, tar_pattern, emb_dir=None, shuffle_buffer=100, group_text_len=True, group_window=1024,
+                 text_max_length=320, pad_multiple=8, shared_bucket=False, corrupted_csv=None, output_fields=None,
+                 is_val=False, seed=None, batch_size=128, image_size=256, log_dir=None):
+        seed = int(os.environ.get("GPIC_SHARD_SEED", 0)) if seed is None else seed
+        super().__init__(os.path.join(tar_dir, tar_pattern), emb_dir, seed=seed, image_size=image_size,
+                         group_window=group_window if group_text_len else batch_size, group_batch=batch_size,
+                         pad_multiple=pad_multiple, text_max_length=text_max_length, shared_bucket=shared_bucket,
+                         log_dir=log_dir)
+        self.is_val = is_val
+
+
+def gpic_jsonl_save_fn(image, metadata, root_path):
+    """One HWC uint8 array -> <root>/<caption_type>_<key>.png."""
+    from PIL import Image
+    Image.fromarray(image).save(os.path.join(root_path, f"{metadata['caption_type']}_{metadata['key']}.png"))
+
+
+class GPICJsonlDataset(torch.utils.data.Dataset):
+    """Prediction prompts from a JSONL file of {key, caption, caption_type} records; each prompt is sampled
+    num_samples_per_instance times, sample i starting from randn(latent_shape) of a CPU generator seeded i, the same
+    noise for every prompt (reference baselines/PixelGen/src/data/dataset/gpic_jsonl_dataset.py:25-69)."""
+
+    def __init__(self, jsonl_path, num_samples_per_instance=1, latent_shape=(3, 256, 256)):
+        import json
+        with open(jsonl_path) as f:
+            self.records = [json.loads(line) for line in f if line.strip()]
+        self.num_samples_per_instance = num_samples_per_instance
+        self.latent_shape = list(latent_shape)
+
+    def __len__(self):
+        return len(self.records) * self.num_samples_per_instance
+
+    def __getitem__(self, idx):
+        rec = self.records[idx // self.num_samples_per_instance]
+        sample = idx % self.num_samples_per_instance
+        noise = torch.randn(self.latent_shape, generator=torch.Generator().manual_seed(sample), dtype=torch.float32)
+        meta = {"key": rec["key"], "caption": rec["caption"], "caption_type": rec["caption_type"], "seed": sample,
+                "save_fn": gpic_jsonl_save_fn}
+        return noise, rec["caption"], meta

@@ -75,11 +75,24 @@ def collate_captions(embs, pad_multiple=8, max_length=320, pad_to=None):
     return out, mask
 
 
+_BAD_MASKS = {}  # device -> int32 count of caption masks that were not left-aligned (checked on the host later)
+
+
 def assert_left_aligned(mask):
-    """Every mask row is a prefix of Trues (the attention kernels count a caption's keys from position 0)."""
+    """Every mask row is a prefix of Trues (the attention kernels count a caption's keys from position 0).
+    On the host it raises at once; on a GPU the check stays on the device (no sync, no device-side assert that would
+    take the context down): violations are counted, and mask_errors() reports them at a log step."""
     n = mask.sum(1, keepdim=True)
     ok = (mask == (torch.arange(mask.shape[1], device=mask.device)[None] < n)).all()
     if mask.is_cuda:
-        torch._assert_async(ok)
+        c = _BAD_MASKS.get(mask.device)
+        if c is None:
+            c = _BAD_MASKS[mask.device] = torch.zeros((), dtype=torch.int32, device=mask.device)
+        c.add_((~ok).to(torch.int32))
     else:
         assert bool(ok), "caption masks must be left-aligned"
+
+
+def mask_errors(device=None):
+    """Host-side count of non-left-aligned caption masks seen on the device(s) so far (one sync)."""
+    return sum(int(c.item()) for d, c in _BAD_MASKS.items() if device is None or d == torch.device(device))

@@ -100,3 +100,8 @@ class JiTTrainer:
         if backward:
             pred.backward(g)
         return per
+
+
+def constant(alpha, sigma):
+    """Loss weight 1 at every noise level (reference training_JiT.constant)."""
+    return 1.0

@@ -271,13 +271,36 @@ class DataParallel:
             self.flat.data16[lo:lo + b.seg].copy_(self.flat.data[lo:lo + b.seg])
             _all_gather_inplace(self.flat.data16[b.start:b.end], b.seg, self.rank, self.world, self.group)
 
+    def own_ranges(self):
+        """[start, end) ranges of the flat buffers this rank keeps current (None in ddp mode: all of them)."""
+        if self.mode == "ddp":
+            return None
+        return ([(b.start + self.rank * b.seg, b.start + (self.rank + 1) * b.seg) for b in self._sharded()] +
+                [(b.start, b.end) for b in self.layout.buckets if b.replicated])
+
     @torch.no_grad()
-    def gather_master(self):
-        """zero mode: every rank's fp32 masters from their owners (for checkpoints)."""
+    def gather_flat(self, buf):
+        """zero mode: every owner segment of a flat-layout buffer (fp32 masters, the EMA) from its owner."""
         if self.mode == "ddp":
             return
         for b in self._sharded():
-            _all_gather_inplace(self.flat.data[b.start:b.end], b.seg, self.rank, self.world, self.group)
+            _all_gather_inplace(buf[b.start:b.end], b.seg, self.rank, self.world, self.group)
+
+    def gather_master(self):
+        """zero mode: every rank's fp32 masters from their owners (for checkpoints)."""
+        self.gather_flat(self.flat.data)
+
+    def prepare_checkpoint(self, opt, ema=None, full=True):
+        """Collective (every rank calls it): the full fp32 weights, EMA and (full=True) optimizer state on every rank,
+        so the checkpoint builder sees the unsharded state."""
+        if self.mode == "ddp":
+            return
+        self.gather_master()
+        if ema is not None and ema.buf is not None:
+            ema.join()
+            self.gather_flat(ema.buf)
+        if full:
+            self.gather_optimizer_state(opt)
 
     @torch.no_grad()
     def gather_optimizer_state(self, opt):

@@ -10,8 +10,11 @@ import torch
 
 
 class SimpleEMA:
-    def __init__(self, flat, decay=0.9999, every_n_steps=1, off=None):
+    def __init__(self, flat, decay=0.9999, every_n_steps=1, off=None, ranges=None):
         self.flat = flat
+        # zero mode: only these [start, end) ranges of the flat buffer are current on this rank (its owned segments
+        # and the replicated bucket), so only they are averaged; a checkpoint gathers the rest from their owners
+        self.ranges = ranges
         self.decay, self.every_n_steps = decay, every_n_steps
         self.off = (os.environ.get("GPIC_MFU_NO_EMA") == "1") if off is None else off
         self.buf = None if self.off else flat.data.clone()
@@ -30,9 +33,16 @@ class SimpleEMA:
                 self._stream = torch.cuda.Stream(device=self.buf.device)
             self._stream.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(self._stream):
-                self.buf.lerp_(self.flat.data, 1.0 - self.decay)
+                self._lerp()
         else:
+            self._lerp()
+
+    def _lerp(self):
+        if self.ranges is None:
             self.buf.lerp_(self.flat.data, 1.0 - self.decay)
+            return
+        for a, b in self.ranges:
+            self.buf[a:b].lerp_(self.flat.data[a:b], 1.0 - self.decay)
 
     def join(self):
         if self._stream is not None:

@@ -41,6 +41,8 @@ class Trainer:
             optimizer.owned = dp.owned
         self.global_step = 0
         self.copy_stream = None
+        self.last_grad_norm = None  # device scalar: the pre-clip global norm of the last step
+        self.encode = None  # optional autoencoder encode applied to the float images (PixelAE with scale/shift)
 
     # --------------------------------------------------------------------------------------------- construction
     @classmethod
@@ -81,30 +83,46 @@ class Trainer:
         """One optimizer step over this rank's batch, split into `accum` micro-batches.
         images: uint8 [B, H, W, 3] or float [B, 3, H, W] in [-1, 1] (host pinned or device);
         captions [B, T, D] (bf16); caption_mask [B, T] bool or None. Returns the batch-mean loss (device scalar)."""
-        dev = self.flat.data.device if self.flat is not None else next(self.model.parameters()).device
         B = images.shape[0]
         assert B % self.accum == 0
         mb = B // self.accum
+        micros = []
+        for i in range(self.accum):
+            sl = slice(i * mb, (i + 1) * mb)
+            micros.append((images[sl], captions[sl], caption_mask[sl] if caption_mask is not None else None,
+                           t[sl] if t is not None else None, noise[sl] if noise is not None else None))
+        return self.train_micro(micros)
+
+    def train_micro(self, micros):
+        """One optimizer step over a list of micro-batches (images, captions, mask[, t, noise]); the micro-batches may
+        have different caption lengths T (length-grouped or bucketed loaders). Gradients are the mean over all images
+        of all micro-batches of all ranks (micro-batches of equal size)."""
+        dev = self.flat.data.device if self.flat is not None else next(self.model.parameters()).device
         if self.flat is not None:
             self.flat.zero_grad()
+        n = len(micros)
         losses = []
-        for i in range(self.accum):
-            if self.dp is not None and i == self.accum - 1:
+        for i, mbatch in enumerate(micros):
+            images, captions, mask = mbatch[0], mbatch[1], mbatch[2]
+            t = mbatch[3] if len(mbatch) > 3 else None
+            noise = mbatch[4] if len(mbatch) > 4 else None
+            if self.dp is not None and i == n - 1:
                 self.dp.arm()
-            sl = slice(i * mb, (i + 1) * mb)
-            x = self._to_device(images[sl], dev)
+            x = self._to_device(images, dev)
             x = uint8_to_float(x) if x.dtype == torch.uint8 else x.float()
-            y = self._to_device(captions[sl], dev).to(torch.bfloat16)
-            m = self._to_device(caption_mask[sl], dev) if caption_mask is not None else None
-            ti = t[sl].to(dev) if t is not None else None
-            ni = noise[sl].to(dev) if noise is not None else None
+            if self.encode is not None:
+                x = self.encode(x)
+            y = self._to_device(captions, dev).to(torch.bfloat16)
+            m = self._to_device(mask, dev) if mask is not None else None
+            ti = t.to(dev) if t is not None else None
+            ni = noise.to(dev) if noise is not None else None
             # mean over this rank's images and over ranks (the collectives sum)
             per = self.obj.train_step(self.model, x, y, m, t=ti, noise=ni,
-                                      grad_scale=1.0 / (x.numel() * self.accum * self.world))
+                                      grad_scale=1.0 / (x.numel() * n * self.world))
             losses.append(per)
         if self.dp is not None:
             self.dp.finish_grads()
-        self.clip_grad()
+        self.last_grad_norm = self.clip_grad()
         self.opt.step()
         if self.sched is not None:
             self.sched.step()
