@@ -82,3 +82,29 @@ def adamw_lr_rule(n_params):
 def muon_wd_rule(muon_lr, steps):
     """Muon weight decay = 5 / (lr x steps) (README.md:36-41)."""
     return 5.0 / (muon_lr * steps)
+
+
+def dp_mode(size):
+    """Data-parallel mode of a ladder size: the reference shards from d14 up (FSDP2, jobs/final_ladder.sh:30); here
+    zero mode (reduce-scatter to owners, sharded optimizer state) from d14, ddp below."""
+    s = SIZES[size] if isinstance(size, str) else size
+    return "zero" if s.width >= 1280 else "ddp"
+
+
+def shell_vars(size, gpus=8):
+    """The launch variables of a size as shell assignments (consumed by jobs/final_ladder.sh): width, layers, steps,
+    learning rates, weight decay, micro-batch, warmup/cooldown, accumulation for `gpus` GPUs, data-parallel mode."""
+    s = SIZES[size]
+    wu, cd = s.schedule()
+    acc = GLOBAL_BATCH // gpus // s.micro_batch
+    return (f"D={s.width} NB={s.image_layers} NT={s.text_layers} S={s.steps} MLR={s.muon_lr} ALR={s.adamw_lr} "
+            f"WDK={s.muon_wd} MB={s.micro_batch} WU={wu} CD={cd} ACC={acc} DP={dp_mode(s)}")
+
+
+if __name__ == "__main__":
+    import sys
+    if len(sys.argv) >= 3 and sys.argv[1] == "--shell":
+        print(shell_vars(sys.argv[2], int(sys.argv[3]) if len(sys.argv) > 3 else 8))
+    else:
+        for name, s in SIZES.items():
+            print(name, shell_vars(name))
