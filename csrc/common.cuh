@@ -88,7 +88,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // --------------------------------------------------------------------------------------------------------------- TMA
-// Tiled bulk-tensor loads into this CTA's shared memory (no cluster multicast anywhere in this code base).
+// Tiled bulk-tensor loads into this CTA's own shared memory only.
 __device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y, int z) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "

@@ -9,7 +9,7 @@
 // batched alpha/beta epilogue.
 //
 // Structure (one CTA per SM, persistent over output tiles of 128 x 256):
-//   warp 0      TMA producer: 4-stage ring of (A 128x64, B 256x64) bf16 tiles, 128-byte swizzle, no multicast
+//   warp 0      TMA producer: 4-stage ring of (A 128x64, B 256x64) bf16 tiles, 128-byte swizzle, one CTA per load
 //   warp 1      TMEM owner and MMA issuer: tcgen05.mma M=128 N=256 K=16, one elected thread
 //   warps 2..5  epilogue: tcgen05.ld of the accumulator (double-buffered in TMEM, 2 x 256 columns), fused
 //               elementwise work, vector stores to global memory
