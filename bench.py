@@ -267,7 +267,7 @@ def main():
     ap.add_argument("--global-batch", type=int, default=1024)
     ap.add_argument("--caption-len", type=int, default=128)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--dp", default="ddp", choices=["ddp", "zero"],
+    ap.add_argument("--dp", default="zero", choices=["ddp", "zero"],
                     help="data-parallel mode of our arm: all-reduce (the reference's DDP sizes) or reduce-scatter to "
                          "owners with sharded optimizer state (its FSDP2 sizes)")
     a = ap.parse_args()

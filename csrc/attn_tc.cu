@@ -292,6 +292,337 @@ __global__ void __launch_bounds__(atc::THREADS, 1)
   }
 }
 
+// ==================================================================================== forward, two query tiles
+// Persistent; work item = (sample, head, 256 queries). Two softmax warpgroups each own one 128-query tile (A, B) and
+// share every K/V tile the TMA warp loads. The MMA warp ping-pongs between them, so the tensor core works on one tile
+// while the other's softmax runs:
+//     S_A(0) S_B(0) | PV_A(0) S_A(1) | PV_B(0) S_B(1) | PV_A(1) S_A(2) | ...
+// Q (two tiles) and K/V are double-buffered across items. TMEM: S_A [0,128), S_B [128,256), O_A [256,320),
+// O_B [320,384).
+namespace at2 {
+constexpr int BQ = 128, BKV = 128, D = 64;
+constexpr int THREADS = 320;                 // warp 0 TMA, warp 1 MMA, warps 2..5 softmax A, 6..9 softmax B
+constexpr int QT = BQ * D * 2;               // 16 KiB: one Q tile
+constexpr int KVT = BKV * D * 2;             // 16 KiB: one K or V tile
+constexpr int PT = BQ * BKV * 2;             // 32 KiB: one P tile
+constexpr int OFF_Q = 0;                     // [2 buffers][A, B]
+constexpr int OFF_KV = OFF_Q + 4 * QT;       // [2 stages][K, V]
+constexpr int OFF_P = OFF_KV + 4 * KVT;      // [A, B]
+constexpr int OFF_BAR = OFF_P + 2 * PT;
+constexpr int SMEM = OFF_BAR + 256 + 1024;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t C_S = 0, C_O = 256;       // + X * 128 (S), + X * 64 (O)
+}  // namespace at2
+
+struct AttnTc2Params {
+  const int *n0, *n1;
+  int Lq, L0, L1, H;
+  int nt0, nt1, nqp, items;
+  float scale_log2;
+  bf16* o;
+  int64_t ldo;
+  float* lse;
+  int* err;
+};
+
+__device__ __forceinline__ int at2_live_tiles(const AttnTc2Params& p, int n0b, int n1b) {
+  int n = 0;
+  for (int j = 0; j < p.nt0; ++j) n += (j * at2::BKV < n0b) ? 1 : 0;
+  for (int j = 0; j < p.nt1; ++j) n += (j * at2::BKV < n1b) ? 1 : 0;
+  return n;
+}
+
+// j-th live key tile of a sample -> storage tile index (source 0 tiles first)
+__device__ __forceinline__ int at2_tile(const AttnTc2Params& p, int n0b, int n1b, int live) {
+  for (int j = 0; j < p.nt0; ++j)
+    if (j * at2::BKV < n0b && live-- == 0) return j;
+  for (int j = 0; j < p.nt1; ++j)
+    if (j * at2::BKV < n1b && live-- == 0) return p.nt0 + j;
+  return -1;
+}
+
+__global__ void __launch_bounds__(at2::THREADS)
+    attn_fwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK0,
+                        const __grid_constant__ CUtensorMap tmV0, const __grid_constant__ CUtensorMap tmK1,
+                        const __grid_constant__ CUtensorMap tmV1, const AttnTc2Params p) {
+  using namespace at2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* q_full = bars;        // [2]
+  uint64_t* q_empty = bars + 2;   // [2]
+  uint64_t* kv_full = bars + 4;   // [2]
+  uint64_t* kv_empty = bars + 6;  // [2]
+  uint64_t* s_full = bars + 8;    // [A, B]
+  uint64_t* p_full = bars + 10;   // [A, B]  (4 warps arrive)
+  uint64_t* o_done = bars + 12;   // [A, B]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      uint32_t g = 0;  // global live key-tile counter (K/V ring position)
+      int ii = 0;
+      for (int item = blockIdx.x; item < p.items && !*abort_flag; item += gridDim.x, ++ii) {
+        const int bh = item / p.nqp, qp = item - bh * p.nqp, b = bh / p.H, h = bh - b * p.H;
+        const int n0b = p.n0[b], n1b = p.n1[b];
+        const int q0 = qp * 2 * BQ;
+        const bool liveB = q0 + BQ < p.Lq;
+        const int qb = ii & 1;
+        if (!mbar_wait(&q_empty[qb], ((ii >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&q_full[qb], (liveB ? 2 : 1) * QT);
+        tma_load_3d(&tmQ, &q_full[qb], smem + OFF_Q + (qb * 2) * QT, h * D, q0, b);
+        if (liveB) tma_load_3d(&tmQ, &q_full[qb], smem + OFF_Q + (qb * 2 + 1) * QT, h * D, q0 + BQ, b);
+        const int n = at2_live_tiles(p, n0b, n1b);
+        for (int it = 0; it < n; ++it, ++g) {
+          const int st = g & 1;
+          if (!mbar_wait(&kv_empty[st], ((g >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
+          const int j = at2_tile(p, n0b, n1b, it);
+          uint8_t* k = smem + OFF_KV + st * 2 * KVT;
+          mbar_arrive_expect_tx(&kv_full[st], 2 * KVT);
+          if (j < p.nt0) {
+            tma_load_3d(&tmK0, &kv_full[st], k, h * D, j * BKV, b);
+            tma_load_3d(&tmV0, &kv_full[st], k + KVT, h * D, j * BKV, b);
+          } else {
+            tma_load_3d(&tmK1, &kv_full[st], k, h * D, (j - p.nt0) * BKV, b);
+            tma_load_3d(&tmV1, &kv_full[st], k + KVT, h * D, (j - p.nt0) * BKV, b);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_bf16_f32(BQ, BKV, 0, 0);
+      constexpr uint32_t idesc_o = idesc_bf16_f32(BQ, D, 0, 1);
+      uint32_t g = 0;   // K/V ring and tile-A barrier phases: every live key tile
+      uint32_t gB = 0;  // tile-B barrier phases: key tiles of items whose tile B holds queries
+      int ii = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < p.items && !*abort_flag; item += gridDim.x, ++ii) {
+        const int bh = item / p.nqp, qp = item - bh * p.nqp, b = bh / p.H;
+        const int n0b = p.n0[b], n1b = p.n1[b];
+        const bool liveB = qp * 2 * BQ + BQ < p.Lq;
+        const int qb = ii & 1;
+        const int n = at2_live_tiles(p, n0b, n1b);
+        if (!mbar_wait(&q_full[qb], (ii >> 1) & 1, abort_flag, p.err, kErrWaitFull)) break;
+        tc_fence_after();
+        const uint32_t qa = smem_u32(smem + OFF_Q + (qb * 2) * QT);
+        auto issue_s = [&](int X, uint32_t gg) {
+          const uint32_t kb = smem_u32(smem + OFF_KV + (gg & 1) * 2 * KVT);
+          const uint32_t qx = qa + X * QT;
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k)
+            umma_f16(tmem + C_S + X * BKV, smem_desc_sw128(qx + k * 32, 16, 1024),
+                     smem_desc_sw128(kb + k * 32, 16, 1024), idesc_s, k != 0 ? 1u : 0u);
+          umma_commit(&s_full[X]);
+        };
+        auto issue_pv = [&](int X, uint32_t gg, bool first) {
+          const uint32_t pa = smem_u32(smem + OFF_P + X * PT);
+          const uint32_t vb = smem_u32(smem + OFF_KV + (gg & 1) * 2 * KVT + KVT);
+#pragma unroll
+          for (int k = 0; k < BKV / 16; ++k)
+            umma_f16(tmem + C_O + X * D, smem_desc_sw128(pa + (k >> 2) * (PT / 2) + (k & 3) * 32, 16, 1024),
+                     smem_desc_sw128(vb + k * 2048, 8192, 1024), idesc_o, (!first || k != 0) ? 1u : 0u);
+          umma_commit(&o_done[X]);
+        };
+        if (n > 0) {
+          if (!mbar_wait(&kv_full[g & 1], (g >> 1) & 1, abort_flag, p.err, kErrWaitFull)) break;
+          tc_fence_after();
+          issue_s(0, g);
+          if (liveB) issue_s(1, g);
+        }
+        for (int it = 0; it < n; ++it, ++g) {
+          const bool more = it + 1 < n;
+          if (!mbar_wait(&p_full[0], g & 1, abort_flag, p.err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_pv(0, g, it == 0);
+          if (more) {
+            if (!mbar_wait(&kv_full[(g + 1) & 1], ((g + 1) >> 1) & 1, abort_flag, p.err, kErrWaitFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_s(0, g + 1);
+          }
+          if (liveB) {
+            if (!mbar_wait(&p_full[1], gB & 1, abort_flag, p.err, kErrWaitFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(1, g, it == 0);
+            ++gB;
+          }
+          umma_commit(&kv_empty[g & 1]);
+          if (more && liveB) issue_s(1, g + 1);
+        }
+        umma_commit(&q_empty[qb]);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------------------------------- softmax warpgroups
+    const int X = (warp - 2) >> 2;  // 0: tile A, 1: tile B
+    const int quarter = warp & 3;   // TMEM lane quarter this warp may access
+    const int row = quarter * 32 + lane;
+    const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
+    uint8_t* pb = smem + OFF_P + X * PT;
+    uint32_t g = 0;  // this warpgroup's key tiles so far (its barriers' phases)
+    bool ok = true;
+    for (int item = blockIdx.x; ok && item < p.items && !*abort_flag; item += gridDim.x) {
+      const int bh = item / p.nqp, qp = item - bh * p.nqp, b = bh / p.H, h = bh - b * p.H;
+      const int n0b = p.n0[b], n1b = p.n1[b];
+      const int q0 = qp * 2 * BQ + X * BQ;
+      const int n = at2_live_tiles(p, n0b, n1b);
+      if (q0 >= p.Lq) continue;  // tile B past the queries: the MMA warp skips it too
+      float m = -INFINITY, l = 0.f;
+      for (int it = 0; it < n; ++it, ++g) {
+        const int j = at2_tile(p, n0b, n1b, it);
+        const bool got = __all_sync(0xffffffffu, mbar_wait(&s_full[X], g & 1, abort_flag, p.err, kErrWaitAccFull));
+        if (!got) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        // valid keys of this tile: a prefix [0, nv)
+        const int nv = j < p.nt0 ? min(BKV, min(n0b, p.L0) - j * BKV) : min(BKV, min(n1b, p.L1) - (j - p.nt0) * BKV);
+        // pass 1: the row maximum, 32 columns at a time (TMEM reads are cheap; registers are not)
+        float mt = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < BKV / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(trow + C_S + X * BKV + c * 32, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int k = 0; k < 32; ++k)
+            if (c * 32 + k < nv) mt = fmaxf(mt, __uint_as_float(r[k]));
+        }
+        const float mn = fmaxf(m, mt * p.scale_log2);
+        const float corr = exp2f(m - mn);
+        m = mn;
+        if (it >= 1) {
+          // O and the P buffer are free once the previous P V product completed; S(g) was issued after PV(g-1), so
+          // by now this wait returns at once
+          const bool done =
+              __all_sync(0xffffffffu, mbar_wait(&o_done[X], (g - 1) & 1, abort_flag, p.err, kErrWaitAccFull));
+          if (!done) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (!__all_sync(0xffffffffu, corr == 1.f)) {
+#pragma unroll
+            for (int c = 0; c < D / 16; ++c) {
+              uint32_t r[16];
+              tmem_ld16(trow + C_O + X * D + c * 16, r);
+              tmem_wait_ld();
+#pragma unroll
+              for (int k = 0; k < 16; ++k) r[k] = __float_as_uint(__uint_as_float(r[k]) * corr);
+              tmem_st16(trow + C_O + X * D + c * 16, r);
+            }
+            tmem_wait_st();
+          }
+        }
+        // pass 2: P = exp2(s * scale - max) straight into the shared-memory P tile (bf16, 128-byte swizzle: two
+        // 64-key atoms); the row sum in fp32
+        float ps = 0.f;
+#pragma unroll
+        for (int c = 0; c < BKV / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(trow + C_S + X * BKV + c * 32, r);
+          tmem_wait_ld();
+          uint32_t w[16];
+#pragma unroll
+          for (int k = 0; k < 32; k += 2) {
+            const float e0 = c * 32 + k < nv ? exp2f(fmaf(__uint_as_float(r[k]), p.scale_log2, -mn)) : 0.f;
+            const float e1 = c * 32 + k + 1 < nv ? exp2f(fmaf(__uint_as_float(r[k + 1]), p.scale_log2, -mn)) : 0.f;
+            ps += e0 + e1;
+            w[k / 2] = pack_bf16(e0, e1);
+          }
+          // 32 keys = chunks 4 (c & 1) .. 4 (c & 1) + 3 of atom c / 2
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const int ch = (c & 1) * 4 + q4;
+            *reinterpret_cast<uint4*>(pb + (c >> 1) * (PT / 2) + row * 128 + ((ch ^ (row & 7)) << 4)) =
+                make_uint4(w[4 * q4], w[4 * q4 + 1], w[4 * q4 + 2], w[4 * q4 + 3]);
+          }
+        }
+        l = l * corr + ps;
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[X]);
+      }
+      if (!ok) break;
+      // epilogue: O / l and the log-sum-exp (natural log); rows past Lq are not stored
+      const int qrow = q0 + row;
+      if (n > 0) {
+        const bool done =
+            __all_sync(0xffffffffu, mbar_wait(&o_done[X], (g - 1) & 1, abort_flag, p.err, kErrWaitAccFull));
+        if (!done) break;
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        uint4* dst = reinterpret_cast<uint4*>(p.o + ((int64_t)b * p.Lq + min(qrow, p.Lq - 1)) * p.ldo + h * D);
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(trow + C_O + X * D + c * 32, r);
+          tmem_wait_ld();
+          if (qrow < p.Lq) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              dst[c * 4 + k] = make_uint4(pack_bf16(__uint_as_float(r[8 * k + 0]) * inv, __uint_as_float(r[8 * k + 1]) * inv),
+                                          pack_bf16(__uint_as_float(r[8 * k + 2]) * inv, __uint_as_float(r[8 * k + 3]) * inv),
+                                          pack_bf16(__uint_as_float(r[8 * k + 4]) * inv, __uint_as_float(r[8 * k + 5]) * inv),
+                                          pack_bf16(__uint_as_float(r[8 * k + 6]) * inv, __uint_as_float(r[8 * k + 7]) * inv));
+          }
+        }
+        tc_fence_before();
+        if (qrow < p.Lq) p.lse[((int64_t)b * p.H + h) * p.Lq + qrow] = (m + log2f(l)) * atc::kLn2;
+      } else if (qrow < p.Lq) {  // no valid key: zero output, lse = -inf (nothing to attend to)
+        uint4* dst = reinterpret_cast<uint4*>(p.o + ((int64_t)b * p.Lq + qrow) * p.ldo + h * D);
+#pragma unroll
+        for (int k = 0; k < D / 8; ++k) dst[k] = make_uint4(0, 0, 0, 0);
+        p.lse[((int64_t)b * p.H + h) * p.Lq + qrow] = -INFINITY;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
 // ====================================================================================================== torch glue
 // 3-D map over a token-major view [B * L rows, C] with row stride ld: dims (C, L, B), box (64, 128, 1).
 static CUtensorMap seq_map(const at::Tensor& t, int64_t L) {
@@ -301,7 +632,7 @@ static CUtensorMap seq_map(const at::Tensor& t, int64_t L) {
 
 void attn_fwd_tc(const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0, const c10::optional<at::Tensor>& k1,
                  const c10::optional<at::Tensor>& v1, const at::Tensor& n0, const at::Tensor& n1, const at::Tensor& o,
-                 const at::Tensor& lse, int64_t Lq, int64_t L0, int64_t L1, double scale) {
+                 const at::Tensor& lse, int64_t Lq, int64_t L0, int64_t L1, double scale, int64_t version) {
   TORCH_CHECK(q.is_cuda() && q.size(1) % 64 == 0, "attn_fwd_tc: head dim 64");
   TORCH_CHECK(n0.scalar_type() == at::kInt && n1.scalar_type() == at::kInt, "int32 key counts expected");
   const at::cuda::CUDAGuard guard(q.device());
@@ -324,14 +655,44 @@ void attn_fwd_tc(const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0
                                   atc::BQ);
   CUtensorMap mk0 = seq_map(k0, L0), mv0 = seq_map(v0, L0);
   CUtensorMap mk1 = has1 ? seq_map(*k1, L1) : mk0, mv1 = has1 ? seq_map(*v1, L1) : mv0;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, atc::SMEM);
-    attr = true;
-  }
   const int B = (int)(q.size(0) / Lq);
-  dim3 grid((unsigned)((Lq + atc::BQ - 1) / atc::BQ), (unsigned)(B * p.H));
-  attn_fwd_tc_kernel<<<grid, atc::THREADS, atc::SMEM, at::cuda::getCurrentCUDAStream()>>>(mq, mk0, mv0, mk1, mv1, p);
+  if (version == 1) {
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(attn_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, atc::SMEM);
+      attr = true;
+    }
+    dim3 grid((unsigned)((Lq + atc::BQ - 1) / atc::BQ), (unsigned)(B * p.H));
+    attn_fwd_tc_kernel<<<grid, atc::THREADS, atc::SMEM, at::cuda::getCurrentCUDAStream()>>>(mq, mk0, mv0, mk1, mv1,
+                                                                                             p);
+    NG_LAUNCH_CHECK();
+    return;
+  }
+  AttnTc2Params p2{};
+  p2.n0 = p.n0;
+  p2.n1 = p.n1;
+  p2.Lq = p.Lq;
+  p2.L0 = p.L0;
+  p2.L1 = p.L1;
+  p2.H = p.H;
+  p2.nt0 = p.nt0;
+  p2.nt1 = p.nt1;
+  p2.nqp = (int)((Lq + 2 * at2::BQ - 1) / (2 * at2::BQ));
+  p2.items = B * p.H * p2.nqp;
+  p2.scale_log2 = p.scale_log2;
+  p2.o = p.o;
+  p2.ldo = p.ldo;
+  p2.lse = p.lse;
+  p2.err = p.err;
+  static bool attr2 = false;
+  static int sms = 0;
+  if (!attr2) {
+    cudaFuncSetAttribute(attn_fwd_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, at2::SMEM);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, q.get_device());
+    attr2 = true;
+  }
+  const int grid = std::max(1, std::min(p2.items, sms));
+  attn_fwd_tc2_kernel<<<grid, at2::THREADS, at2::SMEM, at::cuda::getCurrentCUDAStream()>>>(mq, mk0, mv0, mk1, mv1, p2);
   NG_LAUNCH_CHECK();
 }
 
@@ -635,6 +996,339 @@ __global__ void __launch_bounds__(atb::THREADS, 1)
   }
 }
 
+// ================================================================================ backward, persistent version
+// Work item = (128-key tile, sample, head); a CTA loops over items with K/V double-buffered, so the next item's loads
+// and S^T/dP^T MMAs overlap this item's dK/dV epilogue. Eight compute warps: two per TMEM lane quarter, warp half h
+// owns query columns [64h, 64h + 64) of S^T/dP^T (= one 64-query swizzle atom of P^T/dS^T), d columns
+// [32h, 32h + 32) of dQ, dK, dV. dQ tiles are staged for their TMA reduce-add in the warp's own 4 KiB slice of the
+// P^T tile, which the dV MMA has finished reading when dQ is ready.
+// TMEM: S^T [0,128), dP^T [128,256), dV [256,320), dK [320,384), dQ [384,448).
+namespace ab2 {
+constexpr int BQ = 128, BK = 128, D = 64;
+constexpr int THREADS = 320;                       // warp 0 TMA, warp 1 MMA, warps 2..9 compute
+constexpr int T16 = BK * D * 2;                    // 16 KiB
+constexpr int PT = BK * BQ * 2;                    // 32 KiB
+constexpr int OFF_KV = 0;                          // [2 buffers][K, V]
+constexpr int OFF_QD = OFF_KV + 4 * T16;           // [2 stages][Q, dO]
+constexpr int OFF_P = OFF_QD + 4 * T16;            // P^T
+constexpr int OFF_DS = OFF_P + PT;                 // dS^T
+constexpr int OFF_LD = OFF_DS + PT;                // per compute warp: lse (log2 units) and delta of its 64 queries
+constexpr int OFF_BAR = OFF_LD + 8 * 2 * 64 * 4;
+constexpr int SMEM = OFF_BAR + 256 + 1024;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320, C_DQ = 384;
+}  // namespace ab2
+
+struct AttnTcBwd2Params {
+  const int *n0, *n1;
+  int Lq, L0, L1, H;
+  int nt0, nt1, nq, items;
+  float scale, scale_log2;
+  const float* lse;
+  const float* delta;
+  bf16 *dk0, *dv0, *dk1, *dv1;
+  int64_t lddk0, lddv0, lddk1, lddv1;
+  int* err;
+};
+
+struct Bwd2Item {
+  int b, h, kt0, Lsrc, nvalid;
+  bool src1, live;
+};
+
+__device__ __forceinline__ Bwd2Item bwd2_item(const AttnTcBwd2Params& p, int item) {
+  Bwd2Item it;
+  const int nt = p.nt0 + p.nt1;
+  const int j = item % nt, bh = item / nt;
+  it.b = bh / p.H;
+  it.h = bh - it.b * p.H;
+  it.src1 = j >= p.nt0;
+  it.kt0 = (it.src1 ? j - p.nt0 : j) * ab2::BK;
+  it.Lsrc = it.src1 ? p.L1 : p.L0;
+  it.nvalid = it.src1 ? p.n1[it.b] : p.n0[it.b];
+  it.live = it.kt0 < it.nvalid && it.kt0 < it.Lsrc;
+  return it;
+}
+
+__global__ void __launch_bounds__(ab2::THREADS)
+    attn_bwd_tc2_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmDO,
+                        const __grid_constant__ CUtensorMap tmK0, const __grid_constant__ CUtensorMap tmV0,
+                        const __grid_constant__ CUtensorMap tmK1, const __grid_constant__ CUtensorMap tmV1,
+                        const __grid_constant__ CUtensorMap tmDQ, const AttnTcBwd2Params p) {
+  using namespace ab2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* kv_full = bars;         // [2]
+  uint64_t* kv_empty = bars + 2;    // [2]
+  uint64_t* qd_full = bars + 4;     // [2]
+  uint64_t* qd_empty = bars + 6;    // [2]
+  uint64_t* st_full = bars + 8;
+  uint64_t* ps_full = bars + 9;     // 8 warps
+  uint64_t* dq_full = bars + 10;
+  uint64_t* dq_empty = bars + 11;   // 8 warps
+  uint64_t* dkv_full = bars + 12;
+  uint64_t* dkv_empty = bars + 13;  // 8 warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&qd_full[i], 1);
+      mbar_init(&qd_empty[i], 1);
+    }
+    mbar_init(st_full, 1);
+    mbar_init(ps_full, 8);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 8);
+    mbar_init(dkv_full, 1);
+    mbar_init(dkv_empty, 8);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      uint32_t li = 0, gq = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < p.items && !*abort_flag; item += gridDim.x) {
+        const Bwd2Item w = bwd2_item(p, item);
+        if (!w.live) continue;
+        const int kb = li & 1;
+        if (!mbar_wait(&kv_empty[kb], ((li >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
+        mbar_arrive_expect_tx(&kv_full[kb], 2 * T16);
+        tma_load_3d(w.src1 ? &tmK1 : &tmK0, &kv_full[kb], smem + OFF_KV + kb * 2 * T16, w.h * D, w.kt0, w.b);
+        tma_load_3d(w.src1 ? &tmV1 : &tmV0, &kv_full[kb], smem + OFF_KV + kb * 2 * T16 + T16, w.h * D, w.kt0, w.b);
+        for (int i = 0; i < p.nq; ++i, ++gq) {
+          const int st = gq & 1;
+          if (!mbar_wait(&qd_empty[st], ((gq >> 1) & 1) ^ 1, abort_flag, p.err, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&qd_full[st], 2 * T16);
+          tma_load_3d(&tmQ, &qd_full[st], smem + OFF_QD + st * 2 * T16, w.h * D, i * BQ, w.b);
+          tma_load_3d(&tmDO, &qd_full[st], smem + OFF_QD + st * 2 * T16 + T16, w.h * D, i * BQ, w.b);
+        }
+        ++li;
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_bf16_f32(BK, BQ, 0, 0);
+      constexpr uint32_t id_kv = idesc_bf16_f32(BK, D, 0, 1);
+      constexpr uint32_t id_q = idesc_bf16_f32(BQ, D, 1, 1);
+      const uint32_t aP = smem_u32(smem + OFF_P), aDS = smem_u32(smem + OFF_DS);
+      uint32_t li = 0, gq = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < p.items && !*abort_flag; item += gridDim.x) {
+        const Bwd2Item w = bwd2_item(p, item);
+        if (!w.live) continue;
+        const int kb = li & 1;
+        if (!mbar_wait(&kv_full[kb], (li >> 1) & 1, abort_flag, p.err, kErrWaitFull)) break;
+        tc_fence_after();
+        const uint32_t aK = smem_u32(smem + OFF_KV + kb * 2 * T16), aV = aK + T16;
+        for (int i = 0; i < p.nq; ++i, ++gq) {
+          const int st = gq & 1;
+          if (!mbar_wait(&qd_full[st], (gq >> 1) & 1, abort_flag, p.err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t aQ = smem_u32(smem + OFF_QD + st * 2 * T16), aDO = aQ + T16;
+#pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            umma_f16(tmem + C_S, smem_desc_sw128(aK + k * 32, 16, 1024), smem_desc_sw128(aQ + k * 32, 16, 1024), id_s,
+                     k != 0 ? 1u : 0u);
+            umma_f16(tmem + C_DP, smem_desc_sw128(aV + k * 32, 16, 1024), smem_desc_sw128(aDO + k * 32, 16, 1024),
+                     id_s, k != 0 ? 1u : 0u);
+          }
+          umma_commit(st_full);
+          if (!mbar_wait(ps_full, gq & 1, abort_flag, p.err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          if (i == 0 && li >= 1 && !mbar_wait(dkv_empty, (li - 1) & 1, abort_flag, p.err, kErrWaitAccEmpty)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < BQ / 16; ++k) {
+            const uint32_t ka = (k >> 2) * (PT / 2) + (k & 3) * 32;
+            umma_f16(tmem + C_DV, smem_desc_sw128(aP + ka, 16, 1024), smem_desc_sw128(aDO + k * 2048, 8192, 1024),
+                     id_kv, (i != 0 || k != 0) ? 1u : 0u);
+            umma_f16(tmem + C_DK, smem_desc_sw128(aDS + ka, 16, 1024), smem_desc_sw128(aQ + k * 2048, 8192, 1024),
+                     id_kv, (i != 0 || k != 0) ? 1u : 0u);
+          }
+          if (gq >= 1 && !mbar_wait(dq_empty, (gq - 1) & 1, abort_flag, p.err, kErrWaitAccEmpty)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16(tmem + C_DQ, smem_desc_sw128(aDS + k * 2048, PT / 2, 1024),
+                     smem_desc_sw128(aK + k * 2048, 8192, 1024), id_q, k != 0 ? 1u : 0u);
+          umma_commit(dq_full);
+          umma_commit(&qd_empty[st]);
+        }
+        if (!ok) break;
+        umma_commit(dkv_full);
+        umma_commit(&kv_empty[kb]);
+        ++li;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------------------------------ compute warps
+    const int quarter = warp & 3, hh = (warp - 2) >> 2;
+    const int r = quarter * 32 + lane;  // key row (P/dS, dK/dV) or query row (dQ) of this thread
+    const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
+    float* wl = reinterpret_cast<float*>(smem + OFF_LD) + (warp - 2) * 128;  // [lse 64][delta 64]
+    uint8_t* slice = smem + OFF_P + hh * (PT / 2) + quarter * 4096;        // this warp's 4 KiB of P^T
+    uint32_t li = 0, gq = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; ok && item < p.items && !*abort_flag; item += gridDim.x) {
+      const Bwd2Item w = bwd2_item(p, item);
+      bf16* dk_base = w.src1 ? p.dk1 : p.dk0;
+      bf16* dv_base = w.src1 ? p.dv1 : p.dv0;
+      const int64_t lddk = w.src1 ? p.lddk1 : p.lddk0, lddv = w.src1 ? p.lddv1 : p.lddv0;
+      const int s_row = w.kt0 + r;
+      const int64_t grow = (int64_t)w.b * w.Lsrc + min(s_row, w.Lsrc - 1);
+      if (!w.live) {  // no valid key in the tile: zero gradients for its rows
+        if (s_row < w.Lsrc) {
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            reinterpret_cast<uint4*>(dk_base + grow * lddk + w.h * D + hh * 32)[k] = make_uint4(0, 0, 0, 0);
+            reinterpret_cast<uint4*>(dv_base + grow * lddv + w.h * D + hh * 32)[k] = make_uint4(0, 0, 0, 0);
+          }
+        }
+        continue;
+      }
+      const bool key_ok = s_row < w.nvalid && s_row < w.Lsrc;
+      const float* lse_bh = p.lse + ((int64_t)w.b * p.H + w.h) * p.Lq;
+      const float* del_bh = p.delta + ((int64_t)w.b * p.H + w.h) * p.Lq;
+      for (int i = 0; i < p.nq; ++i, ++gq) {
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int qg = i * BQ + hh * 64 + k * 32 + lane;
+          wl[k * 32 + lane] = qg < p.Lq ? lse_bh[qg] * atc::kLog2e : INFINITY;
+          wl[64 + k * 32 + lane] = qg < p.Lq ? del_bh[qg] : 0.f;
+        }
+        if (lane == 0) bulk_wait_read0();  // the previous dQ tile staged in this slice has been read
+        __syncwarp();
+        if (!__all_sync(0xffffffffu, mbar_wait(st_full, gq & 1, abort_flag, p.err, kErrWaitAccFull))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          uint32_t rs[32], rd[32];
+          tmem_ld32(trow + C_S + hh * 64 + c * 32, rs);
+          tmem_ld32(trow + C_DP + hh * 64 + c * 32, rd);
+          tmem_wait_ld();
+          uint32_t wp[16], wd[16];
+#pragma unroll
+          for (int k = 0; k < 32; k += 2) {
+            const int qc = c * 32 + k;
+            const float p0 = key_ok ? exp2f(fmaf(__uint_as_float(rs[k]), p.scale_log2, -wl[qc])) : 0.f;
+            const float p1 = key_ok ? exp2f(fmaf(__uint_as_float(rs[k + 1]), p.scale_log2, -wl[qc + 1])) : 0.f;
+            wp[k / 2] = pack_bf16(p0, p1);
+            wd[k / 2] = pack_bf16(p0 * (__uint_as_float(rd[k]) - wl[64 + qc]),
+                                  p1 * (__uint_as_float(rd[k + 1]) - wl[64 + qc + 1]));
+          }
+          // 32 queries = chunks 4c .. 4c + 3 of the warp's 64-query atom
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            const int ch = c * 4 + q4;
+            const uint32_t off = hh * (PT / 2) + r * 128 + ((ch ^ (r & 7)) << 4);
+            *reinterpret_cast<uint4*>(smem + OFF_P + off) = make_uint4(wp[4 * q4], wp[4 * q4 + 1], wp[4 * q4 + 2],
+                                                                       wp[4 * q4 + 3]);
+            *reinterpret_cast<uint4*>(smem + OFF_DS + off) = make_uint4(wd[4 * q4], wd[4 * q4 + 1], wd[4 * q4 + 2],
+                                                                        wd[4 * q4 + 3]);
+          }
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ps_full);
+        // dQ_i (rows are queries now): scale, stage in this warp's P^T slice, reduce-add by TMA
+        if (!__all_sync(0xffffffffu, mbar_wait(dq_full, gq & 1, abort_flag, p.err, kErrWaitAccFull))) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        {
+          uint32_t rq[32];
+          tmem_ld32(trow + C_DQ + hh * 32, rq);
+          tmem_wait_ld();
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch)
+            *reinterpret_cast<float4*>(slice + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
+                make_float4(__uint_as_float(rq[4 * ch]) * p.scale, __uint_as_float(rq[4 * ch + 1]) * p.scale,
+                            __uint_as_float(rq[4 * ch + 2]) * p.scale, __uint_as_float(rq[4 * ch + 3]) * p.scale);
+        }
+        tc_fence_before();
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(dq_empty);
+          tma_reduce_add_3d(&tmDQ, slice, w.h * D + hh * 32, i * BQ + quarter * 32, w.b);
+          bulk_commit();
+        }
+      }
+      if (!ok) break;
+      // dV, dK of the item: 32 d columns of this warp half, key rows of its quarter
+      if (!__all_sync(0xffffffffu, mbar_wait(dkv_full, li & 1, abort_flag, p.err, kErrWaitAccFull))) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {
+        uint32_t rr[32];
+        tmem_ld32(trow + (which ? C_DK : C_DV) + hh * 32, rr);
+        tmem_wait_ld();
+        if (s_row < w.Lsrc) {
+          const float sc = which ? p.scale : 1.f;
+          uint4* dst = reinterpret_cast<uint4*>((which ? dk_base + grow * lddk : dv_base + grow * lddv) + w.h * D +
+                                                hh * 32);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            dst[k] = make_uint4(pack_bf16(__uint_as_float(rr[8 * k]) * sc, __uint_as_float(rr[8 * k + 1]) * sc),
+                                pack_bf16(__uint_as_float(rr[8 * k + 2]) * sc, __uint_as_float(rr[8 * k + 3]) * sc),
+                                pack_bf16(__uint_as_float(rr[8 * k + 4]) * sc, __uint_as_float(rr[8 * k + 5]) * sc),
+                                pack_bf16(__uint_as_float(rr[8 * k + 6]) * sc, __uint_as_float(rr[8 * k + 7]) * sc));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dkv_empty);
+      ++li;
+    }
+    if (lane == 0) bulk_wait0();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
 // dq_acc[row, c] (fp32, TMA reduce-add target) -> dq (bf16, strided view)
 __global__ void dq_store_kernel(const float* __restrict__ acc, bf16* __restrict__ dq, int64_t lddq, int64_t rows,
                                 int C) {
@@ -662,7 +1356,8 @@ void attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& 
                  const c10::optional<at::Tensor>& k1, const c10::optional<at::Tensor>& v1, const at::Tensor& n0,
                  const at::Tensor& n1, const at::Tensor& o, const at::Tensor& lse, const at::Tensor& dq,
                  const at::Tensor& dk0, const at::Tensor& dv0, const c10::optional<at::Tensor>& dk1,
-                 const c10::optional<at::Tensor>& dv1, int64_t Lq, int64_t L0, int64_t L1, double scale) {
+                 const c10::optional<at::Tensor>& dv1, int64_t Lq, int64_t L0, int64_t L1, double scale,
+                 int64_t version) {
   TORCH_CHECK(q.is_cuda() && q.size(1) % 64 == 0, "attn_bwd_tc: head dim 64");
   TORCH_CHECK(n0.scalar_type() == at::kInt && n1.scalar_type() == at::kInt, "int32 key counts expected");
   for (const at::Tensor* t : {&dout, &o, &dq, &dk0, &dv0})
@@ -708,14 +1403,51 @@ void attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& 
   CUtensorMap mk0 = seq_map(k0, L0), mv0 = seq_map(v0, L0);
   CUtensorMap mk1 = has1 ? seq_map(*k1, L1) : mk0, mv1 = has1 ? seq_map(*v1, L1) : mv0;
   CUtensorMap mdq = make_tmap_f32_box(acc.data_ptr(), C, Lq, B, C, C * Lq, 32, 32);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, atb::SMEM);
-    attr = true;
+  if (version == 1) {
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(attn_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, atb::SMEM);
+      attr = true;
+    }
+    dim3 grid((unsigned)(p.nt0 + p.nt1), (unsigned)(B * p.H));
+    attn_bwd_tc_kernel<<<grid, atb::THREADS, atb::SMEM, s>>>(mq, mdo, mk0, mv0, mk1, mv1, mdq, p);
+    NG_LAUNCH_CHECK();
+  } else {
+    AttnTcBwd2Params p2{};
+    p2.n0 = p.n0;
+    p2.n1 = p.n1;
+    p2.Lq = p.Lq;
+    p2.L0 = p.L0;
+    p2.L1 = p.L1;
+    p2.H = p.H;
+    p2.nt0 = p.nt0;
+    p2.nt1 = p.nt1;
+    p2.nq = p.nq;
+    p2.items = (int)B * p.H * (p.nt0 + p.nt1);
+    p2.scale = p.scale;
+    p2.scale_log2 = p.scale_log2;
+    p2.lse = p.lse;
+    p2.delta = p.delta;
+    p2.dk0 = p.dk0;
+    p2.dv0 = p.dv0;
+    p2.dk1 = p.dk1;
+    p2.dv1 = p.dv1;
+    p2.lddk0 = p.lddk0;
+    p2.lddv0 = p.lddv0;
+    p2.lddk1 = p.lddk1;
+    p2.lddv1 = p.lddv1;
+    p2.err = p.err;
+    static bool attr2 = false;
+    static int sms = 0;
+    if (!attr2) {
+      cudaFuncSetAttribute(attn_bwd_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ab2::SMEM);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, q.get_device());
+      attr2 = true;
+    }
+    const int grid = std::max(1, std::min(p2.items, sms));
+    attn_bwd_tc2_kernel<<<grid, ab2::THREADS, ab2::SMEM, s>>>(mq, mdo, mk0, mv0, mk1, mv1, mdq, p2);
+    NG_LAUNCH_CHECK();
   }
-  dim3 grid((unsigned)(p.nt0 + p.nt1), (unsigned)(B * p.H));
-  attn_bwd_tc_kernel<<<grid, atb::THREADS, atb::SMEM, s>>>(mq, mdo, mk0, mv0, mk1, mv1, mdq, p);
-  NG_LAUNCH_CHECK();
   const int64_t n8 = q.size(0) * (C / 8);
   dq_store_kernel<<<(unsigned)((n8 + 255) / 256), 256, 0, s>>>(acc.data_ptr<float>(),
                                                                reinterpret_cast<bf16*>(dq.data_ptr()), dq.stride(0),

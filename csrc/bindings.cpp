@@ -45,12 +45,12 @@ void patchify(const at::Tensor& img, const at::Tensor& tok, int64_t p);
 void unpatchify(const at::Tensor& tok, const at::Tensor& img, int64_t p);
 void attn_fwd_tc(const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0, const c10::optional<at::Tensor>& k1,
                  const c10::optional<at::Tensor>& v1, const at::Tensor& n0, const at::Tensor& n1, const at::Tensor& o,
-                 const at::Tensor& lse, int64_t Lq, int64_t L0, int64_t L1, double scale);
+                 const at::Tensor& lse, int64_t Lq, int64_t L0, int64_t L1, double scale, int64_t version);
 void attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0,
                  const c10::optional<at::Tensor>& k1, const c10::optional<at::Tensor>& v1, const at::Tensor& n0,
                  const at::Tensor& n1, const at::Tensor& o, const at::Tensor& lse, const at::Tensor& dq,
                  const at::Tensor& dk0, const at::Tensor& dv0, const c10::optional<at::Tensor>& dk1,
-                 const c10::optional<at::Tensor>& dv1, int64_t Lq, int64_t L0, int64_t L1, double scale);
+                 const c10::optional<at::Tensor>& dv1, int64_t Lq, int64_t L0, int64_t L1, double scale, int64_t version);
 void colsum(const at::Tensor& src, const at::Tensor& out, bool accumulate);
 void add_rows(const at::Tensor& a, const at::Tensor& table, const at::Tensor& out, int64_t period);
 }  // namespace ng
@@ -66,8 +66,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_norm_bwd", &ng::qk_norm_bwd);
   m.def("attn_fwd", &ng::attn_fwd);
   m.def("attn_bwd", &ng::attn_bwd);
-  m.def("attn_fwd_tc", &ng::attn_fwd_tc, "masked attention forward on tcgen05/TMEM");
-  m.def("attn_bwd_tc", &ng::attn_bwd_tc, "masked attention backward on tcgen05/TMEM");
+  m.def("attn_fwd_tc", &ng::attn_fwd_tc, "masked attention forward on tcgen05/TMEM (version 2: persistent, two query "
+        "tiles per CTA; version 1: one query tile per CTA)", py::arg("q"), py::arg("k0"), py::arg("v0"), py::arg("k1"),
+        py::arg("v1"), py::arg("n0"), py::arg("n1"), py::arg("o"), py::arg("lse"), py::arg("Lq"), py::arg("L0"),
+        py::arg("L1"), py::arg("scale"), py::arg("version") = 2);
+  m.def("attn_bwd_tc", &ng::attn_bwd_tc, "masked attention backward on tcgen05/TMEM (version 2: persistent, 8 compute "
+        "warps; version 1: CTA per key tile)", py::arg("dout"), py::arg("q"), py::arg("k0"), py::arg("v0"),
+        py::arg("k1"), py::arg("v1"), py::arg("n0"), py::arg("n1"), py::arg("o"), py::arg("lse"), py::arg("dq"),
+        py::arg("dk0"), py::arg("dv0"), py::arg("dk1"), py::arg("dv1"), py::arg("Lq"), py::arg("L0"), py::arg("L1"),
+        py::arg("scale"), py::arg("version") = 2);
   m.def("gate_bwd", &ng::gate_bwd);
   m.def("fm_prep", &ng::fm_prep);
   m.def("fm_loss", &ng::fm_loss);

@@ -40,10 +40,12 @@ def _keys_cpu(k0, v0, L0, n0, k1, v1, L1, n1, B, H):
     return torch.stack(ks), torch.stack(vs), torch.stack(masks)
 
 
-def attn_fwd(q, Lq, k0, v0, L0, n0, k1=None, v1=None, L1=0, n1=None, scale=0.125, impl="tc"):
+def attn_fwd(q, Lq, k0, v0, L0, n0, k1=None, v1=None, L1=0, n1=None, scale=0.125, impl="tc1"):
     """q [B*Lq, H*64]; k0/v0 [B*L0, H*64]; k1/v1 [B*L1, H*64] or None; n0/n1: int or int32 [B] valid-key counts.
     Returns (o [B*Lq, H*64] bf16, lse [B, H, Lq] fp32). On CUDA the forward runs on tcgen05/TMEM
-    (csrc/attn_tc.cu); impl="mma" selects the warp-level mma.sync kernel (csrc/attention.cu), kept as a test oracle."""
+    (csrc/attn_tc.cu; impl="tc1", the default: one 128-query tile per CTA; impl="tc": a persistent kernel with two
+    query tiles per CTA ping-ponging on the tensor core); impl="mma" selects the warp-level mma.sync kernel
+    (csrc/attention.cu), kept as a test oracle."""
     rows, C = q.shape
     B, H = rows // Lq, C // HEAD
     n0 = _lens(n0, B, q.device)
@@ -59,8 +61,8 @@ def attn_fwd(q, Lq, k0, v0, L0, n0, k1=None, v1=None, L1=0, n1=None, scale=0.125
         return o.to(torch.bfloat16), lse
     o = torch.empty(rows, C, device=q.device, dtype=torch.bfloat16)
     lse = torch.empty(B, H, Lq, device=q.device, dtype=torch.float32)
-    if impl == "tc":
-        ext().attn_fwd_tc(q, k0, v0, k1, v1, n0, n1, o, lse, Lq, L0, L1, scale)
+    if impl in ("tc", "tc1"):
+        ext().attn_fwd_tc(q, k0, v0, k1, v1, n0, n1, o, lse, Lq, L0, L1, scale, 1 if impl == "tc1" else 2)
     else:
         ext().attn_fwd(q, k0, v0, k1, v1, n0, n1, o, lse, Lq, L0, L1, scale)
     return o, lse
@@ -117,6 +119,9 @@ def attn_bwd(do, q, Lq, k0, v0, L0, n0, o, lse, k1=None, v1=None, L1=0, n1=None,
     if k1 is not None:
         dk1 = alloc(dk1, B * L1)
         dv1 = alloc(dv1, B * L1)
-    fn = ext().attn_bwd_tc if impl == "tc" else ext().attn_bwd
-    fn(do, q, k0, v0, k1, v1, n0, n1, o, lse, dq, dk0, dv0, dk1, dv1, Lq, L0, L1, scale)
+    if impl in ("tc", "tc1"):
+        ext().attn_bwd_tc(do, q, k0, v0, k1, v1, n0, n1, o, lse, dq, dk0, dv0, dk1, dv1, Lq, L0, L1, scale,
+                          1 if impl == "tc1" else 2)
+    else:
+        ext().attn_bwd(do, q, k0, v0, k1, v1, n0, n1, o, lse, dq, dk0, dv0, dk1, dv1, Lq, L0, L1, scale)
     return dq, dk0, dv0, dk1, dv1

@@ -113,7 +113,7 @@ def test_attention(joint):
         _close(a, b, what=name)
 
 
-@pytest.mark.parametrize("case", ["joint", "text", "joint_long"])
+@pytest.mark.parametrize("case", ["joint", "text", "joint_long", "text_long", "odd"])
 def test_attention_tc_forward(case):
     """tcgen05 forward against the fp32 reference and the mma.sync kernel (partial tiles, skipped tiles, T > 128)."""
     from nano_gpic_b200.ops import attention as A
@@ -124,6 +124,11 @@ def test_attention_tc_forward(case):
         Lq, L0, L1, n0, n1 = 256, 256, 72, 256, torch.tensor([72, 5, 40], dtype=torch.int32, device="cuda")
     elif case == "joint_long":
         Lq, L0, L1, n0, n1 = 256, 256, 200, 256, torch.tensor([200, 129, 3], dtype=torch.int32, device="cuda")
+    elif case == "text_long":  # several query-tile pairs per sample, tile B of the last pair past the queries
+        Lq, L0, L1, n0, n1 = 320, 320, 0, torch.tensor([320, 130, 1], dtype=torch.int32, device="cuda"), None
+    elif case == "odd":
+        Lq, L0, L1, n0, n1 = 200, 200, 40, torch.tensor([200, 150, 7], dtype=torch.int32, device="cuda"), \
+            torch.tensor([40, 0, 17], dtype=torch.int32, device="cuda")
     else:
         Lq, L0, L1, n0, n1 = 72, 72, 0, torch.tensor([72, 9, 33], dtype=torch.int32, device="cuda"), None
     qkv = torch.randn(B * Lq, 3 * C, device="cuda").bfloat16()
@@ -134,6 +139,8 @@ def test_attention_tc_forward(case):
     else:
         k1 = v1 = None
     o, lse = A.attn_fwd(q, Lq, k0, v0, L0, n0, k1, v1, L1, n1, impl="tc")
+    o1, lse1 = A.attn_fwd(q, Lq, k0, v0, L0, n0, k1, v1, L1, n1, impl="tc1")
+    _close(o, o1, rtol=1e-2, atol=1e-2, what="o: two-tile vs one-tile kernel")
     om, lsem = A.attn_fwd(q, Lq, k0, v0, L0, n0, k1, v1, L1, n1, impl="mma")
     oc, lsec = A.attn_fwd(*_cpu(q), Lq, *_cpu(k0, v0), L0, n0 if isinstance(n0, int) else n0.cpu(),
                           *_cpu(k1, v1), L1, n1.cpu() if n1 is not None else None)
@@ -144,7 +151,7 @@ def test_attention_tc_forward(case):
     assert status.read() == 0
 
 
-@pytest.mark.parametrize("case", ["joint", "text", "joint_long", "odd"])
+@pytest.mark.parametrize("case", ["joint", "text", "joint_long", "odd", "text_long"])
 def test_attention_tc_backward(case):
     """tcgen05 backward against the fp32 autograd reference and the mma.sync kernels; dK/dV of padded keys are zero."""
     from nano_gpic_b200.ops import attention as A
@@ -158,6 +165,8 @@ def test_attention_tc_backward(case):
     elif case == "odd":
         Lq, L0, L1, n0, n1 = 200, 200, 40, torch.tensor([200, 150, 7], dtype=torch.int32, device="cuda"), \
             torch.tensor([40, 0, 17], dtype=torch.int32, device="cuda")
+    elif case == "text_long":  # 3 key tiles, the third one dead for two samples
+        Lq, L0, L1, n0, n1 = 320, 320, 0, torch.tensor([320, 130, 1], dtype=torch.int32, device="cuda"), None
     else:
         Lq, L0, L1, n0, n1 = 72, 72, 0, torch.tensor([72, 9, 33], dtype=torch.int32, device="cuda"), None
     qkv = torch.randn(B * Lq, 3 * C, device="cuda").bfloat16()
@@ -169,6 +178,7 @@ def test_attention_tc_backward(case):
         k1 = v1 = None
     o, lse = A.attn_fwd(q, Lq, k0, v0, L0, n0, k1, v1, L1, n1)
     do = torch.randn_like(o)
+    g1 = A.attn_bwd(do, q, Lq, k0, v0, L0, n0, o, lse, k1, v1, L1, n1, impl="tc1")
     dqkv = torch.full_like(qkv, 7.0)  # strided destinations, like the fused qkv gradient
     dkv = torch.full((B * L1, 2 * C), 7.0, device="cuda", dtype=torch.bfloat16) if L1 else None
     g = A.attn_bwd(do, q, Lq, k0, v0, L0, n0, o, lse, k1, v1, L1, n1, dq=dqkv[:, :C], dk0=dqkv[:, C:2 * C],
@@ -177,10 +187,11 @@ def test_attention_tc_backward(case):
     n0c = n0 if isinstance(n0, int) else n0.cpu()
     gc = A.attn_bwd(*_cpu(do, q), Lq, *_cpu(k0, v0), L0, n0c, *_cpu(o, lse, k1, v1), L1,
                     n1.cpu() if n1 is not None else None)
-    for name, a, m, c in zip(["dq", "dk0", "dv0", "dk1", "dv1"], g, gm, gc):
+    for name, a, m, c, a1 in zip(["dq", "dk0", "dv0", "dk1", "dv1"], g, gm, gc, g1):
         if a is None:
             continue
         _close(a, c, what=name + " vs fp32")
         _close(a, m, what=name + " vs mma")
+        _close(a, a1, rtol=1e-2, atol=1e-2, what=name + " persistent vs one CTA per key tile")
     from nano_gpic_b200.ops import status
     assert status.read() == 0
