@@ -187,27 +187,26 @@ __global__ void __launch_bounds__(atc::THREADS, 1)
         break;
       }
       tc_fence_after();
+      // the whole S row of this thread: four TMEM reads in flight, one wait
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < BKV / 32; ++c) tmem_ld32(trow + st * BKV + c * 32, sr[c]);
+      tmem_wait_ld();
+      // valid keys of this tile form a prefix [0, nv)
+      const int nv = j < p.nt0 ? min(BKV, min(n0b, p.L0) - j * BKV) : min(BKV, min(n1b, p.L1) - (j - p.nt0) * BKV);
       float s[BKV];
-#pragma unroll
-      for (int c = 0; c < BKV / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(trow + st * BKV + c * 32, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int k = 0; k < 32; ++k) s[c * 32 + k] = __uint_as_float(r[k]);
-      }
       float mt = -INFINITY;
 #pragma unroll
       for (int c = 0; c < BKV; ++c) {
-        s[c] = atc_key_valid(j, c, p, n0b, n1b) ? s[c] * p.scale_log2 : -INFINITY;
+        s[c] = c < nv ? __uint_as_float(sr[c >> 5][c & 31]) * p.scale_log2 : -INFINITY;
         mt = fmaxf(mt, s[c]);
       }
       const float mn = fmaxf(m, mt);
-      const float corr = exp2f(m - mn);  // 0 on the first tile (m = -inf)
+      const float corr = ex2_ftz(m - mn);  // 0 on the first tile (m = -inf)
       float ps = 0.f;
 #pragma unroll
       for (int c = 0; c < BKV; ++c) {
-        s[c] = exp2f(s[c] - mn);
+        s[c] = ex2_ftz(s[c] - mn);
         ps += s[c];
       }
       l = l * corr + ps;
@@ -525,7 +524,7 @@ __global__ void __launch_bounds__(at2::THREADS)
             if (c * 32 + k < nv) mt = fmaxf(mt, __uint_as_float(r[k]));
         }
         const float mn = fmaxf(m, mt * p.scale_log2);
-        const float corr = exp2f(m - mn);
+        const float corr = ex2_ftz(m - mn);
         m = mn;
         if (it >= 1) {
           // O and the P buffer are free once the previous P V product completed; S(g) was issued after PV(g-1), so
@@ -561,8 +560,8 @@ __global__ void __launch_bounds__(at2::THREADS)
           uint32_t w[16];
 #pragma unroll
           for (int k = 0; k < 32; k += 2) {
-            const float e0 = c * 32 + k < nv ? exp2f(fmaf(__uint_as_float(r[k]), p.scale_log2, -mn)) : 0.f;
-            const float e1 = c * 32 + k + 1 < nv ? exp2f(fmaf(__uint_as_float(r[k + 1]), p.scale_log2, -mn)) : 0.f;
+            const float e0 = c * 32 + k < nv ? ex2_ftz(fmaf(__uint_as_float(r[k]), p.scale_log2, -mn)) : 0.f;
+            const float e1 = c * 32 + k + 1 < nv ? ex2_ftz(fmaf(__uint_as_float(r[k + 1]), p.scale_log2, -mn)) : 0.f;
             ps += e0 + e1;
             w[k / 2] = pack_bf16(e0, e1);
           }
@@ -1012,8 +1011,8 @@ constexpr int OFF_KV = 0;                          // [2 buffers][K, V]
 constexpr int OFF_QD = OFF_KV + 4 * T16;           // [2 stages][Q, dO]
 constexpr int OFF_P = OFF_QD + 4 * T16;            // P^T
 constexpr int OFF_DS = OFF_P + PT;                 // dS^T
-constexpr int OFF_LD = OFF_DS + PT;                // per compute warp: lse (log2 units) and delta of its 64 queries
-constexpr int OFF_BAR = OFF_LD + 8 * 2 * 64 * 4;
+constexpr int OFF_LD = OFF_DS + PT;                // [2 stages][128 queries] float2 (lse in log2 units, delta)
+constexpr int OFF_BAR = OFF_LD + 2 * BQ * 8;
 constexpr int SMEM = OFF_BAR + 256 + 1024;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 320, C_DQ = 384;
@@ -1024,8 +1023,7 @@ struct AttnTcBwd2Params {
   int Lq, L0, L1, H;
   int nt0, nt1, nq, items;
   float scale, scale_log2;
-  const float* lse;
-  const float* delta;
+  const float2* ld;  // [B, H, nq * 128] (lse * log2(e), delta); rows past Lq hold (+inf, 0)
   bf16 *dk0, *dv0, *dk1, *dv1;
   int64_t lddk0, lddv0, lddk1, lddv1;
   int* err;
@@ -1117,9 +1115,11 @@ __global__ void __launch_bounds__(ab2::THREADS)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&qd_full[st], 2 * T16);
+          mbar_arrive_expect_tx(&qd_full[st], 2 * T16 + BQ * 8);
           tma_load_3d(&tmQ, &qd_full[st], smem + OFF_QD + st * 2 * T16, w.h * D, i * BQ, w.b);
           tma_load_3d(&tmDO, &qd_full[st], smem + OFF_QD + st * 2 * T16 + T16, w.h * D, i * BQ, w.b);
+          bulk_load(smem + OFF_LD + st * BQ * 8, p.ld + ((int64_t)w.b * p.H + w.h) * p.nq * BQ + i * BQ, BQ * 8,
+                    &qd_full[st]);
         }
         ++li;
       }
@@ -1196,7 +1196,7 @@ __global__ void __launch_bounds__(ab2::THREADS)
     const int quarter = warp & 3, hh = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;  // key row (P/dS, dK/dV) or query row (dQ) of this thread
     const uint32_t trow = tmem + ((uint32_t)(quarter * 32) << 16);
-    float* wl = reinterpret_cast<float*>(smem + OFF_LD) + (warp - 2) * 128;  // [lse 64][delta 64]
+    const float2* lds = reinterpret_cast<const float2*>(smem + OFF_LD);   // [2 stages][128]
     uint8_t* slice = smem + OFF_P + hh * (PT / 2) + quarter * 4096;        // this warp's 4 KiB of P^T
     uint32_t li = 0, gq = 0;
     bool ok = true;
@@ -1218,16 +1218,8 @@ __global__ void __launch_bounds__(ab2::THREADS)
         continue;
       }
       const bool key_ok = s_row < w.nvalid && s_row < w.Lsrc;
-      const float* lse_bh = p.lse + ((int64_t)w.b * p.H + w.h) * p.Lq;
-      const float* del_bh = p.delta + ((int64_t)w.b * p.H + w.h) * p.Lq;
       for (int i = 0; i < p.nq; ++i, ++gq) {
-        __syncwarp();
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int qg = i * BQ + hh * 64 + k * 32 + lane;
-          wl[k * 32 + lane] = qg < p.Lq ? lse_bh[qg] * atc::kLog2e : INFINITY;
-          wl[64 + k * 32 + lane] = qg < p.Lq ? del_bh[qg] : 0.f;
-        }
+        const float2* ldq = lds + (gq & 1) * BQ + hh * 64;  // this warp's 64 queries: (lse log2, delta)
         if (lane == 0) bulk_wait_read0();  // the previous dQ tile staged in this slice has been read
         __syncwarp();
         if (!__all_sync(0xffffffffu, mbar_wait(st_full, gq & 1, abort_flag, p.err, kErrWaitAccFull))) {
@@ -1237,29 +1229,29 @@ __global__ void __launch_bounds__(ab2::THREADS)
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < 2; ++c) {
-          uint32_t rs[32], rd[32];
-          tmem_ld32(trow + C_S + hh * 64 + c * 32, rs);
-          tmem_ld32(trow + C_DP + hh * 64 + c * 32, rd);
+          // S^T and dP^T of 32 queries: both TMEM reads in flight, one wait (all four would exceed the registers)
+          uint32_t rs[1][32], rd[1][32];
+          tmem_ld32(trow + C_S + hh * 64 + c * 32, rs[0]);
+          tmem_ld32(trow + C_DP + hh * 64 + c * 32, rd[0]);
           tmem_wait_ld();
-          uint32_t wp[16], wd[16];
-#pragma unroll
-          for (int k = 0; k < 32; k += 2) {
-            const int qc = c * 32 + k;
-            const float p0 = key_ok ? exp2f(fmaf(__uint_as_float(rs[k]), p.scale_log2, -wl[qc])) : 0.f;
-            const float p1 = key_ok ? exp2f(fmaf(__uint_as_float(rs[k + 1]), p.scale_log2, -wl[qc + 1])) : 0.f;
-            wp[k / 2] = pack_bf16(p0, p1);
-            wd[k / 2] = pack_bf16(p0 * (__uint_as_float(rd[k]) - wl[64 + qc]),
-                                  p1 * (__uint_as_float(rd[k + 1]) - wl[64 + qc + 1]));
-          }
-          // 32 queries = chunks 4c .. 4c + 3 of the warp's 64-query atom
+          // 32 queries = 16-byte chunks 4c .. 4c + 3 of the warp's 64-query atom, 8 queries per chunk
 #pragma unroll
           for (int q4 = 0; q4 < 4; ++q4) {
+            uint32_t wp[4], wd[4];
+#pragma unroll
+            for (int k = 0; k < 8; k += 2) {
+              const int kk = q4 * 8 + k;
+              const float2 a0 = ldq[c * 32 + kk], a1 = ldq[c * 32 + kk + 1];
+              const float p0 = key_ok ? ex2_ftz(fmaf(__uint_as_float(rs[0][kk]), p.scale_log2, -a0.x)) : 0.f;
+              const float p1 = key_ok ? ex2_ftz(fmaf(__uint_as_float(rs[0][kk + 1]), p.scale_log2, -a1.x)) : 0.f;
+              wp[k / 2] = pack_bf16(p0, p1);
+              wd[k / 2] = pack_bf16(p0 * (__uint_as_float(rd[0][kk]) - a0.y),
+                                    p1 * (__uint_as_float(rd[0][kk + 1]) - a1.y));
+            }
             const int ch = c * 4 + q4;
             const uint32_t off = hh * (PT / 2) + r * 128 + ((ch ^ (r & 7)) << 4);
-            *reinterpret_cast<uint4*>(smem + OFF_P + off) = make_uint4(wp[4 * q4], wp[4 * q4 + 1], wp[4 * q4 + 2],
-                                                                       wp[4 * q4 + 3]);
-            *reinterpret_cast<uint4*>(smem + OFF_DS + off) = make_uint4(wd[4 * q4], wd[4 * q4 + 1], wd[4 * q4 + 2],
-                                                                        wd[4 * q4 + 3]);
+            *reinterpret_cast<uint4*>(smem + OFF_P + off) = make_uint4(wp[0], wp[1], wp[2], wp[3]);
+            *reinterpret_cast<uint4*>(smem + OFF_DS + off) = make_uint4(wd[0], wd[1], wd[2], wd[3]);
           }
         }
         fence_proxy_async_smem();
@@ -1350,6 +1342,34 @@ __global__ void dq_store_kernel(const float* __restrict__ acc, bf16* __restrict_
 void attn_delta(const bf16* dout, int64_t lddo, const bf16* o, int64_t ldo, float* delta, int rows, int Lq, int H,
                 cudaStream_t s);
 
+// ld[b, h, q] = (lse * log2(e), sum_d dO * O) for q < Lq; (+inf, 0) for Lq <= q < Lqp (padding rows then give P = 0)
+__global__ void attn_ld_kernel(const bf16* __restrict__ dout, int64_t lddo, const bf16* __restrict__ o, int64_t ldo,
+                               const float* __restrict__ lse, float2* __restrict__ ld, int B, int H, int Lq, int Lqp) {
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= (int64_t)B * H * Lqp) return;
+  const int q = (int)(t % Lqp);
+  const int64_t bh = t / Lqp;
+  const int b = (int)(bh / H), h = (int)(bh - (int64_t)b * H);
+  if (q >= Lq) {
+    ld[t] = make_float2(INFINITY, 0.f);
+    return;
+  }
+  const int64_t row = (int64_t)b * Lq + q;
+  const uint4* a = reinterpret_cast<const uint4*>(dout + row * lddo + h * 64);
+  const uint4* c = reinterpret_cast<const uint4*>(o + row * ldo + h * 64);
+  float acc = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const uint4 x = a[i], y = c[i];
+    const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      acc += __uint_as_float(xs[k] << 16) * __uint_as_float(ys[k] << 16) +
+             __uint_as_float(xs[k] & 0xffff0000u) * __uint_as_float(ys[k] & 0xffff0000u);
+  }
+  ld[t] = make_float2(lse[bh * Lq + q] * atc::kLog2e, acc);
+}
+
 // Same contract as attn_bwd (csrc/attention.cu): delta = rowsum(dO * O), then the tcgen05 kernel, whose dQ partials
 // (one per key tile) are summed by TMA reduce-adds into a zeroed fp32 buffer and stored as bf16 at the end.
 void attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0,
@@ -1392,10 +1412,22 @@ void attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& 
   }
   p.err = status_word();
   auto s = at::cuda::getCurrentCUDAStream();
-  at::Tensor delta = at::empty({B, (int64_t)p.H, Lq}, q.options().dtype(at::kFloat));
-  attn_delta(reinterpret_cast<const bf16*>(dout.data_ptr()), dout.stride(0), reinterpret_cast<const bf16*>(o.data_ptr()),
-             o.stride(0), delta.data_ptr<float>(), (int)q.size(0), (int)Lq, p.H, s);
-  p.delta = delta.data_ptr<float>();
+  at::Tensor delta, ldt;
+  if (version == 1) {
+    delta = at::empty({B, (int64_t)p.H, Lq}, q.options().dtype(at::kFloat));
+    attn_delta(reinterpret_cast<const bf16*>(dout.data_ptr()), dout.stride(0),
+               reinterpret_cast<const bf16*>(o.data_ptr()), o.stride(0), delta.data_ptr<float>(), (int)q.size(0),
+               (int)Lq, p.H, s);
+    p.delta = delta.data_ptr<float>();
+  } else {
+    const int64_t Lqp = (int64_t)p.nq * atb::BQ;
+    ldt = at::empty({B, (int64_t)p.H, Lqp, 2}, q.options().dtype(at::kFloat));
+    const int64_t n = B * p.H * Lqp;
+    attn_ld_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+        reinterpret_cast<const bf16*>(dout.data_ptr()), dout.stride(0), reinterpret_cast<const bf16*>(o.data_ptr()),
+        o.stride(0), lse.data_ptr<float>(), reinterpret_cast<float2*>(ldt.data_ptr()), (int)B, p.H, (int)Lq, (int)Lqp);
+    NG_LAUNCH_CHECK();
+  }
   at::Tensor acc = at::empty({q.size(0), C}, q.options().dtype(at::kFloat));
   cudaMemsetAsync(acc.data_ptr(), 0, acc.numel() * sizeof(float), s);
   CUtensorMap mq = make_tmap_bf16(q.data_ptr(), C, Lq, B, q.stride(0), q.stride(0) * Lq, 64, 128);
@@ -1426,8 +1458,7 @@ void attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& 
     p2.items = (int)B * p.H * (p.nt0 + p.nt1);
     p2.scale = p.scale;
     p2.scale_log2 = p.scale_log2;
-    p2.lse = p.lse;
-    p2.delta = p.delta;
+    p2.ld = reinterpret_cast<const float2*>(ldt.data_ptr());
     p2.dk0 = p.dk0;
     p2.dv0 = p.dv0;
     p2.dk1 = p.dk1;

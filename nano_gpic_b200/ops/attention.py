@@ -40,11 +40,11 @@ def _keys_cpu(k0, v0, L0, n0, k1, v1, L1, n1, B, H):
     return torch.stack(ks), torch.stack(vs), torch.stack(masks)
 
 
-def attn_fwd(q, Lq, k0, v0, L0, n0, k1=None, v1=None, L1=0, n1=None, scale=0.125, impl="tc1"):
+def attn_fwd(q, Lq, k0, v0, L0, n0, k1=None, v1=None, L1=0, n1=None, scale=0.125, impl="tc"):
     """q [B*Lq, H*64]; k0/v0 [B*L0, H*64]; k1/v1 [B*L1, H*64] or None; n0/n1: int or int32 [B] valid-key counts.
     Returns (o [B*Lq, H*64] bf16, lse [B, H, Lq] fp32). On CUDA the forward runs on tcgen05/TMEM
-    (csrc/attn_tc.cu; impl="tc1", the default: one 128-query tile per CTA; impl="tc": a persistent kernel with two
-    query tiles per CTA ping-ponging on the tensor core); impl="mma" selects the warp-level mma.sync kernel
+    (csrc/attn_tc.cu; impl="tc", the default: a persistent kernel with two query tiles per CTA ping-ponging on the
+    tensor core; impl="tc1": one 128-query tile per CTA); impl="mma" selects the warp-level mma.sync kernel
     (csrc/attention.cu), kept as a test oracle."""
     rows, C = q.shape
     B, H = rows // Lq, C // HEAD

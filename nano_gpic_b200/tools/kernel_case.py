@@ -15,6 +15,7 @@ def main():
     ap.add_argument("--d", type=int, default=1024)
     ap.add_argument("--t", type=int, default=128, help="caption length (attention cases)")
     ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--impl", default=None, help="attention implementation (tc, tc1, mma)")
     a = ap.parse_args()
     from nano_gpic_b200.ops import attention as A, gemm as G, norm as NR, status
     torch.manual_seed(0)
@@ -40,11 +41,13 @@ def main():
         lens = torch.randint(1, T + 1, (B,), device="cuda", dtype=torch.int32)
         o, lse = A.attn_fwd(qkv[:, :d], L, qkv[:, d:2 * d], qkv[:, 2 * d:], L, L, kv[:, :d], kv[:, d:], T, lens)
         do = r(M, d)
+        kw = {"impl": a.impl} if a.impl else {}
         if a.case == "attn_fwd":
-            fn = lambda: A.attn_fwd(qkv[:, :d], L, qkv[:, d:2 * d], qkv[:, 2 * d:], L, L, kv[:, :d], kv[:, d:], T, lens)
+            fn = lambda: A.attn_fwd(qkv[:, :d], L, qkv[:, d:2 * d], qkv[:, 2 * d:], L, L, kv[:, :d], kv[:, d:], T, lens,
+                                    **kw)
         else:
             fn = lambda: A.attn_bwd(do, qkv[:, :d], L, qkv[:, d:2 * d], qkv[:, 2 * d:], L, L, o, lse, kv[:, :d],
-                                    kv[:, d:], T, lens)
+                                    kv[:, d:], T, lens, **kw)
     elif a.case == "rms_bwd":
         x, dh = r(M, d), r(M, d)
         w = torch.ones(d, device="cuda")
