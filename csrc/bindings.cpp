@@ -46,6 +46,7 @@ void unpatchify(const at::Tensor& tok, const at::Tensor& img, int64_t p);
 void attn_fwd_tc(const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0, const c10::optional<at::Tensor>& k1,
                  const c10::optional<at::Tensor>& v1, const at::Tensor& n0, const at::Tensor& n1, const at::Tensor& o,
                  const at::Tensor& lse, int64_t Lq, int64_t L0, int64_t L1, double scale, int64_t version);
+void gemm_set_pair(int64_t on);
 void attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0,
                  const c10::optional<at::Tensor>& k1, const c10::optional<at::Tensor>& v1, const at::Tensor& n0,
                  const at::Tensor& n1, const at::Tensor& o, const at::Tensor& lse, const at::Tensor& dq,
@@ -66,6 +67,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_norm_bwd", &ng::qk_norm_bwd);
   m.def("attn_fwd", &ng::attn_fwd);
   m.def("attn_bwd", &ng::attn_bwd);
+  m.def("gemm_set_pair", &ng::gemm_set_pair, "use CTA-pair (cta_group::2) GEMM tiles when M >= 256 (default on)");
   m.def("attn_fwd_tc", &ng::attn_fwd_tc, "masked attention forward on tcgen05/TMEM (version 2: persistent, two query "
         "tiles per CTA; version 1: one query tile per CTA)", py::arg("q"), py::arg("k0"), py::arg("v0"), py::arg("k1"),
         py::arg("v1"), py::arg("n0"), py::arg("n1"), py::arg("o"), py::arg("lse"), py::arg("Lq"), py::arg("L0"),

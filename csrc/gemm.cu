@@ -38,10 +38,13 @@ constexpr int TMEM_COLS = 512;
 // Per-epilogue shared-memory plan. Epilogues that read inputs or write several outputs per tile (SwiGLU forward and
 // backward, the gated residual) trade one mainloop stage (48 KiB) for a deeper epilogue pipeline: a ring of IN_RING
 // prefetched input tiles and two output slots, so neither input latency nor store drain sits on the critical path.
-template <int EPI>
+// PAIR: the CTA-pair kernel (cta_group::2, 256 x 256 tiles per pair): a stage holds this CTA's 128 rows of A and 128
+// columns of B (32 KiB), so the ring is deeper.
+template <int EPI, bool PAIR = false>
 struct EpiCfg {
   static constexpr bool HEAVY = EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_BWD || EPI == EPI_GATED;
-  static constexpr int STAGES = HEAVY ? 3 : 4;
+  static constexpr int STAGE_BYTES = PAIR ? gemm_cfg::A_BYTES + gemm_cfg::B_BYTES / 2 : gemm_cfg::STAGE_BYTES;
+  static constexpr int STAGES = PAIR ? (HEAVY ? 5 : 6) : (HEAVY ? 3 : 4);
   // one output slot holds every 32x32 output tile of a chunk (bf16 2 KiB, fp32 4 KiB)
   static constexpr int OUT_SLOT = EPI == EPI_SWIGLU ? 6144
                                   : (EPI == EPI_F32 || EPI == EPI_GATED || EPI == EPI_SWIGLU_BWD) ? 4096
@@ -51,7 +54,7 @@ struct EpiCfg {
   static constexpr int IN_RING = IN_SLOT == 0 ? 0 : (EPI == EPI_GATED ? 2 : 1);
   static constexpr int WARP_BYTES = (OUT_SLOTS * OUT_SLOT + IN_RING * IN_SLOT + 1023) / 1024 * 1024;
   static constexpr int EPI_BYTES = 8 * WARP_BYTES;
-  static constexpr int SMEM = STAGES * gemm_cfg::STAGE_BYTES + EPI_BYTES + 1024 /*align slack*/ + 512 /*barriers*/;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align slack*/ + 512 /*barriers*/;
   static_assert(SMEM <= 232448, "shared memory budget of one sm_100 CTA");
 };
 
@@ -191,18 +194,25 @@ __device__ __forceinline__ void st_tile_f32(uint8_t* buf, int r, const float (&v
     *reinterpret_cast<float4*>(buf + sw128(r, j)) = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
 }
 
-template <int AMN, int BMN, int EPI>
+// PAIR = true: launched as 2-CTA clusters; CTA r of a pair computes rows [256 mb + 128 r, +128) of a 256 x 256 tile.
+// Its TMA warp loads its 128 rows of A and its 128 columns of B (counted on CTA 0's `full` barrier), CTA 0's MMA
+// thread issues M = 256 tcgen05.mma.cta_group::2 over both CTAs' shared memory into both CTAs' TMEM and releases the
+// stages / signals the accumulators in both CTAs; each CTA's epilogue drains its own rows and frees the accumulator
+// on CTA 0's barrier. Per CTA and k-block 32 KiB are loaded instead of 48 KiB.
+template <int AMN, int BMN, int EPI, bool PAIR>
 __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmOut2,
                         const __grid_constant__ CUtensorMap tmRes, const __grid_constant__ CUtensorMap tmAux,
                         const EpiParams p) {
   using namespace gemm_cfg;
-  using Cfg = EpiCfg<EPI>;
+  using Cfg = EpiCfg<EPI, PAIR>;
   constexpr int STAGES = Cfg::STAGES;
+  constexpr int SB = Cfg::STAGE_BYTES;
+  constexpr int BMP = PAIR ? 2 * BM : BM;  // rows of one tile (of the pair)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + Cfg::EPI_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * SB + Cfg::EPI_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -212,8 +222,11 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t crank = PAIR ? cluster_ctarank() : 0;
+  const int tile0 = PAIR ? blockIdx.x >> 1 : blockIdx.x;  // this CTA's (pair's) first tile; stride = #clusters
+  const int tstep = PAIR ? gridDim.x >> 1 : gridDim.x;
   // SwiGLU tiles cover 128 output columns of each half: the MMA's N extent is still 256
-  const int num_m = (p.M + BM - 1) / BM;
+  const int num_m = (p.M + BMP - 1) / BMP;
   const int num_n = (EPI == EPI_SWIGLU) ? (p.half_n + 127) / 128 : (p.N + BN - 1) / BN;
   const int num_k = (p.K + BK - 1) / BK;
   const int splits = p.k_splits > 1 ? p.k_splits : 1;
@@ -227,12 +240,15 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 8);
+      mbar_init(&acc_empty[a], PAIR ? 16 : 8);  // the epilogue warps of both CTAs free CTA 0's accumulators
     }
     mbar_init(drain, 1);
     for (int e = 0; e < 16; ++e) mbar_init(&in_bar[e], 1);
     *abort_flag = 0;
-    fence_barrier_init();
+    if (PAIR)
+      fence_mbarrier_init_cluster();
+    else
+      fence_barrier_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_map(&tmA);
@@ -245,11 +261,17 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
     if (EPI == EPI_SWIGLU_BWD) tma_prefetch_map(&tmAux);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // the peer's barriers are initialised before anything signals them
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -259,37 +281,58 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;  // stages filled since the start (for draining on abort)
-      for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+      for (int t = tile0; t < total && !*abort_flag; t += tstep) {
         int bs, mb, nb;
         tile_coords(t, num_m, num_n, bs, mb, nb);
         const int b = bs / splits, sp = bs - b * splits;
         const int kb0 = sp * kps, kb1 = min(num_k, kb0 + kps);
+        const int arow = mb * BMP + (int)crank * BM;  // this CTA's first row of A
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
-          uint8_t* sA = smem + stage * STAGE_BYTES;
+          uint8_t* sA = smem + stage * SB;
           uint8_t* sB = sA + A_BYTES;
-          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
           const int k0 = kb * BK;
-          if (AMN == 0) {
-            tma_load_3d(&tmA, &full[stage], sA, k0, mb * BM, b);
-          } else {
-            tma_load_3d(&tmA, &full[stage], sA, mb * BM, k0, b);
-            tma_load_3d(&tmA, &full[stage], sA + 8192, mb * BM + 64, k0, b);
-          }
-          if (BMN == 0) {
-            int r0, r1;
-            if (EPI == EPI_SWIGLU) {
-              r0 = nb * 128;
-              r1 = p.half_n + nb * 128;
+          if (PAIR) {
+            // both CTAs' bytes are counted on CTA 0's full barrier; only CTA 0 announces them
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            if (crank == 0) mbar_arrive_expect_tx(&full[stage], 2 * SB);
+            if (AMN == 0) {
+              tma_load_3d_pair(&tmA, fb, sA, k0, arow, b);
             } else {
-              r0 = nb * BN;
-              r1 = nb * BN + 128;
+              tma_load_3d_pair(&tmA, fb, sA, arow, k0, b);
+              tma_load_3d_pair(&tmA, fb, sA + 8192, arow + 64, k0, b);
             }
-            tma_load_3d(&tmB, &full[stage], sB, k0, r0, b);
-            tma_load_3d(&tmB, &full[stage], sB + 16384, k0, r1, b);
+            if (BMN == 0) {
+              const int r0 = EPI == EPI_SWIGLU ? (crank == 0 ? nb * 128 : p.half_n + nb * 128)
+                                               : nb * BN + (int)crank * 128;
+              tma_load_3d_pair(&tmB, fb, sB, k0, r0, b);
+            } else {
+              tma_load_3d_pair(&tmB, fb, sB, nb * BN + (int)crank * 128, k0, b);
+              tma_load_3d_pair(&tmB, fb, sB + 8192, nb * BN + (int)crank * 128 + 64, k0, b);
+            }
           } else {
+            mbar_arrive_expect_tx(&full[stage], SB);
+            if (AMN == 0) {
+              tma_load_3d(&tmA, &full[stage], sA, k0, arow, b);
+            } else {
+              tma_load_3d(&tmA, &full[stage], sA, arow, k0, b);
+              tma_load_3d(&tmA, &full[stage], sA + 8192, arow + 64, k0, b);
+            }
+            if (BMN == 0) {
+              int r0, r1;
+              if (EPI == EPI_SWIGLU) {
+                r0 = nb * 128;
+                r1 = p.half_n + nb * 128;
+              } else {
+                r0 = nb * BN;
+                r1 = nb * BN + 128;
+              }
+              tma_load_3d(&tmB, &full[stage], sB, k0, r0, b);
+              tma_load_3d(&tmB, &full[stage], sB + 16384, k0, r1, b);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) tma_load_3d(&tmB, &full[stage], sB + j * 8192, nb * BN + 64 * j, k0, b);
+              for (int j = 0; j < 4; ++j) tma_load_3d(&tmB, &full[stage], sB + j * 8192, nb * BN + 64 * j, k0, b);
+            }
           }
           ++issued;
           if (++stage == STAGES) {
@@ -298,8 +341,9 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
           }
         }
       }
-      if (*abort_flag) {
-        // unwinding: let the copies already issued land before the CTA's shared memory goes away
+      if (*abort_flag && (!PAIR || crank == 0)) {
+        // unwinding: let the copies already issued land before the CTA's shared memory goes away (for a pair, CTA 0's
+        // full barriers count both CTAs' copies)
         const uint64_t t0 = globaltimer_ns();
         int s = stage;
         uint32_t ph = phase;
@@ -319,13 +363,22 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN, AMN, BMN);
+    if (lane == 0 && crank == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BMP, BN, AMN, BMN);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool issued_any = false;
-      for (int t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x, ++it) {
+      // release / signal a barrier of this CTA and, for a pair, the same barrier of the peer
+      auto commit_both = [&](uint64_t* bar) {
+        if (PAIR) {
+          umma_commit_pair(smem_u32(bar));
+          umma_commit_pair(mapa_shared(smem_u32(bar), 1));
+        } else {
+          umma_commit(bar);
+        }
+      };
+      for (int t = tile0; t < total && !*abort_flag; t += tstep, ++it) {
         const int a = it & 1;
         const uint32_t aph = (it >> 1) & 1;
         if (!mbar_wait(&acc_empty[a], aph ^ 1, abort_flag, p.err, kErrWaitAccEmpty)) break;
@@ -340,7 +393,7 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sa = smem_u32(smem + stage * SB);
           const uint32_t sb = sa + A_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
@@ -348,21 +401,27 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
                                          : smem_desc_sw128(sa + k * 2048, 8192, 1024);
             const uint64_t db = BMN == 0 ? smem_desc_sw128(sb + k * 32, 16, 1024)
                                          : smem_desc_sw128(sb + k * 2048, 8192, 1024);
-            umma_f16(d_tmem, da, db, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+            if (PAIR)
+              umma_f16_pair(d_tmem, da, db, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+            else
+              umma_f16(d_tmem, da, db, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
           }
           issued_any = true;
-          umma_commit(&empty[stage]);
+          commit_both(&empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
         if (!ok) break;
-        umma_commit(&acc_full[a]);
+        commit_both(&acc_full[a]);
       }
       if (*abort_flag && issued_any) {
         // unwinding: wait for the MMAs in flight before TMEM is released
-        umma_commit(drain);
+        if (PAIR)
+          umma_commit_pair(smem_u32(drain));
+        else
+          umma_commit(drain);
         const uint64_t t0 = globaltimer_ns();
         while (!mbar_try_wait(drain, 0)) {
           if (globaltimer_ns() - t0 > NG_WAIT_BUDGET_NS) {
@@ -384,19 +443,19 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
     constexpr int NCW = NCH / 2;  // chunks per warp per tile
     constexpr int R = Cfg::IN_RING;
     const int q = warp & 3, e = warp - 2, h = e >> 2;
-    uint8_t* wbase = smem + STAGES * STAGE_BYTES + e * Cfg::WARP_BYTES;
+    uint8_t* wbase = smem + STAGES * SB + e * Cfg::WARP_BYTES;
     uint8_t* ibase = wbase + Cfg::OUT_SLOTS * Cfg::OUT_SLOT;
     uint64_t* ibar = &in_bar[e * 2];
     const bool has_in = R > 0 && (EPI != EPI_AXPBY || p.beta != 0.f);
-    const int my_tiles = blockIdx.x < total ? (total - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const int my_tiles = tile0 < total ? (total - 1 - tile0) / tstep + 1 : 0;
     const int n_chunks = my_tiles * NCW;  // this warp's chunk sequence, in processing order
     // issue the input loads of chunk L (linear index over this warp's chunks) into ring slot L % R
     auto issue_in = [&](int L) {
       if (!has_in || L >= n_chunks) return;
       const int i = L / NCW, c = h + 2 * (L - (L / NCW) * NCW);
       int bs, mb, nb;
-      tile_coords(blockIdx.x + i * gridDim.x, num_m, num_n, bs, mb, nb);
-      const int row0 = mb * BM + q * 32;
+      tile_coords(tile0 + i * tstep, num_m, num_n, bs, mb, nb);
+      const int row0 = mb * BMP + (int)crank * BM + q * 32;
       const int col = (EPI == EPI_SWIGLU ? nb * 128 : nb * BN) + c * 32;
       uint64_t* bar = &ibar[L % R];
       uint8_t* dst = ibase + (L % R) * Cfg::IN_SLOT;
@@ -413,16 +472,15 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
       for (int L = 0; L < R; ++L) issue_in(L);
     int it = 0, L = 0, oslot = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++it) {
+    for (int t = tile0; t < total && ok; t += tstep, ++it) {
       const int a = it & 1;
       const uint32_t aph = (it >> 1) & 1;
-      const bool got = mbar_wait(&acc_full[a], aph, abort_flag, p.err, kErrWaitAccFull);
-      __syncwarp();
+      const bool got = __all_sync(0xffffffffu, mbar_wait(&acc_full[a], aph, abort_flag, p.err, kErrWaitAccFull));
       if (!got) break;
       tc_fence_after();
       int bs, mb, nb;
       tile_coords(t, num_m, num_n, bs, mb, nb);
-      const int row0 = mb * BM + q * 32;
+      const int row0 = mb * BMP + (int)crank * BM + q * 32;
       const int row = row0 + lane;
       const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + a * BN;
 #pragma unroll 1
@@ -548,7 +606,12 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[a]);
+      if (lane == 0) {
+        if (PAIR)
+          mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[a]), 0));
+        else
+          mbar_arrive(&acc_empty[a]);
+      }
     }
     // every store has finished before the CTA (and its shared memory) goes away; on an abort, the input loads still
     // in flight land first (bounded wait)
@@ -569,9 +632,13 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (PAIR) cluster_sync();  // the peer no longer reads this CTA's shared memory or signals its barriers
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if (PAIR)
+      tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -684,31 +751,80 @@ struct EpiMaps {
   CUtensorMap out, out2, res, aux;
 };
 
-template <int AMN, int BMN, int EPI>
-static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps& em, const EpiParams& p, int grid,
-                     cudaStream_t s) {
-  auto kern = gemm_tcgen05_kernel<AMN, BMN, EPI>;
+// CTA pairs (cta_group::2) for GEMMs with at least two 128-row blocks; NG_GEMM_PAIR=0 or gemm_set_pair(0) turns them
+// off (A/B timing, tests of both paths).
+static int g_pair_mode = -1;
+void gemm_set_pair(int64_t on) { g_pair_mode = on ? 1 : 0; }
+bool gemm_use_pair(int64_t M) {
+  if (g_pair_mode < 0) {
+    const char* e = getenv("NG_GEMM_PAIR");
+    g_pair_mode = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return g_pair_mode == 1 && M >= 256;
+}
+
+template <int AMN, int BMN, int EPI, bool PAIR>
+static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps& em, const EpiParams& p,
+                     int64_t tiles, cudaStream_t s) {
+  auto kern = gemm_tcgen05_kernel<AMN, BMN, EPI, PAIR>;
+  constexpr int smem = EpiCfg<EPI, PAIR>::SMEM;
   static bool attr_set = false;
+  static int max_clusters = 0;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.blockDim = dim3(gemm_cfg::THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  if (PAIR) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
   if (!attr_set) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, EpiCfg<EPI>::SMEM);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (PAIR) {
+      cfg.gridDim = dim3(2 * (num_sms() / 2));
+      cudaOccupancyMaxActiveClusters(&max_clusters, kern, &cfg);
+      if (max_clusters <= 0) max_clusters = num_sms() / 2;
+    }
     attr_set = true;
   }
-  kern<<<grid, gemm_cfg::THREADS, EpiCfg<EPI>::SMEM, s>>>(ta, tb, em.out, em.out2, em.res, em.aux, p);
+  // persistent: one CTA (pair) per SM (pair) that can be resident at once
+  const int64_t units = PAIR ? std::min<int64_t>(tiles, max_clusters) : std::min<int64_t>(tiles, num_sms());
+  cfg.gridDim = dim3((unsigned)(PAIR ? 2 * units : units));
+  TORCH_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, em.out, em.out2, em.res, em.aux, p) == cudaSuccess,
+              "gemm launch failed");
   NG_LAUNCH_CHECK();
 }
 
-template <int AMN, int BMN>
+template <int AMN, int BMN, bool PAIR>
 static void dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps& em, const EpiParams& p,
-                         int grid, cudaStream_t s) {
+                         int64_t tiles, cudaStream_t s) {
   switch (epi) {
-    case EPI_BF16: return launch_t<AMN, BMN, EPI_BF16>(ta, tb, em, p, grid, s);
-    case EPI_F32: return launch_t<AMN, BMN, EPI_F32>(ta, tb, em, p, grid, s);
-    case EPI_AXPBY: return launch_t<AMN, BMN, EPI_AXPBY>(ta, tb, em, p, grid, s);
-    case EPI_GATED: return launch_t<AMN, BMN, EPI_GATED>(ta, tb, em, p, grid, s);
-    case EPI_SWIGLU: return launch_t<AMN, BMN, EPI_SWIGLU>(ta, tb, em, p, grid, s);
-    case EPI_SWIGLU_BWD: return launch_t<AMN, BMN, EPI_SWIGLU_BWD>(ta, tb, em, p, grid, s);
+    case EPI_BF16: return launch_t<AMN, BMN, EPI_BF16, PAIR>(ta, tb, em, p, tiles, s);
+    case EPI_F32: return launch_t<AMN, BMN, EPI_F32, PAIR>(ta, tb, em, p, tiles, s);
+    case EPI_AXPBY: return launch_t<AMN, BMN, EPI_AXPBY, PAIR>(ta, tb, em, p, tiles, s);
+    case EPI_GATED: return launch_t<AMN, BMN, EPI_GATED, PAIR>(ta, tb, em, p, tiles, s);
+    case EPI_SWIGLU: return launch_t<AMN, BMN, EPI_SWIGLU, PAIR>(ta, tb, em, p, tiles, s);
+    case EPI_SWIGLU_BWD: return launch_t<AMN, BMN, EPI_SWIGLU_BWD, PAIR>(ta, tb, em, p, tiles, s);
     default: TORCH_CHECK(false, "unknown GEMM epilogue ", epi);
   }
+}
+
+template <bool PAIR>
+static void dispatch_major(int a_mn, int b_mn, int epi, const CUtensorMap& ta, const CUtensorMap& tb,
+                           const EpiMaps& em, const EpiParams& p, int64_t tiles, cudaStream_t s) {
+  if (!a_mn && !b_mn)
+    dispatch_epi<0, 0, PAIR>(epi, ta, tb, em, p, tiles, s);
+  else if (!a_mn && b_mn)
+    dispatch_epi<0, 1, PAIR>(epi, ta, tb, em, p, tiles, s);
+  else if (a_mn && b_mn)
+    dispatch_epi<1, 1, PAIR>(epi, ta, tb, em, p, tiles, s);
+  else
+    dispatch_epi<1, 0, PAIR>(epi, ta, tb, em, p, tiles, s);
 }
 
 void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
@@ -749,10 +865,10 @@ void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   p.k_splits = g.k_splits > 1 ? g.k_splits : 1;
   p.kb_per_split = g.kb_per_split;
   p.err = g.err;
-  const int num_m = (g.M + BM - 1) / BM;
+  const bool pair = gemm_use_pair(g.M);
+  const int num_m = (g.M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM);
   const int num_n = g.epi == EPI_SWIGLU ? (g.half_n + 127) / 128 : (g.N + BN - 1) / BN;
   const int64_t tiles = (int64_t)g.batch * (g.k_splits > 1 ? g.k_splits : 1) * num_m * num_n;
-  const int grid = (int)std::min<int64_t>(tiles, num_sms());
   // epilogue maps: the output(s) and the input tiles the epilogue reads
   const int zb = g.k_splits > 1 ? g.k_splits : g.batch;
   EpiMaps em;
@@ -768,15 +884,11 @@ void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   if (g.epi == EPI_GATED || (g.epi == EPI_AXPBY && g.beta != 0.f && g.res != nullptr))
     em.res = epi_map_bf16(g.res, g.N, g.M, g.batch, g.ldr, g.res_bs);
   if (g.epi == EPI_SWIGLU_BWD) em.aux = epi_map_bf16(g.aux, 2 * (int64_t)g.half_n, g.M, 1, g.ld_aux, 0);
-  NG_TRACE("[gemm]   maps ok, grid=%d tiles=%lld\n", grid, (long long)tiles);
-  if (!g.a_mn && !g.b_mn)
-    dispatch_epi<0, 0>(g.epi, ta, tb, em, p, grid, stream);
-  else if (!g.a_mn && g.b_mn)
-    dispatch_epi<0, 1>(g.epi, ta, tb, em, p, grid, stream);
-  else if (g.a_mn && g.b_mn)
-    dispatch_epi<1, 1>(g.epi, ta, tb, em, p, grid, stream);
+  NG_TRACE("[gemm]   maps ok, pair=%d tiles=%lld\n", (int)pair, (long long)tiles);
+  if (pair)
+    dispatch_major<true>(g.a_mn, g.b_mn, g.epi, ta, tb, em, p, tiles, stream);
   else
-    dispatch_epi<1, 0>(g.epi, ta, tb, em, p, grid, stream);
+    dispatch_major<false>(g.a_mn, g.b_mn, g.epi, ta, tb, em, p, tiles, stream);
   NG_TRACE("[gemm]   launched\n");
 }
 
@@ -869,7 +981,9 @@ void gemm_torch(const at::Tensor& A, bool a_mn, int64_t lda, int64_t a_bs, const
   auto stream = at::cuda::getCurrentCUDAStream();
   // Weight gradients with few output tiles (e.g. a 1024 x 1024 dW is 32 tiles for 148 SMs) but a long reduction
   // (all tokens): split K over CTAs, each split writes an fp32 slice, then one ordered reduction adds the slices.
-  const int64_t tiles = (int64_t)((M + 127) / 128) * ((N + 255) / 256);
+  // (counted in CTAs: a CTA pair's 256-row tile occupies two)
+  const int64_t tiles = gemm_use_pair(M) ? 2 * ((M + 255) / 256) * ((N + 255) / 256)
+                                         : ((M + 127) / 128) * ((N + 255) / 256);
   const int64_t nkb = (K + 63) / 64;
   if (epi == EPI_F32 && batch == 1 && tiles * 2 <= num_sms() && nkb >= 16 && ldo == N) {
     int splits = (int)std::min<int64_t>(num_sms() / tiles, nkb / 8);

@@ -46,12 +46,17 @@ def bench_gemm(d, batch, rows):
         w = (torch.randn(n, k, device="cuda") * 0.02).bfloat16()
         dy = torch.randn(m, n, device="cuda").bfloat16()
         fl = 2.0 * m * n * k
+        from nano_gpic_b200._ext import ext
         res = {}
-        res["fwd_ours"] = time_fn(lambda: gemm.linear(x, w))
+        for pair in (1, 0):  # CTA-pair (cta_group::2) tiles, then single-CTA tiles
+            ext().gemm_set_pair(pair)
+            sfx = "ours" if pair else "ours1cta"
+            res["fwd_" + sfx] = time_fn(lambda: gemm.linear(x, w))
+            res["dgrad_" + sfx] = time_fn(lambda: gemm.linear_dgrad(dy, w))
+            res["wgrad_" + sfx] = time_fn(lambda: gemm.linear_wgrad(dy, x))
+        ext().gemm_set_pair(1)
         res["fwd_cublas"] = time_fn(lambda: x @ w.t())
-        res["dgrad_ours"] = time_fn(lambda: gemm.linear_dgrad(dy, w))
         res["dgrad_cublas"] = time_fn(lambda: dy @ w)
-        res["wgrad_ours"] = time_fn(lambda: gemm.linear_wgrad(dy, x))
         res["wgrad_cublas"] = time_fn(lambda: dy.t() @ x)
         row = {"kernel": "gemm", "name": name, "M": m, "N": n, "K": k}
         for kk, v in res.items():

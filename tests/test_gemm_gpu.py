@@ -89,3 +89,26 @@ def test_bmm_axpby(b_mn):
     out = gemm.bmm_axpby(A, B, b_mn, alpha=0.5, beta=-1.5, C=C)
     Bm = B.float() if b_mn else B.float().transpose(1, 2)
     _close(out, 0.5 * (A.float() @ Bm) - 1.5 * C.float())
+
+
+@pytest.mark.parametrize("pair", [True, False])
+def test_pair_and_single_cta_agree(pair):
+    """The CTA-pair (cta_group::2) tiles and the single-CTA tiles give the same results on every operand layout."""
+    from nano_gpic_b200 import _ext
+    from nano_gpic_b200.ops import gemm as G, status
+    torch.manual_seed(5)
+    x, w, dy = _r(600, 512), _r(768, 512, scale=0.05), _r(600, 768)
+    try:
+        _ext.ext().gemm_set_pair(1 if pair else 0)
+        y = G.linear(x, w)
+        dx = G.linear_dgrad(dy, w)
+        dw = G.linear_wgrad(dy, x)
+    finally:
+        _ext.ext().gemm_set_pair(1)
+    ref_y = (x.float() @ w.float().t())
+    ref_dx = (dy.float() @ w.float())
+    ref_dw = (dy.float().t() @ x.float())
+    for a, b, name in ((y, ref_y, "fwd"), (dx, ref_dx, "dgrad"), (dw, ref_dw, "wgrad")):
+        err = (a.float() - b).abs().max().item()
+        assert err <= 2e-2 * b.abs().max().item() + 1e-2, (name, pair, err)
+    assert status.read() == 0
