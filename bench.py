@@ -131,6 +131,7 @@ def run_ours(a, rank, world, dev):
     from nano_gpic_b200.ops import status
     from nano_gpic_b200.train.trainer import Trainer
     tr = Trainer.for_ladder(a.size, device=dev, world=world, rank=rank, micro_batch=a.micro_batch, dp=a.dp,
+                            transport=a.transport,
                             global_batch=a.global_batch)
     B = a.global_batch // world
     dev_batch = synthetic_batch(B, a.caption_len, 2048, seed=1000 + rank, device=dev)
@@ -267,6 +268,8 @@ def main():
     ap.add_argument("--global-batch", type=int, default=1024)
     ap.add_argument("--caption-len", type=int, default=128)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--transport", default="nccl", choices=["nccl", "p2p"],
+                    help="zero mode: NCCL collectives or this framework's peer-memory kernels")
     ap.add_argument("--dp", default="zero", choices=["ddp", "zero"],
                     help="data-parallel mode of our arm: all-reduce (the reference's DDP sizes) or reduce-scatter to "
                          "owners with sharded optimizer state (its FSDP2 sizes)")
@@ -312,7 +315,9 @@ def main():
                "config": {"model": f"JiT-T2I {a.size} (width {s.width}, {s.image_layers} image + {s.text_layers} text "
                                    f"layers, {s.heads} heads x 64)", "global_batch": a.global_batch,
                           "seq_len": 256 + T, "image_tokens": 256, "caption_tokens": T,
-                          "micro_batch": a.micro_batch or s.micro_batch, "parallelism": f"dp{world}" + ("-zero" if getattr(a, "dp", "ddp") == "zero" and a.impl == "ours" else ""),
+                          "micro_batch": a.micro_batch or s.micro_batch, "parallelism": f"dp{world}" + (("-zero" + ("-p2p" if a.transport == "p2p" and world > 1 else ""))
+                                                        if getattr(a, "dp", "ddp") == "zero" and a.impl == "ours"
+                                                        else ""),
                           "optimizer": "Muon (split, NS5 bf16) + AdamW, clip 1.0, WarmupFlatCooldown",
                           "l2": "inputs larger than L2 (1.3 GB of step inputs per rank, activations >> 126 MB)"},
                "clocks": clocks,

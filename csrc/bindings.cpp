@@ -47,6 +47,18 @@ void attn_fwd_tc(const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0
                  const c10::optional<at::Tensor>& v1, const at::Tensor& n0, const at::Tensor& n1, const at::Tensor& o,
                  const at::Tensor& lse, int64_t Lq, int64_t L0, int64_t L1, double scale, int64_t version);
 void gemm_set_pair(int64_t on);
+at::Tensor p2p_alloc(int64_t nbytes, int64_t device);
+at::Tensor p2p_export(const at::Tensor& t);
+int64_t p2p_import(const at::Tensor& handle, int64_t device);
+void p2p_close(int64_t ptr);
+void p2p_reduce_scatter(const at::Tensor& grad, const at::Tensor& recv, const std::vector<int64_t>& peer_recv,
+                        const at::Tensor& flags, const std::vector<int64_t>& peer_flags, const at::Tensor& acks,
+                        const std::vector<int64_t>& peer_acks, const at::Tensor& counters, const at::Tensor& sumsq,
+                        int64_t rank, int64_t nb, int64_t b, int64_t start, int64_t seg, int64_t epoch);
+void p2p_bcast_bf16(const at::Tensor& master, const std::vector<int64_t>& peer_w16, const std::vector<int64_t>& peer_flags,
+                    const at::Tensor& counters, int64_t rank, int64_t nb, int64_t b, int64_t off, int64_t n,
+                    int64_t epoch);
+void p2p_wait(const at::Tensor& flags, int64_t world, int64_t rank, int64_t nb, int64_t b0, int64_t b1, int64_t epoch);
 void attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0,
                  const c10::optional<at::Tensor>& k1, const c10::optional<at::Tensor>& v1, const at::Tensor& n0,
                  const at::Tensor& n1, const at::Tensor& o, const at::Tensor& lse, const at::Tensor& dq,
@@ -67,6 +79,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_norm_bwd", &ng::qk_norm_bwd);
   m.def("attn_fwd", &ng::attn_fwd);
   m.def("attn_bwd", &ng::attn_bwd);
+  m.def("p2p_alloc", &ng::p2p_alloc, "cudaMalloc'd, zero-filled, IPC-shareable bytes");
+  m.def("p2p_export", &ng::p2p_export, "CUDA IPC handle of a p2p_alloc tensor");
+  m.def("p2p_import", &ng::p2p_import, "open a peer's CUDA IPC handle; returns its device address here");
+  m.def("p2p_close", &ng::p2p_close);
+  m.def("p2p_reduce_scatter", &ng::p2p_reduce_scatter, "peer-memory reduce-scatter of one gradient bucket");
+  m.def("p2p_bcast_bf16", &ng::p2p_bcast_bf16, "owner's fp32 segment -> bf16 in every rank's weights, with flags");
+  m.def("p2p_wait", &ng::p2p_wait, "wait (bounded) for every peer's weight flags of a bucket range");
   m.def("gemm_set_pair", &ng::gemm_set_pair, "use CTA-pair (cta_group::2) GEMM tiles when M >= 256 (default on)");
   m.def("attn_fwd_tc", &ng::attn_fwd_tc, "masked attention forward on tcgen05/TMEM (version 2: persistent, two query "
         "tiles per CTA; version 1: one query tile per CTA)", py::arg("q"), py::arg("k0"), py::arg("v0"), py::arg("k1"),

@@ -44,14 +44,16 @@ template <int EPI, bool PAIR = false>
 struct EpiCfg {
   static constexpr bool HEAVY = EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_BWD || EPI == EPI_GATED;
   static constexpr int STAGE_BYTES = PAIR ? gemm_cfg::A_BYTES + gemm_cfg::B_BYTES / 2 : gemm_cfg::STAGE_BYTES;
-  static constexpr int STAGES = PAIR ? (HEAVY ? 5 : 6) : (HEAVY ? 3 : 4);
+  // SwiGLU backward reads two input tiles per chunk: with pairs it keeps two chunks of inputs in flight (one stage
+  // fewer in the mainloop ring)
+  static constexpr int STAGES = PAIR ? (EPI == EPI_SWIGLU_BWD ? 4 : (HEAVY ? 5 : 6)) : (HEAVY ? 3 : 4);
   // one output slot holds every 32x32 output tile of a chunk (bf16 2 KiB, fp32 4 KiB)
   static constexpr int OUT_SLOT = EPI == EPI_SWIGLU ? 6144
                                   : (EPI == EPI_F32 || EPI == EPI_GATED || EPI == EPI_SWIGLU_BWD) ? 4096
                                                                                                   : 2048;
   static constexpr int OUT_SLOTS = (EPI == EPI_BF16) ? 2 : 1;
   static constexpr int IN_SLOT = EPI == EPI_SWIGLU_BWD ? 4096 : (EPI == EPI_GATED || EPI == EPI_AXPBY) ? 2048 : 0;
-  static constexpr int IN_RING = IN_SLOT == 0 ? 0 : (EPI == EPI_GATED ? 2 : 1);
+  static constexpr int IN_RING = IN_SLOT == 0 ? 0 : ((EPI == EPI_GATED || (PAIR && EPI == EPI_SWIGLU_BWD)) ? 2 : 1);
   static constexpr int WARP_BYTES = (OUT_SLOTS * OUT_SLOT + IN_RING * IN_SLOT + 1023) / 1024 * 1024;
   static constexpr int EPI_BYTES = 8 * WARP_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align slack*/ + 512 /*barriers*/;

@@ -198,6 +198,143 @@ __global__ void __launch_bounds__(256) rms_mod_bwd_kernel(const bf16* __restrict
   }
 }
 
+// Bandwidth-shaped variant for C = 256 * VPL (the ladder widths 768 .. 1792). Phase 1: a warp per row, lane l owning
+// columns 8 (l + 32 k), k < VPL: dh, x, dres are read once, the row's mean(dxn * xn) reduced in the warp and dx written
+// at once. Phase 2: the column sums for d_shift, d_scale, d_w over the chunk's rows (dh and x again, now from L2), all
+// 256 threads busy: G2 groups of C / 8 threads take alternate rows and are added up in shared memory.
+template <bool MOD, int VPL>
+__global__ void __launch_bounds__(256) rms_mod_bwd_kernel2(const bf16* __restrict__ dh, const bf16* __restrict__ x,
+                                                           const float* __restrict__ rstd, const float* __restrict__ w,
+                                                           const bf16* __restrict__ scale, int64_t ld_sc,
+                                                           const bf16* __restrict__ dres, bf16* __restrict__ dx,
+                                                           float* __restrict__ part, int M, int rpg) {
+  constexpr int C = 256 * VPL, NV = C / 8;
+  constexpr int G2 = 256 / NV;  // row groups in phase 2
+  __shared__ float red[G2 > 1 ? (G2 - 1) * 3 * C : 1];
+  const int g = blockIdx.y, chunk = blockIdx.x;
+  const int r0 = g * rpg + chunk * BWD_ROWS;
+  const int r1 = min(min(g * rpg + rpg, r0 + BWD_ROWS), M);
+  const int nrows = r1 - r0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bf16* sc_row = MOD ? scale + (int64_t)g * ld_sc : nullptr;
+  // ---- phase 1
+  for (int rr = warp; rr < nrows; rr += 8) {
+    const int64_t row = r0 + rr;
+    const float r = rstd[row];
+    uint4 dv[VPL], xv[VPL], rv[VPL];
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int v = lane + 32 * k;
+      dv[k] = reinterpret_cast<const uint4*>(dh + row * C)[v];
+      xv[k] = reinterpret_cast<const uint4*>(x + row * C)[v];
+      rv[k] = dres != nullptr ? reinterpret_cast<const uint4*>(dres + row * C)[v] : make_uint4(0, 0, 0, 0);
+    }
+    float acc = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int c0 = 8 * (lane + 32 * k);
+      float d[8], xf[8], wf[8], sc[8];
+      unpack8(dv[k], d);
+      unpack8(xv[k], xf);
+      load_w8(w, c0, wf);
+      if (MOD) {
+        unpack8(__ldg(reinterpret_cast<const uint4*>(sc_row + c0)), sc);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sc[j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc += d[j] * (1.f + sc[j]) * wf[j] * xf[j] * r;
+    }
+    const float cm = warp_sum(acc) / (float)C;
+#pragma unroll
+    for (int k = 0; k < VPL; ++k) {
+      const int c0 = 8 * (lane + 32 * k);
+      float d[8], xf[8], wf[8], sc[8], rs[8], o[8];
+      unpack8(dv[k], d);
+      unpack8(xv[k], xf);
+      unpack8(rv[k], rs);
+      load_w8(w, c0, wf);
+      if (MOD) {
+        unpack8(__ldg(reinterpret_cast<const uint4*>(sc_row + c0)), sc);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) sc[j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float xn = xf[j] * r;
+        o[j] = r * (d[j] * (1.f + sc[j]) * wf[j] - xn * cm) + rs[j];
+      }
+      reinterpret_cast<uint4*>(dx + row * C)[lane + 32 * k] = pack8(o);
+    }
+  }
+  // ---- phase 2
+  const int v = threadIdx.x % NV, grp = threadIdx.x / NV;
+  const bool active = grp < G2;
+  const int c0 = v * 8;
+  float wf[8], sc[8];
+  float psh[8], psc[8], pw[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) psh[j] = psc[j] = pw[j] = 0.f;
+  if (active) {
+    load_w8(w, c0, wf);
+    if (MOD) {
+      unpack8(__ldg(reinterpret_cast<const uint4*>(sc_row + c0)), sc);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sc[j] = 0.f;
+    }
+#pragma unroll 2
+    for (int rr = grp; rr < nrows; rr += G2) {
+      const int64_t row = r0 + rr;
+      const float r = rstd[row];
+      float d[8], xf[8];
+      unpack8(*reinterpret_cast<const uint4*>(dh + row * C + c0), d);
+      unpack8(*reinterpret_cast<const uint4*>(x + row * C + c0), xf);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float xn = xf[j] * r;
+        psh[j] += d[j];
+        psc[j] += d[j] * wf[j] * xn;
+        pw[j] += d[j] * (1.f + sc[j]) * xn;
+      }
+    }
+  }
+  if (G2 > 1) {
+    if (active && grp > 0) {
+      float* dst = red + (grp - 1) * 3 * C;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        dst[c0 + j] = psh[j];
+        dst[C + c0 + j] = psc[j];
+        dst[2 * C + c0 + j] = pw[j];
+      }
+    }
+    __syncthreads();
+    if (grp != 0) return;
+    for (int q = 0; q < G2 - 1; ++q) {
+      const float* src = red + q * 3 * C;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        psh[j] += src[c0 + j];
+        psc[j] += src[C + c0 + j];
+        pw[j] += src[2 * C + c0 + j];
+      }
+    }
+  } else if (!active) {
+    return;
+  }
+  const int cid = g * gridDim.x + chunk;
+  float* pp = part + (int64_t)cid * 3 * C;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    pp[c0 + j] = psh[j];
+    pp[C + c0 + j] = psc[j];
+    pp[2 * C + c0 + j] = pw[j];
+  }
+}
+
 // d_shift/d_scale [G, C] (strided fp32 views, may be null) from the chunk partials of each group; d_w [C] += all.
 __global__ void rms_mod_bwd_reduce(const float* __restrict__ part, int G, int chunks, int C, float* dshift,
                                    int64_t ld_dsh, float* dscale, int64_t ld_dsc, float* dw) {
@@ -366,7 +503,31 @@ void rms_mod_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& rs
   auto s = at::cuda::getCurrentCUDAStream();
   at::Tensor part = at::empty({(int64_t)G * chunks * 3 * C}, x.options().dtype(at::kFloat));
   dim3 grid(chunks, G);
-  if (mod)
+  const bf16* scp = mod ? bptr(scale) : nullptr;
+  const int64_t ldsc = mod ? ld_of(scale) : 0;
+  bool done = true;
+#define NG_RMS_BWD2(V)                                                                                               \
+  if (mod)                                                                                                           \
+    rms_mod_bwd_kernel2<true, V><<<grid, 256, 0, s>>>(                                                              \
+        reinterpret_cast<const bf16*>(dh.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),                   \
+        rstd.data_ptr<float>(), w.data_ptr<float>(), scp, ldsc, bptr(dres), reinterpret_cast<bf16*>(dx.data_ptr()), \
+        part.data_ptr<float>(), M, rows_per_group);                                                                  \
+  else                                                                                                               \
+    rms_mod_bwd_kernel2<false, V><<<grid, 256, 0, s>>>(                                                             \
+        reinterpret_cast<const bf16*>(dh.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),                   \
+        rstd.data_ptr<float>(), w.data_ptr<float>(), nullptr, 0, bptr(dres), reinterpret_cast<bf16*>(dx.data_ptr()), \
+        part.data_ptr<float>(), M, rows_per_group);
+  switch (C) {
+    case 768: NG_RMS_BWD2(3) break;
+    case 1024: NG_RMS_BWD2(4) break;
+    case 1280: NG_RMS_BWD2(5) break;
+    case 1536: NG_RMS_BWD2(6) break;
+    case 1792: NG_RMS_BWD2(7) break;
+    default: done = false;
+  }
+#undef NG_RMS_BWD2
+  if (done) {
+  } else if (mod)
     rms_mod_bwd_kernel<true><<<grid, 256, 0, s>>>(
         reinterpret_cast<const bf16*>(dh.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),
         rstd.data_ptr<float>(), w.data_ptr<float>(), bptr(scale), ld_of(scale), bptr(dres),

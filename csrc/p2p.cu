@@ -1,0 +1,282 @@
+// Peer-to-peer collectives over NVLink / NVSwitch for the sharded (zero) data-parallel mode: buffers allocated with
+// cudaMalloc and shared between the ranks of one node by CUDA IPC, and kernels that move data with plain stores into
+// peer memory and synchronise with epoch flags (bounded waits; no NCCL on these paths).
+//
+// Reduce-scatter of one gradient bucket (the bucket is [W owner segments of `seg` fp32]):
+//   push kernel    rank r writes its segment for owner o into o's receive buffer slot r (for every o != r), after o
+//                  has acknowledged the previous epoch's data in that slot; the last CTA then raises flag[r][b] = epoch
+//                  in every owner's flag array (release, system scope).
+//   reduce kernel  the owner waits for flag[r][b] >= epoch from every r, sums its own segment and the W - 1 received
+//                  segments in rank order (deterministic), writes the sum in place and a per-CTA sum of squares (the
+//                  global-norm clip), and the last CTA acknowledges the epoch to every sender.
+// The push kernel never waits for anything the same step produces, so the reduce kernel's waits always resolve,
+// whatever the number of resident CTAs. Weight broadcast: every owner writes its bf16 segment of a bucket into every
+// peer's compute-weight buffer and raises a flag; the consumer waits for all flags before the next forward.
+// Reference: the NCCL reduce-scatter / all-gather of the reference's FSDP2 path (baselines/PixelGen/src/utils/
+// fsdp_setup.py:116-148); this is the same data movement as plain NVLink stores.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "status.h"
+
+namespace ng {
+
+#ifndef NG_PEER_WAIT_NS
+#define NG_PEER_WAIT_NS 60000000000ull  // a peer may legitimately be far behind (first steps, stragglers): 60 s
+#endif
+
+struct PeerTable {
+  int64_t p[8];  // device addresses of the same buffer on ranks 0..W-1 (this rank's own address at [rank])
+};
+
+__device__ __forceinline__ long long ld_acquire_sys(const long long* p) {
+  long long v;
+  asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(long long* p, long long v) {
+  asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// waits (bounded) until *flag >= epoch; returns false and raises an error on timeout
+__device__ bool wait_flag(const long long* flag, long long epoch, int* err) {
+  if (ld_acquire_sys(flag) >= epoch) return true;
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t n = 0;
+  while (ld_acquire_sys(flag) < epoch) {
+    if ((++n & 1023u) == 0 && globaltimer_ns() - t0 > NG_PEER_WAIT_NS) {
+      raise_error(err, kErrPeerFlag);
+      return false;
+    }
+  }
+  return true;
+}
+
+// flags / acks arrays are [W][nb] int64 on every rank: entry [r][b] on rank o = the last epoch of bucket b that rank
+// r pushed to o (flags) / that owner r consumed from o (acks).
+__global__ void __launch_bounds__(256) p2p_push_kernel(const float* __restrict__ grad, PeerTable recv, PeerTable flags,
+                                                       long long* __restrict__ acks, unsigned int* counter, int W,
+                                                       int rank, int nb, int b, int64_t start, int64_t seg,
+                                                       long long epoch, int* err) {
+  // 1) every owner consumed the previous epoch of this bucket (its slot for us may be overwritten)
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    for (int o = 0; o < W; ++o)
+      if (o != rank && !wait_flag(acks + (int64_t)o * nb + b, epoch - 1, err)) ok = 0;
+  }
+  __syncthreads();
+  if (ok) {
+    // 2) our segment for owner o -> o's receive slot `rank`, as float4 stores into peer memory
+    const int64_t n4 = seg / 4;
+    const int64_t total = (int64_t)(W - 1) * n4;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+      int o = (int)(i / n4);
+      const int64_t j = i - (int64_t)o * n4;
+      if (o >= rank) ++o;
+      const float4* src = reinterpret_cast<const float4*>(grad + start + (int64_t)o * seg) + j;
+      float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(recv.p[o]) + start + (int64_t)rank * seg) + j;
+      *dst = *src;
+    }
+  }
+  // 3) the last CTA raises our flag for this bucket at every owner (after everyone's stores are visible)
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int done = atomicAdd(counter, 1u);
+    if (done == gridDim.x - 1) {
+      *counter = 0;
+      __threadfence_system();
+      for (int o = 0; o < W; ++o)
+        if (o != rank) st_release_sys(reinterpret_cast<long long*>(flags.p[o]) + (int64_t)rank * nb + b, epoch);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) p2p_reduce_kernel(float* __restrict__ grad, const float* __restrict__ recv,
+                                                         const long long* __restrict__ flags, PeerTable acks,
+                                                         unsigned int* counter, float* __restrict__ sumsq, int W,
+                                                         int rank, int nb, int b, int64_t start, int64_t seg,
+                                                         long long epoch, int* err) {
+  __shared__ int ok;
+  __shared__ float red[8];
+  if (threadIdx.x == 0) {
+    ok = 1;
+    for (int r = 0; r < W; ++r)
+      if (r != rank && !wait_flag(flags + (int64_t)r * nb + b, epoch, err)) ok = 0;
+  }
+  __syncthreads();
+  float sq = 0.f;
+  if (ok) {
+    const int64_t n4 = seg / 4;
+    float4* mine = reinterpret_cast<float4*>(grad + start + (int64_t)rank * seg);
+    for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n4; j += (int64_t)gridDim.x * blockDim.x) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int r = 0; r < W; ++r) {  // rank order: the same sum on every run
+        const float4 v = r == rank ? mine[j] : reinterpret_cast<const float4*>(recv + start + (int64_t)r * seg)[j];
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+      mine[j] = acc;
+      sq += acc.x * acc.x + acc.y * acc.y + acc.z * acc.z + acc.w * acc.w;
+    }
+  }
+  // per-CTA partial of the sum of squares (summed in CTA order by the host side: deterministic)
+  sq = warp_sum(sq);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sq;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+    sumsq[blockIdx.x] = t;
+  }
+  // the last CTA acknowledges the epoch to every sender (their slots here may be reused)
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int done = atomicAdd(counter, 1u);
+    if (done == gridDim.x - 1) {
+      *counter = 0;
+      __threadfence_system();
+      for (int r = 0; r < W; ++r)
+        if (r != rank) st_release_sys(reinterpret_cast<long long*>(acks.p[r]) + (int64_t)rank * nb + b, epoch);
+    }
+  }
+}
+
+// Weight broadcast of one bucket: fp32 master segment of this owner -> bf16 at the same offsets in every rank's
+// compute-weight buffer (its own included); then flag[rank][b] = epoch at every peer.
+__global__ void __launch_bounds__(256) p2p_bcast_bf16_kernel(const float* __restrict__ master, PeerTable w16,
+                                                             PeerTable flags, unsigned int* counter, int W, int rank,
+                                                             int nb, int b, int64_t off, int64_t n, long long epoch) {
+  const int64_t n8 = n / 8;
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n8; j += (int64_t)gridDim.x * blockDim.x) {
+    const float4 a = reinterpret_cast<const float4*>(master + off)[2 * j];
+    const float4 c = reinterpret_cast<const float4*>(master + off)[2 * j + 1];
+    uint4 v;
+    v.x = pack_bf16(a.x, a.y);
+    v.y = pack_bf16(a.z, a.w);
+    v.z = pack_bf16(c.x, c.y);
+    v.w = pack_bf16(c.z, c.w);
+    for (int r = 0; r < W; ++r)
+      reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(w16.p[r]) + off)[j] = v;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int done = atomicAdd(counter, 1u);
+    if (done == gridDim.x - 1) {
+      *counter = 0;
+      __threadfence_system();
+      for (int r = 0; r < W; ++r)
+        if (r != rank) st_release_sys(reinterpret_cast<long long*>(flags.p[r]) + (int64_t)rank * nb + b, epoch);
+    }
+  }
+}
+
+// waits (one thread) until flags[r][b] >= epoch for every r != rank and every bucket b in [b0, b1)
+__global__ void p2p_wait_kernel(const long long* __restrict__ flags, int W, int rank, int nb, int b0, int b1,
+                                long long epoch, int* err) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  for (int b = b0; b < b1; ++b)
+    for (int r = 0; r < W; ++r)
+      if (r != rank && !wait_flag(flags + (int64_t)r * nb + b, epoch, err)) return;
+}
+
+// ------------------------------------------------------------------------------------------------------ host
+static void deleter(void* p) { cudaFree(p); }
+
+at::Tensor p2p_alloc(int64_t nbytes, int64_t device) {
+  const at::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  void* p = nullptr;
+  TORCH_CHECK(cudaMalloc(&p, (size_t)nbytes) == cudaSuccess, "p2p_alloc: cudaMalloc failed");
+  TORCH_CHECK(cudaMemset(p, 0, (size_t)nbytes) == cudaSuccess, "p2p_alloc: cudaMemset failed");
+  return torch::from_blob(p, {nbytes}, deleter, at::TensorOptions().dtype(at::kByte).device(at::kCUDA, device));
+}
+
+at::Tensor p2p_export(const at::Tensor& t) {
+  cudaIpcMemHandle_t h;
+  TORCH_CHECK(cudaIpcGetMemHandle(&h, t.data_ptr()) == cudaSuccess, "cudaIpcGetMemHandle failed");
+  at::Tensor out = at::empty({(int64_t)sizeof(h)}, at::TensorOptions().dtype(at::kByte));
+  memcpy(out.data_ptr(), &h, sizeof(h));
+  return out;
+}
+
+int64_t p2p_import(const at::Tensor& handle, int64_t device) {
+  const at::cuda::CUDAGuard guard((c10::DeviceIndex)device);
+  cudaIpcMemHandle_t h;
+  TORCH_CHECK(handle.numel() == (int64_t)sizeof(h), "p2p_import: bad handle");
+  memcpy(&h, handle.data_ptr(), sizeof(h));
+  void* p = nullptr;
+  TORCH_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess,
+              "cudaIpcOpenMemHandle failed (peer access between these GPUs?)");
+  return reinterpret_cast<int64_t>(p);
+}
+
+void p2p_close(int64_t ptr) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)); }
+
+static PeerTable table(const std::vector<int64_t>& v) {
+  TORCH_CHECK(v.size() <= 8, "at most 8 ranks");
+  PeerTable t{};
+  for (size_t i = 0; i < v.size(); ++i) t.p[i] = v[i];
+  return t;
+}
+
+static int grid_for(int64_t n_vec, int device) {
+  static int sms = 0;
+  if (sms == 0) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+  return (int)std::max<int64_t>(1, std::min<int64_t>((n_vec + 255) / 256, 2 * sms));
+}
+
+// push + reduce of bucket b (grad, recv: local fp32 flat buffers; flags/acks: local int64 [W][nb] arrays and the
+// peers' addresses of the same arrays); sumsq receives one partial per reduce CTA (its length bounds the grid).
+void p2p_reduce_scatter(const at::Tensor& grad, const at::Tensor& recv, const std::vector<int64_t>& peer_recv,
+                        const at::Tensor& flags, const std::vector<int64_t>& peer_flags, const at::Tensor& acks,
+                        const std::vector<int64_t>& peer_acks, const at::Tensor& counters, const at::Tensor& sumsq,
+                        int64_t rank, int64_t nb, int64_t b, int64_t start, int64_t seg, int64_t epoch) {
+  const int W = (int)peer_recv.size();
+  TORCH_CHECK(seg % 4 == 0 && start % 4 == 0, "p2p_reduce_scatter: 16-byte aligned segments expected");
+  const at::cuda::CUDAGuard guard(grad.device());
+  auto s = at::cuda::getCurrentCUDAStream();
+  unsigned int* ctr = reinterpret_cast<unsigned int*>(counters.data_ptr<int>());
+  const int dev = grad.get_device();
+  const int gp = grid_for((int64_t)(W - 1) * (seg / 4), dev);
+  p2p_push_kernel<<<gp, 256, 0, s>>>(grad.data_ptr<float>(), table(peer_recv), table(peer_flags),
+                                     reinterpret_cast<long long*>(acks.data_ptr<int64_t>()), ctr + 2 * b, W, (int)rank,
+                                     (int)nb, (int)b, start, seg, (long long)epoch, status_word());
+  NG_LAUNCH_CHECK();
+  const int gr = std::min<int>(grid_for(seg / 4, dev), (int)sumsq.numel());
+  p2p_reduce_kernel<<<gr, 256, 0, s>>>(grad.data_ptr<float>(), recv.data_ptr<float>(),
+                                       reinterpret_cast<const long long*>(flags.data_ptr<int64_t>()), table(peer_acks),
+                                       ctr + 2 * b + 1, sumsq.data_ptr<float>(), W, (int)rank, (int)nb, (int)b, start,
+                                       seg, (long long)epoch, status_word());
+  NG_LAUNCH_CHECK();
+}
+
+void p2p_bcast_bf16(const at::Tensor& master, const std::vector<int64_t>& peer_w16, const std::vector<int64_t>& peer_flags,
+                    const at::Tensor& counters, int64_t rank, int64_t nb, int64_t b, int64_t off, int64_t n,
+                    int64_t epoch) {
+  const int W = (int)peer_w16.size();
+  TORCH_CHECK(n % 8 == 0 && off % 8 == 0, "p2p_bcast_bf16: 16-byte aligned segments expected");
+  const at::cuda::CUDAGuard guard(master.device());
+  unsigned int* ctr = reinterpret_cast<unsigned int*>(counters.data_ptr<int>());
+  p2p_bcast_bf16_kernel<<<grid_for(n / 8, master.get_device()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      master.data_ptr<float>(), table(peer_w16), table(peer_flags), ctr, W, (int)rank, (int)nb, (int)b, off, n,
+      (long long)epoch);
+  NG_LAUNCH_CHECK();
+}
+
+void p2p_wait(const at::Tensor& flags, int64_t world, int64_t rank, int64_t nb, int64_t b0, int64_t b1,
+              int64_t epoch) {
+  const at::cuda::CUDAGuard guard(flags.device());
+  p2p_wait_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const long long*>(flags.data_ptr<int64_t>()), (int)world, (int)rank, (int)nb, (int)b0, (int)b1,
+      (long long)epoch, status_word());
+  NG_LAUNCH_CHECK();
+}
+
+}  // namespace ng

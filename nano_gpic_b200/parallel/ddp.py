@@ -20,6 +20,12 @@ finishes gradients, owners inside each bucket), gradient collectives overlapped 
         bf16 weights once (all-gather): less than DDP's all-reduce + Muon all-gather, and less than FSDP2 + two
         all-to-alls.
 
+Transport (zero mode): "nccl" (reduce_scatter_tensor / all_gather_into_tensor per bucket, the baseline) or "p2p"
+(P2PTransport below: this package's kernels over CUDA-IPC peer memory: each rank pushes its gradient segments into
+the owners' receive slots with NVLink stores and epoch flags, the owner sums them in rank order together with the
+sum of squares for the clip, and after the update each owner writes its bf16 weights straight into every rank's
+compute-weight buffer; csrc/p2p.cu).
+
 Overlap: the model calls `hook(n)` at the start of each block's backward on the LAST micro-batch, meaning the first n
 backward stages (final layer, image blocks from the last, text blocks from the last) hold final gradients; every
 bucket made only of finished stages is reduced at once on a side CUDA stream, under the rest of the backward.
@@ -169,10 +175,70 @@ def _all_gather_inplace(buf, seg, rank, world, group):
         dist.all_gather_into_tensor(buf, buf[rank * seg:(rank + 1) * seg], group=group)
 
 
+class P2PTransport:
+    """Peer buffers of one node for zero mode: the flat gradient (fp32), a receive buffer of the same size, the bf16
+    compute weights, and int64 [W][nb] flag / acknowledgement arrays, all cudaMalloc'd and opened by every rank through
+    CUDA IPC. Collective setup (every rank constructs it)."""
+
+    MAX_PARTIALS = 512  # sum-of-squares partials per bucket (bounds the reduce kernel's grid)
+
+    def __init__(self, numel, n_buckets, device, group=None):
+        from .._ext import ext
+        self.ext = ext()
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        assert self.world <= 8, "peer-memory transport: one node of at most 8 GPUs"
+        self.nb = n_buckets
+        dev = torch.device(device).index
+        W, nb = self.world, n_buckets
+        alloc = lambda nbytes: self.ext.p2p_alloc(int(nbytes), dev)
+        self.raw = {"grad": alloc(numel * 4), "recv": alloc(numel * 4), "w16": alloc(numel * 2),
+                    "flags": alloc(W * nb * 8), "acks": alloc(W * nb * 8), "wflags": alloc(W * nb * 8)}
+        self.grad = self.raw["grad"].view(torch.float32)
+        self.recv = self.raw["recv"].view(torch.float32)
+        self.w16 = self.raw["w16"].view(torch.bfloat16)
+        self.flags = self.raw["flags"].view(torch.int64)
+        self.acks = self.raw["acks"].view(torch.int64)
+        self.wflags = self.raw["wflags"].view(torch.int64)
+        self.counters = torch.zeros(2 * nb + 2, dtype=torch.int32, device=device)
+        self.bcast_counter = torch.zeros(2, dtype=torch.int32, device=device)
+        self.sumsq = torch.zeros(nb, self.MAX_PARTIALS, dtype=torch.float32, device=device)
+        mine = {k: self.ext.p2p_export(v).tolist() for k, v in self.raw.items()}
+        every = [None] * W
+        dist.all_gather_object(every, mine, group=group)
+        self.peer = {}
+        self._opened = []
+        for k, v in self.raw.items():
+            ptrs = []
+            for r in range(W):
+                if r == self.rank:
+                    ptrs.append(v.data_ptr())
+                else:
+                    p = self.ext.p2p_import(torch.tensor(every[r][k], dtype=torch.uint8), dev)
+                    self._opened.append(p)
+                    ptrs.append(p)
+            self.peer[k] = ptrs
+        dist.barrier(group=group)
+
+    def reduce_scatter(self, b, start, seg, epoch):
+        """Bucket b ([W segments of seg fp32] at start): this rank's segment becomes the sum over ranks."""
+        self.sumsq[b].zero_()
+        self.ext.p2p_reduce_scatter(self.grad, self.recv, self.peer["recv"], self.flags, self.peer["flags"], self.acks,
+                                    self.peer["acks"], self.counters, self.sumsq[b], self.rank, self.nb, b, start,
+                                    seg, epoch)
+
+    def broadcast_weights(self, master, b, off, n, epoch):
+        self.ext.p2p_bcast_bf16(master, self.peer["w16"], self.peer["wflags"], self.bcast_counter, self.rank, self.nb,
+                                b, off, n, epoch)
+
+    def wait_weights(self, b0, b1, epoch):
+        self.ext.p2p_wait(self.wflags, self.world, self.rank, self.nb, b0, b1, epoch)
+
+
 class DataParallel:
     """The gradient / weight synchronisation of one data-parallel group over a Layout's flat buffers."""
 
-    def __init__(self, model, layout, flat, group=None, overlap=True):
+    def __init__(self, model, layout, flat, group=None, overlap=True, p2p=None):
         self.model, self.layout, self.flat, self.group = model, layout, flat, group
         self.mode = layout.mode
         self.world = dist.get_world_size(group)
@@ -183,6 +249,8 @@ class DataParallel:
         self.comm = torch.cuda.Stream(device=flat.grad.device) if self.cuda else None
         self._launched = set()
         self.early = 0  # buckets launched under the backward in the last step (overlap statistics)
+        self.p2p = p2p  # P2PTransport (zero mode over peer memory) or None (NCCL)
+        self.epoch = 0  # optimizer steps synchronised so far (the peer flags' epochs)
         # zero mode: the parameters this rank updates (its own and the replicated ones)
         self.owned = None if self.mode == "ddp" else {id(p) for p in layout.params
                                                       if layout.owner[id(p)] in (self.rank, None)}
@@ -191,6 +259,7 @@ class DataParallel:
     def arm(self):
         """Before the backward of the last micro-batch: reduce buckets as their stages finish."""
         self._launched = set()
+        self.epoch += 1
         if self.overlap:
             self.model._bwd_hook = self._stages_done
 
@@ -213,6 +282,8 @@ class DataParallel:
     def _reduce(self, g, b):
         if self.mode == "ddp" or b.replicated:
             dist.all_reduce(g, op=dist.ReduceOp.SUM, group=self.group)
+        elif self.p2p is not None:
+            self.p2p.reduce_scatter(self.layout.buckets.index(b), b.start, b.seg, self.epoch)
         else:
             _reduce_scatter_inplace(g, b.seg, self.rank, self.group)
 
@@ -245,8 +316,11 @@ class DataParallel:
             return self.flat.grad.norm()
         g = self.flat.grad
         z = torch.zeros((), device=g.device)
-        sq = sum((s.pow(2).sum() for s in (g[b.start + self.rank * b.seg:b.start + (self.rank + 1) * b.seg]
-                                           for b in self._sharded())), z)
+        if self.p2p is not None:  # the reduce kernels left per-CTA partial sums of squares (fixed order: deterministic)
+            sq = self.p2p.sumsq.sum()
+        else:
+            sq = sum((s.pow(2).sum() for s in (g[b.start + self.rank * b.seg:b.start + (self.rank + 1) * b.seg]
+                                               for b in self._sharded())), z)
         dist.all_reduce(sq, op=dist.ReduceOp.SUM, group=self.group)
         sq = sq + sum((g[b.start:b.end].pow(2).sum() for b in self.layout.buckets if b.replicated), z)
         return sq.sqrt()
@@ -263,13 +337,19 @@ class DataParallel:
         if self.mode == "ddp":
             self.flat.sync_bf16()
             return
-        for b in self.layout.buckets:
+        for i, b in enumerate(self.layout.buckets):
             if b.replicated:
                 self.flat.data16[b.start:b.end].copy_(self.flat.data[b.start:b.end])
                 continue
             lo = b.start + self.rank * b.seg
+            if self.p2p is not None:  # owner -> bf16 into every rank's weights, then flags
+                self.p2p.broadcast_weights(self.flat.data, i, lo, b.seg, self.epoch)
+                continue
             self.flat.data16[lo:lo + b.seg].copy_(self.flat.data[lo:lo + b.seg])
             _all_gather_inplace(self.flat.data16[b.start:b.end], b.seg, self.rank, self.world, self.group)
+        if self.p2p is not None:  # the next forward reads every owner's weights: wait (on the compute stream) for the
+            # sharded buckets' flags (they come first; the replicated bucket was refreshed locally above)
+            self.p2p.wait_weights(0, len(self._sharded()), self.epoch)
 
     def own_ranges(self):
         """[start, end) ranges of the flat buffers this rank keeps current (None in ddp mode: all of them)."""
@@ -344,12 +424,20 @@ class DataParallel:
         self.flat.sync_bf16()
 
 
-def make_data_parallel(model, world, mode="ddp", bucket_mb=1000, device=None, group=None, overlap=True):
+def make_data_parallel(model, world, mode="ddp", bucket_mb=1000, device=None, group=None, overlap=True,
+                       transport="nccl"):
     """Layout + flat buffers + DataParallel for `model` (Muon tags must already be set). bucket_mb counts fp32
-    gradient bytes, as the reference's bucket_cap_mb."""
+    gradient bytes, as the reference's bucket_cap_mb. transport "p2p" (zero mode, CUDA, one node): this package's
+    peer-memory kernels instead of NCCL for the reduce-scatter and the weight all-gather."""
     layout = Layout(model, world, mode, bucket_numel=bucket_mb * 1024 * 1024 // 4)
-    flat = layout.flat(model, device=device)
-    dp = DataParallel(model, layout, flat, group=group, overlap=overlap) if world > 1 else None
+    p2p = None
+    if world > 1 and mode == "zero" and transport == "p2p":
+        p2p = P2PTransport(layout.numel, len(layout.buckets), device, group=group)
+        flat = FlatParams(model, device=device, params=layout.params, offsets=layout.offsets, numel=layout.numel,
+                          grad_buf=p2p.grad, data16_buf=p2p.w16)
+    else:
+        flat = layout.flat(model, device=device)
+    dp = DataParallel(model, layout, flat, group=group, overlap=overlap, p2p=p2p) if world > 1 else None
     return layout, flat, dp
 
 

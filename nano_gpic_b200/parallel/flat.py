@@ -22,7 +22,7 @@ class FlatParams:
     """params/offsets/numel: an explicit layout (e.g. the data-parallel planner's bucket and owner order, with padding);
     by default the module's trainable parameters back to back."""
 
-    def __init__(self, module, device=None, params=None, offsets=None, numel=None):
+    def __init__(self, module, device=None, params=None, offsets=None, numel=None, grad_buf=None, data16_buf=None):
         self.module = module
         self.params = list(params) if params is not None else [p for p in module.parameters() if p.requires_grad]
         names = {id(p): n for n, p in module.named_parameters()}
@@ -41,8 +41,10 @@ class FlatParams:
             assert all(o + p.numel() <= off for o, p in zip(self.offsets, self.params))
         self.numel = off
         self.data = torch.zeros(off, dtype=torch.float32, device=device)
-        self.grad = torch.zeros(off, dtype=torch.float32, device=device)
-        self.data16 = torch.zeros(off, dtype=torch.bfloat16, device=device)
+        # grad_buf / data16_buf: externally allocated storage (e.g. peer-shared memory), zero-filled, >= numel elements
+        self.grad = grad_buf[:off] if grad_buf is not None else torch.zeros(off, dtype=torch.float32, device=device)
+        self.data16 = (data16_buf[:off] if data16_buf is not None
+                       else torch.zeros(off, dtype=torch.bfloat16, device=device))
         for p, o in zip(self.params, self.offsets):
             n = p.numel()
             self.data[o:o + n].copy_(p.detach().reshape(-1).to(device=device, dtype=torch.float32))

@@ -47,9 +47,11 @@ class Trainer:
     # --------------------------------------------------------------------------------------------- construction
     @classmethod
     def for_ladder(cls, size="d12", device="cuda", world=1, rank=0, micro_batch=None, global_batch=GLOBAL_BATCH,
-                   max_steps=None, dp="ddp", seed=0, model_kwargs=None, bucket_mb=1000, overlap=True):
+                   max_steps=None, dp="ddp", seed=0, model_kwargs=None, bucket_mb=1000, overlap=True,
+                   transport="nccl"):
         """dp: "ddp" (all-reduce, as the reference's DDP sizes) or "zero" (reduce-scatter to owners, sharded
-        optimizer state; the role of the reference's FSDP2 sizes)."""
+        optimizer state; the role of the reference's FSDP2 sizes). transport (zero mode): "nccl" or "p2p" (this
+        package's peer-memory kernels)."""
         s = SIZES[size]
         torch.manual_seed(seed)
         kw = s.model_kwargs()
@@ -58,7 +60,7 @@ class Trainer:
         tag_muon_params(model)
         from ..parallel.ddp import make_data_parallel
         _, flat, reducer = make_data_parallel(model, world, mode="ddp" if dp == "nccl" else dp, bucket_mb=bucket_mb,
-                                              device=device, overlap=overlap)
+                                              device=device, overlap=overlap, transport=transport)
         mb = micro_batch or s.micro_batch
         per_rank = global_batch // world
         assert per_rank % mb == 0, (global_batch, world, mb)

@@ -17,7 +17,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, mode, out):
+def _worker(rank, world, port, mode, out, transport="nccl"):
     import datetime
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -28,7 +28,8 @@ def _worker(rank, world, port, mode, out):
     try:
         from nano_gpic_b200.train.trainer import Trainer
         tr = Trainer.for_ladder("d12", device=dev, world=world, rank=rank, micro_batch=8, global_batch=32, dp=mode,
-                                bucket_mb=40, model_kwargs={"num_blocks": 3, "num_text_blocks": 1})
+                                bucket_mb=40, model_kwargs={"num_blocks": 3, "num_text_blocks": 1},
+                                transport=transport)
         g = torch.Generator().manual_seed(11)
         for s in range(3):
             img = torch.randint(0, 256, (32, 256, 256, 3), dtype=torch.uint8, generator=g)
@@ -39,6 +40,8 @@ def _worker(rank, world, port, mode, out):
             sl = slice(rank * 16, (rank + 1) * 16)
             loss = tr.train_step(img[sl], cap[sl], mask[sl], t=t[sl], noise=noise[sl])
         torch.cuda.synchronize()
+        from nano_gpic_b200.ops import status
+        assert status.read() == 0
         tr.dp.gather_master()
         early = tr.dp.early
         if rank == 0:
@@ -62,3 +65,17 @@ def test_ddp_and_zero_agree(tmp_path):
         tol = 5e-2 if "adaLN_modulation.0.weight" in n else 1e-2
         err = float((p - b["params"][n]).norm() / (p.norm() + 1e-12))
         assert err < tol, (n, err)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_p2p_transport_matches_nccl(tmp_path):
+    """zero mode over this package's peer-memory kernels gives the NCCL transport's weights (with 2 ranks the
+    rank-ordered sum is the same as NCCL's, so bit for bit)."""
+    res = {}
+    for tr in ("nccl", "p2p"):
+        out = str(tmp_path / f"{tr}.pt")
+        mp.spawn(_worker, args=(2, _port(), "zero", out, tr), nprocs=2, join=True)
+        res[tr] = torch.load(out)
+    for n, p in res["nccl"]["params"].items():
+        assert torch.equal(p, res["p2p"]["params"][n]), n
+    assert res["p2p"]["early"] >= 1
