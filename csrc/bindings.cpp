@@ -59,6 +59,11 @@ void p2p_bcast_bf16(const at::Tensor& master, const std::vector<int64_t>& peer_w
                     const at::Tensor& counters, int64_t rank, int64_t nb, int64_t b, int64_t off, int64_t n,
                     int64_t epoch);
 void p2p_wait(const at::Tensor& flags, int64_t world, int64_t rank, int64_t nb, int64_t b0, int64_t b1, int64_t epoch);
+void p2p_fused_apply(const at::Tensor& table_t, int64_t nent, const at::Tensor& p, const at::Tensor& g,
+                     const at::Tensor& m1, const at::Tensor& m2, const at::Tensor& upd,
+                     const c10::optional<at::Tensor>& ema, const std::vector<int64_t>& peer_w16,
+                     const std::vector<int64_t>& peer_wflags, const at::Tensor& counters, std::vector<double> scalars,
+                     int64_t rank, int64_t nb, int64_t b, int64_t epoch);
 void attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0,
                  const c10::optional<at::Tensor>& k1, const c10::optional<at::Tensor>& v1, const at::Tensor& n0,
                  const at::Tensor& n1, const at::Tensor& o, const at::Tensor& lse, const at::Tensor& dq,
@@ -85,6 +90,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_close", &ng::p2p_close);
   m.def("p2p_reduce_scatter", &ng::p2p_reduce_scatter, "peer-memory reduce-scatter of one gradient bucket");
   m.def("p2p_bcast_bf16", &ng::p2p_bcast_bf16, "owner's fp32 segment -> bf16 in every rank's weights, with flags");
+  m.def("p2p_fused_apply", &ng::p2p_fused_apply,
+        "sharded AdamW / Muon apply + EMA of one bucket's owned parameters, bf16 weights into every rank, flags");
   m.def("p2p_wait", &ng::p2p_wait, "wait (bounded) for every peer's weight flags of a bucket range");
   m.def("gemm_set_pair", &ng::gemm_set_pair, "use CTA-pair (cta_group::2) GEMM tiles when M >= 256 (default on)");
   m.def("attn_fwd_tc", &ng::attn_fwd_tc, "masked attention forward on tcgen05/TMEM (version 2: persistent, two query "

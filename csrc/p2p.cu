@@ -187,6 +187,91 @@ __global__ void p2p_wait_kernel(const long long* __restrict__ flags, int W, int 
       if (r != rank && !wait_flag(flags + (int64_t)r * nb + b, epoch, err)) return;
 }
 
+// Fused optimizer apply of one bucket's owned parameters, then the bf16 weights to every rank (the sharded update
+// and the weight all-gather in one kernel). One CTA per table entry (a chunk of one parameter):
+//   kind 0 (AdamW, decoupled decay):  p *= 1 - lr wd;  m = b1 m + (1 - b1) g;  v = b2 v + (1 - b2) g^2;
+//                                     p -= (lr / bc1) m / (sqrt(v) / sqrt(bc2) + eps)
+//   kind 1 (Muon unit):               p = p (1 - lr_m wd_m) + coef_scale * O      (O: the Newton-Schulz output, bf16;
+//                                     coef_scale = -lr_m * coef of the entry)
+// then ema = lerp(ema, p, 1 - decay) when an EMA buffer is given, and bf16(p) into every rank's weights at the same
+// offset. Gradients arrive clipped. Reference optimizer: baselines/PixelGen/src/optim/muon.py:64-254 (MuonAdamW);
+// torch AdamW for the vectors.
+struct ApplyEntry {
+  int64_t off;
+  int32_t n;
+  int32_t kind;
+  float coef;
+  float pad;
+};
+
+struct ApplyScalars {
+  float lr_a, wd_a, b1, b2, eps, bc1, rsqrt_bc2;  // AdamW (bias corrections of this step)
+  float lr_m, wd_m;                             // Muon
+  float ema_keep;                               // EMA decay (used when ema != nullptr)
+};
+
+__global__ void __launch_bounds__(256) fused_apply_kernel(const ApplyEntry* __restrict__ tab, int nent, float* p,
+                                                          const float* __restrict__ g, float* m1, float* m2,
+                                                          const __nv_bfloat16* __restrict__ upd, float* ema,
+                                                          PeerTable w16, PeerTable wflags, unsigned int* counter,
+                                                          ApplyScalars sc, int W, int rank, int nb, int b,
+                                                          long long epoch) {
+  if ((int)blockIdx.x < nent) {
+    const ApplyEntry e = tab[blockIdx.x];
+    const float keep_a = 1.f - sc.lr_a * sc.wd_a, keep_m = 1.f - sc.lr_m * sc.wd_m;
+    const float step_a = sc.lr_a / sc.bc1, mscale = -sc.lr_m * e.coef;
+    for (int i0 = threadIdx.x * 8; i0 < e.n; i0 += blockDim.x * 8) {
+      const int cnt = min(8, e.n - i0);
+      const int64_t o = e.off + i0;
+      float pv[8], nv[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        if (k >= cnt) {
+          nv[k] = 0.f;
+          continue;
+        }
+        pv[k] = p[o + k];
+        float x;
+        if (e.kind == 0) {
+          const float gk = g[o + k];
+          const float m = sc.b1 * m1[o + k] + (1.f - sc.b1) * gk;
+          const float v = sc.b2 * m2[o + k] + (1.f - sc.b2) * gk * gk;
+          m1[o + k] = m;
+          m2[o + k] = v;
+          x = pv[k] * keep_a - step_a * m / (sqrtf(v) * sc.rsqrt_bc2 + sc.eps);
+        } else {
+          x = pv[k] * keep_m + mscale * __bfloat162float(upd[o + k]);
+        }
+        p[o + k] = x;
+        if (ema != nullptr) ema[o + k] = x + sc.ema_keep * (ema[o + k] - x);
+        nv[k] = x;
+      }
+      if (cnt == 8 && (o & 7) == 0) {
+        uint4 v;
+        v.x = pack_bf16(nv[0], nv[1]);
+        v.y = pack_bf16(nv[2], nv[3]);
+        v.z = pack_bf16(nv[4], nv[5]);
+        v.w = pack_bf16(nv[6], nv[7]);
+        for (int r = 0; r < W; ++r) *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(w16.p[r]) + o) = v;
+      } else {
+        for (int r = 0; r < W; ++r)
+          for (int k = 0; k < cnt; ++k) reinterpret_cast<__nv_bfloat16*>(w16.p[r])[o + k] = __float2bfloat16_rn(nv[k]);
+      }
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int done = atomicAdd(counter, 1u);
+    if (done == gridDim.x - 1) {
+      *counter = 0;
+      __threadfence_system();
+      for (int r = 0; r < W; ++r)
+        if (r != rank) st_release_sys(reinterpret_cast<long long*>(wflags.p[r]) + (int64_t)rank * nb + b, epoch);
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------------------ host
 static void deleter(void* p) { cudaFree(p); }
 
@@ -267,6 +352,37 @@ void p2p_bcast_bf16(const at::Tensor& master, const std::vector<int64_t>& peer_w
   p2p_bcast_bf16_kernel<<<grid_for(n / 8, master.get_device()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       master.data_ptr<float>(), table(peer_w16), table(peer_flags), ctr, W, (int)rank, (int)nb, (int)b, off, n,
       (long long)epoch);
+  NG_LAUNCH_CHECK();
+}
+
+// table: int64 tensor [nent, 3] on the device (ApplyEntry rows: off | n, kind | coef, pad as raw bits); scalars:
+// lr_a, wd_a, b1, b2, eps, bc1, rsqrt_bc2, lr_m, wd_m, ema_keep.
+void p2p_fused_apply(const at::Tensor& table_t, int64_t nent, const at::Tensor& p, const at::Tensor& g,
+                     const at::Tensor& m1, const at::Tensor& m2, const at::Tensor& upd,
+                     const c10::optional<at::Tensor>& ema, const std::vector<int64_t>& peer_w16,
+                     const std::vector<int64_t>& peer_wflags, const at::Tensor& counters, std::vector<double> scalars,
+                     int64_t rank, int64_t nb, int64_t b, int64_t epoch) {
+  static_assert(sizeof(ApplyEntry) == 24, "ApplyEntry layout");
+  TORCH_CHECK(scalars.size() == 10, "p2p_fused_apply: 10 scalars");
+  TORCH_CHECK(table_t.numel() * 8 >= nent * (int64_t)sizeof(ApplyEntry), "p2p_fused_apply: table too small");
+  const at::cuda::CUDAGuard guard(p.device());
+  ApplyScalars sc;
+  sc.lr_a = (float)scalars[0];
+  sc.wd_a = (float)scalars[1];
+  sc.b1 = (float)scalars[2];
+  sc.b2 = (float)scalars[3];
+  sc.eps = (float)scalars[4];
+  sc.bc1 = (float)scalars[5];
+  sc.rsqrt_bc2 = (float)scalars[6];
+  sc.lr_m = (float)scalars[7];
+  sc.wd_m = (float)scalars[8];
+  sc.ema_keep = (float)scalars[9];
+  float* ema_p = (ema.has_value() && ema->defined()) ? ema->data_ptr<float>() : nullptr;
+  fused_apply_kernel<<<(unsigned)std::max<int64_t>(1, nent), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const ApplyEntry*>(table_t.data_ptr()), (int)nent, p.data_ptr<float>(), g.data_ptr<float>(),
+      m1.data_ptr<float>(), m2.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(upd.data_ptr()), ema_p,
+      table(peer_w16), table(peer_wflags), reinterpret_cast<unsigned int*>(counters.data_ptr<int>()), sc,
+      (int)peer_w16.size(), (int)rank, (int)nb, (int)b, (long long)epoch);
   NG_LAUNCH_CHECK();
 }
 

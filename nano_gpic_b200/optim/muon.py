@@ -102,6 +102,12 @@ class MuonAdamW(torch.optim.Optimizer):
         # zero mode (nano_gpic_b200.parallel.ddp): ids of the parameters this rank owns; the step touches only those,
         # Muon orthogonalises all their units locally (their reduced gradients are whole on this rank)
         self.owned = None
+        # fused apply (zero mode over peer memory): for the parameters in `defer["ids"]` the step leaves the Muon
+        # output O in the flat bf16 buffer defer["upd"] and keeps AdamW state as views of defer["m1"] / defer["m2"];
+        # the data-parallel layer's kernel applies both (and the weight broadcast). `deferred` holds this step's
+        # scalars for it.
+        self.defer = None
+        self.deferred = None
 
     @staticmethod
     def update_coef(group, shape):
@@ -163,6 +169,15 @@ class MuonAdamW(torch.optim.Optimizer):
             ins = [grads[i][r0:r1].lerp(bufs[i][r0:r1], beta) if group["nesterov"] else bufs[i][r0:r1]
                    for i, r0, r1 in us]
             outs.append((shape, us, msign(torch.stack(ins), steps=group["ns_steps"], dtype=self.ns_dtype)))
+        if self.defer is not None:  # the fused kernel applies W <- W (1 - lr wd) - lr coef O
+            d = self.defer
+            for shape, us, O in outs:
+                for (i, r0, r1), o in zip(us, O):
+                    p = params[i]
+                    base = d["off"][id(p)] + r0 * p.shape[1]
+                    d["upd"][base:base + o.numel()].copy_(o.reshape(-1))
+            self.deferred = dict(self.deferred or {}, lr_m=lr, wd_m=wd or 0.0)
+            return
         if wd:
             torch._foreach_mul_(params, 1 - lr * wd)
         for shape, us, O in outs:
@@ -216,11 +231,39 @@ class MuonAdamW(torch.optim.Optimizer):
         return full
 
     @torch.no_grad()
+    def _adamw_deferred(self, group):
+        """AdamW state of the fused-apply parameters as views of the flat buffers; the step count and this step's
+        scalars for the kernel."""
+        d = self.defer
+        steps = []
+        for p in group["params"]:
+            if id(p) not in d["ids"]:
+                continue
+            st = self.state[p]
+            if "exp_avg" not in st:
+                o = d["off"][id(p)]
+                st["step"] = torch.zeros((), dtype=torch.float32, device=p.device)
+                st["exp_avg"] = d["m1"][o:o + p.numel()].view(p.shape)
+                st["exp_avg_sq"] = d["m2"][o:o + p.numel()].view(p.shape)
+            steps.append(st["step"])
+        if steps:
+            torch._foreach_add_(steps, 1.0)
+        d["steps"] = d.get("steps", 0) + 1
+        b1, b2 = group["betas"]
+        t = d["steps"]
+        self.deferred = dict(self.deferred or {}, lr_a=group["lr"], wd_a=group["weight_decay"], b1=b1, b2=b2,
+                             eps=group["eps"], bc1=1 - b1 ** t, rsqrt_bc2=(1 - b2 ** t) ** -0.5)
+
+    @torch.no_grad()
     def _adamw_step(self, group):
         from torch.optim.adam import adam as _adam_fn
+        if self.defer is not None:
+            self._adamw_deferred(group)
         params, grads, m1, m2, steps = [], [], [], [], []
         for p in group["params"]:
             if p.grad is None or (self.owned is not None and id(p) not in self.owned):
+                continue
+            if self.defer is not None and id(p) in self.defer["ids"]:
                 continue
             st = self.state[p]
             if not st:

@@ -200,6 +200,11 @@ class P2PTransport:
         self.flags = self.raw["flags"].view(torch.int64)
         self.acks = self.raw["acks"].view(torch.int64)
         self.wflags = self.raw["wflags"].view(torch.int64)
+        # flat optimizer state and Muon output for the fused apply (only this rank's owned ranges are used)
+        self.m1 = torch.zeros(numel, dtype=torch.float32, device=device)
+        self.m2 = torch.zeros(numel, dtype=torch.float32, device=device)
+        self.upd = torch.zeros(numel, dtype=torch.bfloat16, device=device)
+        self.tables = None
         self.counters = torch.zeros(2 * nb + 2, dtype=torch.int32, device=device)
         self.bcast_counter = torch.zeros(2, dtype=torch.int32, device=device)
         self.sumsq = torch.zeros(nb, self.MAX_PARTIALS, dtype=torch.float32, device=device)
@@ -231,6 +236,47 @@ class P2PTransport:
         self.ext.p2p_bcast_bf16(master, self.peer["w16"], self.peer["wflags"], self.bcast_counter, self.rank, self.nb,
                                 b, off, n, epoch)
 
+    CHUNK = 16384
+
+    def build_tables(self, layout, flat, rank, opt):
+        """Per sharded bucket, the [off, n | kind << 32, coef] rows of this rank's owned parameters (chunks of at most
+        CHUNK elements); registers the deferred mode with the optimizer."""
+        import struct
+        off_of = {id(p): o for p, o in zip(flat.params, flat.offsets)}
+        muon_group = next((g for g in opt.param_groups if g.get("use_muon")), None)
+        ids = set()
+        self.tables = []
+        for b in layout.buckets:
+            if b.replicated:
+                continue
+            rows = []
+            for p in b.params:
+                if layout.owner[id(p)] != rank:
+                    continue
+                ids.add(id(p))
+                muon = getattr(p, "_muon_parts", None) is not None
+                coef = 0.0
+                if muon:
+                    parts = p._muon_parts if muon_group["split"] else 1
+                    coef = opt.update_coef(muon_group, (p.shape[0] // parts, p.shape[1]))
+                o0 = off_of[id(p)]
+                for c in range(0, p.numel(), self.CHUNK):
+                    n = min(self.CHUNK, p.numel() - c)
+                    w2 = struct.unpack("<q", struct.pack("<ff", coef, 0.0))[0]
+                    rows.append([o0 + c, n | ((1 if muon else 0) << 32), w2])
+            t = torch.tensor(rows if rows else [[0, 0, 0]], dtype=torch.int64, device=self.grad.device)
+            self.tables.append((t, len(rows)))
+        opt.defer = {"ids": ids, "off": off_of, "upd": self.upd, "m1": self.m1, "m2": self.m2}
+
+    def fused_apply(self, i, master, grad, ema_buf, scal, epoch):
+        t, n = self.tables[i]
+        vals = [scal.get("lr_a", 0.0), scal.get("wd_a", 0.0), scal.get("b1", 0.9), scal.get("b2", 0.95),
+                scal.get("eps", 1e-8), scal.get("bc1", 1.0), scal.get("rsqrt_bc2", 1.0), scal.get("lr_m", 0.0),
+                scal.get("wd_m", 0.0), scal.get("ema_keep", 1.0)]
+        self.ext.p2p_fused_apply(t, n, master, grad, self.m1, self.m2, self.upd, ema_buf, self.peer["w16"],
+                                 self.peer["wflags"], self.bcast_counter, [float(v) for v in vals], self.rank, self.nb,
+                                 i, epoch)
+
     def wait_weights(self, b0, b1, epoch):
         self.ext.p2p_wait(self.wflags, self.world, self.rank, self.nb, b0, b1, epoch)
 
@@ -251,9 +297,36 @@ class DataParallel:
         self.early = 0  # buckets launched under the backward in the last step (overlap statistics)
         self.p2p = p2p  # P2PTransport (zero mode over peer memory) or None (NCCL)
         self.epoch = 0  # optimizer steps synchronised so far (the peer flags' epochs)
+        self.opt = None  # with p2p: the optimizer whose owned-parameter update the fused kernel applies
+        self.ema_buf = None  # with p2p + fused apply: the EMA's flat buffer (owned ranges updated by the kernel)
+        self.ema_keep = 1.0
         # zero mode: the parameters this rank updates (its own and the replicated ones)
         self.owned = None if self.mode == "ddp" else {id(p) for p in layout.params
                                                       if layout.owner[id(p)] in (self.rank, None)}
+
+    @torch.no_grad()
+    def after_load(self):
+        """After optimizer state was loaded: the fused kernel's flat AdamW state takes the loaded values and the state
+        entries become its views again."""
+        if self.p2p is None or self.opt is None:
+            return
+        d = self.opt.defer
+        for p, st in self.opt.state.items():
+            if id(p) not in d["ids"] or "exp_avg" not in st:
+                continue
+            o = d["off"][id(p)]
+            for k, buf in (("exp_avg", d["m1"]), ("exp_avg_sq", d["m2"])):
+                v = buf[o:o + p.numel()]
+                v.copy_(st[k].reshape(-1).to(v.device))
+                st[k] = v.view(p.shape)
+            d["steps"] = int(float(st["step"]))
+
+    def attach_optimizer(self, opt):
+        """zero mode over peer memory: the update of the owned parameters (AdamW and the Muon apply) runs in the
+        fused kernel together with the weight broadcast."""
+        if self.p2p is not None:
+            self.opt = opt
+            self.p2p.build_tables(self.layout, self.flat, self.rank, opt)
 
     # ----------------------------------------------------------------------------------------- gradients
     def arm(self):
@@ -342,6 +415,10 @@ class DataParallel:
                 self.flat.data16[b.start:b.end].copy_(self.flat.data[b.start:b.end])
                 continue
             lo = b.start + self.rank * b.seg
+            if self.p2p is not None and self.opt is not None:  # update + EMA + bf16 to every rank, then flags
+                scal = dict(self.opt.deferred or {}, ema_keep=self.ema_keep)
+                self.p2p.fused_apply(i, self.flat.data, self.flat.grad, self.ema_buf, scal, self.epoch)
+                continue
             if self.p2p is not None:  # owner -> bf16 into every rank's weights, then flags
                 self.p2p.broadcast_weights(self.flat.data, i, lo, b.seg, self.epoch)
                 continue

