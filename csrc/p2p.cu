@@ -69,16 +69,22 @@ __global__ void __launch_bounds__(256) p2p_push_kernel(const float* __restrict__
   }
   __syncthreads();
   if (ok) {
-    // 2) our segment for owner o -> o's receive slot `rank`, as float4 stores into peer memory
+    // 2) our segment for owner o -> o's receive slot `rank`, as float4 stores into peer memory. Work unit = one
+    //    warp's 512 contiguous bytes for one owner; consecutive units rotate over the owners, starting after this
+    //    rank, so every receiver takes data from all senders at once instead of all senders targeting one owner.
     const int64_t n4 = seg / 4;
-    const int64_t total = (int64_t)(W - 1) * n4;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-      int o = (int)(i / n4);
-      const int64_t j = i - (int64_t)o * n4;
-      if (o >= rank) ++o;
-      const float4* src = reinterpret_cast<const float4*>(grad + start + (int64_t)o * seg) + j;
-      float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(recv.p[o]) + start + (int64_t)rank * seg) + j;
-      *dst = *src;
+    const int64_t nchunk = (n4 + 31) / 32;
+    const int64_t units = (int64_t)(W - 1) * nchunk;
+    const int lane = threadIdx.x & 31;
+    const int64_t wpb = blockDim.x >> 5;
+    for (int64_t u = blockIdx.x * wpb + (threadIdx.x >> 5); u < units; u += gridDim.x * wpb) {
+      const int o = (rank + 1 + (int)(u % (W - 1))) % W;
+      const int64_t j = (u / (W - 1)) * 32 + lane;
+      if (j < n4) {
+        const float4* src = reinterpret_cast<const float4*>(grad + start + (int64_t)o * seg) + j;
+        float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(recv.p[o]) + start + (int64_t)rank * seg) + j;
+        *dst = *src;
+      }
     }
   }
   // 3) the last CTA raises our flag for this bucket at every owner (after everyone's stores are visible)

@@ -225,6 +225,15 @@ class P2PTransport:
             self.peer[k] = ptrs
         dist.barrier(group=group)
 
+    def close(self):
+        """Collective: unmap the peers' buffers (before any rank frees its own)."""
+        torch.cuda.synchronize()
+        dist.barrier()
+        for p in self._opened:
+            self.ext.p2p_close(p)
+        self._opened = []
+        dist.barrier()
+
     def reduce_scatter(self, b, start, seg, epoch):
         """Bucket b ([W segments of seg fp32] at start): this rank's segment becomes the sum over ranks."""
         self.sumsq[b].zero_()
