@@ -82,6 +82,26 @@ class Trainer:
             return t
         return t.to(dev, non_blocking=True)
 
+    def _stage(self, mbatch, dev):
+        """(images, captions, mask, t, noise) of one micro-batch on the device. Host tensors (pinned) are copied on a
+        side stream that the compute stream then waits for, so the copies of micro-batch i + 1 overlap the compute of
+        micro-batch i."""
+        items = [mbatch[k] if len(mbatch) > k else None for k in range(5)]
+        host = dev.type == "cuda" and any(t is not None and t.device.type == "cpu" for t in items)
+        if not host:
+            return tuple(self._to_device(t, dev) if t is not None else None for t in items), None
+        if self.copy_stream is None:
+            self.copy_stream = torch.cuda.Stream(device=dev)
+        cur = torch.cuda.current_stream(dev)
+        with torch.cuda.stream(self.copy_stream):  # fresh device memory, pinned host sources: nothing to wait for
+            out = tuple(t.to(dev, non_blocking=True) if t is not None else None for t in items)
+            ready = torch.cuda.Event()
+            ready.record(self.copy_stream)
+        for t in out:
+            if t is not None:
+                t.record_stream(cur)  # freed only after the compute stream's uses
+        return out, ready
+
     def train_step(self, images, captions, caption_mask=None, t=None, noise=None):
         """One optimizer step over this rank's batch, split into `accum` micro-batches.
         images: uint8 [B, H, W, 3] or float [B, 3, H, W] in [-1, 1] (host pinned or device);
@@ -105,20 +125,19 @@ class Trainer:
             self.flat.zero_grad()
         n = len(micros)
         losses = []
-        for i, mbatch in enumerate(micros):
-            images, captions, mask = mbatch[0], mbatch[1], mbatch[2]
-            t = mbatch[3] if len(mbatch) > 3 else None
-            noise = mbatch[4] if len(mbatch) > 4 else None
+        staged = self._stage(micros[0], dev)
+        for i in range(n):
+            (x, y, m, ti, ni), ready = staged
+            if ready is not None:  # this micro-batch's copies, enqueued one micro-batch earlier
+                torch.cuda.current_stream(dev).wait_event(ready)
+            if i + 1 < n:  # the next micro-batch's host -> device copies run on a side stream under this one's compute
+                staged = self._stage(micros[i + 1], dev)
             if self.dp is not None and i == n - 1:
                 self.dp.arm()
-            x = self._to_device(images, dev)
             x = uint8_to_float(x) if x.dtype == torch.uint8 else x.float()
             if self.encode is not None:
                 x = self.encode(x)
-            y = self._to_device(captions, dev).to(torch.bfloat16)
-            m = self._to_device(mask, dev) if mask is not None else None
-            ti = t.to(dev) if t is not None else None
-            ni = noise.to(dev) if noise is not None else None
+            y = y.to(torch.bfloat16)
             # mean over this rank's images and over ranks (the collectives sum)
             per = self.obj.train_step(self.model, x, y, m, t=ti, noise=ni,
                                       grad_scale=1.0 / (x.numel() * n * self.world))
