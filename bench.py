@@ -131,7 +131,8 @@ def run_ours(a, rank, world, dev):
     from nano_gpic_b200.ops import status
     from nano_gpic_b200.train.trainer import Trainer
     tr = Trainer.for_ladder(a.size, device=dev, world=world, rank=rank, micro_batch=a.micro_batch, dp=a.dp,
-                            transport=a.transport,
+                            transport=a.transport, fp8=None if a.fp8 == "none" else a.fp8,
+                            recompute=None if a.recompute == "none" else a.recompute,
                             global_batch=a.global_batch)
     B = a.global_batch // world
     dev_batch = synthetic_batch(B, a.caption_len, 2048, seed=1000 + rank, device=dev)
@@ -268,6 +269,10 @@ def main():
     ap.add_argument("--global-batch", type=int, default=1024)
     ap.add_argument("--caption-len", type=int, default=128)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--recompute", default="none", choices=["none", "image", "all"],
+                    help="activation checkpointing of the image (and text) blocks")
+    ap.add_argument("--fp8", default="none", choices=["none", "mx"],
+                    help="mx: the image blocks' forward GEMMs in MXFP8 (the d12-FP8 config); default bf16")
     ap.add_argument("--transport", default="nccl", choices=["nccl", "p2p"],
                     help="zero mode: NCCL collectives or this framework's peer-memory kernels")
     ap.add_argument("--dp", default="zero", choices=["ddp", "zero"],
@@ -308,7 +313,8 @@ def main():
                "unit": "images/s", "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms, 2),
                "higher_is_better": True, "scaling": "strong",
                "vs_baseline": round(value / PUBLISHED[a.size], 4) if a.size in PUBLISHED else None,
-               "dtype": "bf16", "data": "synthetic (uint8 images uniform, N(0,1) caption features, random-length "
+               "dtype": "bf16" if a.fp8 == "none" or a.impl == "reference" else
+                        "bf16 + MXFP8 forward GEMMs (image-block qkv_x/proj/w12/w3)", "data": "synthetic (uint8 images uniform, N(0,1) caption features, random-length "
                                          "masks; random-init weights)",
                "mfu": round(mfu, 4), "mfu_peak": f"{pk / 1e12:.1f} TFLOP/s bf16 ({pk_src})",
                "model_tflops_per_gpu": round(value * flops_img / world / 1e12, 1),
@@ -319,6 +325,7 @@ def main():
                                                         if getattr(a, "dp", "ddp") == "zero" and a.impl == "ours"
                                                         else ""),
                           "optimizer": "Muon (split, NS5 bf16) + AdamW, clip 1.0, WarmupFlatCooldown",
+                          "recompute": a.recompute if a.impl == "ours" else "none",
                           "l2": "inputs larger than L2 (1.3 GB of step inputs per rank, activations >> 126 MB)"},
                "clocks": clocks,
                "e2e": {"value": round(a.global_batch / (e2e_ms / 1000.0), 1) if e2e_ms else None, "unit": "images/s",

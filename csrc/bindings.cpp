@@ -47,6 +47,11 @@ void attn_fwd_tc(const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0
                  const c10::optional<at::Tensor>& v1, const at::Tensor& n0, const at::Tensor& n1, const at::Tensor& o,
                  const at::Tensor& lse, int64_t Lq, int64_t L0, int64_t L1, double scale, int64_t version);
 void gemm_set_pair(int64_t on);
+std::vector<at::Tensor> mx_quant(const at::Tensor& x);
+void gemm_mx_torch(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor& B, const at::Tensor& sfb,
+                   const at::Tensor& out, int64_t epi, int64_t N, const c10::optional<at::Tensor>& out2,
+                   const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& res,
+                   const c10::optional<at::Tensor>& gate, int64_t rows_per_group, int64_t half_n);
 at::Tensor p2p_alloc(int64_t nbytes, int64_t device);
 at::Tensor p2p_export(const at::Tensor& t);
 int64_t p2p_import(const at::Tensor& handle, int64_t device);
@@ -93,6 +98,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_fused_apply", &ng::p2p_fused_apply,
         "sharded AdamW / Muon apply + EMA of one bucket's owned parameters, bf16 weights into every rank, flags");
   m.def("p2p_wait", &ng::p2p_wait, "wait (bounded) for every peer's weight flags of a bucket range");
+  m.def("mx_quant", &ng::mx_quant, "bf16 [rows, K] -> MXFP8 (e4m3 values, E8M0 scale blocks)");
+  m.def("gemm_mx", &ng::gemm_mx_torch, "MXFP8 block-scaled tcgen05 GEMM with the bf16 / gated / SwiGLU epilogues");
   m.def("gemm_set_pair", &ng::gemm_set_pair, "use CTA-pair (cta_group::2) GEMM tiles when M >= 256 (default on)");
   m.def("attn_fwd_tc", &ng::attn_fwd_tc, "masked attention forward on tcgen05/TMEM (version 2: persistent, two query "
         "tiles per CTA; version 1: one query tile per CTA)", py::arg("q"), py::arg("k0"), py::arg("v0"), py::arg("k1"),

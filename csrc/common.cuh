@@ -180,6 +180,40 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// ------------------------------------------------------------------------------------ MXFP8 (block-scaled) MMA
+// D[tmem] (+)= (A * sfA)[smem] * (B * sfB)[smem]^T with E4M3 A and B and one E8M0 scale per 32 values along K; the
+// scale factors are read from tensor memory. M = 128, K = 32 per instruction; issued by one thread.
+__device__ __forceinline__ void umma_mxf8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%4], [%5], p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
+      : "memory");
+}
+
+// Instruction descriptor of kind::mxf8f6f4.block_scale: E4M3 A and B (format 0), both K-major, fp32 accumulator,
+// E8M0 scales (bit 23); the scale-factor byte of A (bits 29-30) and of B (bits 4-5) are OR-ed in per instruction.
+__host__ __device__ constexpr uint32_t idesc_mxf8_f32(int M, int N) {
+  return ((uint32_t)(N >> 3) << 17) | (1u << 23) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Shared -> tensor memory: 32 rows of 16 bytes (a 512-byte scale-factor block) into lanes 0-31 of each of the four lane
+// quarters, 4 columns from taddr. Ordered with the tcgen05.mma instructions issued by the same thread.
+__device__ __forceinline__ void tmem_cp_32x128_x4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
+// Shared-memory descriptor of a 512-byte scale-factor block: no swizzle, rows of 16 bytes, 8-row groups 128 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_sf(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)(128u >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  return d;
+}
+
 // Arrives once on `bar` when every tcgen05.mma issued so far by this thread has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))

@@ -33,6 +33,16 @@ constexpr int B_BYTES = BN * BK * 2;  // 32 KiB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int THREADS = 320;  // producer, MMA, 8 epilogue warps (two per TMEM lane quarter)
 constexpr int TMEM_COLS = 512;
+// MXFP8 (block-scaled e4m3) tiles: 128 x 256 x 128 bytes per stage (the bf16 tile's bytes), plus the stage's scale
+// factors: one 512-byte block for A's 128 rows and two for B's 256 rows. Both accumulators (256 columns each) and the
+// 12 scale-factor columns must fit the 512 TMEM columns, so the second accumulator starts at column 224 and shares the
+// first one's last 32 columns: the epilogue reads that shared chunk first and releases it (barrier `ovl`) before the
+// rest of the tile, so the next tile's MMAs wait for one chunk read, not for the whole epilogue.
+constexpr int MX_BK = 128;      // K elements (bytes) per stage
+constexpr int MX_SF_STAGE = 1536;
+constexpr int MX_ACC1 = 224;    // TMEM column of the second accumulator
+constexpr int MX_SFA_COL = 480;  // 4 columns: A's scale factors of the stage (32 lanes x 4 row groups x 4 k-blocks)
+constexpr int MX_SFB_COL = 488;  // 8 columns: B's scale factors (two 128-row blocks)
 }  // namespace gemm_cfg
 
 // Per-epilogue shared-memory plan. Epilogues that read inputs or write several outputs per tile (SwiGLU forward and
@@ -40,13 +50,16 @@ constexpr int TMEM_COLS = 512;
 // prefetched input tiles and two output slots, so neither input latency nor store drain sits on the critical path.
 // PAIR: the CTA-pair kernel (cta_group::2, 256 x 256 tiles per pair): a stage holds this CTA's 128 rows of A and 128
 // columns of B (32 KiB), so the ring is deeper.
-template <int EPI, bool PAIR = false>
+// MX: e4m3 operands with block scales (1-CTA tiles, K-major A and B); the scale factors take 1.5 KiB per stage, so
+// the ring has 3 stages.
+template <int EPI, bool PAIR = false, bool MX = false>
 struct EpiCfg {
   static constexpr bool HEAVY = EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_BWD || EPI == EPI_GATED;
   static constexpr int STAGE_BYTES = PAIR ? gemm_cfg::A_BYTES + gemm_cfg::B_BYTES / 2 : gemm_cfg::STAGE_BYTES;
   // SwiGLU backward reads two input tiles per chunk: with pairs it keeps two chunks of inputs in flight (one stage
   // fewer in the mainloop ring)
-  static constexpr int STAGES = PAIR ? (EPI == EPI_SWIGLU_BWD ? 4 : (HEAVY ? 5 : 6)) : (HEAVY ? 3 : 4);
+  static constexpr int STAGES = MX ? 3 : PAIR ? (EPI == EPI_SWIGLU_BWD ? 4 : (HEAVY ? 5 : 6)) : (HEAVY ? 3 : 4);
+  static constexpr int SF_BYTES = MX ? STAGES * gemm_cfg::MX_SF_STAGE : 0;
   // one output slot holds every 32x32 output tile of a chunk (bf16 2 KiB, fp32 4 KiB)
   static constexpr int OUT_SLOT = EPI == EPI_SWIGLU ? 6144
                                   : (EPI == EPI_F32 || EPI == EPI_GATED || EPI == EPI_SWIGLU_BWD) ? 4096
@@ -56,7 +69,7 @@ struct EpiCfg {
   static constexpr int IN_RING = IN_SLOT == 0 ? 0 : ((EPI == EPI_GATED || (PAIR && EPI == EPI_SWIGLU_BWD)) ? 2 : 1);
   static constexpr int WARP_BYTES = (OUT_SLOTS * OUT_SLOT + IN_RING * IN_SLOT + 1023) / 1024 * 1024;
   static constexpr int EPI_BYTES = 8 * WARP_BYTES;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + 1024 /*align slack*/ + 512 /*barriers*/;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + SF_BYTES + 1024 /*align slack*/ + 512 /*barriers*/;
   static_assert(SMEM <= 232448, "shared memory budget of one sm_100 CTA");
 };
 
@@ -79,6 +92,8 @@ struct EpiParams {
   int accumulate;
   int k_splits;      // >1: split-K, each split writes its own fp32 slice out + split * out_bs
   int kb_per_split;  // k-blocks (of BK) per split
+  const uint8_t* sfa;  // MX: scale-factor blocks of A: [ceil(M / 128) row blocks][K / 128][512 bytes]
+  const uint8_t* sfb;  // MX: scale-factor blocks of B (row blocks of the B tensor's rows)
   int* err;
 };
 
@@ -201,26 +216,31 @@ __device__ __forceinline__ void st_tile_f32(uint8_t* buf, int r, const float (&v
 // thread issues M = 256 tcgen05.mma.cta_group::2 over both CTAs' shared memory into both CTAs' TMEM and releases the
 // stages / signals the accumulators in both CTAs; each CTA's epilogue drains its own rows and frees the accumulator
 // on CTA 0's barrier. Per CTA and k-block 32 KiB are loaded instead of 48 KiB.
-template <int AMN, int BMN, int EPI, bool PAIR>
+template <int AMN, int BMN, int EPI, bool PAIR, bool MX>
 __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmOut2,
                         const __grid_constant__ CUtensorMap tmRes, const __grid_constant__ CUtensorMap tmAux,
                         const EpiParams p) {
   using namespace gemm_cfg;
-  using Cfg = EpiCfg<EPI, PAIR>;
+  static_assert(!MX || (!PAIR && AMN == 0 && BMN == 0), "MX tiles: one CTA, K-major A and B");
+  using Cfg = EpiCfg<EPI, PAIR, MX>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int SB = Cfg::STAGE_BYTES;
   constexpr int BMP = PAIR ? 2 * BM : BM;  // rows of one tile (of the pair)
+  constexpr int BKE = MX ? MX_BK : BK;     // K elements per stage
+  constexpr int ACC_STRIDE = MX ? MX_ACC1 : BN;  // TMEM column distance of the two accumulators
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * SB + Cfg::EPI_BYTES);
+  uint8_t* sf_smem = smem + STAGES * SB + Cfg::EPI_BYTES;  // MX: [STAGES][1536] scale-factor blocks
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * SB + Cfg::EPI_BYTES + Cfg::SF_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* acc_full = empty + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* drain = acc_empty + 2;
   uint64_t* in_bar = drain + 1;  // [8 epilogue warps][2]: input ring slots
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(in_bar + 16);
+  uint64_t* ovl = in_bar + 16;    // MX: [2] the chunk an accumulator shares with the other one has been read
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(ovl + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -230,7 +250,7 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
   // SwiGLU tiles cover 128 output columns of each half: the MMA's N extent is still 256
   const int num_m = (p.M + BMP - 1) / BMP;
   const int num_n = (EPI == EPI_SWIGLU) ? (p.half_n + 127) / 128 : (p.N + BN - 1) / BN;
-  const int num_k = (p.K + BK - 1) / BK;
+  const int num_k = (p.K + BKE - 1) / BKE;
   const int splits = p.k_splits > 1 ? p.k_splits : 1;
   const int kps = splits > 1 ? p.kb_per_split : num_k;
   const int total = p.batch * splits * num_m * num_n;
@@ -246,6 +266,8 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
     }
     mbar_init(drain, 1);
     for (int e = 0; e < 16; ++e) mbar_init(&in_bar[e], 1);
+    mbar_init(&ovl[0], 8);
+    mbar_init(&ovl[1], 8);
     *abort_flag = 0;
     if (PAIR)
       fence_mbarrier_init_cluster();
@@ -293,8 +315,21 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.err, kErrWaitEmpty)) break;
           uint8_t* sA = smem + stage * SB;
           uint8_t* sB = sA + A_BYTES;
-          const int k0 = kb * BK;
-          if (PAIR) {
+          const int k0 = kb * BKE;
+          if (MX) {
+            // A rows [arow, +128) and B rows of the tile, 128 e4m3 values of K each, plus their scale-factor blocks
+            const int kt = num_k;  // scale-factor blocks per row block
+            const int r0 = EPI == EPI_SWIGLU ? nb * 128 : nb * BN;
+            const int r1 = EPI == EPI_SWIGLU ? p.half_n + nb * 128 : nb * BN + 128;
+            uint8_t* sf = sf_smem + stage * MX_SF_STAGE;
+            mbar_arrive_expect_tx(&full[stage], SB + MX_SF_STAGE);
+            tma_load_3d(&tmA, &full[stage], sA, k0, arow, 0);
+            tma_load_3d(&tmB, &full[stage], sB, k0, r0, 0);
+            tma_load_3d(&tmB, &full[stage], sB + 16384, k0, r1, 0);
+            bulk_load(sf, p.sfa + ((int64_t)mb * kt + kb) * 512, 512, &full[stage]);
+            bulk_load(sf + 512, p.sfb + ((int64_t)(r0 / 128) * kt + kb) * 512, 512, &full[stage]);
+            bulk_load(sf + 1024, p.sfb + ((int64_t)(r1 / 128) * kt + kb) * 512, 512, &full[stage]);
+          } else if (PAIR) {
             // both CTAs' bytes are counted on CTA 0's full barrier; only CTA 0 announces them
             const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
             if (crank == 0) mbar_arrive_expect_tx(&full[stage], 2 * SB);
@@ -366,7 +401,7 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------------------------------ MMA issuer
     if (lane == 0 && crank == 0) {
-      constexpr uint32_t idesc = idesc_bf16_f32(BMP, BN, AMN, BMN);
+      constexpr uint32_t idesc = MX ? idesc_mxf8_f32(BM, BN) : idesc_bf16_f32(BMP, BN, AMN, BMN);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -384,8 +419,10 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
         const int a = it & 1;
         const uint32_t aph = (it >> 1) & 1;
         if (!mbar_wait(&acc_empty[a], aph ^ 1, abort_flag, p.err, kErrWaitAccEmpty)) break;
+        // MX: the previous tile's accumulator shares 32 columns with this one; its epilogue has read them
+        if (MX && it > 0 && !mbar_wait(&ovl[a ^ 1], ((it - 1) >> 1) & 1, abort_flag, p.err, kErrWaitAccEmpty)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + a * BN;
+        const uint32_t d_tmem = tmem_base + a * ACC_STRIDE;
         bool ok = true;
         const int sp = (t / (num_m * num_n)) % splits;
         const int kb0 = sp * kps, kb1 = min(num_k, kb0 + kps);
@@ -397,8 +434,24 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * SB);
           const uint32_t sb = sa + A_BYTES;
+          if (MX) {
+            // this stage's scale factors into TMEM (executed in order with the MMAs before and after), then four
+            // K = 32 MMAs, each using scale-factor byte k of every 32-bit TMEM word
+            const uint32_t ssf = smem_u32(sf_smem + stage * MX_SF_STAGE);
+            tmem_cp_32x128_x4(tmem_base + MX_SFA_COL, smem_desc_sf(ssf));
+            tmem_cp_32x128_x4(tmem_base + MX_SFB_COL, smem_desc_sf(ssf + 512));
+            tmem_cp_32x128_x4(tmem_base + MX_SFB_COL + 4, smem_desc_sf(ssf + 1024));
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
+            for (int k = 0; k < MX_BK / 32; ++k) {
+              const uint64_t da = smem_desc_sw128(sa + k * 32, 16, 1024);
+              const uint64_t db = smem_desc_sw128(sb + k * 32, 16, 1024);
+              const uint32_t id = idesc | ((uint32_t)k << 29) | ((uint32_t)k << 4);
+              umma_mxf8(d_tmem, da, db, id, (tmem_base + MX_SFA_COL) | ((uint32_t)k << 30),
+                        (tmem_base + MX_SFB_COL) | ((uint32_t)k << 30), (kb != kb0 || k != 0) ? 1u : 0u);
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < (MX ? 0 : BK / 16); ++k) {
             const uint64_t da = AMN == 0 ? smem_desc_sw128(sa + k * 32, 16, 1024)
                                          : smem_desc_sw128(sa + k * 2048, 8192, 1024);
             const uint64_t db = BMN == 0 ? smem_desc_sw128(sb + k * 32, 16, 1024)
@@ -451,10 +504,13 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
     const bool has_in = R > 0 && (EPI != EPI_AXPBY || p.beta != 0.f);
     const int my_tiles = tile0 < total ? (total - 1 - tile0) / tstep + 1 : 0;
     const int n_chunks = my_tiles * NCW;  // this warp's chunk sequence, in processing order
+    // chunk of the k-th step of this warp's i-th tile: ascending, except that an MX tile in the first accumulator goes
+    // backwards, so that its last chunk (the columns the second accumulator shares) is read first
+    auto chunk_at = [&](int i, int k) { return (MX && !(i & 1)) ? h + 2 * (NCW - 1 - k) : h + 2 * k; };
     // issue the input loads of chunk L (linear index over this warp's chunks) into ring slot L % R
     auto issue_in = [&](int L) {
       if (!has_in || L >= n_chunks) return;
-      const int i = L / NCW, c = h + 2 * (L - (L / NCW) * NCW);
+      const int i = L / NCW, c = chunk_at(i, L - (L / NCW) * NCW);
       int bs, mb, nb;
       tile_coords(tile0 + i * tstep, num_m, num_n, bs, mb, nb);
       const int row0 = mb * BMP + (int)crank * BM + q * 32;
@@ -484,9 +540,10 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
       tile_coords(t, num_m, num_n, bs, mb, nb);
       const int row0 = mb * BMP + (int)crank * BM + q * 32;
       const int row = row0 + lane;
-      const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + a * BN;
+      const uint32_t tb = tmem_base + ((uint32_t)(q * 32) << 16) + a * ACC_STRIDE;
 #pragma unroll 1
-      for (int c = h; c < NCH; c += 2, ++L) {
+      for (int k = 0; k < NCW; ++k, ++L) {
+        const int c = chunk_at(it, k);
         const int col = (EPI == EPI_SWIGLU ? nb * 128 : nb * BN) + c * 32;
         const bool live = col < ((EPI == EPI_SWIGLU) ? p.half_n : p.N);  // warp-uniform
         uint32_t r1[32], r2[32];
@@ -494,6 +551,12 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
         tmem_ld32(tb + c * 32, r1);
         if (EPI == EPI_SWIGLU) tmem_ld32(tb + 128 + c * 32, r2);
         tmem_wait_ld();
+        if (MX && k == 0) {
+          // the first chunk (which includes the shared columns) is in registers: the next tile may overwrite them
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ovl[a]);
+        }
         // per-sample gate / bias values (global, shared by the warp's lanes) before waiting for the inputs
         float gv[32], bv[32];
         if (live && (EPI == EPI_GATED || EPI == EPI_BF16)) load_bias(p.bias, bv, col, p.N);
@@ -765,11 +828,11 @@ bool gemm_use_pair(int64_t M) {
   return g_pair_mode == 1 && M >= 256;
 }
 
-template <int AMN, int BMN, int EPI, bool PAIR>
+template <int AMN, int BMN, int EPI, bool PAIR, bool MX = false>
 static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps& em, const EpiParams& p,
                      int64_t tiles, cudaStream_t s) {
-  auto kern = gemm_tcgen05_kernel<AMN, BMN, EPI, PAIR>;
-  constexpr int smem = EpiCfg<EPI, PAIR>::SMEM;
+  auto kern = gemm_tcgen05_kernel<AMN, BMN, EPI, PAIR, MX>;
+  constexpr int smem = EpiCfg<EPI, PAIR, MX>::SMEM;
   static bool attr_set = false;
   static int max_clusters = 0;
   cudaLaunchConfig_t cfg = {};
@@ -835,12 +898,27 @@ void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   NG_TRACE("[gemm] M=%d N=%d K=%d batch=%d a_mn=%d b_mn=%d epi=%d lda=%lld ldb=%lld ldo=%lld splits=%d A=%p B=%p out=%p\n",
            g.M, g.N, g.K, g.batch, g.a_mn, g.b_mn, g.epi, (long long)g.lda, (long long)g.ldb, (long long)g.ldo,
            g.k_splits, g.A, g.B, g.out);
-  // operand tensor maps: K-major [rows, K] boxes of 64 x 128; MN-major [K, rows] boxes of 64 x 64
-  CUtensorMap ta = g.a_mn ? make_tmap_bf16(g.A, g.M, g.K, g.batch, g.lda, g.a_bs, 64, 64)
-                          : make_tmap_bf16(g.A, g.K, g.M, g.batch, g.lda, g.a_bs, 64, 128);
   const int64_t b_rows = g.b_rows > 0 ? g.b_rows : g.N;
-  CUtensorMap tb = g.b_mn ? make_tmap_bf16(g.B, b_rows, g.K, g.batch, g.ldb, g.b_bs, 64, 64)
-                          : make_tmap_bf16(g.B, g.K, b_rows, g.batch, g.ldb, g.b_bs, 64, 128);
+  CUtensorMap ta, tb;
+  if (g.mx) {
+    // e4m3 operands, K-major, boxes of 128 bytes x 128 rows (the bf16 tile's bytes)
+    TORCH_CHECK(!g.a_mn && !g.b_mn && g.batch == 1 && g.k_splits <= 1 && g.K % MX_BK == 0,
+                "MXFP8 GEMM: K-major A and B, one batch, K a multiple of 128");
+    TORCH_CHECK(g.epi == EPI_BF16 || g.epi == EPI_GATED || g.epi == EPI_SWIGLU, "MXFP8 GEMM: unsupported epilogue");
+    TORCH_CHECK(g.sfa != nullptr && g.sfb != nullptr && (reinterpret_cast<uintptr_t>(g.sfa) & 15) == 0 &&
+                    (reinterpret_cast<uintptr_t>(g.sfb) & 15) == 0,
+                "MXFP8 GEMM: 16-byte aligned scale factors expected");
+    TORCH_CHECK(g.epi != EPI_SWIGLU || g.half_n % 128 == 0, "MXFP8 SwiGLU: half width a multiple of 128");
+    ta = make_tmap(g.A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K, g.M, 1, g.lda, 0, MX_BK, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    tb = make_tmap(g.B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K, b_rows, 1, g.ldb, 0, MX_BK, 128,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    // operand tensor maps: K-major [rows, K] boxes of 64 x 128; MN-major [K, rows] boxes of 64 x 64
+    ta = g.a_mn ? make_tmap_bf16(g.A, g.M, g.K, g.batch, g.lda, g.a_bs, 64, 64)
+                : make_tmap_bf16(g.A, g.K, g.M, g.batch, g.lda, g.a_bs, 64, 128);
+    tb = g.b_mn ? make_tmap_bf16(g.B, b_rows, g.K, g.batch, g.ldb, g.b_bs, 64, 64)
+                : make_tmap_bf16(g.B, g.K, b_rows, g.batch, g.ldb, g.b_bs, 64, 128);
+  }
   EpiParams p;
   p.M = g.M;
   p.N = g.N;
@@ -866,8 +944,10 @@ void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   p.accumulate = g.accumulate;
   p.k_splits = g.k_splits > 1 ? g.k_splits : 1;
   p.kb_per_split = g.kb_per_split;
+  p.sfa = static_cast<const uint8_t*>(g.sfa);
+  p.sfb = static_cast<const uint8_t*>(g.sfb);
   p.err = g.err;
-  const bool pair = gemm_use_pair(g.M);
+  const bool pair = !g.mx && gemm_use_pair(g.M);
   const int num_m = (g.M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM);
   const int num_n = g.epi == EPI_SWIGLU ? (g.half_n + 127) / 128 : (g.N + BN - 1) / BN;
   const int64_t tiles = (int64_t)g.batch * (g.k_splits > 1 ? g.k_splits : 1) * num_m * num_n;
@@ -887,7 +967,13 @@ void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     em.res = epi_map_bf16(g.res, g.N, g.M, g.batch, g.ldr, g.res_bs);
   if (g.epi == EPI_SWIGLU_BWD) em.aux = epi_map_bf16(g.aux, 2 * (int64_t)g.half_n, g.M, 1, g.ld_aux, 0);
   NG_TRACE("[gemm]   maps ok, pair=%d tiles=%lld\n", (int)pair, (long long)tiles);
-  if (pair)
+  if (g.mx) {
+    switch (g.epi) {
+      case EPI_BF16: launch_t<0, 0, EPI_BF16, false, true>(ta, tb, em, p, tiles, stream); break;
+      case EPI_GATED: launch_t<0, 0, EPI_GATED, false, true>(ta, tb, em, p, tiles, stream); break;
+      default: launch_t<0, 0, EPI_SWIGLU, false, true>(ta, tb, em, p, tiles, stream); break;
+    }
+  } else if (pair)
     dispatch_major<true>(g.a_mn, g.b_mn, g.epi, ta, tb, em, p, tiles, stream);
   else
     dispatch_major<false>(g.a_mn, g.b_mn, g.epi, ta, tb, em, p, tiles, stream);

@@ -45,6 +45,12 @@ struct GemmArgs {
   float alpha = 1.f, beta = 0.f;
   int accumulate = 0;
   int k_splits = 1, kb_per_split = 0;
+  // MXFP8: A and B are e4m3 (K-major, row strides in bytes) with E8M0 scale factors, one per 32 values along K,
+  // in blocks of 128 rows x 4 values: [ceil(rows / 128)][K / 128][512 bytes], byte (r % 32) * 16 + (r / 32 % 4) * 4
+  // + (k / 32 % 4) for row r, column k. B's scale factors cover every 128-row block a tile touches.
+  int mx = 0;
+  const void* sfa = nullptr;
+  const void* sfb = nullptr;
   int* err = nullptr;
 };
 

@@ -17,6 +17,7 @@ real token) or None (all T tokens real). The caption-length handling is the refe
 caption keys are masked out of every attention.
 """
 import math
+import os
 
 import torch
 import torch.nn as nn
@@ -25,6 +26,7 @@ import torch.nn.functional as F
 from ..ops import attention as A
 from ..ops import elementwise as E
 from ..ops import gemm as G
+from ..ops import mx as MXO
 from ..ops import norm as NR
 from ..ops import qk as QK
 from .layers import Linear, RMSNorm, rope_tables, sincos_pos_embed, timestep_freq
@@ -56,6 +58,19 @@ def grad_of(p):
 
 def _wgrad(dy, x, p):
     G.linear_wgrad(dy, x, out=grad_of(p), accumulate=True)
+
+
+def _mx_weights(blk):
+    """MXFP8 copies of an image block's forward GEMM weights (qkv_x, proj, w12, w3), made from the bf16 compute weights
+    once per weight version (JiT_T2I.weights_changed() after every optimizer step or load)."""
+    ver = getattr(blk, "_wver", 0)
+    c = getattr(blk, "_mxw", None)
+    if c is None or c[0] != ver:
+        a = blk.attn
+        c = (ver, {"qkv_x": MXO.quant(w16(a.qkv_x)), "proj": MXO.quant(w16(a.proj)),
+                   "w12": MXO.quant(w16(blk.mlp.w12)), "w3": MXO.quant(w16(blk.mlp.w3))})
+        blk._mxw = c
+    return c[1]
 
 
 def _bias_grad(dy, p):
@@ -180,7 +195,8 @@ def _stage_hook(hook):
 
 class _TextBlockFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, y, mod, anchor, blk, lens, T, hook=None):
+    def _run(y, mod, blk, lens, T):
+        """The block's forward: (output, the activations its backward reads)."""
         C = y.shape[1]
         a = blk.attn
         n1, n2 = blk.norm1, blk.norm2
@@ -193,15 +209,24 @@ class _TextBlockFn(torch.autograd.Function):
         h2, r2 = NR.rms_mod_fwd(y2, f32(n2.weight), mod[:, 3 * C:4 * C], mod[:, 4 * C:5 * C], T, n2.variance_epsilon)
         act, pre = G.swiglu_linear(h2, w16(blk.mlp.w12))
         y3, ym = G.linear_gated_residual(act, w16(blk.mlp.w3), None, y2, mod[:, 5 * C:6 * C], T)
+        return y3, (h1, r1, qkv, q, rq, k, rk, o, lse, y2, ya, h2, r2, act, pre, ym)
+
+    @staticmethod
+    def forward(ctx, y, mod, anchor, blk, lens, T, hook=None):
+        y3, acts = _TextBlockFn._run(y, mod, blk, lens, T)
         ctx.blk, ctx.T, ctx.hook = blk, T, hook
-        ctx.save_for_backward(y, mod, lens, h1, r1, qkv, q, rq, k, rk, o, lse, y2, ya, h2, r2, act, pre, ym)
+        ctx.recompute = getattr(blk, "_recompute", False)
+        ctx.save_for_backward(y, mod, lens, *(() if ctx.recompute else acts))
         return y3
 
     @staticmethod
     def backward(ctx, dy3):
-        (y, mod, lens, h1, r1, qkv, q, rq, k, rk, o, lse, y2, ya, h2, r2, act, pre, ym) = ctx.saved_tensors
+        y, mod, lens, *acts = ctx.saved_tensors
         blk, T = ctx.blk, ctx.T
         _stage_hook(ctx.hook)
+        if ctx.recompute:  # activation checkpointing: rerun the forward from the saved inputs
+            acts = _TextBlockFn._run(y, mod, blk, lens, T)[1]
+        (h1, r1, qkv, q, rq, k, rk, o, lse, y2, ya, h2, r2, act, pre, ym) = acts
         a = blk.attn
         C = y.shape[1]
         dy3 = dy3.contiguous()
@@ -233,32 +258,50 @@ class _TextBlockFn(torch.autograd.Function):
 
 class _ImageBlockFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, yt, mod, anchor, blk, lens, L, T, cos, sin, hook=None):
+    def _run(x, yt, mod, blk, lens, L, T, cos, sin):
+        """The block's forward: (output, the activations its backward reads)."""
         C = x.shape[1]
         a = blk.attn
         n1, n2 = blk.norm1, blk.norm2
+        # fp8 == "mx": the four big forward GEMMs read MXFP8 operands (reference fp8_native.py, phase 1); the saved
+        # activations and the whole backward stay bf16
+        mxw = _mx_weights(blk) if getattr(blk, "_fp8", False) else None
         h1, r1 = NR.rms_mod_fwd(x, f32(n1.weight), mod[:, 0:C], mod[:, C:2 * C], L, n1.variance_epsilon)
-        qkv = G.linear(h1, w16(a.qkv_x))
+        qkv = G.linear(h1, w16(a.qkv_x)) if mxw is None else MXO.linear(MXO.quant(h1), mxw["qkv_x"])
         kvy = G.linear(yt, w16(a.kv_y))
         q, rq = QK.qk_norm_fwd(qkv[:, 0:C], f32(a.q_norm.weight), cos, sin, L, a.q_norm.variance_epsilon)
         kx, rkx = QK.qk_norm_fwd(qkv[:, C:2 * C], f32(a.k_norm.weight), cos, sin, L, a.k_norm.variance_epsilon)
         ky, rky = QK.qk_norm_fwd(kvy[:, 0:C], f32(a.k_norm.weight), eps=a.k_norm.variance_epsilon)
         o, lse = A.attn_fwd(q, L, kx, qkv[:, 2 * C:], L, L, ky, kvy[:, C:], T, lens)
-        x2, ya = G.linear_gated_residual(o, w16(a.proj), f32(a.proj.bias), x, mod[:, 2 * C:3 * C], L)
+        if mxw is None:
+            x2, ya = G.linear_gated_residual(o, w16(a.proj), f32(a.proj.bias), x, mod[:, 2 * C:3 * C], L)
+        else:
+            x2, ya = MXO.linear_gated_residual(MXO.quant(o), mxw["proj"], f32(a.proj.bias), x, mod[:, 2 * C:3 * C], L)
         h2, r2 = NR.rms_mod_fwd(x2, f32(n2.weight), mod[:, 3 * C:4 * C], mod[:, 4 * C:5 * C], L, n2.variance_epsilon)
-        act, pre = G.swiglu_linear(h2, w16(blk.mlp.w12))
-        x3, ym = G.linear_gated_residual(act, w16(blk.mlp.w3), None, x2, mod[:, 5 * C:6 * C], L)
+        if mxw is None:
+            act, pre = G.swiglu_linear(h2, w16(blk.mlp.w12))
+            x3, ym = G.linear_gated_residual(act, w16(blk.mlp.w3), None, x2, mod[:, 5 * C:6 * C], L)
+        else:
+            act, pre = MXO.swiglu_linear(MXO.quant(h2), mxw["w12"])
+            x3, ym = MXO.linear_gated_residual(MXO.quant(act), mxw["w3"], None, x2, mod[:, 5 * C:6 * C], L)
+        return x3, (h1, r1, qkv, kvy, q, rq, kx, rkx, ky, rky, o, lse, x2, ya, h2, r2, act, pre, ym)
+
+    @staticmethod
+    def forward(ctx, x, yt, mod, anchor, blk, lens, L, T, cos, sin, hook=None):
+        x3, acts = _ImageBlockFn._run(x, yt, mod, blk, lens, L, T, cos, sin)
         ctx.blk, ctx.L, ctx.T, ctx.hook = blk, L, T, hook
-        ctx.save_for_backward(x, yt, mod, lens, cos, sin, h1, r1, qkv, kvy, q, rq, kx, rkx, ky, rky, o, lse, x2, ya,
-                              h2, r2, act, pre, ym)
+        ctx.recompute = getattr(blk, "_recompute", False)
+        ctx.save_for_backward(x, yt, mod, lens, cos, sin, *(() if ctx.recompute else acts))
         return x3
 
     @staticmethod
     def backward(ctx, dx3):
-        (x, yt, mod, lens, cos, sin, h1, r1, qkv, kvy, q, rq, kx, rkx, ky, rky, o, lse, x2, ya, h2, r2, act, pre,
-         ym) = ctx.saved_tensors
+        x, yt, mod, lens, cos, sin, *acts = ctx.saved_tensors
         blk, L, T = ctx.blk, ctx.L, ctx.T
         _stage_hook(ctx.hook)
+        if ctx.recompute:  # activation checkpointing: rerun the forward from the saved inputs
+            acts = _ImageBlockFn._run(x, yt, mod, blk, lens, L, T, cos, sin)[1]
+        (h1, r1, qkv, kvy, q, rq, kx, rkx, ky, rky, o, lse, x2, ya, h2, r2, act, pre, ym) = acts
         a = blk.attn
         C = x.shape[1]
         dx3 = dx3.contiguous()
@@ -395,7 +438,7 @@ class _UnpatchifyFn(torch.autograd.Function):
 class JiT_T2I(nn.Module):
     def __init__(self, input_size=256, in_channels=4, num_groups=12, hidden_size=1152, num_blocks=18,
                  num_text_blocks=4, patch_size=2, txt_embed_dim=1024, txt_max_length=100, bottleneck_dim=256,
-                 weight_path=None, load_ema=False):
+                 weight_path=None, load_ema=False, fp8=None, recompute=None):
         super().__init__()
         assert hidden_size % num_groups == 0 and hidden_size // num_groups == 64, "head dim 64 expected"
         self.in_channels = self.out_channels = in_channels
@@ -420,6 +463,37 @@ class JiT_T2I(nn.Module):
             p._replicate = True
         self._rope = {}
         self._bwd_hook = None  # set by the data-parallel layer around the last micro-batch's backward
+        if fp8 is None and os.environ.get("GPIC_MFU_FP8", "") not in ("", "0", "off"):
+            fp8 = "mx"  # the reference's switch (GPIC_MFU_FP8=native) selects this package's MXFP8 GEMMs
+        self.set_fp8(fp8)
+        self.set_recompute(recompute)
+
+    # -------------------------------------------------------------------------------------- activation memory
+    def set_recompute(self, mode):
+        """Activation checkpointing (no counterpart in the reference): None keeps every block's activations for the
+        backward; "image" keeps only the image blocks' inputs and reruns their forward in the backward; "all" does the
+        same for the text blocks too. Trades one extra forward of those blocks for their activation memory."""
+        assert mode in (None, "image", "all"), f"recompute mode {mode!r}: None, 'image' or 'all'"
+        self.recompute = mode
+        for blk in self.blocks:
+            blk._recompute = mode is not None
+        for blk in self.text_refine_blocks:
+            blk._recompute = mode == "all"
+
+    # ------------------------------------------------------------------------------------------------- fp8
+    def set_fp8(self, mode):
+        """None: bf16 GEMMs everywhere. "mx": the image blocks' qkv_x / proj / w12 / w3 forward GEMMs in MXFP8."""
+        assert mode in (None, "mx"), f"fp8 mode {mode!r}: None or 'mx'"
+        self.fp8 = mode
+        for blk in self.blocks:
+            blk._fp8 = mode == "mx"
+        self.weights_changed()
+
+    def weights_changed(self):
+        """Marks the weights as updated (after an optimizer step or a load): derived copies are rebuilt lazily."""
+        self._wver = getattr(self, "_wver", 0) + 1
+        for blk in self.blocks:
+            blk._wver = self._wver
 
     # ------------------------------------------------------------------------------------------------- init
     def initialize_weights(self):

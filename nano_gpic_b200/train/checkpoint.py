@@ -78,6 +78,8 @@ def load_into(trainer, ck, strict=True, load_optimizer=True, ema=None):
             ema.load_tensors(e)
     if getattr(trainer, "flat", None) is not None:
         trainer.flat.sync_bf16()
+    if hasattr(trainer.model, "weights_changed"):
+        trainer.model.weights_changed()
     if load_optimizer and ck.get("optimizer_states"):
         trainer.opt.load_state_dict(ck["optimizer_states"][0])
         for st in trainer.opt.state.values():  # Lightning restores the state on the CPU; the fused AdamW wants it here

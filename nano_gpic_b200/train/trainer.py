@@ -49,14 +49,19 @@ class Trainer:
     @classmethod
     def for_ladder(cls, size="d12", device="cuda", world=1, rank=0, micro_batch=None, global_batch=GLOBAL_BATCH,
                    max_steps=None, dp="ddp", seed=0, model_kwargs=None, bucket_mb=1000, overlap=True,
-                   transport="nccl"):
+                   transport="nccl", fp8=None, recompute=None):
         """dp: "ddp" (all-reduce, as the reference's DDP sizes) or "zero" (reduce-scatter to owners, sharded
         optimizer state; the role of the reference's FSDP2 sizes). transport (zero mode): "nccl" or "p2p" (this
-        package's peer-memory kernels)."""
+        package's peer-memory kernels). fp8: None (bf16) or "mx" (MXFP8 forward GEMMs in the image blocks). recompute:
+        None, "image" or "all" (activation checkpointing of those blocks)."""
         s = SIZES[size]
         torch.manual_seed(seed)
         kw = s.model_kwargs()
         kw.update(model_kwargs or {})
+        if fp8 is not None:
+            kw["fp8"] = fp8
+        if recompute is not None:
+            kw["recompute"] = recompute
         model = JiT_T2I(**kw).to(device)
         tag_muon_params(model)
         from ..parallel.ddp import make_data_parallel
@@ -152,6 +157,8 @@ class Trainer:
             self.dp.refresh_weights()
         elif self.flat is not None:
             self.flat.sync_bf16()
+        if hasattr(self.model, "weights_changed"):
+            self.model.weights_changed()
         self.global_step += 1
         return torch.cat(losses).mean()
 

@@ -75,3 +75,29 @@ def test_forward_and_grads_match_reference():
         if e1 > max(2 * e2, 2e-2):
             bad.append((n, round(e1, 4), round(e2, 4)))
     assert not bad, bad
+
+
+def test_recompute_matches_stored_activations():
+    """Activation checkpointing reruns each block's forward in the backward: same output and gradients, bit for bit."""
+    from nano_gpic_b200.models.jit_t2i import JiT_T2I
+    torch.manual_seed(0)
+    net = JiT_T2I(input_size=32, in_channels=3, num_groups=2, hidden_size=128, num_blocks=2, num_text_blocks=1,
+                  patch_size=16, txt_embed_dim=2048, txt_max_length=8)
+    with torch.no_grad():
+        for prm in net.parameters():
+            prm.add_(torch.randn_like(prm) * 0.02)
+    x, t = torch.randn(2, 3, 32, 32), torch.rand(2)
+    y = torch.randn(2, 8, 2048).to(torch.bfloat16)
+    m = torch.ones(2, 8, dtype=torch.bool)
+    m[1, 5:] = False
+    res = []
+    for mode in (None, "all"):
+        net.set_recompute(mode)
+        net.zero_grad(set_to_none=True)
+        o = net(x, t, y, y_mask=m)
+        o.float().square().mean().backward()
+        res.append((o.detach().clone(), [p.grad.clone() for p in net.parameters() if p.grad is not None]))
+    assert torch.equal(res[0][0], res[1][0])
+    assert len(res[0][1]) == len(res[1][1])
+    for a, b in zip(res[0][1], res[1][1]):
+        assert torch.equal(a, b)
