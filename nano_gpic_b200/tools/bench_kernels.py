@@ -2,7 +2,7 @@
 torch.matmul, SDPA, torch elementwise), timed with CUDA events after warm-up, inputs larger than L2 where the shape
 allows, reported as TFLOP/s or GB/s and as a fraction of MEASURED_PEAKS.json.
 
-    python -m nano_gpic_b200.tools.bench_kernels [--only gemm,attn,norm] [--d 1024] [--batch 128] [--json out.json]
+    python -m nano_gpic_b200.tools.bench_kernels [--only gemm,fused,attn,mx] [--d 1024] [--batch 128] [--json out.json]
 """
 import argparse
 import json
@@ -130,6 +130,47 @@ def bench_attn(d, batch, rows, T=128):
     print(json.dumps(row), flush=True)
 
 
+def bench_mx(d, batch, rows):
+    """The image block's forward GEMMs (qkv_x, proj + gated residual, w12 + SwiGLU, w3 + gated residual) in MXFP8 on
+    the tcgen05 block-scaled kernel, against the bf16 kernel with the same epilogue and cuBLASLt's MXFP8 GEMM
+    (torch._scaled_mm with the same e4m3 operands and E8M0 scale blocks, plain bf16 output), plus the quantizer."""
+    from nano_gpic_b200.ops import gemm, mx
+    M = batch * 256
+    pk, _, src = peaks()
+    r = lambda *s: (torch.randn(*s, device="cuda") * 0.5).bfloat16()
+    res, mod = r(M, d), r(batch, 6 * d)
+    cases = [("qkv_x", M, 3 * d, d, "lin"), ("proj", M, d, d, "gated"), ("w12", M, 8 * d, d, "swiglu"),
+             ("w3", M, d, 4 * d, "gated")]
+    for name, m, n, k, kind in cases:
+        x, w = r(m, k), r(n, k)
+        xq, wq = mx.quant(x), mx.quant(w)
+        if kind == "lin":
+            fb, fm = (lambda: gemm.linear(x, w)), (lambda: mx.linear(xq, wq))
+        elif kind == "gated":
+            g = mod[:, 2 * d:2 * d + n] if n == d else mod[:, :n]
+            fb = lambda: gemm.linear_gated_residual(x, w, None, res, g, 256)
+            fm = lambda: mx.linear_gated_residual(xq, wq, None, res, g, 256)
+        else:
+            fb, fm = (lambda: gemm.swiglu_linear(x, w)), (lambda: mx.swiglu_linear(xq, wq))
+        fl = 2.0 * m * n * k
+        tb, tm, tq = time_fn(fb), time_fn(fm), time_fn(lambda: mx.quant(x))
+        row = {"kernel": "gemm_mxfp8", "name": name, "M": m, "N": n, "K": k, "epilogue": kind,
+               "mx_us": round(tm * 1e6, 1), "bf16_us": round(tb * 1e6, 1), "quant_us": round(tq * 1e6, 1),
+               "mx_tflops": round(fl / tm / 1e12, 1), "bf16_tflops": round(fl / tb / 1e12, 1),
+               "mx_frac_of_" + src + "_bf16": round(fl / tm / 1e12 / pk, 3)}
+        try:
+            e8 = torch.float8_e8m0fnu
+            a8, b8 = xq.q.view(torch.float8_e4m3fn), wq.q.view(torch.float8_e4m3fn)
+            sa, sb = xq.sf.view(e8).flatten(), wq.sf.view(e8).flatten()
+            tc = time_fn(lambda: torch._scaled_mm(a8, b8.t(), scale_a=sa, scale_b=sb, out_dtype=torch.bfloat16))
+            row["cublaslt_mx_us"] = round(tc * 1e6, 1)
+            row["cublaslt_mx_tflops"] = round(fl / tc / 1e12, 1)
+        except Exception as e:  # torch build without the MX path
+            row["cublaslt_mx"] = f"unavailable: {type(e).__name__}: {str(e)[:120]}"
+        rows.append(row)
+        print(json.dumps(row), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm")
@@ -145,6 +186,8 @@ def main():
         bench_fused(a.d, a.batch, rows)
     if "attn" in only:
         bench_attn(a.d, a.batch, rows)
+    if "mx" in only:
+        bench_mx(a.d, a.batch, rows)
     if a.json:
         with open(a.json, "w") as f:
             json.dump(rows, f, indent=1)
