@@ -17,6 +17,7 @@ import torch
 from torch.utils.data import DataLoader, IterableDataset, get_worker_info
 
 from .augment import random_crop_arr
+from .pil_resize import CropPlan, ResizeBatch, plan_random_crop
 from .buckets import EDGES, bucket_of
 from .tars import gpic_samples
 from .text_cache import TextCache, collate_captions
@@ -85,8 +86,13 @@ class EpochShuffledShards:
 class GPICDataset(IterableDataset):
     def __init__(self, tar_pattern, emb_dir, seed=0, image_size=256, group_window=1024, group_batch=128,
                  pad_multiple=8, text_max_length=320, shared_bucket=False, bucket_edges=EDGES, log_dir=None,
-                 min_crop_frac=0.8, max_crop_frac=1.0):
+                 min_crop_frac=0.8, max_crop_frac=1.0, gpu_resize=None):
         super().__init__()
+        # gpu_resize (reference lever C, GPIC_MFU_GPU_RESIZE): workers plan the region crop and the bicubic passes run
+        # on the GPU for the whole batch (data/pil_resize.py), byte-identical to the crop done in Pillow
+        if gpu_resize is None:
+            gpu_resize = os.environ.get("GPIC_MFU_GPU_RESIZE", "0") == "1"
+        self.gpu_resize = bool(gpu_resize)
         self.urls = expand_pattern(tar_pattern)
         self.emb_dir, self.seed, self.image_size = emb_dir, seed, image_size
         self.group_window, self.group_batch = group_window, group_batch
@@ -143,8 +149,12 @@ class GPICDataset(IterableDataset):
     def _finish(self, s, rng):
         import io
         from PIL import Image
-        img = random_crop_arr(Image.open(io.BytesIO(s["image"])).convert("RGB"), self.image_size, *self.crop, rng=rng)
-        return (torch.from_numpy(np.asarray(img, dtype=np.uint8)), s["caption"],
+        pil = Image.open(io.BytesIO(s["image"])).convert("RGB")
+        if self.gpu_resize:
+            img = plan_random_crop(pil, self.image_size, *self.crop, rng=rng)
+        else:
+            img = torch.from_numpy(np.asarray(random_crop_arr(pil, self.image_size, *self.crop, rng=rng), dtype=np.uint8))
+        return (img, s["caption"],
                 {"caption_type": s["caption_type"], "text_emb": s["text_emb"], "pad_to": s.get("pad_to")})
 
     def __iter__(self):
@@ -166,7 +176,10 @@ class GPICDataset(IterableDataset):
             yield out
 
     def collate(self, samples):
-        imgs = torch.stack([s[0] for s in samples])
+        if isinstance(samples[0][0], CropPlan):  # GPU resize: the batch's crops run on the device (ResizeBatch.run)
+            imgs = ResizeBatch([s[0] for s in samples], self.image_size)
+        else:
+            imgs = torch.stack([s[0] for s in samples])
         emb, mask = collate_captions([s[2]["text_emb"] for s in samples], self.pad_multiple, self.text_max_length,
                                      pad_to=samples[0][2].get("pad_to"))
         return imgs, [s[1] for s in samples], {"caption_type": [s[2]["caption_type"] for s in samples],

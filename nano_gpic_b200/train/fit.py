@@ -23,6 +23,7 @@ import torch
 import torch.distributed as dist
 
 from ..config.cli import get_dotted, instantiate, is_spec, resolve, run_dir, strategy_mode, write_config
+from ..data.pil_resize import ResizeBatch
 from .callbacks import EMASpec, Warmup
 from .checkpoint import AsyncWriter, build_checkpoint, find_resume, load_into, save_sync
 from .trainer import Trainer
@@ -179,6 +180,8 @@ def fit(cfg):
             micros = []
             for _ in range(accum):
                 img, caps, meta = next(it)
+                if isinstance(img, ResizeBatch):  # the bicubic crop passes of the batch, on the device
+                    img = img.run(dev)
                 if cond is not None:
                     y, uncond = cond(caps, meta)
                     mask = meta.get("y_mask")
