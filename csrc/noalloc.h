@@ -2,9 +2,9 @@
 //
 // This entry point has no counterpart in the reference (wenhaochai/nano-gpic); it is an addition of this library.
 //
-// Who needs it: callers that cannot allocate device memory at the moment they call. For example: code running inside
-// a CUDA stream capture, where cudaMalloc is not allowed; embedders with their own fixed memory pool that forbid any
-// allocation behind their back; and hosts that call from a plain C runtime with no PyTorch caching allocator. The
+// Who needs it: callers that cannot allocate device memory at the moment they call. For example: embedders that hand
+// the GPU's memory to their own fixed pool and forbid any allocation behind their back, real-time loops that must not
+// pay for an allocation, and hosts that call from a plain C runtime with no PyTorch caching allocator. The
 // regular entry point (rms_mod_bwd in csrc/norm.cu) gets its scratch from PyTorch's allocator. This one takes the same
 // inputs and outputs but keeps its scratch, the per-chunk partial column sums, in a fixed device array inside the
 // library, so it calls no cudaMalloc, cudaFree or any other allocating routine.
@@ -15,7 +15,7 @@
 // nothing is launched.
 //
 // Set-up: the first call on each device looks up the array's device address (cudaGetSymbolAddress) with that device
-// current. Make that first call outside any stream capture. Later calls do no set-up.
+// current. Make that first call before any stream capture begins. Later calls do no set-up.
 //
 // Sharing: every call on a device uses the same array, and the array keeps the last call's contents. Each call
 // overwrites every value it reads, so nothing has to start at zero. Calls that overlap on the GPU (on different

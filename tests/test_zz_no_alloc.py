@@ -1,6 +1,6 @@
 """The no-allocation entry point ng_rms_mod_bwd_noalloc (csrc/noalloc.h), called through its exported C symbol, against
 the regular allocating entry point of the same backward. It is for callers that cannot allocate device memory when
-they call (inside a stream capture, under a fixed memory pool, or from plain C without PyTorch's allocator).
+they call (under a fixed memory pool, in an allocation-free loop, or from plain C without PyTorch's allocator).
 
 This file is collected last on purpose: if it fails, a run that stops at the first failure has run every other test.
 """
