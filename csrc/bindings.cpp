@@ -48,6 +48,8 @@ void attn_fwd_tc(const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0
                  const at::Tensor& lse, int64_t Lq, int64_t L0, int64_t L1, double scale, int64_t version);
 void gemm_set_pair(int64_t on);
 std::vector<at::Tensor> mx_quant(const at::Tensor& x);
+void muon_gather(const at::Tensor& tab, double beta, bool nesterov, int64_t max_numel);
+void muon_apply(const at::Tensor& tab, double decay, int64_t max_numel);
 void resize_passes(const at::Tensor& src, const at::Tensor& tab, const at::Tensor& desc, const at::Tensor& tmp,
                    const at::Tensor& out, int64_t max_h, int64_t max_w);
 void gemm_mx_torch(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor& B, const at::Tensor& sfb,
@@ -101,6 +103,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "sharded AdamW / Muon apply + EMA of one bucket's owned parameters, bf16 weights into every rank, flags");
   m.def("p2p_wait", &ng::p2p_wait, "wait (bounded) for every peer's weight flags of a bucket range");
   m.def("resize_passes", &ng::resize_passes, "Pillow-exact bicubic crop passes for a packed batch");
+  m.def("muon_gather", &ng::muon_gather, "stacked Nesterov inputs of every Muon unit from a pointer table");
+  m.def("muon_apply", &ng::muon_apply, "param = param * decay + coef * update for every Muon unit from a pointer table");
   m.def("mx_quant", &ng::mx_quant, "bf16 [rows, K] -> MXFP8 (e4m3 values, E8M0 scale blocks)");
   m.def("gemm_mx", &ng::gemm_mx_torch, "MXFP8 block-scaled tcgen05 GEMM with the bf16 / gated / SwiGLU epilogues");
   m.def("gemm_set_pair", &ng::gemm_set_pair, "use CTA-pair (cta_group::2) GEMM tiles when M >= 256 (default on)");

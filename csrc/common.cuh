@@ -205,6 +205,21 @@ __device__ __forceinline__ void tmem_cp_32x128_x4(uint32_t taddr, uint64_t sdesc
   asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
 }
 
+// CTA-pair forms: one thread of CTA 0 issues them; the copy runs in both CTAs (each from its own shared memory at the
+// same offset into its own tensor memory), the MMA is M = 256 over both CTAs' A rows and B halves.
+__device__ __forceinline__ void tmem_cp_32x128_x4_pair(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+__device__ __forceinline__ void umma_mxf8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                               uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %6, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%4], [%5], p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
+      : "memory");
+}
+
 // Shared-memory descriptor of a 512-byte scale-factor block: no swizzle, rows of 16 bytes, 8-row groups 128 bytes apart.
 __device__ __forceinline__ uint64_t smem_desc_sf(uint32_t saddr) {
   uint64_t d = 0;

@@ -50,15 +50,16 @@ constexpr int MX_SFB_COL = 488;  // 8 columns: B's scale factors (two 128-row bl
 // prefetched input tiles and two output slots, so neither input latency nor store drain sits on the critical path.
 // PAIR: the CTA-pair kernel (cta_group::2, 256 x 256 tiles per pair): a stage holds this CTA's 128 rows of A and 128
 // columns of B (32 KiB), so the ring is deeper.
-// MX: e4m3 operands with block scales (1-CTA tiles, K-major A and B); the scale factors take 1.5 KiB per stage, so
-// the ring has 3 stages.
+// MX: e4m3 operands with block scales (K-major A and B); the scale factors take 1.5 KiB per stage per CTA, so the
+// ring has 3 stages (one CTA, 49.5 KiB a stage) or 4-5 (CTA pairs, 33.5 KiB a stage).
 template <int EPI, bool PAIR = false, bool MX = false>
 struct EpiCfg {
   static constexpr bool HEAVY = EPI == EPI_SWIGLU || EPI == EPI_SWIGLU_BWD || EPI == EPI_GATED;
   static constexpr int STAGE_BYTES = PAIR ? gemm_cfg::A_BYTES + gemm_cfg::B_BYTES / 2 : gemm_cfg::STAGE_BYTES;
   // SwiGLU backward reads two input tiles per chunk: with pairs it keeps two chunks of inputs in flight (one stage
   // fewer in the mainloop ring)
-  static constexpr int STAGES = MX ? 3 : PAIR ? (EPI == EPI_SWIGLU_BWD ? 4 : (HEAVY ? 5 : 6)) : (HEAVY ? 3 : 4);
+  static constexpr int STAGES = MX ? (PAIR ? (EPI == EPI_GATED ? 4 : 5) : 3)
+                                   : PAIR ? (EPI == EPI_SWIGLU_BWD ? 4 : (HEAVY ? 5 : 6)) : (HEAVY ? 3 : 4);
   static constexpr int SF_BYTES = MX ? STAGES * gemm_cfg::MX_SF_STAGE : 0;
   // one output slot holds every 32x32 output tile of a chunk (bf16 2 KiB, fp32 4 KiB)
   static constexpr int OUT_SLOT = EPI == EPI_SWIGLU ? 6144
@@ -221,9 +222,10 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CUtensorMap tmOut, const __grid_constant__ CUtensorMap tmOut2,
                         const __grid_constant__ CUtensorMap tmRes, const __grid_constant__ CUtensorMap tmAux,
+                        const __grid_constant__ CUtensorMap tmSfa, const __grid_constant__ CUtensorMap tmSfb,
                         const EpiParams p) {
   using namespace gemm_cfg;
-  static_assert(!MX || (!PAIR && AMN == 0 && BMN == 0), "MX tiles: one CTA, K-major A and B");
+  static_assert(!MX || (AMN == 0 && BMN == 0), "MX tiles: K-major A and B");
   using Cfg = EpiCfg<EPI, PAIR, MX>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int SB = Cfg::STAGE_BYTES;
@@ -266,8 +268,8 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
     }
     mbar_init(drain, 1);
     for (int e = 0; e < 16; ++e) mbar_init(&in_bar[e], 1);
-    mbar_init(&ovl[0], 8);
-    mbar_init(&ovl[1], 8);
+    mbar_init(&ovl[0], PAIR ? 16 : 8);  // (a pair: the epilogue warps of both CTAs)
+    mbar_init(&ovl[1], PAIR ? 16 : 8);
     *abort_flag = 0;
     if (PAIR)
       fence_mbarrier_init_cluster();
@@ -277,6 +279,10 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_map(&tmA);
     tma_prefetch_map(&tmB);
+    if (MX && PAIR) {
+      tma_prefetch_map(&tmSfa);
+      tma_prefetch_map(&tmSfb);
+    }
   }
   if (warp >= 2 && lane == 0) {
     tma_prefetch_map(&tmOut);
@@ -316,7 +322,22 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
           uint8_t* sA = smem + stage * SB;
           uint8_t* sB = sA + A_BYTES;
           const int k0 = kb * BKE;
-          if (MX) {
+          if (MX && PAIR) {
+            // this CTA's 128 rows of A and its 128 rows (half) of B, its A scale block and BOTH B scale blocks (the
+            // M = 256 MMA reads all 256 columns' scales from each CTA's tensor memory); the scale blocks come by tensor
+            // TMA so that, like the operand tiles, their bytes count on CTA 0's barrier
+            const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+            const int rb = EPI == EPI_SWIGLU ? (crank == 0 ? nb * 128 : p.half_n + nb * 128) : nb * BN + (int)crank * 128;
+            const int sb0 = EPI == EPI_SWIGLU ? nb : 2 * nb;
+            const int sb1 = EPI == EPI_SWIGLU ? p.half_n / 128 + nb : 2 * nb + 1;
+            uint8_t* sf = sf_smem + stage * MX_SF_STAGE;
+            if (crank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (SB + MX_SF_STAGE));
+            tma_load_3d_pair(&tmA, fb, sA, k0, arow, 0);
+            tma_load_3d_pair(&tmB, fb, sB, k0, rb, 0);
+            tma_load_3d_pair(&tmSfa, fb, sf, 0, kb, arow / 128);
+            tma_load_3d_pair(&tmSfb, fb, sf + 512, 0, kb, sb0);
+            tma_load_3d_pair(&tmSfb, fb, sf + 1024, 0, kb, sb1);
+          } else if (MX) {
             // A rows [arow, +128) and B rows of the tile, 128 e4m3 values of K each, plus their scale-factor blocks
             const int kt = num_k;  // scale-factor blocks per row block
             const int r0 = EPI == EPI_SWIGLU ? nb * 128 : nb * BN;
@@ -401,7 +422,7 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------------------------------ MMA issuer
     if (lane == 0 && crank == 0) {
-      constexpr uint32_t idesc = MX ? idesc_mxf8_f32(BM, BN) : idesc_bf16_f32(BMP, BN, AMN, BMN);
+      constexpr uint32_t idesc = MX ? idesc_mxf8_f32(BMP, BN) : idesc_bf16_f32(BMP, BN, AMN, BMN);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -438,16 +459,26 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
             // this stage's scale factors into TMEM (executed in order with the MMAs before and after), then four
             // K = 32 MMAs, each using scale-factor byte k of every 32-bit TMEM word
             const uint32_t ssf = smem_u32(sf_smem + stage * MX_SF_STAGE);
-            tmem_cp_32x128_x4(tmem_base + MX_SFA_COL, smem_desc_sf(ssf));
-            tmem_cp_32x128_x4(tmem_base + MX_SFB_COL, smem_desc_sf(ssf + 512));
-            tmem_cp_32x128_x4(tmem_base + MX_SFB_COL + 4, smem_desc_sf(ssf + 1024));
+            if (PAIR) {
+              tmem_cp_32x128_x4_pair(tmem_base + MX_SFA_COL, smem_desc_sf(ssf));
+              tmem_cp_32x128_x4_pair(tmem_base + MX_SFB_COL, smem_desc_sf(ssf + 512));
+              tmem_cp_32x128_x4_pair(tmem_base + MX_SFB_COL + 4, smem_desc_sf(ssf + 1024));
+            } else {
+              tmem_cp_32x128_x4(tmem_base + MX_SFA_COL, smem_desc_sf(ssf));
+              tmem_cp_32x128_x4(tmem_base + MX_SFB_COL, smem_desc_sf(ssf + 512));
+              tmem_cp_32x128_x4(tmem_base + MX_SFB_COL + 4, smem_desc_sf(ssf + 1024));
+            }
 #pragma unroll
             for (int k = 0; k < MX_BK / 32; ++k) {
               const uint64_t da = smem_desc_sw128(sa + k * 32, 16, 1024);
               const uint64_t db = smem_desc_sw128(sb + k * 32, 16, 1024);
               const uint32_t id = idesc | ((uint32_t)k << 29) | ((uint32_t)k << 4);
-              umma_mxf8(d_tmem, da, db, id, (tmem_base + MX_SFA_COL) | ((uint32_t)k << 30),
-                        (tmem_base + MX_SFB_COL) | ((uint32_t)k << 30), (kb != kb0 || k != 0) ? 1u : 0u);
+              const uint32_t sfa = (tmem_base + MX_SFA_COL) | ((uint32_t)k << 30);
+              const uint32_t sfb = (tmem_base + MX_SFB_COL) | ((uint32_t)k << 30);
+              if (PAIR)
+                umma_mxf8_pair(d_tmem, da, db, id, sfa, sfb, (kb != kb0 || k != 0) ? 1u : 0u);
+              else
+                umma_mxf8(d_tmem, da, db, id, sfa, sfb, (kb != kb0 || k != 0) ? 1u : 0u);
             }
           }
 #pragma unroll
@@ -555,7 +586,12 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
           // the first chunk (which includes the shared columns) is in registers: the next tile may overwrite them
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&ovl[a]);
+          if (lane == 0) {
+            if (PAIR)
+              mbar_arrive_cluster(mapa_shared(smem_u32(&ovl[a]), 0));
+            else
+              mbar_arrive(&ovl[a]);
+          }
         }
         // per-sample gate / bias values (global, shared by the warp's lanes) before waiting for the inputs
         float gv[32], bv[32];
@@ -813,7 +849,7 @@ static int num_sms() {
 }
 
 struct EpiMaps {
-  CUtensorMap out, out2, res, aux;
+  CUtensorMap out, out2, res, aux, sfa, sfb;
 };
 
 // CTA pairs (cta_group::2) for GEMMs with at least two 128-row blocks; NG_GEMM_PAIR=0 or gemm_set_pair(0) turns them
@@ -860,7 +896,7 @@ static void launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const EpiMaps
   // persistent: one CTA (pair) per SM (pair) that can be resident at once
   const int64_t units = PAIR ? std::min<int64_t>(tiles, max_clusters) : std::min<int64_t>(tiles, num_sms());
   cfg.gridDim = dim3((unsigned)(PAIR ? 2 * units : units));
-  TORCH_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, em.out, em.out2, em.res, em.aux, p) == cudaSuccess,
+  TORCH_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, em.out, em.out2, em.res, em.aux, em.sfa, em.sfb, p) == cudaSuccess,
               "gemm launch failed");
   NG_LAUNCH_CHECK();
 }
@@ -947,7 +983,9 @@ void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   p.sfa = static_cast<const uint8_t*>(g.sfa);
   p.sfb = static_cast<const uint8_t*>(g.sfb);
   p.err = g.err;
-  const bool pair = !g.mx && gemm_use_pair(g.M);
+  // MX on CTA pairs: opt-in (NG_MX_PAIR=1) until validated on the GPU
+  static const bool mx_pair = getenv("NG_MX_PAIR") != nullptr && getenv("NG_MX_PAIR")[0] == '1';
+  const bool pair = gemm_use_pair(g.M) && (!g.mx || mx_pair);
   const int num_m = (g.M + (pair ? 2 * BM : BM) - 1) / (pair ? 2 * BM : BM);
   const int num_n = g.epi == EPI_SWIGLU ? (g.half_n + 127) / 128 : (g.N + BN - 1) / BN;
   const int64_t tiles = (int64_t)g.batch * (g.k_splits > 1 ? g.k_splits : 1) * num_m * num_n;
@@ -960,14 +998,28 @@ void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     const int64_t ocols = g.epi == EPI_SWIGLU ? g.half_n : (g.epi == EPI_SWIGLU_BWD ? 2 * (int64_t)g.half_n : g.N);
     em.out = epi_map_bf16(g.out, ocols, g.M, zb, g.ldo, g.out_bs);
   }
-  em.out2 = em.res = em.aux = em.out;
+  em.out2 = em.res = em.aux = em.sfa = em.sfb = em.out;
+  if (g.mx && pair) {
+    // scale blocks as [row blocks][K / 128][128 x u32]: one 512-byte box per (k-block, row block)
+    const int64_t kt = g.K / MX_BK;
+    em.sfa = make_tmap(g.sfa, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, 128, kt, (g.M + 255) / 256 * 2, 128, kt * 128, 128, 1,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+    em.sfb = make_tmap(g.sfb, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, 128, kt, (b_rows + 255) / 256 * 2, 128, kt * 128, 128,
+                       1, CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
   if (g.epi == EPI_GATED) em.out2 = epi_map_bf16(g.out2, g.N, g.M, 1, g.ldo2, 0);
   if (g.epi == EPI_SWIGLU) em.out2 = epi_map_bf16(g.out2, 2 * (int64_t)g.half_n, g.M, 1, g.ldo2, 0);
   if (g.epi == EPI_GATED || (g.epi == EPI_AXPBY && g.beta != 0.f && g.res != nullptr))
     em.res = epi_map_bf16(g.res, g.N, g.M, g.batch, g.ldr, g.res_bs);
   if (g.epi == EPI_SWIGLU_BWD) em.aux = epi_map_bf16(g.aux, 2 * (int64_t)g.half_n, g.M, 1, g.ld_aux, 0);
   NG_TRACE("[gemm]   maps ok, pair=%d tiles=%lld\n", (int)pair, (long long)tiles);
-  if (g.mx) {
+  if (g.mx && pair) {
+    switch (g.epi) {
+      case EPI_BF16: launch_t<0, 0, EPI_BF16, true, true>(ta, tb, em, p, tiles, stream); break;
+      case EPI_GATED: launch_t<0, 0, EPI_GATED, true, true>(ta, tb, em, p, tiles, stream); break;
+      default: launch_t<0, 0, EPI_SWIGLU, true, true>(ta, tb, em, p, tiles, stream); break;
+    }
+  } else if (g.mx) {
     switch (g.epi) {
       case EPI_BF16: launch_t<0, 0, EPI_BF16, false, true>(ta, tb, em, p, tiles, stream); break;
       case EPI_GATED: launch_t<0, 0, EPI_GATED, false, true>(ta, tb, em, p, tiles, stream); break;

@@ -21,6 +21,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops import gemm as G
+from ..ops import optim as OPT
 
 NS_COEFFS = (3.4445, -4.7750, 2.0315)
 FUSED_PARTS = {"attn.qkv_x.weight": 3, "attn.qkv.weight": 3, "attn.kv_y.weight": 2, "mlp.w12.weight": 2,
@@ -166,9 +167,10 @@ class MuonAdamW(torch.optim.Optimizer):
                 by_shape.setdefault((rows, p.shape[1]), []).append((i, k * rows, (k + 1) * rows))
         outs = []
         for shape, us in by_shape.items():
-            ins = [grads[i][r0:r1].lerp(bufs[i][r0:r1], beta) if group["nesterov"] else bufs[i][r0:r1]
-                   for i, r0, r1 in us]
-            outs.append((shape, us, msign(torch.stack(ins), steps=group["ns_steps"], dtype=self.ns_dtype)))
+            ins = OPT.stack_nesterov([grads[i][r0:r1] for i, r0, r1 in us], [bufs[i][r0:r1] for i, r0, r1 in us],
+                                     beta, group["nesterov"])
+            O = msign(ins, steps=group["ns_steps"], dtype=self.ns_dtype)
+            outs.append((shape, us, O.contiguous() if O.is_cuda else O))
         if self.defer is not None:  # the fused kernel applies W <- W (1 - lr wd) - lr coef O
             d = self.defer
             for shape, us, O in outs:
@@ -178,12 +180,10 @@ class MuonAdamW(torch.optim.Optimizer):
                     d["upd"][base:base + o.numel()].copy_(o.reshape(-1))
             self.deferred = dict(self.deferred or {}, lr_m=lr, wd_m=wd or 0.0)
             return
-        if wd:
-            torch._foreach_mul_(params, 1 - lr * wd)
-        for shape, us, O in outs:
-            coef = -lr * self.update_coef(group, shape)
-            for (i, r0, r1), o in zip(us, O):
-                params[i][r0:r1].add_(o, alpha=coef)
+        # weight decay and W += coef O for every unit in one launch (units partition each matrix's rows)
+        items = [(params[i][r0:r1], o, -lr * self.update_coef(group, shape))
+                 for shape, us, O in outs for (i, r0, r1), o in zip(us, O)]
+        OPT.apply_updates(items, 1 - lr * wd if wd else 1.0)
 
     @torch.no_grad()
     def _muon_step(self, group):
@@ -204,25 +204,31 @@ class MuonAdamW(torch.optim.Optimizer):
             self._plan = self._build_plan(group)
         plan = self._plan
         dev = params[0].device
-        shard = torch.zeros(plan["shard"], dtype=self.ns_dtype, device=dev)
+        single = plan["world"] == 1
+        shard = None if single else torch.zeros(plan["shard"], dtype=self.ns_dtype, device=dev)
+        local = {}  # one rank: each unit's update straight from the Newton-Schulz output
         for shape, us in plan["mine"].items():
-            ins = []
-            for u in us:
-                g, m = grads[u["p"]][u["r0"]:u["r1"]], bufs[u["p"]][u["r0"]:u["r1"]]
-                ins.append(g.lerp(m, beta) if group["nesterov"] else m)
-            O = msign(torch.stack(ins), steps=group["ns_steps"], dtype=self.ns_dtype)
+            ins = OPT.stack_nesterov([grads[u["p"]][u["r0"]:u["r1"]] for u in us],
+                                     [bufs[u["p"]][u["r0"]:u["r1"]] for u in us], beta, group["nesterov"])
+            O = msign(ins, steps=group["ns_steps"], dtype=self.ns_dtype)
+            O = O.contiguous() if O.is_cuda else O
             for u, o in zip(us, O):
-                shard[u["off"]:u["off"] + o.numel()].copy_(o.reshape(-1))
-        if plan["world"] > 1:
+                if single:
+                    local[(u["p"], u["r0"])] = o
+                else:
+                    shard[u["off"]:u["off"] + o.numel()].copy_(o.reshape(-1))
+        if not single:
             full = self.exchange(shard, plan) if self.exchange is not None else self._all_gather(shard, plan)
-        else:
-            full = shard
-        if wd:
-            torch._foreach_mul_(params, 1 - lr * wd)
+        items = []
         for u in plan["units"]:
-            o0 = u["owner"] * plan["shard"] + u["off"]
-            src = full[o0:o0 + math.prod(u["shape"])].view(u["shape"])
-            params[u["p"]][u["r0"]:u["r1"]].add_(src, alpha=-lr * self.update_coef(group, u["shape"]))
+            if single:
+                src = local[(u["p"], u["r0"])]
+            else:
+                o0 = u["owner"] * plan["shard"] + u["off"]
+                src = full[o0:o0 + math.prod(u["shape"])].view(u["shape"])
+            items.append((params[u["p"]][u["r0"]:u["r1"]], src, -lr * self.update_coef(group, u["shape"])))
+        # weight decay and W += coef O for every unit in one launch (units partition each matrix's rows)
+        OPT.apply_updates(items, 1 - lr * wd if wd else 1.0)
 
     @staticmethod
     def _all_gather(shard, plan):

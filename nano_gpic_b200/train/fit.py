@@ -24,6 +24,7 @@ import torch.distributed as dist
 
 from ..config.cli import get_dotted, instantiate, is_spec, resolve, run_dir, strategy_mode, write_config
 from ..data.pil_resize import ResizeBatch
+from ..parallel.rebalance import Rebalancer
 from .callbacks import EMASpec, Warmup
 from .checkpoint import AsyncWriter, build_checkpoint, find_resume, load_into, save_sync
 from .trainer import Trainer
@@ -173,6 +174,10 @@ def fit(cfg):
         reseed(int(cfg.get("seed_everything") or 0), trainer.global_step)
 
     log_every = int(tcfg.get("log_every_n_steps") or 100)
+    # sample rebalancing over ranks by caption length (reference levers E / E2): trainer.rebalance or
+    # GPIC_MFU_REBALANCE = 1 (device exchange) or 2 (host exchange before the copy)
+    rebal_mode = int(get_dotted(cfg, "trainer.rebalance", os.environ.get("GPIC_MFU_REBALANCE", "0")) or 0)
+    rebal = Rebalancer() if rebal_mode and dist.is_initialized() and dist.get_world_size() > 1 else None
     t_log, n_log = time.perf_counter(), 0
     try:
         while trainer.global_step < max_steps and not ctx.stop:
@@ -189,6 +194,10 @@ def fit(cfg):
                         y, mask = obj.caption_dropout(y.to(dev), mask, uncond.to(dev))
                 else:
                     y, mask = meta["text_emb"], meta["text_mask"]
+                if rebal is not None and mask is not None:
+                    if rebal_mode == 1 or img.is_cuda:  # lever E: exchange on the device (NCCL)
+                        img, y, mask = img.to(dev), y.to(dev), mask.to(dev)
+                    img, y, mask = rebal(img, y, mask)  # host tensors (lever E2): exchange over gloo
                 micros.append((img, y, mask))
             for c in callbacks:
                 c.on_step_start(ctx, step)
