@@ -67,7 +67,8 @@ void p2p_reduce_scatter(const at::Tensor& grad, const at::Tensor& recv, const st
 void p2p_bcast_bf16(const at::Tensor& master, const std::vector<int64_t>& peer_w16, const std::vector<int64_t>& peer_flags,
                     const at::Tensor& counters, int64_t rank, int64_t nb, int64_t b, int64_t off, int64_t n,
                     int64_t epoch);
-void p2p_wait(const at::Tensor& flags, int64_t world, int64_t rank, int64_t nb, int64_t b0, int64_t b1, int64_t epoch);
+void p2p_wait(const at::Tensor& flags, int64_t world, int64_t rank, int64_t nb, int64_t b0, int64_t b1, int64_t epoch,
+              int64_t budget_ns);
 void p2p_fused_apply(const at::Tensor& table_t, int64_t nent, const at::Tensor& p, const at::Tensor& g,
                      const at::Tensor& m1, const at::Tensor& m2, const at::Tensor& upd,
                      const c10::optional<at::Tensor>& ema, const std::vector<int64_t>& peer_w16,
@@ -101,7 +102,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("p2p_bcast_bf16", &ng::p2p_bcast_bf16, "owner's fp32 segment -> bf16 in every rank's weights, with flags");
   m.def("p2p_fused_apply", &ng::p2p_fused_apply,
         "sharded AdamW / Muon apply + EMA of one bucket's owned parameters, bf16 weights into every rank, flags");
-  m.def("p2p_wait", &ng::p2p_wait, "wait (bounded) for every peer's weight flags of a bucket range");
+  m.def("p2p_wait", &ng::p2p_wait, "wait (bounded) for every peer's weight flags of a bucket range", py::arg("flags"),
+        py::arg("world"), py::arg("rank"), py::arg("nb"), py::arg("b0"), py::arg("b1"), py::arg("epoch"),
+        py::arg("budget_ns") = 0);
   m.def("resize_passes", &ng::resize_passes, "Pillow-exact bicubic crop passes for a packed batch");
   m.def("muon_gather", &ng::muon_gather, "stacked Nesterov inputs of every Muon unit from a pointer table");
   m.def("muon_apply", &ng::muon_apply, "param = param * decay + coef * update for every Muon unit from a pointer table");

@@ -40,13 +40,14 @@ __device__ __forceinline__ void st_release_sys(long long* p, long long v) {
   asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-// waits (bounded) until *flag >= epoch; returns false and raises an error on timeout
-__device__ bool wait_flag(const long long* flag, long long epoch, int* err) {
+// waits (bounded by budget_ns) until *flag >= epoch; returns false and raises an error on timeout
+__device__ bool wait_flag(const long long* flag, long long epoch, int* err,
+                          unsigned long long budget_ns = NG_PEER_WAIT_NS) {
   if (ld_acquire_sys(flag) >= epoch) return true;
   const uint64_t t0 = globaltimer_ns();
   uint32_t n = 0;
   while (ld_acquire_sys(flag) < epoch) {
-    if ((++n & 1023u) == 0 && globaltimer_ns() - t0 > NG_PEER_WAIT_NS) {
+    if ((++n & 1023u) == 0 && globaltimer_ns() - t0 > budget_ns) {
       raise_error(err, kErrPeerFlag);
       return false;
     }
@@ -186,11 +187,11 @@ __global__ void __launch_bounds__(256) p2p_bcast_bf16_kernel(const float* __rest
 
 // waits (one thread) until flags[r][b] >= epoch for every r != rank and every bucket b in [b0, b1)
 __global__ void p2p_wait_kernel(const long long* __restrict__ flags, int W, int rank, int nb, int b0, int b1,
-                                long long epoch, int* err) {
+                                long long epoch, unsigned long long budget_ns, int* err) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   for (int b = b0; b < b1; ++b)
     for (int r = 0; r < W; ++r)
-      if (r != rank && !wait_flag(flags + (int64_t)r * nb + b, epoch, err)) return;
+      if (r != rank && !wait_flag(flags + (int64_t)r * nb + b, epoch, err, budget_ns)) return;
 }
 
 // Fused optimizer apply of one bucket's owned parameters, then the bf16 weights to every rank (the sharded update
@@ -392,12 +393,13 @@ void p2p_fused_apply(const at::Tensor& table_t, int64_t nent, const at::Tensor& 
   NG_LAUNCH_CHECK();
 }
 
+// budget_ns <= 0: the default peer budget (NG_PEER_WAIT_NS)
 void p2p_wait(const at::Tensor& flags, int64_t world, int64_t rank, int64_t nb, int64_t b0, int64_t b1,
-              int64_t epoch) {
+              int64_t epoch, int64_t budget_ns) {
   const at::cuda::CUDAGuard guard(flags.device());
   p2p_wait_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const long long*>(flags.data_ptr<int64_t>()), (int)world, (int)rank, (int)nb, (int)b0, (int)b1,
-      (long long)epoch, status_word());
+      (long long)epoch, budget_ns > 0 ? (unsigned long long)budget_ns : NG_PEER_WAIT_NS, status_word());
   NG_LAUNCH_CHECK();
 }
 
