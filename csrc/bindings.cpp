@@ -18,6 +18,9 @@ void rms_mod_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& rs
                  const c10::optional<at::Tensor>& scale, const c10::optional<at::Tensor>& dres, const at::Tensor& dx,
                  const c10::optional<at::Tensor>& dw, const c10::optional<at::Tensor>& dshift,
                  const c10::optional<at::Tensor>& dscale, int64_t rpg);
+void rms_mod_fwd_mx(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& shift,
+                    const c10::optional<at::Tensor>& scale, const at::Tensor& h, const at::Tensor& rstd,
+                    const at::Tensor& q, const at::Tensor& sf, int64_t rpg, double eps);
 void layernorm_fwd(const at::Tensor& x, const at::Tensor& h, const at::Tensor& mu, const at::Tensor& rstd, double eps);
 void layernorm_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& mu, const at::Tensor& rstd,
                    const at::Tensor& dx);
@@ -108,6 +111,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("resize_passes", &ng::resize_passes, "Pillow-exact bicubic crop passes for a packed batch");
   m.def("muon_gather", &ng::muon_gather, "stacked Nesterov inputs of every Muon unit from a pointer table");
   m.def("muon_apply", &ng::muon_apply, "param = param * decay + coef * update for every Muon unit from a pointer table");
+  m.def("rms_mod_fwd_mx", &ng::rms_mod_fwd_mx, "RMSNorm + adaLN modulate forward that also writes h in MXFP8");
   m.def("mx_quant", &ng::mx_quant, "bf16 [rows, K] -> MXFP8 (e4m3 values, E8M0 scale blocks)");
   m.def("gemm_mx", &ng::gemm_mx_torch, "MXFP8 block-scaled tcgen05 GEMM with the bf16 / gated / SwiGLU epilogues");
   m.def("gemm_set_pair", &ng::gemm_set_pair, "use CTA-pair (cta_group::2) GEMM tiles when M >= 256 (default on)");

@@ -5,6 +5,7 @@
 #pragma once
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -377,6 +378,30 @@ __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
+}
+
+// ---------------------------------------------------------------------------------------------------- MXFP8 casts
+// Block scale of OCP MXFP8 with e4m3 values: e = ceil(log2(amax / 448)), so amax / 2^e <= 448 and nothing saturates;
+// 0 for an all-zero block, clamped to the E8M0 range. Read off the bits of the quotient: its exponent, plus one unless
+// it is a power of two. The stored scale byte is e + 127.
+__device__ __forceinline__ int mx_scale_exp(float amax) {
+  if (!(amax > 0.f)) return 0;
+  const uint32_t b = __float_as_uint(__fdiv_rn(amax, 448.f));
+  const int E = (int)((b >> 23) & 0xFFu);
+  const int e = E == 0 ? -127 : E - 127 + ((b & 0x7FFFFFu) != 0u ? 1 : 0);
+  return max(-127, min(127, e));
+}
+
+// four floats -> four e4m3 bytes (round to nearest even, saturating), the first in the lowest byte
+__device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
+  const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
+  return (lo & 0xFFFFu) | (hi << 16);
+}
+
+// byte offset of the scale of row r, 32-column block kb in the 128-row x 4-scale blocks (kt blocks of 128 columns)
+__device__ __forceinline__ int64_t mx_sf_offset(int r, int kb, int kt) {
+  return ((int64_t)(r >> 7) * kt + (kb >> 2)) * 512 + (r & 31) * 16 + ((r >> 5) & 3) * 4 + (kb & 3);
 }
 
 }  // namespace ng

@@ -22,12 +22,6 @@
 
 namespace ng {
 
-__device__ __forceinline__ uint32_t e4m3x4(float a, float b, float c, float d) {
-  const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
-  const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
-  return (lo & 0xFFFFu) | (hi << 16);
-}
-
 // One thread per (row, 32-column block); four consecutive threads hold the four scales of one 32-bit word of the
 // scale layout (K is a multiple of 128, so they sit in the same warp at lanes 4j .. 4j+3).
 __global__ void mx_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int rows, int rows_pad, int K,
@@ -54,14 +48,7 @@ __global__ void mx_quant_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx
     float amax = 0.f;
 #pragma unroll
     for (int j = 0; j < 32; ++j) amax = fmaxf(amax, fabsf(v[j]));
-    int e = 0;
-    if (amax > 0.f) {
-      // ceil(log2(amax / 448)) from the bits of the quotient: its exponent, plus one unless it is a power of two
-      const uint32_t b = __float_as_uint(__fdiv_rn(amax, 448.f));
-      const int E = (int)((b >> 23) & 0xFFu);
-      e = E == 0 ? -127 : E - 127 + ((b & 0x7FFFFFu) != 0u ? 1 : 0);
-      e = max(-127, min(127, e));
-    }
+    const int e = mx_scale_exp(amax);
     byte = (uint32_t)(e + 127);
     const float inv = ldexpf(1.f, -e);
     uint4* dst = reinterpret_cast<uint4*>(q + (int64_t)r * K + kb * 32);

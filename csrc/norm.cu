@@ -53,12 +53,13 @@ __device__ __forceinline__ void load_w8(const float* w, int c, float (&f)[8]) {
 
 constexpr int MAXV = 8;  // 16-byte vectors per lane: C <= 32 * 8 * 8 = 2048
 
-template <bool MOD>
+template <bool MOD, bool MXO = false>
 __global__ void __launch_bounds__(256) rms_mod_fwd_kernel(const bf16* __restrict__ x, const float* __restrict__ w,
                                                           const bf16* __restrict__ shift, int64_t ld_sh,
                                                           const bf16* __restrict__ scale, int64_t ld_sc,
                                                           bf16* __restrict__ h, float* __restrict__ rstd, int M, int C,
-                                                          int rpg, float eps) {
+                                                          int rpg, float eps, uint8_t* __restrict__ q = nullptr,
+                                                          uint8_t* __restrict__ sf = nullptr) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
   if (row >= M) return;
@@ -85,6 +86,7 @@ __global__ void __launch_bounds__(256) rms_mod_fwd_kernel(const bf16* __restrict
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     const int v = lane + 32 * i;
+    uint4 pk = make_uint4(0u, 0u, 0u, 0u);
     if (v < nv) {
       float f[8], wf[8];
       unpack8(xv[i], f);
@@ -99,7 +101,30 @@ __global__ void __launch_bounds__(256) rms_mod_fwd_kernel(const bf16* __restrict
 #pragma unroll
         for (int j = 0; j < 8; ++j) f[j] = wf[j] * (f[j] * r);
       }
-      hr[v] = pack8(f);
+      pk = pack8(f);
+      hr[v] = pk;
+    }
+    if (MXO) {
+      // MXFP8 copy of h (the input of the next MX GEMM): a 32-value block is the 8-value vectors of 4 adjacent lanes;
+      // the values are the bf16-rounded h, so q and the scales equal a separate quantization of h
+      float hv[8];
+      float am = 0.f;
+      if (v < nv) {
+        unpack8(pk, hv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) am = fmaxf(am, fabsf(hv[j]));
+      }
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+      am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+      if (v < nv) {
+        const int e = mx_scale_exp(am);
+        const float inv = ldexpf(1.f, -e);
+        uint2 o;
+        o.x = e4m3x4(hv[0] * inv, hv[1] * inv, hv[2] * inv, hv[3] * inv);
+        o.y = e4m3x4(hv[4] * inv, hv[5] * inv, hv[6] * inv, hv[7] * inv);
+        *reinterpret_cast<uint2*>(q + (int64_t)row * C + v * 8) = o;
+        if ((v & 3) == 0) sf[mx_sf_offset(row, v >> 2, C / 128)] = (uint8_t)(e + 127);
+      }
     }
   }
 }
@@ -485,6 +510,36 @@ void rms_mod_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<a
     rms_mod_fwd_kernel<false><<<grid, 256, 0, s>>>(reinterpret_cast<const bf16*>(x.data_ptr()), w.data_ptr<float>(),
                                                    nullptr, 0, nullptr, 0, reinterpret_cast<bf16*>(h.data_ptr()),
                                                    rstd.data_ptr<float>(), M, C, (int)rpg, (float)eps);
+  NG_LAUNCH_CHECK();
+}
+
+// rms_mod_fwd that also writes h's MXFP8 copy: q [M, C] e4m3, sf the scale blocks of csrc/mx.cu's layout (rows padded
+// to a multiple of 256; padding rows are left as the caller filled them). C a multiple of 128.
+void rms_mod_fwd_mx(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& shift,
+                    const c10::optional<at::Tensor>& scale, const at::Tensor& h, const at::Tensor& rstd,
+                    const at::Tensor& q, const at::Tensor& sf, int64_t rpg, double eps) {
+  check_rows(x);
+  TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous(), "fp32 weight expected");
+  const int M = x.size(0), C = x.size(1);
+  TORCH_CHECK(C % 128 == 0, "rms_mod_fwd_mx: C must be a multiple of 128");
+  TORCH_CHECK(q.scalar_type() == at::kByte && q.is_contiguous() && q.numel() == (int64_t)M * C, "q: [M, C] uint8");
+  TORCH_CHECK(sf.scalar_type() == at::kByte && sf.is_contiguous() &&
+                  sf.numel() >= ((int64_t)M + 255) / 256 * 256 * (C / 32),
+              "sf: scale blocks of [rows padded to 256, C / 32]");
+  const at::cuda::CUDAGuard guard(x.device());
+  auto s = at::cuda::getCurrentCUDAStream();
+  const bool mod = scale.has_value() && scale->defined();
+  dim3 grid((M + 7) / 8);
+  if (mod)
+    rms_mod_fwd_kernel<true, true><<<grid, 256, 0, s>>>(
+        reinterpret_cast<const bf16*>(x.data_ptr()), w.data_ptr<float>(), bptr(shift), ld_of(shift), bptr(scale),
+        ld_of(scale), reinterpret_cast<bf16*>(h.data_ptr()), rstd.data_ptr<float>(), M, C, (int)rpg, (float)eps,
+        q.data_ptr<uint8_t>(), sf.data_ptr<uint8_t>());
+  else
+    rms_mod_fwd_kernel<false, true><<<grid, 256, 0, s>>>(
+        reinterpret_cast<const bf16*>(x.data_ptr()), w.data_ptr<float>(), nullptr, 0, nullptr, 0,
+        reinterpret_cast<bf16*>(h.data_ptr()), rstd.data_ptr<float>(), M, C, (int)rpg, (float)eps,
+        q.data_ptr<uint8_t>(), sf.data_ptr<uint8_t>());
   NG_LAUNCH_CHECK();
 }
 

@@ -266,8 +266,12 @@ class _ImageBlockFn(torch.autograd.Function):
         # fp8 == "mx": the four big forward GEMMs read MXFP8 operands (reference fp8_native.py, phase 1); the saved
         # activations and the whole backward stay bf16
         mxw = _mx_weights(blk) if getattr(blk, "_fp8", False) else None
-        h1, r1 = NR.rms_mod_fwd(x, f32(n1.weight), mod[:, 0:C], mod[:, C:2 * C], L, n1.variance_epsilon)
-        qkv = G.linear(h1, w16(a.qkv_x)) if mxw is None else MXO.linear(MXO.quant(h1), mxw["qkv_x"])
+        if mxw is None:
+            h1, r1 = NR.rms_mod_fwd(x, f32(n1.weight), mod[:, 0:C], mod[:, C:2 * C], L, n1.variance_epsilon)
+            qkv = G.linear(h1, w16(a.qkv_x))
+        else:  # the norm kernel also writes h1's MXFP8 copy
+            h1, r1, h1q = NR.rms_mod_fwd_mx(x, f32(n1.weight), mod[:, 0:C], mod[:, C:2 * C], L, n1.variance_epsilon)
+            qkv = MXO.linear(h1q, mxw["qkv_x"])
         kvy = G.linear(yt, w16(a.kv_y))
         q, rq = QK.qk_norm_fwd(qkv[:, 0:C], f32(a.q_norm.weight), cos, sin, L, a.q_norm.variance_epsilon)
         kx, rkx = QK.qk_norm_fwd(qkv[:, C:2 * C], f32(a.k_norm.weight), cos, sin, L, a.k_norm.variance_epsilon)
@@ -277,12 +281,15 @@ class _ImageBlockFn(torch.autograd.Function):
             x2, ya = G.linear_gated_residual(o, w16(a.proj), f32(a.proj.bias), x, mod[:, 2 * C:3 * C], L)
         else:
             x2, ya = MXO.linear_gated_residual(MXO.quant(o), mxw["proj"], f32(a.proj.bias), x, mod[:, 2 * C:3 * C], L)
-        h2, r2 = NR.rms_mod_fwd(x2, f32(n2.weight), mod[:, 3 * C:4 * C], mod[:, 4 * C:5 * C], L, n2.variance_epsilon)
         if mxw is None:
+            h2, r2 = NR.rms_mod_fwd(x2, f32(n2.weight), mod[:, 3 * C:4 * C], mod[:, 4 * C:5 * C], L,
+                                    n2.variance_epsilon)
             act, pre = G.swiglu_linear(h2, w16(blk.mlp.w12))
             x3, ym = G.linear_gated_residual(act, w16(blk.mlp.w3), None, x2, mod[:, 5 * C:6 * C], L)
         else:
-            act, pre = MXO.swiglu_linear(MXO.quant(h2), mxw["w12"])
+            h2, r2, h2q = NR.rms_mod_fwd_mx(x2, f32(n2.weight), mod[:, 3 * C:4 * C], mod[:, 4 * C:5 * C], L,
+                                            n2.variance_epsilon)
+            act, pre = MXO.swiglu_linear(h2q, mxw["w12"])
             x3, ym = MXO.linear_gated_residual(MXO.quant(act), mxw["w3"], None, x2, mod[:, 5 * C:6 * C], L)
         return x3, (h1, r1, qkv, kvy, q, rq, kx, rkx, ky, rky, o, lse, x2, ya, h2, r2, act, pre, ym)
 

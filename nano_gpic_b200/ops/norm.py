@@ -35,6 +35,26 @@ def rms_mod_fwd(x, w, shift=None, scale=None, rows_per_group=1, eps=1e-6):
     return h, rstd
 
 
+def rms_mod_fwd_mx(x, w, shift=None, scale=None, rows_per_group=1, eps=1e-6):
+    """rms_mod_fwd that also returns h's MXFP8 copy (ops.mx.MX) from the same kernel: (h, rstd, hq). C % 128 == 0."""
+    from . import mx
+    if not x.is_cuda:
+        h, rstd = rms_mod_fwd(x, w, shift, scale, rows_per_group, eps)
+        return h, rstd, mx.quant(h)
+    M, C = x.shape
+    h = torch.empty_like(x)
+    rstd = torch.empty(M, device=x.device, dtype=torch.float32)
+    q = torch.empty(M, C, device=x.device, dtype=torch.uint8)
+    rp = mx.rows_pad(M)
+    shape = (rp // 128, C // 128, 512)
+    if rp == M:
+        sf = torch.empty(shape, device=x.device, dtype=torch.uint8)
+    else:  # rows past M (up to the 256-row padding) keep scale 1
+        sf = torch.full(shape, 127, device=x.device, dtype=torch.uint8)
+    ext().rms_mod_fwd_mx(x, w, shift, scale, h, rstd, q, sf, rows_per_group, eps)
+    return h, rstd, mx.MX(q, sf)
+
+
 def rms_mod_bwd(dh, x, rstd, w, scale=None, rows_per_group=1, dres=None, dw_acc=None, dshift=None, dscale=None):
     """Backward of rms_mod_fwd. Returns dx [M, C] bf16 (plus dres when given).
     dw_acc [C] fp32: d_w is added into it. dshift/dscale [G, C] fp32 views: overwritten (None: not computed)."""

@@ -117,3 +117,21 @@ def test_model_fp8_close_to_bf16():
     assert rel < 0.05, rel
     relg = (grads[1] - grads[0]).norm() / grads[0].norm()
     assert relg < 0.1, relg
+
+
+@pytest.mark.parametrize("M,C,mod", [(512, 1024, True), (300, 384, True), (256, 768, False)])
+def test_norm_with_mx_output_equals_separate_quant(M, C, mod):
+    """The norm kernel's MXFP8 copy of h equals quantizing its bf16 output separately, byte for byte."""
+    from nano_gpic_b200.ops import mx, norm
+    torch.manual_seed(3)
+    x = torch.randn(M, C, device="cuda").to(torch.bfloat16)
+    w = torch.rand(C, device="cuda") + 0.5
+    G = (M + 127) // 128
+    sh = (torch.randn(G, C, device="cuda") * 0.1).to(torch.bfloat16) if mod else None
+    sc = (torch.randn(G, C, device="cuda") * 0.1).to(torch.bfloat16) if mod else None
+    h, r = norm.rms_mod_fwd(x, w, sh, sc, 128)
+    h2, r2, hq = norm.rms_mod_fwd_mx(x, w, sh, sc, 128)
+    ref = mx.quant(h)
+    assert torch.equal(h, h2) and torch.equal(r, r2)
+    assert torch.equal(hq.q, ref.q)
+    assert torch.equal(hq.sf, ref.sf)
