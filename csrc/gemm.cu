@@ -95,6 +95,8 @@ struct EpiParams {
   int kb_per_split;  // k-blocks (of BK) per split
   const uint8_t* sfa;  // MX: scale-factor blocks of A: [ceil(M / 128) row blocks][K / 128][512 bytes]
   const uint8_t* sfb;  // MX: scale-factor blocks of B (row blocks of the B tensor's rows)
+  uint8_t* act_q;      // MX SwiGLU (optional): act [M, half_n] in e4m3, and its scale blocks
+  uint8_t* act_sf;
   int* err;
 };
 
@@ -661,6 +663,30 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
             st_tile_bf16(obuf, lane, v);
             st_tile_bf16(obuf + 2048, lane, x2);
             st_tile_bf16(obuf + 4096, lane, h);
+            if constexpr (MX) {
+              // the MXFP8 copy of act for the next MX GEMM: this lane's 32 columns of its row are one scale block
+              if (p.act_q != nullptr && row < p.M) {
+                float am = 0.f;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                  h[j] = round_bf16(h[j]);
+                  am = fmaxf(am, fabsf(h[j]));
+                }
+                const int e = mx_scale_exp(am);
+                const float inv = ldexpf(1.f, -e);
+                uint4* dq = reinterpret_cast<uint4*>(p.act_q + (int64_t)row * p.half_n + col);
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                  uint4 o;
+                  o.x = e4m3x4(h[16 * j] * inv, h[16 * j + 1] * inv, h[16 * j + 2] * inv, h[16 * j + 3] * inv);
+                  o.y = e4m3x4(h[16 * j + 4] * inv, h[16 * j + 5] * inv, h[16 * j + 6] * inv, h[16 * j + 7] * inv);
+                  o.z = e4m3x4(h[16 * j + 8] * inv, h[16 * j + 9] * inv, h[16 * j + 10] * inv, h[16 * j + 11] * inv);
+                  o.w = e4m3x4(h[16 * j + 12] * inv, h[16 * j + 13] * inv, h[16 * j + 14] * inv, h[16 * j + 15] * inv);
+                  dq[j] = o;
+                }
+                p.act_sf[mx_sf_offset(row, col / 32, p.half_n / 128)] = (uint8_t)(e + 127);
+              }
+            }
           } else if (EPI == EPI_SWIGLU_BWD) {
             // v = d(act) for act columns [col, col+32); ibuf = the saved pre-activation tiles [x1 | x2]
             float x1[32], x2[32], d2[32];
@@ -982,6 +1008,8 @@ void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   p.kb_per_split = g.kb_per_split;
   p.sfa = static_cast<const uint8_t*>(g.sfa);
   p.sfb = static_cast<const uint8_t*>(g.sfb);
+  p.act_q = static_cast<uint8_t*>(g.act_q);
+  p.act_sf = static_cast<uint8_t*>(g.act_sf);
   p.err = g.err;
   // MX on CTA pairs: opt-in (NG_MX_PAIR=1) until validated on the GPU
   static const bool mx_pair = getenv("NG_MX_PAIR") != nullptr && getenv("NG_MX_PAIR")[0] == '1';

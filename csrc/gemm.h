@@ -51,6 +51,9 @@ struct GemmArgs {
   int mx = 0;
   const void* sfa = nullptr;
   const void* sfb = nullptr;
+  // MX SwiGLU only (optional): also write act in MXFP8 (e4m3 [M, half_n] row-major, scale blocks as above)
+  void* act_q = nullptr;
+  void* act_sf = nullptr;
   int* err = nullptr;
 };
 

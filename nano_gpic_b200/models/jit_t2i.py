@@ -289,8 +289,8 @@ class _ImageBlockFn(torch.autograd.Function):
         else:
             h2, r2, h2q = NR.rms_mod_fwd_mx(x2, f32(n2.weight), mod[:, 3 * C:4 * C], mod[:, 4 * C:5 * C], L,
                                             n2.variance_epsilon)
-            act, pre = MXO.swiglu_linear(h2q, mxw["w12"])
-            x3, ym = MXO.linear_gated_residual(MXO.quant(act), mxw["w3"], None, x2, mod[:, 5 * C:6 * C], L)
+            act, pre, actq = MXO.swiglu_linear(h2q, mxw["w12"], quant_act=True)  # act's MX copy from the epilogue
+            x3, ym = MXO.linear_gated_residual(actq, mxw["w3"], None, x2, mod[:, 5 * C:6 * C], L)
         return x3, (h1, r1, qkv, kvy, q, rq, kx, rkx, ky, rky, o, lse, x2, ya, h2, r2, act, pre, ym)
 
     @staticmethod

@@ -79,7 +79,7 @@ def linear(xq, wq, bias=None):
         return G.linear(xq.dequant(), wq.dequant(), bias)
     M, N = xq.shape[0], wq.shape[0]
     out = torch.empty(M, N, device=xq.q.device, dtype=torch.bfloat16)
-    ext().gemm_mx(xq.q, xq.sf, wq.q, wq.sf, out, G.EPI_BF16, N, None, bias, None, None, 1, 0)
+    ext().gemm_mx(xq.q, xq.sf, wq.q, wq.sf, out, G.EPI_BF16, N, None, bias, None, None, 1, 0, None, None)
     return out
 
 
@@ -90,17 +90,31 @@ def linear_gated_residual(xq, wq, bias, res, gate, rows_per_group):
     M, N = xq.shape[0], wq.shape[0]
     out = torch.empty(M, N, device=xq.q.device, dtype=torch.bfloat16)
     y = torch.empty(M, N, device=xq.q.device, dtype=torch.bfloat16)
-    ext().gemm_mx(xq.q, xq.sf, wq.q, wq.sf, out, G.EPI_GATED, N, y, bias, res, gate, rows_per_group, 0)
+    ext().gemm_mx(xq.q, xq.sf, wq.q, wq.sf, out, G.EPI_GATED, N, y, bias, res, gate, rows_per_group, 0, None, None)
     return out, y
 
 
-def swiglu_linear(xq, w12q):
-    """pre = bf16(x W12^T) [M, 2H]; act = bf16(silu(pre[:, :H]) * pre[:, H:]). Returns (act, pre)."""
+def empty_like_rows(rows, K, device):
+    """An MX buffer for a [rows, K] matrix written by a kernel: scale rows past `rows` (padding) hold scale 1."""
+    rp = rows_pad(rows)
+    q = torch.empty(rows, K, device=device, dtype=torch.uint8)
+    shape = (rp // 128, K // 128, 512)
+    sf = (torch.empty(shape, device=device, dtype=torch.uint8) if rp == rows
+          else torch.full(shape, 127, device=device, dtype=torch.uint8))
+    return MX(q, sf)
+
+
+def swiglu_linear(xq, w12q, quant_act=False):
+    """pre = bf16(x W12^T) [M, 2H]; act = bf16(silu(pre[:, :H]) * pre[:, H:]). Returns (act, pre), or with quant_act
+    (act, pre, actq): actq is act in MXFP8, written by the GEMM's epilogue (equal to quant(act))."""
     if not xq.q.is_cuda:
-        return G.swiglu_linear(xq.dequant(), w12q.dequant())
+        act, pre = G.swiglu_linear(xq.dequant(), w12q.dequant())
+        return (act, pre, quant(act)) if quant_act else (act, pre)
     M, H2 = xq.shape[0], w12q.shape[0]
     H = H2 // 2
     act = torch.empty(M, H, device=xq.q.device, dtype=torch.bfloat16)
     pre = torch.empty(M, H2, device=xq.q.device, dtype=torch.bfloat16)
-    ext().gemm_mx(xq.q, xq.sf, w12q.q, w12q.sf, act, G.EPI_SWIGLU, H2, pre, None, None, None, 1, H)
-    return act, pre
+    aq = empty_like_rows(M, H, xq.q.device) if quant_act else None
+    ext().gemm_mx(xq.q, xq.sf, w12q.q, w12q.sf, act, G.EPI_SWIGLU, H2, pre, None, None, None, 1, H,
+                  aq.q if aq is not None else None, aq.sf if aq is not None else None)
+    return (act, pre, aq) if quant_act else (act, pre)

@@ -135,3 +135,16 @@ def test_norm_with_mx_output_equals_separate_quant(M, C, mod):
     assert torch.equal(h, h2) and torch.equal(r, r2)
     assert torch.equal(hq.q, ref.q)
     assert torch.equal(hq.sf, ref.sf)
+
+
+@pytest.mark.parametrize("M,H,K", [(4096, 4096, 1024), (300, 384, 256)])
+def test_mx_swiglu_act_output_equals_separate_quant(M, H, K):
+    """The SwiGLU epilogue's MXFP8 copy of act equals quantizing its bf16 act separately, byte for byte."""
+    from nano_gpic_b200.ops import mx
+    xq, wq, _, _ = _operands(M, 2 * H, K, seed=4)
+    act, pre, aq = mx.swiglu_linear(xq, wq, quant_act=True)
+    act2, pre2 = mx.swiglu_linear(xq, wq)
+    assert torch.equal(act, act2) and torch.equal(pre, pre2)
+    ref = mx.quant(act)
+    assert torch.equal(aq.q, ref.q)
+    assert torch.equal(aq.sf, ref.sf)
