@@ -1,7 +1,7 @@
 """Runs one kernel on one shape a few times: the target of ncu captures (small cases that end by themselves).
 
     python -m nano_gpic_b200.tools.kernel_case --case swiglu_fwd --m 8192 --d 1024 [--reps 3]
-cases: linear_fwd, linear_dgrad, linear_wgrad, swiglu_fwd, swiglu_bwd, gated, attn_fwd, attn_bwd, rms_bwd
+cases: linear_fwd, linear_dgrad, linear_wgrad, swiglu_fwd, swiglu_bwd, gated, attn_fwd, attn_bwd, rms_bwd, gate_bwd
 """
 import argparse
 
@@ -16,6 +16,8 @@ def main():
     ap.add_argument("--t", type=int, default=128, help="caption length (attention cases)")
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--impl", default=None, help="attention implementation (tc, tc1, mma)")
+    ap.add_argument("--time", action="store_true", help="also print the mean time per call (CUDA events, after the "
+                                                          "--reps warm-up calls, 20 timed calls)")
     a = ap.parse_args()
     from nano_gpic_b200.ops import attention as A, gemm as G, norm as NR, status
     torch.manual_seed(0)
@@ -54,7 +56,14 @@ def main():
         mod = r(M // 256, 6 * d)
         h, rstd = NR.rms_mod_fwd(x, w, mod[:, :d], mod[:, d:2 * d], 256)
         dw = torch.zeros(d, device="cuda")
-        fn = lambda: NR.rms_mod_bwd(dh, x, rstd, w, mod[:, d:2 * d], 256, dres=dh, dw_acc=dw)
+        fn = lambda: NR.rms_mod_bwd(dh, x, rstd, w, mod[:, d:2 * d], 256, dres=dh, dw_acc=dw,
+                                    dshift=dsh[:, :d], dscale=dsh[:, d:])
+        dsh = torch.empty(M // 256, 2 * d, device="cuda")
+    elif a.case == "gate_bwd":
+        from nano_gpic_b200.ops import elementwise as E
+        dout, y, mod = r(M, d), r(M, d), r(M // 256, 6 * d)
+        dg = torch.empty(M // 256, d, device="cuda")
+        fn = lambda: E.gate_bwd(dout, y, mod[:, 5 * d:], 256, dgate=dg)
     else:
         raise SystemExit(f"unknown case {a.case}")
     for _ in range(a.reps):
@@ -62,6 +71,14 @@ def main():
     torch.cuda.synchronize()
     status.check()
     print(f"{a.case} ok", flush=True)
+    if a.time:
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(20):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        print(f"{a.case} m={M} d={d}: {s.elapsed_time(e) / 20 * 1000:.1f} us per call", flush=True)
 
 
 if __name__ == "__main__":
