@@ -228,7 +228,7 @@ __global__ void __launch_bounds__(256) rms_mod_bwd_kernel(const bf16* __restrict
 // at once. Phase 2: the column sums for d_shift, d_scale, d_w over the chunk's rows (dh and x again, now from L2), all
 // 256 threads busy: G2 groups of C / 8 threads take alternate rows and are added up in shared memory.
 template <bool MOD, int VPL>
-__global__ void __launch_bounds__(256) rms_mod_bwd_kernel2(const bf16* __restrict__ dh, const bf16* __restrict__ x,
+__global__ void __launch_bounds__(256, VPL <= 4 ? 2 : 1) rms_mod_bwd_kernel2(const bf16* __restrict__ dh, const bf16* __restrict__ x,
                                                            const float* __restrict__ rstd, const float* __restrict__ w,
                                                            const bf16* __restrict__ scale, int64_t ld_sc,
                                                            const bf16* __restrict__ dres, bf16* __restrict__ dx,
@@ -246,13 +246,12 @@ __global__ void __launch_bounds__(256) rms_mod_bwd_kernel2(const bf16* __restric
   for (int rr = warp; rr < nrows; rr += 8) {
     const int64_t row = r0 + rr;
     const float r = rstd[row];
-    uint4 dv[VPL], xv[VPL], rv[VPL];
+    uint4 dv[VPL], xv[VPL];
 #pragma unroll
     for (int k = 0; k < VPL; ++k) {
       const int v = lane + 32 * k;
       dv[k] = reinterpret_cast<const uint4*>(dh + row * C)[v];
       xv[k] = reinterpret_cast<const uint4*>(x + row * C)[v];
-      rv[k] = dres != nullptr ? reinterpret_cast<const uint4*>(dres + row * C)[v] : make_uint4(0, 0, 0, 0);
     }
     float acc = 0.f;
 #pragma unroll
@@ -278,7 +277,9 @@ __global__ void __launch_bounds__(256) rms_mod_bwd_kernel2(const bf16* __restric
       float d[8], xf[8], wf[8], sc[8], rs[8], o[8];
       unpack8(dv[k], d);
       unpack8(xv[k], xf);
-      unpack8(rv[k], rs);
+      // the residual gradient is read only here (not held across the row sum: fewer registers, two CTAs per SM)
+      unpack8(dres != nullptr ? reinterpret_cast<const uint4*>(dres + row * C)[lane + 32 * k] : make_uint4(0, 0, 0, 0),
+              rs);
       load_w8(w, c0, wf);
       if (MOD) {
         unpack8(__ldg(reinterpret_cast<const uint4*>(sc_row + c0)), sc);
