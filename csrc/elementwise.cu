@@ -41,42 +41,91 @@ __device__ __forceinline__ uint4 p8(const float (&f)[8]) {
 // ---------------------------------------------------------------------------------------------------- gate backward
 constexpr int GB_ROWS = 64;
 
+// 256 threads: RG = 256 / (C / 8) row groups (at least 1) of C / 8 threads, one 8-column vector each; a thread takes
+// rows rg, rg + RG, ... of the chunk, four at a time (the loads of four rows are issued before their math), and the
+// row groups' partial sums are added in shared memory in a fixed order (deterministic).
 __global__ void __launch_bounds__(256) gate_bwd_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ y,
                                                        const bf16* __restrict__ gate, int64_t ldg,
                                                        bf16* __restrict__ dy, float* __restrict__ part, int M, int C,
                                                        int rpg) {
+  extern __shared__ float red[];  // [RG - 1][2][C]
   const int g = blockIdx.y, chunk = blockIdx.x;
   const int r0 = g * rpg + chunk * GB_ROWS;
   const int r1 = min(min(g * rpg + rpg, r0 + GB_ROWS), M);
-  const int v = threadIdx.x, nv = C >> 3;
+  const int nv = C >> 3;
+  const int RG = max(1, (int)blockDim.x / nv);
   const int cid = g * gridDim.x + chunk;
-  for (int vv = v; vv < nv; vv += blockDim.x) {
+  for (int base = 0; base < nv * RG; base += blockDim.x) {
+    const int t = base + threadIdx.x;
+    const int vv = t % nv, rg = t / nv;
+    const bool act = t < nv * RG;
     const int c0 = vv * 8;
     float gv[8], pg[8], pb[8];
-    u8(*reinterpret_cast<const uint4*>(gate + (int64_t)g * ldg + c0), gv);
 #pragma unroll
     for (int j = 0; j < 8; ++j) pg[j] = pb[j] = 0.f;
-    for (int row = r0; row < r1; ++row) {
-      float d[8], yy[8], o[8];
-      u8(*reinterpret_cast<const uint4*>(dout + (int64_t)row * C + c0), d);
-      u8(*reinterpret_cast<const uint4*>(y + (int64_t)row * C + c0), yy);
+    if (act) {
+      u8(*reinterpret_cast<const uint4*>(gate + (int64_t)g * ldg + c0), gv);
+      for (int row = r0 + rg; row < r1; row += 4 * RG) {
+        uint4 dv[4], yv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int rr = row + u * RG;
+          if (rr < r1) {
+            dv[u] = *reinterpret_cast<const uint4*>(dout + (int64_t)rr * C + c0);
+            yv[u] = *reinterpret_cast<const uint4*>(y + (int64_t)rr * C + c0);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int rr = row + u * RG;
+          if (rr < r1) {
+            float d[8], yy[8], o[8], ob[8];
+            u8(dv[u], d);
+            u8(yv[u], yy);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              pg[j] += d[j] * yy[j];
+              o[j] = gv[j] * d[j];
+            }
+            const uint4 packed = p8(o);
+            *reinterpret_cast<uint4*>(dy + (int64_t)rr * C + c0) = packed;
+            u8(packed, ob);  // the bias sees the rounded dy that the GEMMs consume
+#pragma unroll
+            for (int j = 0; j < 8; ++j) pb[j] += ob[j];
+          }
+        }
+      }
+    }
+    // row groups 1.. hand their sums to group 0 (a block whose vectors wrap, RG == 1, skips this)
+    if (RG > 1) {
+      if (act && rg > 0) {
+        float* dst = red + (int64_t)(rg - 1) * 2 * C;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          dst[c0 + j] = pg[j];
+          dst[C + c0 + j] = pb[j];
+        }
+      }
+      __syncthreads();
+      if (act && rg == 0) {
+        for (int k = 1; k < RG; ++k) {
+          const float* src = red + (int64_t)(k - 1) * 2 * C;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            pg[j] += src[c0 + j];
+            pb[j] += src[C + c0 + j];
+          }
+        }
+      }
+      __syncthreads();
+    }
+    if (act && rg == 0) {
+      float* pp = part + (int64_t)cid * 2 * C;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        pg[j] += d[j] * yy[j];
-        o[j] = gv[j] * d[j];
+        pp[c0 + j] = pg[j];
+        pp[C + c0 + j] = pb[j];
       }
-      const uint4 packed = p8(o);
-      *reinterpret_cast<uint4*>(dy + (int64_t)row * C + c0) = packed;
-      float ob[8];
-      u8(packed, ob);  // the bias sees the rounded dy that the GEMMs consume
-#pragma unroll
-      for (int j = 0; j < 8; ++j) pb[j] += ob[j];
-    }
-    float* pp = part + (int64_t)cid * 2 * C;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      pp[c0 + j] = pg[j];
-      pp[C + c0 + j] = pb[j];
     }
   }
 }
@@ -237,7 +286,9 @@ void gate_bwd(const at::Tensor& dout, const at::Tensor& y, const at::Tensor& gat
   const int chunks = ((int)rpg + GB_ROWS - 1) / GB_ROWS;
   auto s = at::cuda::getCurrentCUDAStream();
   at::Tensor part = at::empty({(int64_t)G * chunks * 2 * C}, dout.options().dtype(at::kFloat));
-  gate_bwd_kernel<<<dim3(chunks, G), 256, 0, s>>>(
+  const int RG = std::max(1, 256 / (C / 8));
+  const size_t smem = RG > 1 ? (size_t)(RG - 1) * 2 * C * sizeof(float) : 0;
+  gate_bwd_kernel<<<dim3(chunks, G), 256, smem, s>>>(
       reinterpret_cast<const bf16*>(dout.data_ptr()), reinterpret_cast<const bf16*>(y.data_ptr()),
       reinterpret_cast<const bf16*>(gate.data_ptr()), gate.stride(0), reinterpret_cast<bf16*>(dy.data_ptr()),
       part.data_ptr<float>(), M, C, (int)rpg);

@@ -109,3 +109,19 @@ def test_trainer_steps_on_gpu():
     assert all(torch.isfinite(torch.tensor(losses))), losses
     assert losses[-1] < losses[0], losses
     assert status.read() == 0
+
+
+@pytest.mark.parametrize("C", [1024, 768, 1280])
+def test_gate_bwd_model_widths(C):
+    """gate_bwd at the model's widths (two row groups per block at C <= 1024, one above) against the CPU path."""
+    from nano_gpic_b200.ops import elementwise as E
+    g = torch.Generator().manual_seed(C)
+    M, rpg = 3 * 256, 256
+    G = (M + rpg - 1) // rpg
+    dout, yv = torch.randn(M, C, generator=g).bfloat16(), torch.randn(M, C, generator=g).bfloat16()
+    gate = torch.randn(G, 3 * C, generator=g).bfloat16()[:, C:2 * C]
+    dgc, dbc = torch.zeros(G, C), torch.zeros(C)
+    dyc = E.gate_bwd(dout, yv, gate, rpg, dgc, dbc)
+    dgg, dbg = torch.zeros(G, C, device="cuda"), torch.zeros(C, device="cuda")
+    dyg = E.gate_bwd(dout.cuda(), yv.cuda(), gate.cuda(), rpg, dgg, dbg)
+    assert _rel(dyg, dyc) < 1e-2 and _rel(dgg, dgc) < 1e-3 and _rel(dbg, dbc) < 1e-3
