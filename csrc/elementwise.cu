@@ -39,7 +39,7 @@ __device__ __forceinline__ uint4 p8(const float (&f)[8]) {
 }
 
 // ---------------------------------------------------------------------------------------------------- gate backward
-constexpr int GB_ROWS = 64;
+constexpr int GB_ROWS = 32;  // rows per CTA: 1024 CTAs at 128 x 256 rows (2.3 waves of 3 CTAs per SM)
 
 // 256 threads: RG = 256 / (C / 8) row groups (at least 1) of C / 8 threads, one 8-column vector each; a thread takes
 // rows rg, rg + RG, ... of the chunk, four at a time (the loads of four rows are issued before their math), and the
