@@ -9,6 +9,7 @@ optimisation with accumulate_grad_batches and DDP/FSDP2 strategies), as one plai
     loss = tr.train_step(images_u8, captions, caption_mask)          # one optimizer step over this rank's images
 """
 import math
+import os
 
 import torch
 import torch.distributed as dist
@@ -24,6 +25,21 @@ def uint8_to_float(img):
     """uint8 HWC [B, H, W, 3] -> fp32 CHW in [-1, 1]: ToTensor then Normalize(0.5, 0.5), as the reference's lever D
     (baselines/PixelGen/src/data/dataset/gpic_dataset.py:869-881)."""
     return (((img.permute(0, 3, 1, 2).float() / 255.0) - 0.5) / 0.5).contiguous()
+
+
+# NVTX ranges around each micro-batch's forward+backward and around the optimizer step, for nsys / ncu range filters;
+# off unless NG_NVTX=1 (a range costs a host call per push/pop).
+_NVTX = os.environ.get("NG_NVTX", "0") == "1"
+
+
+def _nvtx_push(name):
+    if _NVTX:
+        torch.cuda.nvtx.range_push(name)
+
+
+def _nvtx_pop():
+    if _NVTX:
+        torch.cuda.nvtx.range_pop()
 
 
 class Trainer:
@@ -144,9 +160,12 @@ class Trainer:
                 x = self.encode(x)
             y = y.to(torch.bfloat16)
             # mean over this rank's images and over ranks (the collectives sum)
+            _nvtx_push(f"micro {i} fwd+bwd")
             per = self.obj.train_step(self.model, x, y, m, t=ti, noise=ni,
                                       grad_scale=1.0 / (x.numel() * n * self.world))
+            _nvtx_pop()
             losses.append(per)
+        _nvtx_push("optimizer")
         if self.dp is not None:
             self.dp.finish_grads()
         self.last_grad_norm = self.clip_grad()
@@ -159,6 +178,7 @@ class Trainer:
             self.flat.sync_bf16()
         if hasattr(self.model, "weights_changed"):
             self.model.weights_changed()
+        _nvtx_pop()
         self.global_step += 1
         return torch.cat(losses).mean()
 
