@@ -10,8 +10,11 @@ untimed warm-up steps, then exactly K steps bracketed by a barrier + cuda synchr
 events on the launching stream; the reported time is the max over ranks. Every step's inputs (about 1.3 GB per rank)
 exceed the 126 MB L2. `e2e` repeats the measurement through the public Trainer.train_step API with each step's inputs
 copied from pinned host memory and the loss read back to the host. `--impl reference` runs the unmodified reference
-(baseline/_ref: its JiT_T2I, JiTTrainer, MuonAdamW, WarmupFlatCooldown; torch.compile + bf16 autocast + DDP as its
-Lightning path; SDPA attention because its FA3 binary is Hopper-only) on the same data.
+(baseline/_ref: its JiT_T2I, JiTTrainer, MuonAdamW, WarmupFlatCooldown, bf16 autocast, SDPA attention because its FA3
+binary is Hopper-only) on the same data, with the data parallelism its final ladder uses for the size: whole-model
+torch.compile + DDP below width 1280, FSDP2 per block + ShardMuonAdamW + NoSync accumulation from width 1280 (d14+).
+`parallelism` names the work (dpN: N data-parallel ranks over one global batch) and is the same for both arms;
+`dp_mode` says how each arm carries it out.
 """
 import argparse
 import json
@@ -235,11 +238,98 @@ def reference_step_fn(a, rank, world, dev):
     return step
 
 
+FSDP_WIDTH = 1280  # the reference's final ladder runs FSDP2 from this width up, DDP below (jobs/final_ladder.sh:29-30)
+
+
+def reference_uses_fsdp(size):
+    from nano_gpic_b200.config.ladder import SIZES
+    return SIZES[size].width >= FSDP_WIDTH
+
+
+def reference_fsdp_step_fn(a, rank, world, dev):
+    """The reference's FSDP2 training step for its FSDP sizes (d14 and up), built from its own code as its Lightning
+    path does: fsdp_setup.shard (one fully_shard unit per block, or groups of 7 blocks at width 1280; bf16 compute
+    parameters, fp32 reduce; RMSNorm weights and pos_embed replicated; each block compiled), MuonAdamW turned into
+    ShardMuonAdamW.like (owner all-to-alls around Newton-Schulz), replicated-gradient all-reduce, the global-norm clip
+    over DTensor shards, and NoSync accumulation (no reduce-scatter before the last micro-batch). The levers are those
+    of jobs/final_ladder.sh:29-35 for an FSDP size, minus FA3 (a Hopper-only binary)."""
+    pg = os.path.join(ROOT, "baseline", "_ref", "baselines", "PixelGen")
+    from nano_gpic_b200.config.ladder import SIZES
+    s = SIZES[a.size]
+    os.environ.setdefault("GPIC_MFU_ATTN", "sdpa")
+    for k in ("GPIC_MFU_FSDP", "GPIC_MFU_FSDP_NOSYNC", "GPIC_MFU_LOCAL_OPT", "GPIC_MFU_PATCHIFY", "GPIC_MFU_FUSED_NORM",
+              "GPIC_MFU_FUSED_QK", "GPIC_MFU_NS_FUSED", "GPIC_MFU_MUON_ADD", "GPIC_MFU_NO_EMA"):
+        os.environ.setdefault(k, "1")
+    os.environ.setdefault("GPIC_MFU_FSDP_GROUP", "7" if s.width == 1280 else "1")
+    sys.path.insert(0, pg)
+    from torch.distributed.device_mesh import init_device_mesh
+    from torch.distributed.fsdp import FSDPModule
+    from src.diffusion.flow_matching.scheduling import LinearScheduler
+    from src.diffusion.flow_matching.training_JiT import JiTTrainer, constant
+    from src.models.transformer.JiT_T2I import JiT_T2I
+    from src.optim.muon import MuonAdamW, tag_muon_params
+    from src.optim.muon_fsdp import ShardMuonAdamW
+    from src.utils.fsdp_setup import clip_grad_norm_, is_dtensor, shard, sync_replicated_grads
+    from src.utils.lr_scheduler import WarmupFlatCooldown
+    torch.set_float32_matmul_precision("medium")  # reference patch_bugs.py:5
+    if not dist.is_initialized():  # one GPU: FSDP2 over a group of one rank, as a 1-GPU launch of the same strategy
+        dist.init_process_group("nccl", store=dist.HashStore(), rank=0, world_size=1, device_id=dev)
+    torch.manual_seed(0)
+    net = JiT_T2I(**s.model_kwargs()).to(dev)
+    net.fetch_pos(256 // 16, 256 // 16, dev)
+    mesh = init_device_mesh("cuda", (world,))
+    replicated = shard(net, mesh, compute_bf16=True, compile_blocks=True)
+    tag_muon_params(net)  # after sharding, as its configure_optimizers runs after configure_model
+    params = [p for p in net.parameters() if p.requires_grad]
+    groups = [{"params": [p for p in params if is_dtensor(p)]}, {"params": [p for p in params if not is_dtensor(p)]}]
+    opt = MuonAdamW(groups, lr=s.adamw_lr, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0, muon_lr=s.muon_lr,
+                    muon_weight_decay=s.muon_wd, muon_momentum=0.95, muon_nesterov=True, ns_steps=5, split=True,
+                    fused_adamw=True, ns_dtype="bfloat16", update_scale="mup")
+    opt = ShardMuonAdamW.like(opt, groups)
+    wu, cd = s.schedule()
+    sched = WarmupFlatCooldown(wu, cd, s.steps, min_lr=3e-5)(opt)
+    units = [m for m in net.modules() if isinstance(m, FSDPModule)]
+    trainer = JiTTrainer(scheduler=LinearScheduler(), loss_weight_fn=constant, lognorm_t=True, timeshift=1.0,
+                         P_mean=-0.8, P_std=0.8, t_eps=0.05, null_condition_p=0.0)
+    mb = a.micro_batch or s.micro_batch
+    accum = (a.global_batch // world) // mb
+
+    def to_float(u8):
+        return ((u8.permute(0, 3, 1, 2).float() / 255.0) - 0.5) / 0.5
+
+    def sync(on):  # NoSyncModelParallelStrategy.block_backward_sync
+        for m in units:
+            m.set_requires_gradient_sync(on, recurse=False)
+            m.set_reshard_after_backward(on, recurse=False)
+
+    def step(img, cap, mask):
+        losses = []
+        for i in range(accum):
+            sl = slice(i * mb, (i + 1) * mb)
+            x = to_float(img[sl].to(dev, non_blocking=True))
+            y = cap[sl].to(dev, non_blocking=True)
+            m = mask[sl].to(dev, non_blocking=True)
+            sync(i == accum - 1)
+            with torch.autocast("cuda", dtype=torch.bfloat16):
+                out = trainer(net, None, None, x, y, None, {"y_mask": m})
+                (out["loss"] / accum).backward()
+            losses.append(out["loss"].detach())
+        sync_replicated_grads(replicated)
+        clip_grad_norm_(params, 1.0)
+        opt.step()
+        sched.step()
+        opt.zero_grad(set_to_none=True)
+        return torch.stack(losses).mean()
+
+    return step
+
+
 def run_reference(a, rank, world, dev):
     pg = os.path.join(ROOT, "baseline", "_ref", "baselines", "PixelGen")
     if not os.path.isdir(os.path.join(pg, "src")):
         return None, "baseline/_ref is missing: copy the reference tree there (see DESIGN.md)"
-    step = reference_step_fn(a, rank, world, dev)
+    fsdp = reference_uses_fsdp(a.size)
+    step = (reference_fsdp_step_fn if fsdp else reference_step_fn)(a, rank, world, dev)
     B = a.global_batch // world
     dev_batch = synthetic_batch(B, a.caption_len, 2048, seed=1000 + rank, device=dev)
     host_batches = [synthetic_batch(B, a.caption_len, 2048, seed=2000 + 10 * rank + i, pin=True) for i in range(2)]
@@ -321,9 +411,7 @@ def main():
                "config": {"model": f"JiT-T2I {a.size} (width {s.width}, {s.image_layers} image + {s.text_layers} text "
                                    f"layers, {s.heads} heads x 64)", "global_batch": a.global_batch,
                           "seq_len": 256 + T, "image_tokens": 256, "caption_tokens": T,
-                          "micro_batch": a.micro_batch or s.micro_batch, "parallelism": f"dp{world}" + (("-zero" + ("-p2p" if a.transport == "p2p" and world > 1 else ""))
-                                                        if getattr(a, "dp", "ddp") == "zero" and a.impl == "ours"
-                                                        else ""),
+                          "micro_batch": a.micro_batch or s.micro_batch, "parallelism": f"dp{world}",
                           "optimizer": "Muon (split, NS5 bf16) + AdamW, clip 1.0, WarmupFlatCooldown",
                           "recompute": a.recompute if a.impl == "ours" else "none",
                           "l2": "inputs larger than L2 (1.3 GB of step inputs per rank, activations >> 126 MB)"},
@@ -332,10 +420,19 @@ def main():
                        "h2d_bytes_per_step": B * (256 * 256 * 3 + T * 2048 * 2 + T),
                        "d2h_bytes_per_step": 4} if e2e_ms else None,
                "gpu_launches": launches}
+        # how the data parallelism is carried out, apart from `parallelism` (which names the work: N data-parallel
+        # ranks over one global batch, the same for both arms)
         if a.impl == "reference":
+            fsdp = reference_uses_fsdp(a.size)
+            rec["dp_mode"] = "fsdp2" if fsdp else "ddp"
             rec["impl"] = "reference"
             rec.pop("gpu_launches")
-            rec["reference_path"] = "baseline/_ref (unmodified copy); torch.compile + autocast bf16 + DDP; SDPA"
+            rec["reference_path"] = ("baseline/_ref (unmodified copy); autocast bf16; SDPA; " +
+                                     ("FSDP2 per block (fsdp_setup.shard, blocks compiled), ShardMuonAdamW, NoSync"
+                                      if fsdp else "torch.compile + DDP"))
+        else:
+            rec["dp_mode"] = (a.dp if a.dp == "ddp" else "zero") + ("-p2p" if a.transport == "p2p" and world > 1
+                                                                    else "")
         print(json.dumps(rec), flush=True)
     if dist.is_initialized():
         dist.barrier()

@@ -135,4 +135,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("status_read", &ng::status_read, "read the device error word (synchronizes the current stream)");
   m.def("launch_count", &ng::launch_count, "kernel launches issued by this extension so far (host count)");
   m.def("status_clear", &ng::status_clear, "clear the device error word");
+  m.def("status_copy_async", &ng::status_copy_async, "copy the device error word into a pinned host int32, no wait");
 }

@@ -361,24 +361,37 @@ __global__ void __launch_bounds__(256, VPL <= 4 ? 2 : 1) rms_mod_bwd_kernel2(con
   }
 }
 
-// d_shift/d_scale [G, C] (strided fp32 views, may be null) from the chunk partials of each group; d_w [C] += all.
-__global__ void rms_mod_bwd_reduce(const float* __restrict__ part, int G, int chunks, int C, float* dshift,
-                                   int64_t ld_dsh, float* dscale, int64_t ld_dsc, float* dw) {
+// Reduction of the chunk partials for the no-allocation entry point, in two launches that allocate nothing.
+// Stage 1, grid (ceil(C / 256), G): one thread per (column, group) adds the group's chunk partials in chunk order and
+// writes d_shift / d_scale (strided fp32 views, may be null) and the group's d_w partial into gw [G, C].
+__global__ void rms_mod_bwd_group_reduce(const float* __restrict__ part, int chunks, int C, float* dshift,
+                                         int64_t ld_dsh, float* dscale, int64_t ld_dsc, float* __restrict__ gw) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x, g = blockIdx.y;
+  if (c >= C) return;
+  float a = 0.f, b = 0.f, t = 0.f;
+  for (int k = 0; k < chunks; ++k) {
+    const float* pp = part + (int64_t)(g * chunks + k) * 3 * C;
+    a += pp[c];
+    b += pp[C + c];
+    t += pp[2 * C + c];
+  }
+  if (dshift != nullptr) dshift[(int64_t)g * ld_dsh + c] = a;
+  if (dscale != nullptr) dscale[(int64_t)g * ld_dsc + c] = b;
+  gw[(int64_t)g * C + c] = t;
+}
+
+// Stage 2: d_w[c] += sum over groups of gw[g, c], four independent accumulators (groups g = 4i + j) combined in a
+// fixed order, so the result is the same on every run.
+__global__ void rms_mod_bwd_dw_reduce(const float* __restrict__ gw, int G, int C, float* __restrict__ dw) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
-  float tw = 0.f;
-  for (int g = 0; g < G; ++g) {
-    float a = 0.f, b = 0.f;
-    for (int k = 0; k < chunks; ++k) {
-      const float* pp = part + (int64_t)(g * chunks + k) * 3 * C;
-      a += pp[c];
-      b += pp[C + c];
-      tw += pp[2 * C + c];
-    }
-    if (dshift != nullptr) dshift[(int64_t)g * ld_dsh + c] = a;
-    if (dscale != nullptr) dscale[(int64_t)g * ld_dsc + c] = b;
-  }
-  if (dw != nullptr) dw[c] += tw;
+  float t[4] = {0.f, 0.f, 0.f, 0.f};
+  int g = 0;
+  for (; g + 4 <= G; g += 4)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) t[j] += gw[(int64_t)(g + j) * C + c];
+  for (int j = 0; g < G; ++g, ++j) t[j] += gw[(int64_t)g * C + c];
+  dw[c] += (t[0] + t[1]) + (t[2] + t[3]);
 }
 
 // ------------------------------------------------------------------------------------------------------- LayerNorm
@@ -641,6 +654,7 @@ namespace {
 static __device__ __align__(256) float g_noalloc_rms_scratch[NG_NOALLOC_RMS_SCRATCH_FLOATS];
 
 constexpr int kMaxDevices = 64;
+constexpr int kMaxGridY = 65535;  // the groups are the second grid dimension of the launches
 std::mutex g_noalloc_mu;
 float* g_noalloc_addr[kMaxDevices] = {nullptr};
 
@@ -677,12 +691,15 @@ extern "C" __attribute__((visibility("default"))) int ng_rms_mod_bwd_noalloc(
   const int rpg = mod ? rows_per_group : M;
   const int G = mod ? (M + rpg - 1) / rpg : 1;
   const int chunks = (rpg + BWD_ROWS - 1) / BWD_ROWS;
-  const int64_t need = (int64_t)G * chunks * 3 * C;
+  if (G > kMaxGridY) return NG_NOALLOC_ERR_ARGS;
+  const int64_t need = (int64_t)G * chunks * 3 * C + (int64_t)G * C;  // chunk partials + per-group d_w partials
   if (need > (int64_t)NG_NOALLOC_RMS_SCRATCH_FLOATS) return NG_NOALLOC_ERR_TOO_LARGE;
   int err = NG_NOALLOC_OK;
   float* part = noalloc_scratch(&err);
   if (part == nullptr) return err;
-  cudaGetLastError();  // a launch error from earlier work is not this call's
+  // An error left by earlier work on this thread belongs to its owner: leave it in place and launch nothing, so the
+  // launch checks below only ever see this call's own errors.
+  if (cudaPeekAtLastError() != cudaSuccess) return NG_NOALLOC_ERR_PENDING;
   const dim3 grid(chunks, G);
   const bf16* sc = static_cast<const bf16*>(scale);
   if (mod)
@@ -694,9 +711,14 @@ extern "C" __attribute__((visibility("default"))) int ng_rms_mod_bwd_noalloc(
                                                         rstd, w, nullptr, 0, static_cast<const bf16*>(dres),
                                                         static_cast<bf16*>(dx), part, M, C, rpg);
   if (cudaGetLastError() != cudaSuccess) return NG_NOALLOC_ERR_LAUNCH;
-  rms_mod_bwd_reduce<<<(C + 255) / 256, 256, 0, stream>>>(part, G, chunks, C, mod ? dshift : nullptr, ld_dshift,
-                                                           mod ? dscale : nullptr, ld_dscale, dw);
+  float* gw = part + (int64_t)G * chunks * 3 * C;
+  rms_mod_bwd_group_reduce<<<dim3((C + 255) / 256, G), 256, 0, stream>>>(
+      part, chunks, C, mod ? dshift : nullptr, ld_dshift, mod ? dscale : nullptr, ld_dscale, gw);
   if (cudaGetLastError() != cudaSuccess) return NG_NOALLOC_ERR_LAUNCH;
+  if (dw != nullptr) {
+    rms_mod_bwd_dw_reduce<<<(C + 255) / 256, 256, 0, stream>>>(gw, G, C, dw);
+    if (cudaGetLastError() != cudaSuccess) return NG_NOALLOC_ERR_LAUNCH;
+  }
   return NG_NOALLOC_OK;
 }
 
@@ -705,8 +727,13 @@ extern "C" __attribute__((visibility("default"))) const char* ng_noalloc_error_s
     case NG_NOALLOC_OK: return "ok";
     case NG_NOALLOC_ERR_TOO_LARGE:
       return "ng_rms_mod_bwd_noalloc: the call needs more than NG_NOALLOC_RMS_SCRATCH_FLOATS (2097152) fp32 scratch "
-             "values (ceil(rows_per_group / 64) * groups * 3 * C); use the allocating entry point for it";
-    case NG_NOALLOC_ERR_ARGS: return "ng_rms_mod_bwd_noalloc: bad arguments (null pointer, C % 8 != 0, C > 2048 or a size <= 0)";
+             "values (ceil(rows_per_group / 64) * groups * 3 * C + groups * C); use the allocating entry point for it";
+    case NG_NOALLOC_ERR_ARGS:
+      return "ng_rms_mod_bwd_noalloc: bad arguments (null pointer, C % 8 != 0, C > 2048, a size <= 0, or more than "
+             "65535 groups)";
+    case NG_NOALLOC_ERR_PENDING:
+      return "ng_rms_mod_bwd_noalloc: a CUDA error from earlier work is pending on this thread (cudaPeekAtLastError); "
+             "nothing was launched and the error was left in place";
     case NG_NOALLOC_ERR_SETUP: return "ng_rms_mod_bwd_noalloc: could not resolve the scratch array on this device";
     case NG_NOALLOC_ERR_LAUNCH: return "ng_rms_mod_bwd_noalloc: kernel launch failed";
     default: return "ng_rms_mod_bwd_noalloc: unknown error code";

@@ -55,6 +55,29 @@ __device__ bool wait_flag(const long long* flag, long long epoch, int* err,
   return true;
 }
 
+// Completion of a grid: every CTA adds 1 to the counter, plus kFailBit when its waits gave up (or the status word
+// already held an error). The CTA whose add completes the grid resets the counter and learns whether any CTA failed;
+// only then may it publish a flag or an acknowledgement. A rank whose wait timed out therefore never tells its peers
+// that data is there when it is not: they time out in turn and report on their own status words, instead of reading
+// slots that were never written.
+constexpr unsigned int kFailBit = 1u << 20;  // grids here have at most 2 x 148 CTAs, far below 2^20
+
+// returns true in the one thread (threadIdx.x == 0 of the last CTA) that must publish, false everywhere else
+__device__ __forceinline__ bool grid_done_ok(unsigned int* counter, bool cta_ok) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x != 0) return false;
+  const unsigned int prev = atomicAdd(counter, 1u + (cta_ok ? 0u : kFailBit));
+  if ((prev & (kFailBit - 1)) != gridDim.x - 1) return false;
+  *counter = 0;
+  __threadfence_system();
+  return cta_ok && (prev >> 20) == 0;
+}
+
+__device__ __forceinline__ bool status_clean(const int* err) {
+  return *reinterpret_cast<const volatile int*>(err) == 0;
+}
+
 // flags / acks arrays are [W][nb] int64 on every rank: entry [r][b] on rank o = the last epoch of bucket b that rank
 // r pushed to o (flags) / that owner r consumed from o (acks).
 __global__ void __launch_bounds__(256) p2p_push_kernel(const float* __restrict__ grad, PeerTable recv, PeerTable flags,
@@ -88,18 +111,11 @@ __global__ void __launch_bounds__(256) p2p_push_kernel(const float* __restrict__
       }
     }
   }
-  // 3) the last CTA raises our flag for this bucket at every owner (after everyone's stores are visible)
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned int done = atomicAdd(counter, 1u);
-    if (done == gridDim.x - 1) {
-      *counter = 0;
-      __threadfence_system();
-      for (int o = 0; o < W; ++o)
-        if (o != rank) st_release_sys(reinterpret_cast<long long*>(flags.p[o]) + (int64_t)rank * nb + b, epoch);
-    }
-  }
+  // 3) the last CTA raises our flag for this bucket at every owner (after everyone's stores are visible), unless some
+  //    CTA gave up its wait and moved no data
+  if (grid_done_ok(counter, ok != 0))
+    for (int o = 0; o < W; ++o)
+      if (o != rank) st_release_sys(reinterpret_cast<long long*>(flags.p[o]) + (int64_t)rank * nb + b, epoch);
 }
 
 __global__ void __launch_bounds__(256) p2p_reduce_kernel(float* __restrict__ grad, const float* __restrict__ recv,
@@ -141,26 +157,24 @@ __global__ void __launch_bounds__(256) p2p_reduce_kernel(float* __restrict__ gra
     for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
     sumsq[blockIdx.x] = t;
   }
-  // the last CTA acknowledges the epoch to every sender (their slots here may be reused)
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned int done = atomicAdd(counter, 1u);
-    if (done == gridDim.x - 1) {
-      *counter = 0;
-      __threadfence_system();
-      for (int r = 0; r < W; ++r)
-        if (r != rank) st_release_sys(reinterpret_cast<long long*>(acks.p[r]) + (int64_t)rank * nb + b, epoch);
-    }
-  }
+  // the last CTA acknowledges the epoch to every sender (their slots here may be reused), unless some CTA gave up
+  if (grid_done_ok(counter, ok != 0))
+    for (int r = 0; r < W; ++r)
+      if (r != rank) st_release_sys(reinterpret_cast<long long*>(acks.p[r]) + (int64_t)rank * nb + b, epoch);
 }
 
 // Weight broadcast of one bucket: fp32 master segment of this owner -> bf16 at the same offsets in every rank's
 // compute-weight buffer (its own included); then flag[rank][b] = epoch at every peer.
+// Skipped entirely (no stores, no flags) when the status word already holds an error: the reduction that produced the
+// master may not have happened.
 __global__ void __launch_bounds__(256) p2p_bcast_bf16_kernel(const float* __restrict__ master, PeerTable w16,
                                                              PeerTable flags, unsigned int* counter, int W, int rank,
-                                                             int nb, int b, int64_t off, int64_t n, long long epoch) {
-  const int64_t n8 = n / 8;
+                                                             int nb, int b, int64_t off, int64_t n, long long epoch,
+                                                             const int* err) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = status_clean(err);
+  __syncthreads();
+  const int64_t n8 = ok ? n / 8 : 0;
   for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n8; j += (int64_t)gridDim.x * blockDim.x) {
     const float4 a = reinterpret_cast<const float4*>(master + off)[2 * j];
     const float4 c = reinterpret_cast<const float4*>(master + off)[2 * j + 1];
@@ -172,17 +186,9 @@ __global__ void __launch_bounds__(256) p2p_bcast_bf16_kernel(const float* __rest
     for (int r = 0; r < W; ++r)
       reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(w16.p[r]) + off)[j] = v;
   }
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned int done = atomicAdd(counter, 1u);
-    if (done == gridDim.x - 1) {
-      *counter = 0;
-      __threadfence_system();
-      for (int r = 0; r < W; ++r)
-        if (r != rank) st_release_sys(reinterpret_cast<long long*>(flags.p[r]) + (int64_t)rank * nb + b, epoch);
-    }
-  }
+  if (grid_done_ok(counter, ok != 0))
+    for (int r = 0; r < W; ++r)
+      if (r != rank) st_release_sys(reinterpret_cast<long long*>(flags.p[r]) + (int64_t)rank * nb + b, epoch);
 }
 
 // waits (one thread) until flags[r][b] >= epoch for every r != rank and every bucket b in [b0, b1)
@@ -222,8 +228,12 @@ __global__ void __launch_bounds__(256) fused_apply_kernel(const ApplyEntry* __re
                                                           const __nv_bfloat16* __restrict__ upd, float* ema,
                                                           PeerTable w16, PeerTable wflags, unsigned int* counter,
                                                           ApplyScalars sc, int W, int rank, int nb, int b,
-                                                          long long epoch) {
-  if ((int)blockIdx.x < nent) {
+                                                          long long epoch, const int* err) {
+  // with an error on the status word (a reduction that gave up), nothing is updated and no flag is raised
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = status_clean(err);
+  __syncthreads();
+  if (ok && (int)blockIdx.x < nent) {
     const ApplyEntry e = tab[blockIdx.x];
     const float keep_a = 1.f - sc.lr_a * sc.wd_a, keep_m = 1.f - sc.lr_m * sc.wd_m;
     const float step_a = sc.lr_a / sc.bc1, mscale = -sc.lr_m * e.coef;
@@ -266,17 +276,9 @@ __global__ void __launch_bounds__(256) fused_apply_kernel(const ApplyEntry* __re
       }
     }
   }
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned int done = atomicAdd(counter, 1u);
-    if (done == gridDim.x - 1) {
-      *counter = 0;
-      __threadfence_system();
-      for (int r = 0; r < W; ++r)
-        if (r != rank) st_release_sys(reinterpret_cast<long long*>(wflags.p[r]) + (int64_t)rank * nb + b, epoch);
-    }
-  }
+  if (grid_done_ok(counter, ok != 0))
+    for (int r = 0; r < W; ++r)
+      if (r != rank) st_release_sys(reinterpret_cast<long long*>(wflags.p[r]) + (int64_t)rank * nb + b, epoch);
 }
 
 // ------------------------------------------------------------------------------------------------------ host
@@ -358,7 +360,7 @@ void p2p_bcast_bf16(const at::Tensor& master, const std::vector<int64_t>& peer_w
   unsigned int* ctr = reinterpret_cast<unsigned int*>(counters.data_ptr<int>());
   p2p_bcast_bf16_kernel<<<grid_for(n / 8, master.get_device()), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       master.data_ptr<float>(), table(peer_w16), table(peer_flags), ctr, W, (int)rank, (int)nb, (int)b, off, n,
-      (long long)epoch);
+      (long long)epoch, status_word());
   NG_LAUNCH_CHECK();
 }
 
@@ -389,7 +391,7 @@ void p2p_fused_apply(const at::Tensor& table_t, int64_t nent, const at::Tensor& 
       reinterpret_cast<const ApplyEntry*>(table_t.data_ptr()), (int)nent, p.data_ptr<float>(), g.data_ptr<float>(),
       m1.data_ptr<float>(), m2.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(upd.data_ptr()), ema_p,
       table(peer_w16), table(peer_wflags), reinterpret_cast<unsigned int*>(counters.data_ptr<int>()), sc,
-      (int)peer_w16.size(), (int)rank, (int)nb, (int)b, (long long)epoch);
+      (int)peer_w16.size(), (int)rank, (int)nb, (int)b, (long long)epoch, status_word());
   NG_LAUNCH_CHECK();
 }
 

@@ -41,6 +41,16 @@ static std::atomic<int64_t> g_launches{0};
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 int64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
+// Enqueues a copy of the word into `out` (a pinned int32 host tensor of one element) on the current stream, without
+// waiting: the host reads it later, after an event recorded behind the copy has completed.
+void status_copy_async(const at::Tensor& out) {
+  TORCH_CHECK(out.device().is_cpu() && out.scalar_type() == at::kInt && out.numel() == 1 && out.is_pinned(),
+              "status_copy_async: a pinned int32 host tensor of one element");
+  auto stream = at::cuda::getCurrentCUDAStream();
+  TORCH_CHECK(cudaMemcpyAsync(out.data_ptr<int>(), status_word(), sizeof(int), cudaMemcpyDeviceToHost, stream) ==
+              cudaSuccess);
+}
+
 void status_clear() {
   auto stream = at::cuda::getCurrentCUDAStream();
   TORCH_CHECK(cudaMemsetAsync(status_word(), 0, sizeof(int), stream) == cudaSuccess);

@@ -21,6 +21,31 @@ def clear():
     ext().status_clear()
 
 
+class AsyncCheck:
+    """The status word checked one step late, without a host synchronisation in the step: `post()` enqueues a copy of
+    the word into pinned host memory behind the step's work and records an event; `poll()` (the next step, once that
+    event has completed, which it normally has long before) raises as check() does when the copied word is set."""
+
+    def __init__(self):
+        import torch
+        self.host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.event = None
+
+    def post(self):
+        import torch
+        ext().status_copy_async(self.host)
+        self.event = torch.cuda.Event()
+        self.event.record()
+
+    def poll(self):
+        if self.event is None:
+            return
+        self.event.synchronize()
+        self.event = None
+        if int(self.host[0]):
+            check()
+
+
 def check():
     code = read()
     if code:

@@ -312,6 +312,14 @@ class DataParallel:
         # zero mode: the parameters this rank updates (its own and the replicated ones)
         self.owned = None if self.mode == "ddp" else {id(p) for p in layout.params
                                                       if layout.owner[id(p)] in (self.rank, None)}
+        # peer-memory transport: its kernels record a timed-out wait in the device status word and skip their work.
+        # The word is copied to the host behind each step's weight refresh and read in the next step's finish_grads
+        # (by then long complete), so a lost peer stops the run with NanoCommTimeout one step late, with no host
+        # synchronisation inside a step. Anything with post() / poll() can stand in (tests).
+        self.status = None
+        if p2p is not None:
+            from ..ops.status import AsyncCheck
+            self.status = AsyncCheck()
 
     @torch.no_grad()
     def after_load(self):
@@ -370,8 +378,11 @@ class DataParallel:
             _reduce_scatter_inplace(g, b.seg, self.rank, self.group)
 
     def finish_grads(self):
-        """After the backward: reduce what is left and make the compute stream wait for every collective."""
+        """After the backward: reduce what is left and make the compute stream wait for every collective. Raises
+        NanoCommTimeout when the previous step's peer-memory kernels recorded a timed-out wait."""
         self.model._bwd_hook = None
+        if self.status is not None:
+            self.status.poll()
         self.early = len(self._launched)
         for i in range(len(self.layout.buckets)):
             if i not in self._launched:
@@ -436,6 +447,8 @@ class DataParallel:
         if self.p2p is not None:  # the next forward reads every owner's weights: wait (on the compute stream) for the
             # sharded buckets' flags (they come first; the replicated bucket was refreshed locally above)
             self.p2p.wait_weights(0, len(self._sharded()), self.epoch)
+        if self.status is not None:
+            self.status.post()
 
     def own_ranges(self):
         """[start, end) ranges of the flat buffers this rank keeps current (None in ddp mode: all of them)."""

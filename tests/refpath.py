@@ -1,14 +1,16 @@
-"""Locates the reference source tree (baseline/_ref, an unmodified copy of wenhaochai/nano-gpic) for oracle tests."""
+"""Locates the reference source tree for oracle tests: baseline/_ref (an unmodified copy of wenhaochai/nano-gpic),
+or the directory named by the environment variable NG_REFERENCE_ROOT."""
 import contextlib
 import os
 import sys
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-CANDIDATES = [os.path.join(ROOT, "baseline", "_ref"), "/root/reference"]
 
 
 def ref_root():
-    for c in CANDIDATES:
+    for c in (os.path.join(ROOT, "baseline", "_ref"), os.environ.get("NG_REFERENCE_ROOT")):
+        if not c:
+            continue
         if os.path.isdir(os.path.join(c, "baselines", "PixelGen", "src")):
             return c
     return None

@@ -118,3 +118,53 @@ def test_data_parallel_matches_one_process(mode, single, tmp_path):
     assert res["buckets"] >= 3 and res["early"] >= 1, res  # some buckets were reduced under the backward
     if mode == "zero":
         assert res["owners"] == [0, 1] and res["replicated"] == 1 and res["padding"] < 0.5, res
+
+
+class _LostPeerStatus:
+    """Stands in for the peer-memory transport's device status check: the copy posted after step `at` reports a
+    timed-out peer-flag wait (as the kernels record it), and the next step's poll must raise."""
+
+    def __init__(self, at):
+        self.at, self.posted = at, 0
+
+    def post(self):
+        self.posted += 1
+
+    def poll(self):
+        if self.posted >= self.at:
+            from nano_gpic_b200.ops.status import NanoCommTimeout
+            raise NanoCommTimeout("device status word 6: peer flag never arrived")
+
+
+def _status_worker(rank, world, port, out):
+    import torch.distributed as dist
+    from nano_gpic_b200.ops.status import NanoCommTimeout
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        torch.set_num_threads(2)
+        tr, _ = _trainer(world, "zero")
+        tr.dp.status = _LostPeerStatus(at=1)
+        img, cap, mask, t, noise = _data()
+        per = GLOBAL // world
+        sl = slice(rank * per, (rank + 1) * per)
+        tr.train_step(img[0, sl], cap[0, sl], mask[0, sl], t=t[0, sl], noise=noise[0, sl])
+        try:
+            tr.train_step(img[1, sl], cap[1, sl], mask[1, sl], t=t[1, sl], noise=noise[1, sl])
+            res = "no error"
+        except NanoCommTimeout as e:
+            res = f"raised: {e}"
+        torch.save({"res": res, "steps": tr.global_step}, out + f".{rank}")
+    finally:
+        dist.destroy_process_group()
+
+
+def test_timed_out_peer_wait_stops_the_next_step(tmp_path):
+    """A peer-flag timeout recorded during step k stops training in step k + 1 with NanoCommTimeout on every rank
+    (both ranks see it before the step's first collective, so neither waits on the other)."""
+    out = str(tmp_path / "st")
+    mp.spawn(_status_worker, args=(2, _port(), out), nprocs=2, join=True)
+    for r in range(2):
+        res = torch.load(out + f".{r}")
+        assert res["res"].startswith("raised: device status word 6"), res
+        assert res["steps"] == 1, res

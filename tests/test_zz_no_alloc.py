@@ -82,6 +82,42 @@ def test_noalloc_matches_allocating_entry_point_twice():
         assert (dmod[:, 2 * C:] == -3.0).all()  # columns it does not own stay untouched
 
 
+def test_noalloc_plain_rmsnorm_and_optional_outputs():
+    """The plain-RMSNorm form (no modulation: one group of all rows) without a residual gradient, and the modulated
+    form without a weight gradient, each twice in a row; M is not a multiple of the 64-row chunk, so the last chunk of
+    every group is partial."""
+    from nano_gpic_b200._ext import ext
+    f, err_str = _lib()
+    stream = torch.cuda.current_stream()
+    for rep in range(2):
+        # plain RMSNorm: scale = None, dres = None, dshift / dscale ignored
+        M, C = 1000 + 37 * rep, 512
+        dh, x, _, w, _, rstd = _case(M, C, M, 10 + rep)
+        dx_ref, dw_ref = torch.empty_like(x), torch.zeros(C, device="cuda")
+        ext().rms_mod_bwd(dh, x, rstd, w, None, None, dx_ref, dw_ref, None, None, 1)
+        dx, dw = torch.full_like(x, 5.0), torch.zeros(C, device="cuda")
+        rc = f(_ptr(dh), _ptr(x), _ptr(rstd), _ptr(w), None, 0, None, _ptr(dx), _ptr(dw), None, 0, None, 0, M, C, 0,
+               stream.cuda_stream)
+        assert rc == 0, err_str(rc).decode()
+        _close(dx, dx_ref, what="plain dx")
+        _close(dw, dw_ref, rtol=1e-2, atol=1e-2, what="plain dw")
+        # modulated, dw = None, groups of 100 rows (two chunks, the second partial)
+        M, C, rpg = 700, 256, 100
+        dh, x, dres, w, mod, rstd = _case(M, C, rpg, 20 + rep)
+        G = M // rpg
+        scale = mod[:, C:2 * C]
+        dx_ref, dmod_ref = torch.empty_like(x), torch.zeros(G, 6 * C, device="cuda")
+        ext().rms_mod_bwd(dh, x, rstd, w, scale, dres, dx_ref, None, dmod_ref[:, :C], dmod_ref[:, C:2 * C], rpg)
+        dx, dmod = torch.full_like(x, 5.0), torch.full((G, 6 * C), 9.0, device="cuda")
+        rc = f(_ptr(dh), _ptr(x), _ptr(rstd), _ptr(w), _ptr(scale), scale.stride(0), _ptr(dres), _ptr(dx), None,
+               _ptr(dmod[:, :C]), dmod.stride(0), _ptr(dmod[:, C:2 * C]), dmod.stride(0), M, C, rpg,
+               stream.cuda_stream)
+        assert rc == 0, err_str(rc).decode()
+        _close(dx, dx_ref, what="mod dx")
+        _close(dmod[:, :2 * C], dmod_ref[:, :2 * C], rtol=1e-2, atol=1e-2, what="mod dshift/dscale")
+    torch.cuda.synchronize()
+
+
 def test_noalloc_rejects_oversized_call():
     f, err_str = _lib()
     C, rpg = 1024, 256
@@ -90,3 +126,7 @@ def test_noalloc_rejects_oversized_call():
     rc = f(x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(), 6 * C, None, x.data_ptr(), None,
            None, 0, None, 0, M, C, rpg, torch.cuda.current_stream().cuda_stream)
     assert rc == 1 and b"NG_NOALLOC_RMS_SCRATCH_FLOATS" in err_str(rc)
+    # more groups than a grid dimension holds: an argument error, nothing launched
+    rc = f(x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(), x.data_ptr(), 48, None, x.data_ptr(), None,
+           None, 0, None, 0, 70000, 8, 1, torch.cuda.current_stream().cuda_stream)
+    assert rc == 2 and b"65535" in err_str(rc)
