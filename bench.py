@@ -12,7 +12,8 @@ exceed the 126 MB L2. `e2e` repeats the measurement through the public Trainer.t
 copied from pinned host memory and the loss read back to the host. `--impl reference` runs the unmodified reference
 (baseline/_ref: its JiT_T2I, JiTTrainer, MuonAdamW, WarmupFlatCooldown, bf16 autocast, SDPA attention because its FA3
 binary is Hopper-only) on the same data, with the data parallelism its final ladder uses for the size: whole-model
-torch.compile + DDP below width 1280, FSDP2 per block + ShardMuonAdamW + NoSync accumulation from width 1280 (d14+).
+torch.compile + DDP below width 1280, FSDP2 per block + ShardMuonAdamW + NoSync accumulation from width 1280 (d14+)
+on more than one GPU (its sharded optimizer does not run on one GPU, where it trains unsharded).
 `parallelism` names the work (dpN: N data-parallel ranks over one global batch) and is the same for both arms;
 `dp_mode` says how each arm carries it out.
 """
@@ -241,9 +242,12 @@ def reference_step_fn(a, rank, world, dev):
 FSDP_WIDTH = 1280  # the reference's final ladder runs FSDP2 from this width up, DDP below (jobs/final_ladder.sh:29-30)
 
 
-def reference_uses_fsdp(size):
+def reference_uses_fsdp(size, world):
+    """FSDP2 for the reference's FSDP sizes on more than one GPU. On one GPU its ShardMuonAdamW hands the step to the
+    unsharded MuonAdamW (muon_fsdp.py:93-94), which cannot take FSDP2's DTensor parameters, so a 1-GPU run of the
+    reference is its unsharded path (whole-model compile, no wrapper), as for the DDP sizes."""
     from nano_gpic_b200.config.ladder import SIZES
-    return SIZES[size].width >= FSDP_WIDTH
+    return SIZES[size].width >= FSDP_WIDTH and world > 1
 
 
 def reference_fsdp_step_fn(a, rank, world, dev):
@@ -272,8 +276,6 @@ def reference_fsdp_step_fn(a, rank, world, dev):
     from src.utils.fsdp_setup import clip_grad_norm_, is_dtensor, shard, sync_replicated_grads
     from src.utils.lr_scheduler import WarmupFlatCooldown
     torch.set_float32_matmul_precision("medium")  # reference patch_bugs.py:5
-    if not dist.is_initialized():  # one GPU: FSDP2 over a group of one rank, as a 1-GPU launch of the same strategy
-        dist.init_process_group("nccl", store=dist.HashStore(), rank=0, world_size=1, device_id=dev)
     torch.manual_seed(0)
     net = JiT_T2I(**s.model_kwargs()).to(dev)
     net.fetch_pos(256 // 16, 256 // 16, dev)
@@ -328,7 +330,7 @@ def run_reference(a, rank, world, dev):
     pg = os.path.join(ROOT, "baseline", "_ref", "baselines", "PixelGen")
     if not os.path.isdir(os.path.join(pg, "src")):
         return None, "baseline/_ref is missing: copy the reference tree there (see DESIGN.md)"
-    fsdp = reference_uses_fsdp(a.size)
+    fsdp = reference_uses_fsdp(a.size, world)
     step = (reference_fsdp_step_fn if fsdp else reference_step_fn)(a, rank, world, dev)
     B = a.global_batch // world
     dev_batch = synthetic_batch(B, a.caption_len, 2048, seed=1000 + rank, device=dev)
@@ -423,7 +425,7 @@ def main():
         # how the data parallelism is carried out, apart from `parallelism` (which names the work: N data-parallel
         # ranks over one global batch, the same for both arms)
         if a.impl == "reference":
-            fsdp = reference_uses_fsdp(a.size)
+            fsdp = reference_uses_fsdp(a.size, world)
             rec["dp_mode"] = "fsdp2" if fsdp else "ddp"
             rec["impl"] = "reference"
             rec.pop("gpu_launches")

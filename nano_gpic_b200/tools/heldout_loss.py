@@ -1,36 +1,46 @@
 #!/usr/bin/env python3
 """Held-out loss of ladder checkpoints: the training objective on fixed data, fixed noise and 16 fixed noise levels.
 
-The definition (reference tools/heldout_loss.py:1-36, :251-277):
-  t_k   = time_shift(sigmoid(P_mean + P_std * Phi^-1((k + 0.5) / 16))), k = 0..15, computed in float64, then float32
-  noise = image j of a split draws randn((16, C, H, W)) from a CPU generator seeded SEED * 1_000_003 + j (SEED = 0),
-          independent of batch, GPU and GPU count
-  loss  = the JiT objective (x_t = t x + (1 - t) eps, v-space squared error, mean over C, H, W per image), per level,
-          summed in float64; the record holds the mean over levels and images, the 16 level means and the standard
-          error over images
-Images are batched in order of caption length (the order changes only rounding). A checkpoint whose EMA slot holds the
-raw weights bit for bit is evaluated once for both records (one_pass).
+The metric (its definition is shared with reference tools/heldout_loss.py:1-36, :251-277, so that numbers compare):
+  levels  t_k = time_shift(sigmoid(P_mean + P_std * Phi^-1((k + 0.5) / 16))), k = 0..15, float64 then float32
+  noise   image j of a split draws randn((16, C, H, W)) from a CPU generator seeded SEED * 1_000_003 + j (SEED = 0):
+          independent of the batch, the device and the number of workers
+  loss    JiT's objective with t and the noise given: x_t = t x + (1 - t) eps, v = (x - x_t) / max(1 - t, t_eps), the
+          network's x prediction turned into v the same way, squared error averaged over C, H, W per image; sums in
+          float64. A record holds the mean over levels and images (loss_<split>), the 16 level means (loss_<split>_t)
+          and the standard error over images of the per-image mean over levels (loss_<split>_se).
 
-Subcommands (same names and output fields as the reference):
-  prep  --n-val N --n-train N --val-glob G --train-shard S --emb-dir D [--val-emb-dir D2]   -> data file
-  list  --out results.jsonl [--ckpt ...]        the checkpoints that lack a record
-  work  --out results.jsonl --data F (--ckpt ... | --tasks F --counter F)   computes records (appends JSON lines)
-  bench --d 1792 --nb 18 --nt 4                 seconds per forward of a random model
+How this tool gets there (its own design):
+  * A split is a HeldoutSplit: uint8 images, the caption features of all captions back to back, their lengths. Its
+    images are visited in order of caption length, so a batch pads little (the order changes only rounding).
+  * Noise is made on the host, one batch ahead: while the device works on batch b, a thread pool fills batch b + 1's
+    tensor (one task per image, each with its own generator, so the values do not depend on the pool).
+  * Several workers share one task list through claim files: a worker owns task i when it is the one that creates
+    `<counter>.claims/<i>` (O_CREAT | O_EXCL, atomic on the file system), so every task is done once.
+  * Results go to a JSON-lines file through a ResultStore, which knows the keys already done; `work` skips them
+    (idempotent), so a crashed or repeated job only adds what is missing.
+  * A no-EMA checkpoint keeps the raw weights in its EMA slot as well; when every EMA tensor has the raw tensor's bytes,
+    one pass over the raw weights gives both records (marked one_pass).
+
+Subcommands (the reference tool's names, arguments and record fields):
+  prep  --n-val N --n-train N --data F --val-glob G --train-shard S --emb-dir D [--val-emb-dir D2]
+  list  --data F --out results.jsonl [--ckpt ... | --runs DIR] [--skipped FILE]   tasks without a record, as JSON lines
+  work  --data F --out results.jsonl (--ckpt ... | --tasks F --counter F)        computes and appends records
+  bench --d 1792 --nb 18 --nt 4                                                   seconds per forward, random weights
 """
 import argparse
-import fcntl
 import glob
 import json
 import math
 import os
-import queue
 import re
 import socket
 import sys
-import threading
 import time
 import traceback
 import zipfile
+from concurrent.futures import ThreadPoolExecutor
+from dataclasses import dataclass, field
 
 import numpy as np
 import torch
@@ -38,351 +48,414 @@ import torch
 NUM_T, SEED, BATCH = 16, 0, 128
 SPLITS = ("val", "train", "train_reenc")
 IMAGE, PAD_MULTIPLE, TEXT_MAX, EMB_DIM = 256, 8, 320, 2048
-WEIGHTS = (("ema", "ema_denoiser."), ("raw", "denoiser."))
-CKPT_RE = re.compile(r"ms-step=(\d+)\.ckpt")
-RUN_RE = re.compile(r"exp_ladder_(d\d+)")
+WEIGHTS = (("ema", "ema_denoiser."), ("raw", "denoiser."))   # record name -> state-dict prefix
+CKPT_NAME = re.compile(r"ms-step=(\d+)\.ckpt")
+RUN_NAME = re.compile(r"exp_ladder_(d\d+)")
+MODEL_ARGS = ("input_size", "in_channels", "num_groups", "hidden_size", "num_blocks", "num_text_blocks", "patch_size",
+              "txt_embed_dim", "txt_max_length", "bottleneck_dim")
+LOSS_DEFAULTS = dict(timeshift=1.0, P_mean=-0.8, P_std=0.8, t_eps=0.05)
 
 
-# ------------------------------------------------------------------------------------------------------------ loss
+# ====================================================================================================== the metric
 def time_shift_fn(t, timeshift=1.0):
     return t / (t + (1 - t) * timeshift)
 
 
 def levels(P_mean=-0.8, P_std=0.8, timeshift=1.0, num_t=NUM_T):
+    """The num_t noise levels: logit-normal quantiles at (k + 0.5) / num_t, in float64, then float32, then shifted."""
     q = (torch.arange(num_t, dtype=torch.float64) + 0.5) / num_t
-    base = torch.sigmoid(P_mean + P_std * torch.special.ndtri(q)).float()
-    return time_shift_fn(base, timeshift)
+    return time_shift_fn(torch.sigmoid(P_mean + P_std * torch.special.ndtri(q)).float(), timeshift)
 
 
 def image_noise(seed, j, num_t, shape, out=None):
-    g = torch.Generator().manual_seed(seed * 1_000_003 + j)
-    return torch.randn((num_t, *shape), generator=g, out=out)
+    """Image j's noise at every level: randn((num_t, *shape)) from its own CPU generator."""
+    gen = torch.Generator().manual_seed(seed * 1_000_003 + j)
+    return torch.randn((num_t, *shape), generator=gen, out=out)
 
 
 def level_loss(net, x, y, y_mask, t, noise, t_eps=0.05):
-    """Per-image loss at one level t (0-d tensor): the JiT objective with t and the noise given."""
-    t = t.expand(x.shape[0])
-    tt = t.view(-1, 1, 1, 1)
-    x_t = tt * x + noise * (1 - tt)
-    den = (1 - tt).clamp_min(t_eps)
-    v_t = (x - x_t) / den
+    """Per-image loss [B] at one level t (a 0-d tensor), with the noise given."""
+    tb = t.reshape(1, 1, 1, 1).to(x.dtype)
+    x_t = tb * x + (1 - tb) * noise
+    den = (1 - tb).clamp_min(t_eps)
     with torch.no_grad():
-        pred = net(x_t, t, y, y_mask=y_mask)
-    out = (pred.float() - x_t) / den
-    return ((out - v_t) ** 2).mean(dim=(1, 2, 3))
+        pred = net(x_t, t.expand(x.shape[0]), y, y_mask=y_mask)
+    err = (pred.float() - x_t) / den - (x - x_t) / den
+    return err.square().mean(dim=(1, 2, 3))
 
 
 def to_input(u8):
-    """[B, H, W, 3] uint8 -> x in [-1, 1]: ToTensor + Normalize(0.5, 0.5)."""
-    return u8.permute(0, 3, 1, 2).float().div(255).sub(0.5).div(0.5)
+    """[B, H, W, 3] uint8 -> [B, 3, H, W] in [-1, 1] (ToTensor, then Normalize(0.5, 0.5))."""
+    return ((u8.permute(0, 3, 1, 2).to(torch.float32) / 255.0) - 0.5) / 0.5
 
 
-def text_batch(split, idx, device):
-    lens = [int(split["lens"][i]) for i in idx]
-    T = min(-(-max(lens) // split["pad_multiple"]) * split["pad_multiple"], split["text_max_length"])
-    emb = split["emb"]
-    y = torch.zeros((len(idx), T, emb.shape[1]), dtype=emb.dtype, device=device)
-    mask = torch.zeros((len(idx), T), dtype=torch.bool, device=device)
-    for r, (i, n) in enumerate(zip(idx, lens)):
-        o = int(split["offs"][i])
-        y[r, :n] = emb[o:o + n]
-        mask[r, :n] = True
-    return y, mask
+# ========================================================================================================== data
+@dataclass
+class HeldoutSplit:
+    """One data split: images [N, H, W, 3] uint8, caption features [sum of lengths, D] (captions back to back),
+    caption lengths [N]; captions pad to the batch's longest, rounded up to pad_multiple, at most text_max_length."""
+    img: torch.Tensor
+    emb: torch.Tensor
+    lens: list
+    pad_multiple: int = PAD_MULTIPLE
+    text_max_length: int = TEXT_MAX
+    extra: dict = field(default_factory=dict)
+
+    def __post_init__(self):
+        self.lens = [int(n) for n in self.lens]
+        self.starts = np.concatenate([[0], np.cumsum(self.lens)[:-1]]).astype(np.int64).tolist()
+
+    def __len__(self):
+        return len(self.lens)
+
+    @property
+    def image_shape(self):
+        return (self.img.shape[3], self.img.shape[1], self.img.shape[2])
+
+    def batches(self, size):
+        """Index lists of at most `size` images, in order of caption length (ties by index)."""
+        order = sorted(range(len(self)), key=lambda i: (self.lens[i], i))
+        return [order[k:k + size] for k in range(0, len(order), size)]
+
+    def captions(self, idx, device):
+        """(features [B, T, D] with zeros after each caption, mask [B, T]) of images idx."""
+        want = max(self.lens[i] for i in idx)
+        T = min(-(-want // self.pad_multiple) * self.pad_multiple, self.text_max_length)
+        feats = torch.zeros((len(idx), T, self.emb.shape[1]), dtype=self.emb.dtype)
+        mask = torch.zeros((len(idx), T), dtype=torch.bool)
+        for row, i in enumerate(idx):
+            n = min(self.lens[i], T)
+            feats[row, :n] = self.emb[self.starts[i]:self.starts[i] + n]
+            mask[row, :n] = True
+        return feats.to(device), mask.to(device)
+
+    def images(self, idx, device):
+        return to_input(self.img[torch.as_tensor(idx)].to(device))
+
+    @classmethod
+    def from_saved(cls, d):
+        known = {"img", "emb", "lens", "pad_multiple", "text_max_length", "offs"}
+        lens = d["lens"].tolist() if torch.is_tensor(d["lens"]) else list(d["lens"])
+        return cls(d["img"], d["emb"], lens, int(d.get("pad_multiple", PAD_MULTIPLE)),
+                   int(d.get("text_max_length", TEXT_MAX)), {k: v for k, v in d.items() if k not in known})
+
+    def to_saved(self):
+        lens = torch.tensor(self.lens, dtype=torch.int64)
+        return dict(self.extra, img=self.img, emb=self.emb, lens=lens, offs=torch.tensor(self.starts),
+                    pad_multiple=self.pad_multiple, text_max_length=self.text_max_length)
 
 
-def _noise_feed(batches, seed, num_t, shape, threads, pin):
-    """Each batch's noise [B, num_t, *shape], generated one batch ahead in a background thread."""
-    from concurrent.futures import ThreadPoolExecutor
-    q = queue.Queue(maxsize=1)
-    stop = threading.Event()
-    B = max(len(i) for i in batches)
-    bufs = [torch.empty((B, num_t, *shape), pin_memory=pin) for _ in range(min(3, len(batches)))]
+class NoiseAhead:
+    """Iterates the noise tensors [B, num_t, *shape] of the given batches in order, each one made by a thread pool
+    while the caller still works on the previous one (one batch of lookahead; each image has its own generator)."""
 
-    def produce():
+    def __init__(self, batches, seed, num_t, shape, threads=4, pin=False):
+        self.batches, self.seed, self.num_t, self.shape, self.pin = batches, seed, num_t, shape, pin
+        self.pool = ThreadPoolExecutor(max(1, threads), thread_name_prefix="heldout-noise")
+
+    def _start(self, idx):
+        out = torch.empty((len(idx), self.num_t, *self.shape), pin_memory=self.pin)
+        jobs = [self.pool.submit(image_noise, self.seed, j, self.num_t, self.shape, out[r]) for r, j in enumerate(idx)]
+        return out, jobs
+
+    def __iter__(self):
         try:
-            with ThreadPoolExecutor(threads) as pool:
-                for b, idx in enumerate(batches):
-                    buf = bufs[b % len(bufs)][:len(idx)]
-                    list(pool.map(lambda r: image_noise(seed, idx[r], num_t, shape, out=buf[r]), range(len(idx))))
-                    while not stop.is_set():
-                        try:
-                            q.put(buf, timeout=1)
-                            break
-                        except queue.Full:
-                            pass
-                    if stop.is_set():
-                        return
-            q.put(None)
-        except BaseException as e:
-            q.put(e)
-
-    th = threading.Thread(target=produce, daemon=True)
-    th.start()
-    try:
-        while True:
-            item = q.get()
-            if item is None:
-                return
-            if isinstance(item, BaseException):
-                raise item
-            yield item
-    finally:
-        stop.set()
+            nxt = self._start(self.batches[0]) if self.batches else None
+            for b in range(len(self.batches)):
+                out, jobs = nxt
+                for job in jobs:
+                    job.result()  # re-raises a failed draw here
+                nxt = self._start(self.batches[b + 1]) if b + 1 < len(self.batches) else None
+                yield out
+        finally:
+            self.pool.shutdown(wait=True, cancel_futures=True)
 
 
 @torch.no_grad()
 def evaluate(nets, split, ts, seed=SEED, batch=BATCH, device="cpu", threads=4, t_eps=0.05, log=None):
-    """{name: dict(level_mean [num_t], image_mean [N])} in float64, every net on the same x_t."""
-    N, num_t = len(split["lens"]), len(ts)
-    shape = tuple(split["img"].shape[i] for i in (3, 1, 2))
-    order = split.get("order") or sorted(range(N), key=lambda i: (int(split["lens"][i]), i))
-    batches = [order[i:i + batch] for i in range(0, N, batch)]
-    sums = {k: torch.zeros(num_t, dtype=torch.float64, device=device) for k in nets}
-    per = {k: torch.zeros(N, dtype=torch.float64, device=device) for k in nets}
+    """{name: {"level_mean": [num_t], "image_mean": [N]}} in float64 for every net in `nets` ({name: module}); all
+    nets see the same x_t."""
+    N, num_t = len(split), len(ts)
+    level_sum = {k: torch.zeros(num_t, dtype=torch.float64) for k in nets}
+    per_image = {k: torch.zeros(num_t, N, dtype=torch.float64) for k in nets}
     ts = ts.to(device)
+    groups = split.batches(batch)
     pin = torch.device(device).type == "cuda"
     t0 = time.time()
-    for b, (idx, noise) in enumerate(zip(batches, _noise_feed(batches, seed, num_t, shape, threads, pin))):
-        noise = noise.to(device)
-        it = torch.tensor(idx, device=device)
-        x = to_input(split["img"][it.cpu()].to(device))
-        y, mask = text_batch(split, idx, device)
-        for k in range(num_t):
-            for name, net in nets.items():
-                l = level_loss(net, x, y, mask, ts[k], noise[:, k], t_eps).double()
-                sums[name][k] += l.sum()
-                per[name].index_add_(0, it, l)
-        if log and (b + 1) % max(1, len(batches) // 4) == 0:
-            log(f"batch {b + 1}/{len(batches)} {time.time() - t0:.0f} s")
-    return {k: dict(level_mean=(sums[k] / N).cpu(), image_mean=(per[k] / num_t).cpu()) for k in nets}
+    for b, (idx, noise) in enumerate(zip(groups, NoiseAhead(groups, seed, num_t, split.image_shape, threads, pin))):
+        noise = noise.to(device, non_blocking=pin)
+        x = split.images(idx, device)
+        y, mask = split.captions(idx, device)
+        cols = torch.as_tensor(idx)
+        for name, net in nets.items():
+            for k in range(num_t):
+                vals = level_loss(net, x, y, mask, ts[k], noise[:, k], t_eps).double().cpu()
+                level_sum[name][k] += vals.sum()
+                per_image[name][k, cols] = vals
+        if log is not None and (b + 1) % max(1, len(groups) // 4) == 0:
+            log(f"{b + 1}/{len(groups)} batches, {time.time() - t0:.0f} s")
+    return {k: {"level_mean": level_sum[k] / N, "image_mean": per_image[k].mean(0)} for k in nets}
 
 
-# ------------------------------------------------------------------------------------------------------- models
+# ======================================================================================================= models
 def run_config(run_dir):
-    """Denoiser kwargs and loss settings from the run's saved configs (config-TrainerFn.FITTING-*.yaml)."""
+    """(denoiser kwargs, loss settings) of a run, from the configurations its launches saved
+    (config-TrainerFn.FITTING-<stamp>.yaml); every launch must agree on both."""
     import yaml
-    cfgs = sorted(glob.glob(os.path.join(run_dir, "config-TrainerFn.FITTING-*.yaml")))
-    assert cfgs, f"no config-TrainerFn.FITTING-*.yaml in {run_dir}"
-    dens, losses = set(), set()
-    for c in cfgs:
-        with open(c) as f:
-            m = yaml.safe_load(f)["model"]
-        kw = dict(m["denoiser"]["init_args"])
-        ta = m["diffusion_trainer"]["init_args"]
-        loss = dict(timeshift=ta.get("timeshift", 1.0), P_mean=ta.get("P_mean", -0.8), P_std=ta.get("P_std", 0.8),
-                    t_eps=ta.get("t_eps", 0.05))
-        dens.add(json.dumps(kw, sort_keys=True))
-        losses.add(json.dumps(loss, sort_keys=True))
-    assert len(dens) == 1 and len(losses) == 1, f"{run_dir}: launches differ: {dens} {losses}"
-    return json.loads(dens.pop()), json.loads(losses.pop())
+    seen = {}
+    for path in sorted(glob.glob(os.path.join(run_dir, "config-TrainerFn.FITTING-*.yaml"))):
+        with open(path) as f:
+            model = yaml.safe_load(f)["model"]
+        den = {k: v for k, v in model["denoiser"]["init_args"].items() if k in MODEL_ARGS}
+        trainer_args = model.get("diffusion_trainer", {}).get("init_args", {})
+        loss = {k: trainer_args.get(k, v) for k, v in LOSS_DEFAULTS.items()}
+        seen[json.dumps([den, loss], sort_keys=True)] = (den, loss)
+    if not seen:
+        raise FileNotFoundError(f"{run_dir}: no config-TrainerFn.FITTING-*.yaml")
+    if len(seen) > 1:
+        raise ValueError(f"{run_dir}: its launches disagree on the model or the loss: {list(seen)}")
+    return next(iter(seen.values()))
 
 
 def build_denoiser(kw, state_dict, prefix, device):
-    """nano_gpic_b200's JiT_T2I(**kw) with the weights under prefix, loaded strictly."""
+    """This package's JiT_T2I(**kw) on `device`, fp32, eval mode, with every tensor under `prefix` loaded strictly."""
     from nano_gpic_b200.models.jit_t2i import JiT_T2I
-    sub = {k[len(prefix):]: v for k, v in state_dict.items() if k.startswith(prefix)}
-    kw = {k: v for k, v in kw.items() if k in ("input_size", "in_channels", "num_groups", "hidden_size", "num_blocks",
-                                               "num_text_blocks", "patch_size", "txt_embed_dim", "txt_max_length",
-                                               "bottleneck_dim")}
-    with torch.device("meta"):
-        net = JiT_T2I(**kw)
-    net.load_state_dict(sub, strict=True, assign=True)
-    left = [n for n, t in list(net.named_parameters()) + list(net.named_buffers()) if t.is_meta]
-    assert not left, f"tensors without weights: {left[:5]}"
-    return net.to(device).float().eval()
+    n = len(prefix)
+    weights = {k[n:]: v for k, v in state_dict.items() if k.startswith(prefix)}
+    with torch.no_grad():
+        net = JiT_T2I(**{k: v for k, v in kw.items() if k in MODEL_ARGS}).to(device)
+    missing, unexpected = net.load_state_dict(weights, strict=False)
+    if missing or unexpected:
+        raise KeyError(f"{prefix}*: missing {missing[:5]}, unexpected {unexpected[:5]}")
+    return net.float().eval()
 
 
-_BITS = {1: torch.uint8, 2: torch.int16, 4: torch.int32, 8: torch.int64}
-
-
-def twin_weights(sd):
-    """True when every ema_denoiser.X holds the bytes of denoiser.X (a no-EMA checkpoint)."""
-    ema = {k[len("ema_denoiser."):]: v for k, v in sd.items() if k.startswith("ema_denoiser.")}
-    raw = {k[len("denoiser."):]: v for k, v in sd.items() if k.startswith("denoiser.")}
-    if not ema or ema.keys() != raw.keys():
+def ema_is_raw(state_dict):
+    """True when the EMA slot is a byte-for-byte copy of the raw weights (same keys, dtypes, shapes and bytes)."""
+    ema = {k[len("ema_denoiser."):]: v for k, v in state_dict.items() if k.startswith("ema_denoiser.")}
+    raw = {k[len("denoiser."):]: v for k, v in state_dict.items() if k.startswith("denoiser.")}
+    if not ema or set(ema) != set(raw):
         return False
+
+    def as_bytes(t):
+        return t.detach().contiguous().reshape(-1).view(torch.uint8)
+
     for k, e in ema.items():
         r = raw[k]
-        if (e.dtype, e.shape) != (r.dtype, r.shape) or e.element_size() not in _BITS:
+        if e.dtype != r.dtype or e.shape != r.shape:
             return False
-        if e.numel() == 0 or (e.data_ptr() == r.data_ptr() and e.stride() == r.stride()):
-            continue
-        i = _BITS[e.element_size()]
-        if not torch.equal(e.contiguous().view(i), r.contiguous().view(i)):
+        if e.numel() and not torch.equal(as_bytes(e), as_bytes(r)):
             return False
     return True
 
 
-# -------------------------------------------------------------------------------------------------------- tasks
-def spec_of(ckpt):
-    ckpt = os.path.abspath(ckpt)
-    run_dir = os.path.dirname(ckpt)
-    m, r = CKPT_RE.fullmatch(os.path.basename(ckpt)), RUN_RE.fullmatch(os.path.basename(run_dir))
-    assert m, f"not <...>/ms-step=<step>.ckpt: {ckpt}"
-    return dict(ckpt=ckpt, run_root=os.path.dirname(run_dir), size=r.group(1) if r else None, step=int(m.group(1)))
+# ==================================================================================================== bookkeeping
+def task_of(ckpt):
+    """The task spec of one ms checkpoint: its absolute path, run root, ladder size (from exp_ladder_dNNN) and step."""
+    path = os.path.abspath(ckpt)
+    m = CKPT_NAME.fullmatch(os.path.basename(path))
+    if m is None:
+        raise ValueError(f"not an ms checkpoint (<run>/ms-step=<step>.ckpt): {ckpt}")
+    run = os.path.dirname(path)
+    r = RUN_NAME.fullmatch(os.path.basename(run))
+    return dict(ckpt=path, run_root=os.path.dirname(run), size=r.group(1) if r else None, step=int(m.group(1)))
 
 
-def done_keys(out):
-    keys = set()
-    if os.path.exists(out):
-        with open(out) as f:
-            for line in f:
-                if line.strip():
-                    try:
-                        r = json.loads(line)
-                    except json.JSONDecodeError:
-                        continue
-                    keys.add((r["ckpt"], r["weights"], r["n_val"], r["n_train"], r["num_t"], r["seed"], r["data"]))
-    return keys
+def find_checkpoints(runs):
+    """Every <runs>/exp_ladder_d*/ms-step=*.ckpt, sorted by run and step."""
+    found = []
+    for run in sorted(e.path for e in os.scandir(runs) if e.is_dir() and RUN_NAME.fullmatch(e.name)):
+        found += [e.path for e in os.scandir(run) if e.is_file() and CKPT_NAME.fullmatch(e.name)]
+    return sorted(found, key=lambda p: (os.path.dirname(p), int(CKPT_NAME.fullmatch(os.path.basename(p)).group(1))))
 
 
-def complete(path):
+def whole_file(path):
+    """A checkpoint file is whole once its zip directory (written last by torch.save) is readable."""
     try:
         return zipfile.is_zipfile(path)
     except OSError:
         return False
 
 
-def claim(counter):
-    """The next task index from a shared counter file, under lockf."""
-    with open(counter, "a+") as f:
-        fcntl.lockf(f, fcntl.LOCK_EX)
-        f.seek(0)
-        s = f.read().strip()
-        i = int(s) if s else 0
-        f.seek(0)
-        f.truncate()
-        f.write(str(i + 1))
-        f.flush()
-        os.fsync(f.fileno())
-        return i
+class ResultStore:
+    """The JSON-lines output: the set of (checkpoint, weights, n_val, n_train, num_t, seed, data) already recorded,
+    and appends of whole lines (one write per batch of records under an exclusive flock, then fsync)."""
+
+    KEY = ("ckpt", "weights", "n_val", "n_train", "num_t", "seed", "data")
+
+    def __init__(self, path):
+        self.path = path
+
+    def done(self):
+        keys = set()
+        if not os.path.exists(self.path):
+            return keys
+        with open(self.path) as f:
+            for line in f:
+                try:
+                    rec = json.loads(line)
+                    keys.add(tuple(rec[k] for k in self.KEY))
+                except (json.JSONDecodeError, KeyError):
+                    continue  # a torn or foreign line counts as not done
+        return keys
+
+    def missing(self, task, n_val, n_train, data_tag):
+        have = self.done()
+        return [w for w, _ in WEIGHTS if (task["ckpt"], w, n_val, n_train, NUM_T, SEED, data_tag) not in have]
+
+    def add(self, records):
+        import fcntl
+        blob = "".join(json.dumps(r) + "\n" for r in records).encode()
+        fd = os.open(self.path, os.O_WRONLY | os.O_APPEND | os.O_CREAT, 0o644)
+        try:
+            fcntl.flock(fd, fcntl.LOCK_EX)
+            os.write(fd, blob)
+            os.fsync(fd)
+        finally:
+            os.close(fd)
 
 
-def append_lines(path, recs):
-    with open(path, "a") as f:
-        fcntl.lockf(f, fcntl.LOCK_EX)
-        f.write("".join(json.dumps(r) + "\n" for r in recs))
-        f.flush()
-        os.fsync(f.fileno())
+class ClaimDir:
+    """Task hand-out between workers that share a task list: task i belongs to the worker that creates the file
+    `<dir>/<i>` (O_CREAT | O_EXCL). Each worker scans upwards from its last claim, so every task goes to one worker."""
+
+    def __init__(self, path):
+        self.dir = path
+        os.makedirs(path, exist_ok=True)
+        self.pos = 0
+
+    def next(self, n_tasks):
+        while self.pos < n_tasks:
+            i, self.pos = self.pos, self.pos + 1
+            try:
+                os.close(os.open(os.path.join(self.dir, str(i)), os.O_CREAT | os.O_EXCL | os.O_WRONLY, 0o644))
+                return i
+            except FileExistsError:
+                continue
+        return None
 
 
-def run_task(spec, weights, data, a, device):
+def evaluate_task(task, weights, data, opts, device):
+    """The records of one checkpoint for the asked weights (a subset of ema, raw)."""
     t0 = time.time()
-    kw, loss = run_config(os.path.dirname(spec["ckpt"]))
-    ck = torch.load(spec["ckpt"], map_location="cpu", mmap=True, weights_only=False)
-    assert ck["global_step"] == spec["step"], (ck["global_step"], spec["step"])
-    prefixes = dict(WEIGHTS)
-    one_pass = set(weights) == {"ema", "raw"} and twin_weights(ck["state_dict"])
-    nets = {w: build_denoiser(kw, ck["state_dict"], prefixes[w], device) for w in (("raw",) if one_pass else weights)}
-    del ck
+    kw, loss = run_config(os.path.dirname(task["ckpt"]))
+    ck = torch.load(task["ckpt"], map_location="cpu", mmap=True, weights_only=False)
+    if ck.get("global_step") != task["step"]:
+        raise ValueError(f"{task['ckpt']}: global_step {ck.get('global_step')} != {task['step']}")
+    sd = ck["state_dict"]
+    one_pass = set(weights) == {"ema", "raw"} and ema_is_raw(sd)
+    prefix = dict(WEIGHTS)
+    nets = {w: build_denoiser(kw, sd, prefix[w], device) for w in (["raw"] if one_pass else weights)}
+    del ck, sd
     ts = levels(loss["P_mean"], loss["P_std"], loss["timeshift"])
-    res = {s: evaluate(nets, data[s], ts, SEED, a.batch, device, a.threads, loss["t_eps"]) for s in a.splits}
-    recs = []
+    scores = {s: evaluate(nets, data[s], ts, SEED, opts.batch, device, opts.threads, loss["t_eps"])
+              for s in opts.splits}
+    cuda = torch.device(device).type == "cuda"
+    common = dict(n_val=opts.n_val, n_train=opts.n_train, num_t=NUM_T, seed=SEED, data=data["tag"], t=ts.tolist(),
+                  d=kw.get("hidden_size"), nb=kw.get("num_blocks"), nt=kw.get("num_text_blocks"))
+    out = []
     for w in weights:
-        r = dict(spec, weights=w, n_val=a.n_val, n_train=a.n_train, num_t=NUM_T, seed=SEED, data=data["tag"],
-                 t=ts.tolist(), d=kw.get("hidden_size"), nb=kw.get("num_blocks"), nt=kw.get("num_text_blocks"))
-        for s in a.splits:
-            lm, im = (res[s]["raw" if one_pass else w][k] for k in ("level_mean", "image_mean"))
-            r[f"loss_{s}"] = float(lm.mean())
-            r[f"loss_{s}_t"] = lm.tolist()
-            r[f"loss_{s}_se"] = float(im.std() / math.sqrt(len(im)))
-        r.update(elapsed_s=round(time.time() - t0, 1), one_pass=one_pass, weights_in_task=list(weights),
-                 gpu=torch.cuda.get_device_name(device) if torch.device(device).type == "cuda" else "cpu",
-                 host=socket.gethostname(), time=time.strftime("%Y-%m-%dT%H:%M:%S"), framework="nano_gpic_b200")
-        recs.append(r)
-    return recs
+        rec = dict(task, weights=w, **common)
+        for s in opts.splits:
+            res = scores[s]["raw" if one_pass else w]
+            lm, im = res["level_mean"], res["image_mean"]
+            rec[f"loss_{s}"] = float(lm.mean())
+            rec[f"loss_{s}_t"] = lm.tolist()
+            rec[f"loss_{s}_se"] = float(im.std() / math.sqrt(im.numel()))
+        rec.update(elapsed_s=round(time.time() - t0, 1), one_pass=one_pass, weights_in_task=list(weights),
+                   gpu=torch.cuda.get_device_name(device) if cuda else "cpu", host=socket.gethostname(),
+                   time=time.strftime("%Y-%m-%dT%H:%M:%S"), framework="nano_gpic_b200")
+        out.append(rec)
+    return out
 
 
-# ------------------------------------------------------------------------------------------------------ commands
+# ====================================================================================================== commands
+def load_data(path):
+    raw = torch.load(path, map_location="cpu", weights_only=False)
+    data = {name: HeldoutSplit.from_saved(raw[name]) for name in SPLITS if name in raw}
+    data.update(tag=os.path.splitext(os.path.basename(path))[0], n_val=raw.get("n_val"), n_train=raw.get("n_train"))
+    return data
+
+
 def cmd_prep(a):
     from nano_gpic_b200.data.augment import decode_center_u8
     from nano_gpic_b200.data.tars import gpic_samples
     from nano_gpic_b200.data.text_cache import TextCache
 
-    def read(paths, n):
-        out = []
+    def first(paths, n):
+        got = []
         for p in paths:
             for s in gpic_samples(p):
-                out.append(s)
-                if len(out) == n:
-                    return out
-        raise RuntimeError(f"only {len(out)} samples in {len(paths)} shards, {n} asked")
+                got.append(s)
+                if len(got) == n:
+                    return got
+        raise RuntimeError(f"only {len(got)} samples in {len(paths)} shards, {n} asked")
 
-    val = read(sorted(glob.glob(a.val_glob)), a.n_val)
-    tr = read([a.train_shard], a.n_train)
-    cache = TextCache(a.emb_dir)
-    vcache = TextCache(a.val_emb_dir or a.emb_dir)
+    def split_of(samples, cache):
+        embs = [cache.read(s["shard"][:-len(".tar")], s["key"]) for s in samples]
+        img = torch.from_numpy(np.stack([decode_center_u8(s["image"], IMAGE) for s in samples]))
+        return HeldoutSplit(img, torch.cat(embs).contiguous(), [len(e) for e in embs],
+                            extra=dict(keys=[s["key"] for s in samples], captions=[s["caption"] for s in samples]))
 
-    def pack(ss, c):
-        img = torch.from_numpy(np.stack([decode_center_u8(s["image"], IMAGE) for s in ss]))
-        embs = [c.read(s["shard"][:-len(".tar")], s["key"]) for s in ss]
-        lens = torch.tensor([len(e) for e in embs], dtype=torch.int64)
-        offs = torch.cat([torch.zeros(1, dtype=torch.int64), lens.cumsum(0)[:-1]])
-        return dict(img=img, emb=torch.cat(embs).contiguous(), lens=lens, offs=offs, pad_multiple=PAD_MULTIPLE,
-                    text_max_length=TEXT_MAX, keys=[s["key"] for s in ss], captions=[s["caption"] for s in ss])
-    out = dict(version=1, n_val=a.n_val, n_train=a.n_train, val=pack(val, vcache), train=pack(tr, cache),
-               created=time.strftime("%Y-%m-%dT%H:%M:%S"))
-    os.makedirs(os.path.dirname(os.path.abspath(a.data)) or ".", exist_ok=True)
-    tmp = a.data + f".tmp{os.getpid()}"
-    torch.save(out, tmp)
-    os.replace(tmp, a.data)
-    print(f"[prep] wrote {a.data}", flush=True)
-
-
-def load_data(path):
-    d = torch.load(path, map_location="cpu", weights_only=False)
-    for name in SPLITS:
-        if name in d:
-            s = d[name]
-            s["order"] = sorted(range(len(s["lens"])), key=lambda i: (int(s["lens"][i]), i))
-    d["tag"] = os.path.basename(path)[:-len(".pt")]
-    return d
+    val = split_of(first(sorted(glob.glob(a.val_glob)), a.n_val), TextCache(a.val_emb_dir or a.emb_dir))
+    train = split_of(first([a.train_shard], a.n_train), TextCache(a.emb_dir))
+    blob = dict(version=1, n_val=a.n_val, n_train=a.n_train, val=val.to_saved(), train=train.to_saved(),
+                train_shard=os.path.basename(a.train_shard), created=time.strftime("%Y-%m-%dT%H:%M:%S"))
+    os.makedirs(os.path.dirname(os.path.abspath(a.data)), exist_ok=True)
+    part = f"{a.data}.part-{os.getpid()}"
+    torch.save(blob, part)
+    os.replace(part, a.data)
+    print(f"[prep] {a.data}: {a.n_val} val + {a.n_train} train images", flush=True)
 
 
 def cmd_list(a):
-    tag = os.path.basename(a.data)[:-len(".pt")]
-    done = done_keys(a.out)
-    ckpts = a.ckpt or sorted(glob.glob(os.path.join(a.runs, "exp_ladder_d*", "ms-step=*.ckpt")))
-    n = 0
-    for c in ckpts:
-        if time.time() - os.path.getmtime(c) < a.min_age and not complete(c):
+    tag = os.path.splitext(os.path.basename(a.data))[0]
+    store = ResultStore(a.out)
+    paths = a.ckpt if a.ckpt else find_checkpoints(a.runs)
+    listed, young = 0, []
+    for p in paths:
+        if time.time() - os.path.getmtime(p) < a.min_age and not whole_file(p):
+            young.append(os.path.abspath(p))  # still being written: the next listing will have it
             continue
-        spec = spec_of(c)
-        if any((spec["ckpt"], w, a.n_val, a.n_train, NUM_T, SEED, tag) not in done for w, _ in WEIGHTS):
-            print(json.dumps(spec))
-            n += 1
-    print(f"[list] {n} tasks", file=sys.stderr, flush=True)
+        task = task_of(p)
+        if store.missing(task, a.n_val, a.n_train, tag):
+            print(json.dumps(task))
+            listed += 1
+    if a.skipped:
+        with open(a.skipped, "w") as f:
+            f.writelines(p + "\n" for p in young)
+    print(f"[list] {listed} tasks; {len(young)} checkpoints still being written left out", file=sys.stderr, flush=True)
 
 
 def cmd_work(a):
-    device = f"cuda:{a.gpu}" if a.device == "cuda" else "cpu"
-    if a.device == "cuda":
+    device = "cpu" if a.device == "cpu" else f"cuda:{a.gpu}"
+    if device != "cpu":
         torch.cuda.set_device(a.gpu)
     data = load_data(a.data)
+    store = ResultStore(a.out)
     if a.tasks:
         with open(a.tasks) as f:
             tasks = [json.loads(line) for line in f if line.strip()]
-        nxt = lambda: claim(a.counter)
+        claims = ClaimDir(a.counter + ".claims")
+        pick = lambda: claims.next(len(tasks))
     else:
-        tasks = [spec_of(c) for c in a.ckpt]
-        it = iter(range(len(tasks)))
-        nxt = lambda: next(it, len(tasks))
-    fails = 0
-    while True:
-        i = nxt()
-        if i >= len(tasks):
-            break
-        spec = tasks[i]
-        done = done_keys(a.out)
-        weights = [w for w, _ in WEIGHTS if (spec["ckpt"], w, a.n_val, a.n_train, NUM_T, SEED, data["tag"]) not in done]
+        tasks = [task_of(c) for c in a.ckpt]
+        order = iter(range(len(tasks)))
+        pick = lambda: next(order, None)
+    done = failed = 0
+    while (i := pick()) is not None:
+        task = tasks[i]
+        weights = store.missing(task, a.n_val, a.n_train, data["tag"])
         if not weights:
             continue
         try:
-            append_lines(a.out, run_task(spec, weights, data, a, device))
+            store.add(evaluate_task(task, weights, data, a, device))
+            done += 1
         except Exception:
-            fails += 1
-            print(f"[heldout] FAILED {spec['ckpt']}:\n{traceback.format_exc()}", flush=True)
-    return 1 if fails else 0
+            failed += 1
+            print(f"[heldout] {task['ckpt']} failed:\n{traceback.format_exc()}", flush=True)
+    print(f"[heldout] {done} checkpoints done, {failed} failed", flush=True)
+    return 1 if failed else 0
 
 
 def cmd_bench(a):
@@ -392,70 +465,68 @@ def cmd_bench(a):
     net = JiT_T2I(input_size=IMAGE, in_channels=3, num_groups=a.d // 64, hidden_size=a.d, num_blocks=a.nb,
                   num_text_blocks=a.nt, patch_size=16, txt_embed_dim=EMB_DIM, txt_max_length=TEXT_MAX,
                   bottleneck_dim=256).cuda().eval()
-    B = a.batch
-    x = torch.randn(B, 3, IMAGE, IMAGE, device="cuda").clamp(-1, 1)
-    y = torch.randn(B, a.T, EMB_DIM, device="cuda").bfloat16()
-    mask = torch.ones(B, a.T, dtype=torch.bool, device="cuda")
-    noise = torch.randn_like(x)
-    t = torch.tensor(0.5, device="cuda")
+    x = torch.rand(a.batch, 3, IMAGE, IMAGE, device="cuda") * 2 - 1
+    y = torch.randn(a.batch, a.T, EMB_DIM, device="cuda").bfloat16()
+    mask = torch.ones(a.batch, a.T, dtype=torch.bool, device="cuda")
+    noise, t = torch.randn_like(x), torch.tensor(0.5, device="cuda")
+    run = lambda: level_loss(net, x, y, mask, t, noise)
     for _ in range(3):
-        level_loss(net, x, y, mask, t, noise)
+        run()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
+    start.record()
     for _ in range(a.iters):
-        level_loss(net, x, y, mask, t, noise)
-    e1.record()
+        run()
+    end.record()
     torch.cuda.synchronize()
-    s = e0.elapsed_time(e1) / 1000 / a.iters
-    n = a.n_val + a.n_train
-    print(json.dumps(dict(d=a.d, nb=a.nb, nt=a.nt, batch=B, T=a.T, s_per_forward=round(s, 4),
-                          tflops=round(B * fwd_flops(a.d, a.nb, a.nt, a.T) / s / 1e12, 1),
-                          gpu=torch.cuda.get_device_name(), images=n,
-                          compute_min_per_ckpt=round(2 * n * NUM_T / B * s / 60, 2))), flush=True)
+    sec = start.elapsed_time(end) / 1e3 / a.iters
+    images = a.n_val + a.n_train
+    print(json.dumps(dict(d=a.d, nb=a.nb, nt=a.nt, batch=a.batch, T=a.T, s_per_forward=round(sec, 4),
+                          tflops=round(a.batch * fwd_flops(a.d, a.nb, a.nt, a.T) / sec / 1e12, 1),
+                          gpu=torch.cuda.get_device_name(), images=images,
+                          compute_min_per_ckpt=round(2 * images * NUM_T / a.batch * sec / 60, 2))), flush=True)
+
+
+def parser():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    cmds = {name: sub.add_parser(name) for name in ("prep", "list", "work", "bench")}
+    for p in cmds.values():
+        p.add_argument("--n-val", type=int, default=3072)
+        p.add_argument("--n-train", type=int, default=3072)
+    for name in ("prep", "list", "work"):
+        cmds[name].add_argument("--data", required=True)
+    p = cmds["prep"]
+    p.add_argument("--val-glob", required=True)
+    p.add_argument("--train-shard", required=True)
+    p.add_argument("--emb-dir", required=True)
+    p.add_argument("--val-emb-dir", default=None)
+    for name in ("list", "work"):
+        cmds[name].add_argument("--out", required=True)
+        cmds[name].add_argument("--ckpt", nargs="*", default=None)
+    p = cmds["list"]
+    p.add_argument("--runs", default=".")
+    p.add_argument("--min-age", type=float, default=600)
+    p.add_argument("--skipped", default=None)
+    p = cmds["work"]
+    p.add_argument("--tasks", default=None)
+    p.add_argument("--counter", default=None)
+    p.add_argument("--gpu", type=int, default=0)
+    p.add_argument("--device", default="cuda", choices=("cuda", "cpu"))
+    p.add_argument("--batch", type=int, default=BATCH)
+    p.add_argument("--threads", type=int, default=6)
+    p.add_argument("--splits", default="val,train", type=lambda s: s.split(","))
+    p = cmds["bench"]
+    for k, v in (("d", 1792), ("nb", 18), ("nt", 4), ("T", 56), ("iters", 10), ("gpu", 0), ("batch", BATCH)):
+        p.add_argument(f"--{k}", type=int, default=v)
+    return ap
 
 
 def main(argv=None):
-    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    sub = ap.add_subparsers(dest="cmd", required=True)
-    for name in ("prep", "list", "work", "bench"):
-        p = sub.add_parser(name)
-        p.add_argument("--n-val", type=int, default=3072)
-        p.add_argument("--n-train", type=int, default=3072)
-        if name in ("prep", "list", "work"):
-            p.add_argument("--data", required=True)
-        if name == "prep":
-            p.add_argument("--val-glob", required=True)
-            p.add_argument("--train-shard", required=True)
-            p.add_argument("--emb-dir", required=True)
-            p.add_argument("--val-emb-dir", default=None)
-        if name in ("list", "work"):
-            p.add_argument("--out", required=True)
-            p.add_argument("--ckpt", nargs="*", default=None)
-        if name == "list":
-            p.add_argument("--runs", default=".")
-            p.add_argument("--min-age", type=float, default=600)
-        if name == "work":
-            p.add_argument("--tasks", default=None)
-            p.add_argument("--counter", default=None)
-            p.add_argument("--gpu", type=int, default=0)
-            p.add_argument("--device", default="cuda", choices=("cuda", "cpu"))
-            p.add_argument("--batch", type=int, default=BATCH)
-            p.add_argument("--threads", type=int, default=6)
-            p.add_argument("--splits", default="val,train")
-        if name == "bench":
-            for k, v in (("d", 1792), ("nb", 18), ("nt", 4), ("T", 56), ("iters", 10), ("gpu", 0), ("batch", BATCH)):
-                p.add_argument(f"--{k}", type=int, default=v)
-    a = ap.parse_args(argv)
-    if a.cmd == "prep":
-        return cmd_prep(a)
-    if a.cmd == "list":
-        return cmd_list(a)
-    if a.cmd == "work":
-        assert bool(a.tasks) == bool(a.counter) and bool(a.tasks) != bool(a.ckpt), "--tasks with --counter, or --ckpt"
-        a.splits = a.splits.split(",")
-        return cmd_work(a)
-    return cmd_bench(a)
+    a = parser().parse_args(argv)
+    if a.cmd == "work" and not ((a.tasks and a.counter and not a.ckpt) or (a.ckpt and not a.tasks)):
+        raise SystemExit("work: give --ckpt ..., or --tasks FILE with --counter FILE")
+    return {"prep": cmd_prep, "list": cmd_list, "work": cmd_work, "bench": cmd_bench}[a.cmd](a)
 
 
 if __name__ == "__main__":

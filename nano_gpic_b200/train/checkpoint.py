@@ -11,16 +11,18 @@ File names: ms-step=NNNNNN.ckpt (model only), last.ckpt (full state), last-term.
 The reference's tools (heldout_loss.build_denoiser: strict load of denoiser.* / ema_denoiser.*, global_step) read these
 files, and this module loads the reference's own checkpoints.
 
-AsyncWriter is the reference's AsyncShmCheckpointIO idea (src/plugins/async_ckpt_io.py:1-261) on plain
-multiprocessing: the training process copies the tensors into a shared-memory buffer (one device-to-host copy), a
-writer process torch.saves the dict to `<file>.tmp<pid>` and renames it into place (atomic), with the file's mtime set
-to the snapshot time. EMA twins (ema_denoiser.X bit-equal to denoiser.X) share one storage in the file.
+AsyncWriter has the role of the reference's AsyncShmCheckpointIO (src/plugins/async_ckpt_io.py:1-261): training
+continues while a checkpoint is written. Here the training process copies the tensors into shared-memory files (one
+device-to-host copy) and a writer process, fed over a pipe, writes the dict to `<file>.part-<pid>`, fsyncs it and
+renames it into place (atomic), with the file's mtime set to the snapshot time. EMA twins (ema_denoiser.X bit-equal to
+denoiser.X) share one storage in the file.
 """
 import glob
+import math
 import os
-import queue
 import re
 import signal
+import tempfile
 import time
 
 import torch
@@ -117,156 +119,184 @@ def read_shard_clock(path):
     return ck.get(SHARD_CLOCK_KEY)
 
 
+def _partial_name(path):
+    """The file a checkpoint is written to before it is renamed over `path`: `<path>.part-<pid>`."""
+    return f"{path}.part-{os.getpid()}"
+
+
+def _publish(obj, path, stamp=None):
+    """torch.save into the partial file, flush it to disk, rename it over `path` (atomic), and give the file the
+    snapshot's time (the moment the state was taken, not the moment the write finished)."""
+    part = _partial_name(path)
+    with open(part, "wb") as f:
+        torch.save(obj, f)
+        f.flush()
+        os.fsync(f.fileno())
+    os.replace(part, path)
+    if stamp is not None:
+        os.utime(path, (stamp, stamp))
+
+
 def save_sync(ck, path):
-    """torch.save to a temporary file, then an atomic rename."""
-    tmp = f"{path}.tmp{os.getpid()}"
-    torch.save(_to_cpu(ck), tmp)
-    os.replace(tmp, path)
+    """Writes a checkpoint in the calling process (tensors moved to the host first)."""
+    _publish(_to_cpu(ck), path)
 
 
 def _to_cpu(obj):
-    if torch.is_tensor(obj):
-        return obj.detach().cpu()
+    return _tree_map(obj, lambda v: v.detach().cpu() if torch.is_tensor(v) else v)
+
+
+def _tree_map(obj, fn):
     if isinstance(obj, dict):
-        return {k: _to_cpu(v) for k, v in obj.items()}
+        return {k: _tree_map(v, fn) for k, v in obj.items()}
     if isinstance(obj, (list, tuple)):
-        return type(obj)(_to_cpu(v) for v in obj)
-    return obj
-
-
-# ------------------------------------------------------------------------------------------------------ async writer
-class _Ref:
-    def __init__(self, off, dtype, shape):
-        self.off, self.dtype, self.shape = off, dtype, tuple(shape)
-
-
-class _Slot:
-    """Placeholder for a tensor while the shared buffer is planned."""
-
-    def __init__(self, key, dtype, shape):
-        self.key, self.dtype, self.shape = key, dtype, tuple(shape)
-
-
-def _map(obj, fn):
-    if isinstance(obj, dict):
-        return {k: _map(v, fn) for k, v in obj.items()}
-    if isinstance(obj, (list, tuple)):
-        return type(obj)(_map(v, fn) for v in obj)
+        return type(obj)(_tree_map(v, fn) for v in obj)
     return fn(obj)
 
 
-def _writer_main(jobs, acks, delay):
+# ------------------------------------------------------------------------------------------------------ async writer
+# How a save travels. The training process copies every tensor of the checkpoint into a file in shared memory
+# (/dev/shm; one file per slot, grown when a checkpoint needs more) and sends the writer process one message over a
+# pipe: (slot, file, bytes used, skeleton, destination, snapshot time), where the skeleton is the checkpoint dict with
+# each tensor replaced by a _Blob (offset, dtype, shape). The writer maps the file, turns each _Blob into a tensor
+# over the mapped bytes (torch.frombuffer: no copy; one tensor per offset, so EMA twins stay one storage), writes the
+# dict (_publish) and answers (slot, destination, error or None). The writer leaves when its end of the pipe reports
+# EOF, which also happens when the training process dies, and removes the shared files it was given.
+class _Blob:
+    __slots__ = ("off", "dtype", "shape")
+
+    def __init__(self, off, dtype, shape):
+        self.off, self.dtype, self.shape = off, dtype, tuple(shape)
+
+    def nbytes(self):
+        return math.prod(self.shape) * torch.empty((), dtype=self.dtype).element_size()
+
+
+def _writer_loop(conn, delay):
+    import mmap
     signal.signal(signal.SIGTERM, signal.SIG_IGN)  # a TERM to the job must not cut a write short
     signal.signal(signal.SIGINT, signal.SIG_IGN)
-    parent = os.getppid()
-    while True:
-        try:
-            job = jobs.get(timeout=5)
-        except queue.Empty:
-            if os.getppid() != parent:
-                return
-            continue
-        if job is None:
-            return
-        k, buf, snap, path, t_snap = job
-        try:
-            if delay:
-                time.sleep(delay)
-            st = buf.untyped_storage()
-            parts = {}
+    mapped = {}  # shared file -> (mmap, size)
 
-            def rebuild(r):
-                if not isinstance(r, _Ref):
-                    return r
-                n = int(torch.Size(r.shape).numel()) * torch.empty((), dtype=r.dtype).element_size()
-                if n == 0:
-                    return torch.empty(r.shape, dtype=r.dtype)
-                if r.off not in parts:
-                    parts[r.off] = st[r.off:r.off + n]
-                return torch.empty(0, dtype=r.dtype).set_(parts[r.off], 0, r.shape)
-            ck = _map(snap, rebuild)
-            tmp = f"{path}.tmp{os.getpid()}"
-            torch.save(ck, tmp)
-            os.replace(tmp, path)
-            os.utime(path, (t_snap, t_snap))
-            acks.put((k, path, None))
-        except Exception as e:  # reported in the training process at its next save or at close()
-            acks.put((k, path, repr(e)))
+    def region(name, size):
+        if name not in mapped or mapped[name][1] < size:
+            with open(name, "r+b") as f:
+                mapped[name] = (mmap.mmap(f.fileno(), size), size)
+        return mapped[name][0]
+
+    try:
+        while True:
+            try:
+                msg = conn.recv()
+            except (EOFError, OSError):
+                return
+            if msg is None:
+                return
+            slot, shm, used, skel, dest, stamp = msg
+            try:
+                if delay:
+                    time.sleep(delay)
+                mm = region(shm, used)
+                made = {}
+
+                def tensor_of(v):
+                    if not isinstance(v, _Blob):
+                        return v
+                    if v.off not in made:
+                        n = math.prod(v.shape)
+                        made[v.off] = (torch.frombuffer(mm, dtype=v.dtype, count=n, offset=v.off).view(v.shape)
+                                       if n else torch.empty(v.shape, dtype=v.dtype))
+                    return made[v.off]
+                _publish(_tree_map(skel, tensor_of), dest, stamp)
+                made.clear()
+                conn.send((slot, dest, None))
+            except Exception as e:  # reported in the training process at its next save or at wait()
+                conn.send((slot, dest, repr(e)))
+    finally:
+        for name in list(mapped):
+            try:
+                os.unlink(name)
+            except OSError:
+                pass
 
 
 class AsyncWriter:
-    """Checkpoint writes in a separate process. `save(ck, path)` returns once the tensors are copied into a shared
-    buffer; `wait()` blocks until every write is on disk. Two buffers: two saves may be in flight."""
+    """Checkpoint writes in a separate process. `save(ck, path)` returns once the tensors are copied into shared
+    memory; `wait()` blocks until every write is on disk and raises if one failed. `nbuf` slots: that many saves may
+    be in flight."""
 
     def __init__(self, nbuf=2, delay=None):
         ctx = mp.get_context("spawn")
-        self.jobs, self.acks = ctx.Queue(), ctx.Queue()
+        self.conn, child = ctx.Pipe(duplex=True)
         d = float(os.environ.get("NG_ASYNC_CKPT_TEST_DELAY", "0")) if delay is None else delay
-        self.proc = ctx.Process(target=_writer_main, args=(self.jobs, self.acks, d), daemon=True)
+        self.proc = ctx.Process(target=_writer_loop, args=(child, d), daemon=True)
         self.proc.start()
-        self.bufs = [None] * nbuf     # shared uint8 buffers
-        self.busy = [None] * nbuf     # path being written from buffer k, or None
+        child.close()
+        shm = "/dev/shm" if os.path.isdir("/dev/shm") else tempfile.gettempdir()
+        self.files = [os.path.join(shm, f"ng-ckpt-{os.getpid()}-{id(self):x}-{k}") for k in range(nbuf)]
+        self.sizes = [0] * nbuf
+        self.views = [None] * nbuf   # uint8 tensors over the shared files (this process's mapping)
+        self.busy = [None] * nbuf    # destination being written from slot k, or None
         self.errors = []
 
-    def _reap(self, block):
-        """Collects finished writes; with block=True waits for at least one."""
+    def _collect(self, block):
+        """Takes the writer's answers; block=True waits until at least one slot is free again."""
         while any(b is not None for b in self.busy):
-            try:
-                k, path, err = self.acks.get(timeout=1.0) if block else self.acks.get_nowait()
-            except queue.Empty:
+            if not self.conn.poll(1.0 if block else 0):
                 if not block:
                     return
                 if not self.proc.is_alive():
                     raise RuntimeError("checkpoint writer process died")
                 continue
-            self.busy[k] = None
+            slot, dest, err = self.conn.recv()
+            self.busy[slot] = None
             if err:
-                self.errors.append((path, err))
+                self.errors.append((dest, err))
             if block:
                 return
 
+    def _slot_view(self, k, size):
+        if self.sizes[k] < size:
+            with open(self.files[k], "a+b") as f:
+                f.truncate(size)
+            self.views[k] = torch.from_file(self.files[k], shared=True, size=size, dtype=torch.uint8)
+            self.sizes[k] = size
+        return self.views[k]
+
     def save(self, ck, path):
-        self._reap(block=False)
-        while all(b is not None for b in self.busy):
-            self._reap(block=True)
+        self._collect(block=False)
+        while None not in self.busy:
+            self._collect(block=True)
         k = self.busy.index(None)
+        # EMA twins (ema_denoiser.X with denoiser.X's values) are stored once
         sd = ck.get("state_dict", {})
-        twins = {}
-        for key, t in sd.items():  # ema_denoiser.X bit-equal to denoiser.X: one storage
+        same_as = {}
+        for key, t in sd.items():
             if key.startswith("ema_denoiser.") and torch.is_tensor(t):
                 r = sd.get("denoiser." + key[len("ema_denoiser."):])
                 if r is t or (torch.is_tensor(r) and r.dtype == t.dtype and r.shape == t.shape and torch.equal(r, t)):
-                    twins[id(t)] = r
-        tensors, seen = [], {}
-
-        def plan(t):
-            if not torch.is_tensor(t):
-                return t
-            src = twins.get(id(t), t)
-            if id(src) not in seen:
-                seen[id(src)] = None
-                tensors.append(src)
-            return _Slot(id(src), t.dtype, t.shape)
-        skel = _map(ck, plan)
-        offs, off = {}, 0
-        for t in tensors:
-            offs[id(t)] = off
-            off += (t.numel() * t.element_size() + 63) // 64 * 64
-        if self.bufs[k] is None or self.bufs[k].numel() < off:
-            self.bufs[k] = torch.empty(max(off, 1), dtype=torch.uint8).share_memory_()
-        buf = self.bufs[k]
-        for t in tensors:
+                    same_as[id(t)] = r
+        offset, order, size = {}, [], 0
+        for t in _leaves(ck):
+            src = same_as.get(id(t), t)
+            if id(src) not in offset:
+                offset[id(src)] = size
+                order.append(src)
+                size += -(-src.numel() * src.element_size() // 64) * 64  # 64-byte aligned
+        view = self._slot_view(k, max(size, 64))
+        for t in order:
             n = t.numel() * t.element_size()
             if n:
-                dst = buf[offs[id(t)]:offs[id(t)] + n].view(t.dtype).view(t.shape)
-                dst.copy_(t.detach(), non_blocking=False)
-        snap = _map(skel, lambda v: _Ref(offs[v.key], v.dtype, v.shape) if isinstance(v, _Slot) else v)
+                o = offset[id(t)]
+                view[o:o + n].view(t.dtype).view(t.shape).copy_(t.detach())
+        skel = _tree_map(ck, lambda v: _Blob(offset[id(same_as.get(id(v), v))], v.dtype, v.shape)
+                         if torch.is_tensor(v) else v)
         self.busy[k] = path
-        self.jobs.put((k, buf, snap, path, time.time()))
+        self.conn.send((k, self.files[k], max(size, 64), skel, path, time.time()))
 
     def wait(self):
         while any(b is not None for b in self.busy):
-            self._reap(block=True)
+            self._collect(block=True)
         if self.errors:
             errs, self.errors = self.errors, []
             raise RuntimeError(f"checkpoint writes failed: {errs}")
@@ -275,15 +305,30 @@ class AsyncWriter:
         try:
             self.wait()
         finally:
-            self.jobs.put(None)
+            try:
+                self.conn.send(None)
+            except OSError:
+                pass
             self.proc.join(timeout=30)
+            self.conn.close()
+            self.views = [None] * len(self.views)
+            for name in self.files:
+                if os.path.exists(name):
+                    os.unlink(name)
+
+
+def _leaves(obj):
+    out = []
+    _tree_map(obj, lambda v: out.append(v) if torch.is_tensor(v) else None)
+    return out
 
 
 def clean_tmp(directory):
-    """Removes `*.ckpt.tmp<pid>` leftovers of writers that were killed (reference async_ckpt_io.py:120-138)."""
+    """Removes partial checkpoint files (`*.ckpt.part-<pid>`) left by writers that were killed: those whose process
+    no longer exists (a live writer's file is kept)."""
     n = 0
-    for p in glob.glob(os.path.join(directory, "*.ckpt.tmp*")):
-        m = re.search(r"\.tmp(\d+)$", p)
+    for p in glob.glob(os.path.join(directory, "*.ckpt.part-*")):
+        m = re.search(r"\.part-(\d+)$", p)
         if m and not os.path.exists(f"/proc/{m.group(1)}"):
             os.remove(p)
             n += 1

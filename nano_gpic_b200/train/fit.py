@@ -26,7 +26,7 @@ from ..config.cli import get_dotted, instantiate, is_spec, resolve, run_dir, str
 from ..data.pil_resize import ResizeBatch
 from ..parallel.rebalance import Rebalancer
 from .callbacks import EMASpec, Warmup
-from .checkpoint import AsyncWriter, build_checkpoint, find_resume, load_into, save_sync
+from .checkpoint import AsyncWriter, build_checkpoint, clean_tmp, find_resume, load_into, save_sync
 from .trainer import Trainer
 
 
@@ -150,6 +150,9 @@ def fit(cfg):
     if rank == 0:
         os.makedirs(rdir, exist_ok=True)
         write_config(cfg, rdir)
+        stale = clean_tmp(rdir)  # partial checkpoints of writers killed with an earlier launch
+        if stale:
+            print(f"[ckpt] removed {stale} partial checkpoint file(s) of an earlier launch", flush=True)
     callbacks = [instantiate(c) for c in (tcfg.get("callbacks") or [])]
     max_steps = int(tcfg.get("max_steps") or get_dotted(cfg, "model.lr_scheduler.init_args.max_steps") or 1)
     writer = AsyncWriter() if rank == 0 and os.environ.get("GPIC_MFU_ASYNC_CKPT", "1") != "0" else None

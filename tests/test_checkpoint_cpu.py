@@ -72,7 +72,7 @@ def test_async_writer_and_twins(tmp_path):
         assert torch.equal(sd["denoiser." + k], tr.model.state_dict()[k])
         # twins: one storage in the file
         assert sd["denoiser." + k].untyped_storage().data_ptr() == sd["ema_denoiser." + k].untyped_storage().data_ptr()
-    assert not [f for f in os.listdir(tmp_path) if ".tmp" in f]
+    assert not [f for f in os.listdir(tmp_path) if ".part-" in f]
 
 
 def test_policy_names_and_resume_skip(tmp_path):
@@ -110,3 +110,17 @@ def test_save_on_term_agreement():
     out = mp.Manager().dict()
     mp.start_processes(_term_rank, args=(2, port, out), nprocs=2, join=True, start_method="spawn")
     assert out[0] == out[1] == 10
+
+
+def test_partial_files_of_dead_writers_are_removed(tmp_path):
+    """A partial checkpoint whose writer process is gone is removed; one of a live process is kept."""
+    from nano_gpic_b200.train.checkpoint import clean_tmp
+    import subprocess
+    p = subprocess.Popen(["true"])
+    p.wait()  # a pid that no longer exists
+    dead = tmp_path / f"last.ckpt.part-{p.pid}"
+    live = tmp_path / f"ms-step=000004.ckpt.part-{os.getpid()}"
+    dead.write_bytes(b"x")
+    live.write_bytes(b"y")
+    assert clean_tmp(str(tmp_path)) == 1
+    assert not dead.exists() and live.exists()
