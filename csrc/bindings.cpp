@@ -83,6 +83,7 @@ void attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& 
                  const at::Tensor& n1, const at::Tensor& o, const at::Tensor& lse, const at::Tensor& dq,
                  const at::Tensor& dk0, const at::Tensor& dv0, const c10::optional<at::Tensor>& dk1,
                  const c10::optional<at::Tensor>& dv1, int64_t Lq, int64_t L0, int64_t L1, double scale, int64_t version);
+void attn_prof_set(const c10::optional<at::Tensor>& counters);
 void colsum(const at::Tensor& src, const at::Tensor& out, bool accumulate);
 void add_rows(const at::Tensor& a, const at::Tensor& table, const at::Tensor& out, int64_t period);
 }  // namespace ng
@@ -120,6 +121,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "tiles per CTA; version 1: one query tile per CTA)", py::arg("q"), py::arg("k0"), py::arg("v0"), py::arg("k1"),
         py::arg("v1"), py::arg("n0"), py::arg("n1"), py::arg("o"), py::arg("lse"), py::arg("Lq"), py::arg("L0"),
         py::arg("L1"), py::arg("scale"), py::arg("version") = 2);
+  m.def("attn_prof_set", &ng::attn_prof_set, "cycle counters for the profiled attention kernels (None: off)");
   m.def("attn_bwd_tc", &ng::attn_bwd_tc, "masked attention backward on tcgen05/TMEM (version 2: persistent, 8 compute "
         "warps; version 1: CTA per key tile)", py::arg("dout"), py::arg("q"), py::arg("k0"), py::arg("v0"),
         py::arg("k1"), py::arg("v1"), py::arg("n0"), py::arg("n1"), py::arg("o"), py::arg("lse"), py::arg("dq"),

@@ -113,6 +113,35 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
+// Packed fp32 pairs (sm_100: one instruction for two lanes of work, round to nearest even like the scalar forms).
+__device__ __forceinline__ uint64_t f2_bits(float2 v) {
+  return (uint64_t)__float_as_uint(v.x) | ((uint64_t)__float_as_uint(v.y) << 32);
+}
+__device__ __forceinline__ float2 bits_f2(uint64_t v) {
+  return make_float2(__uint_as_float((uint32_t)v), __uint_as_float((uint32_t)(v >> 32)));
+}
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {  // a * b + c
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return bits_f2(d);
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+// max of three (sm_100 three-input form)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // 2^x on the special-function unit (the PTX ex2.approx.ftz instruction: ~2 ulp, subnormal results flushed to 0;
 // ex2(-inf) = +0). Used for softmax weights, where inputs are <= 0.
 __device__ __forceinline__ float ex2_ftz(float x) {

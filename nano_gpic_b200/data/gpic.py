@@ -34,18 +34,40 @@ def expand_pattern(pattern):
 
 
 def _rank_world():
+    """(rank, world) from torch.distributed, else from RANK / WORLD_SIZE. A world of several ranks whose rank is not
+    known is refused: taking rank 0 would make every rank read rank 0's shards."""
     import torch.distributed as dist
     if dist.is_available() and dist.is_initialized():
         return dist.get_rank(), dist.get_world_size()
-    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    if world > 1 and "RANK" not in os.environ:
+        raise RuntimeError(f"WORLD_SIZE={world} but no RANK and no torch.distributed group: the shard split is unknown")
+    return int(os.environ.get("RANK", 0)), world
 
 
 class EpochShuffledShards:
+    """The shard order of every pass over the data, split over ranks, with a per-rank log of started shards that a
+    resume reads: shards started before the stop are not read again in that pass (reference
+    baselines/PixelGen/src/data/dataset/gpic_dataset.py:64-248).
+
+    Pass p shuffles the urls with Random(seed * 100003 + p); rank r takes every world-th shard from position r. The log
+    `shards_started_rank<r>.txt` gets one line `<time> <pass> <url>` when a shard starts. On construction the log gives
+    the resume point: the newest pass that has a logged shard, minus its logged shards, or the next pass when all of
+    this rank's shards of that pass were started. A torn last line (a worker killed inside its write) is dropped. A log
+    that names a shard this rank would not read in that pass (another seed, shard list or number of ranks) is refused
+    with ValueError rather than silently mixing two splits; so is a change of rank or world between construction and
+    iteration."""
+
     def __init__(self, urls, seed, log_dir=None):
         self.urls, self.seed = list(urls), int(seed)
         self.rank, self.world = _rank_world()
         self.log_path = os.path.join(log_dir, f"shards_started_rank{self.rank}.txt") if log_dir else None
         self.passes, self.skip = self._resume_point() if self.log_path else (0, set())
+
+    def check_rank(self):
+        now = _rank_world()
+        if now != (self.rank, self.world):
+            raise ValueError(f"rank or world changed since the shard split was made: {now} != {(self.rank, self.world)}")
 
     def perm(self, p):
         urls = list(self.urls)
@@ -67,7 +89,13 @@ class EpochShuffledShards:
                     p, started = q, set()
                 if q == p:
                     started.add(parts[2])
-        if len(started) >= len(self.perm(p)[self.rank::self.world]):
+        mine = set(self.perm(p)[self.rank::self.world])
+        foreign = started - mine
+        if foreign:
+            raise ValueError(f"{self.log_path}: pass {p} logs {len(foreign)} shard(s) that rank {self.rank} of "
+                             f"{self.world} does not read with seed {self.seed} (another seed, shard list or number "
+                             f"of ranks?), e.g. {sorted(foreign)[0]}")
+        if started == mine:
             return p + 1, set()
         return p, started
 
@@ -104,6 +132,7 @@ class GPICDataset(IterableDataset):
 
     def _samples(self, p):
         wi = get_worker_info()
+        self.shards.check_rank()
         shards = self.shards.shards_of_pass(p)
         if wi is not None:
             shards = shards[wi.id::wi.num_workers]
@@ -224,10 +253,12 @@ class GPICWebDataset(GPICDataset):
                  text_max_length=320, pad_multiple=8, shared_bucket=False, corrupted_csv=None, output_fields=None,
                  is_val=False, seed=None, batch_size=128, image_size=256, log_dir=None):
         seed = int(os.environ.get("GPIC_SHARD_SEED", 0)) if seed is None else seed
+        if log_dir is None and not is_val:
+            log_dir = os.environ.get("GPIC_SHARD_LOG_DIR")
         super().__init__(os.path.join(tar_dir, tar_pattern), emb_dir, seed=seed, image_size=image_size,
                          group_window=group_window if group_text_len else batch_size, group_batch=batch_size,
                          pad_multiple=pad_multiple, text_max_length=text_max_length, shared_bucket=shared_bucket,
-                         log_dir=log_dir)
+                         log_dir=None if is_val else log_dir)  # only the training set keeps a shard log
         self.is_val = is_val
 
 

@@ -16,6 +16,7 @@ import torch
 from .._ext import ext
 
 HEAD = 64
+_VERSIONS = {"tc": 3, "tc2": 2, "tc1": 1}  # kernel versions of csrc/attn_tc.cu
 
 
 def _lens(n, B, device):
@@ -43,9 +44,10 @@ def _keys_cpu(k0, v0, L0, n0, k1, v1, L1, n1, B, H):
 def attn_fwd(q, Lq, k0, v0, L0, n0, k1=None, v1=None, L1=0, n1=None, scale=0.125, impl="tc"):
     """q [B*Lq, H*64]; k0/v0 [B*L0, H*64]; k1/v1 [B*L1, H*64] or None; n0/n1: int or int32 [B] valid-key counts.
     Returns (o [B*Lq, H*64] bf16, lse [B, H, Lq] fp32). On CUDA the forward runs on tcgen05/TMEM
-    (csrc/attn_tc.cu; impl="tc", the default: a persistent kernel with two query tiles per CTA ping-ponging on the
-    tensor core; impl="tc1": one 128-query tile per CTA); impl="mma" selects the warp-level mma.sync kernel
-    (csrc/attention.cu), kept as a test oracle."""
+    (csrc/attn_tc.cu; impl="tc", the default: version 3, a persistent kernel with two query tiles per CTA, S released
+    as soon as it is in registers, P double-buffered, O rescaled only when a row maximum grows by more than 2^8;
+    impl="tc2": version 2, the same two-tile ping-pong without those three; impl="tc1": one 128-query tile per CTA);
+    impl="mma" selects the warp-level mma.sync kernel (csrc/attention.cu), kept as a test oracle."""
     rows, C = q.shape
     B, H = rows // Lq, C // HEAD
     n0 = _lens(n0, B, q.device)
@@ -61,8 +63,8 @@ def attn_fwd(q, Lq, k0, v0, L0, n0, k1=None, v1=None, L1=0, n1=None, scale=0.125
         return o.to(torch.bfloat16), lse
     o = torch.empty(rows, C, device=q.device, dtype=torch.bfloat16)
     lse = torch.empty(B, H, Lq, device=q.device, dtype=torch.float32)
-    if impl in ("tc", "tc1"):
-        ext().attn_fwd_tc(q, k0, v0, k1, v1, n0, n1, o, lse, Lq, L0, L1, scale, 1 if impl == "tc1" else 2)
+    if impl in _VERSIONS:
+        ext().attn_fwd_tc(q, k0, v0, k1, v1, n0, n1, o, lse, Lq, L0, L1, scale, _VERSIONS[impl])
     else:
         ext().attn_fwd(q, k0, v0, k1, v1, n0, n1, o, lse, Lq, L0, L1, scale)
     return o, lse
@@ -71,8 +73,11 @@ def attn_fwd(q, Lq, k0, v0, L0, n0, k1=None, v1=None, L1=0, n1=None, scale=0.125
 def attn_bwd(do, q, Lq, k0, v0, L0, n0, o, lse, k1=None, v1=None, L1=0, n1=None, scale=0.125,
              dq=None, dk0=None, dv0=None, dk1=None, dv1=None, impl="tc"):
     """Gradients of attn_fwd. dq/dk*/dv* may be given as (strided) views to write into; missing ones are allocated.
-    Returns (dq, dk0, dv0, dk1, dv1). On CUDA the backward runs on tcgen05/TMEM (csrc/attn_tc.cu: CTA per key tile,
-    dK/dV accumulated in TMEM, dQ summed over key tiles by TMA reduce-adds); impl="mma" selects the mma.sync kernels."""
+    Returns (dq, dk0, dv0, dk1, dv1). On CUDA the backward runs on tcgen05/TMEM (csrc/attn_tc.cu; impl="tc", the
+    default: version 3, a persistent CTA per (sample, head) with dQ of its (at most two) query tiles accumulated in
+    TMEM over the key tiles and dK/dV per key tile over the query tiles; longer query sets take version 2;
+    impl="tc2": version 2, a persistent CTA per key tile whose dQ partials are summed by TMA reduce-adds; impl="tc1":
+    one CTA per key tile); impl="mma" selects the mma.sync kernels."""
     rows, C = q.shape
     B, H = rows // Lq, C // HEAD
     n0 = _lens(n0, B, q.device)
@@ -119,9 +124,9 @@ def attn_bwd(do, q, Lq, k0, v0, L0, n0, o, lse, k1=None, v1=None, L1=0, n1=None,
     if k1 is not None:
         dk1 = alloc(dk1, B * L1)
         dv1 = alloc(dv1, B * L1)
-    if impl in ("tc", "tc1"):
+    if impl in _VERSIONS:
         ext().attn_bwd_tc(do, q, k0, v0, k1, v1, n0, n1, o, lse, dq, dk0, dv0, dk1, dv1, Lq, L0, L1, scale,
-                          1 if impl == "tc1" else 2)
+                          _VERSIONS[impl])
     else:
         ext().attn_bwd(do, q, k0, v0, k1, v1, n0, n1, o, lse, dq, dk0, dv0, dk1, dv1, Lq, L0, L1, scale)
     return dq, dk0, dv0, dk1, dv1

@@ -106,9 +106,11 @@ def bench_attn(d, batch, rows, T=128):
     keys = (L + lens.float()).sum().item()
     fl_fwd = 4.0 * L * keys * 64 * H
     res = {"tc_fwd": time_fn(lambda: A.attn_fwd(q, L, k0, v0, L, L, k1, v1, T, lens, impl="tc")),
+           "tc2_fwd": time_fn(lambda: A.attn_fwd(q, L, k0, v0, L, L, k1, v1, T, lens, impl="tc2")),
            "tc1_fwd": time_fn(lambda: A.attn_fwd(q, L, k0, v0, L, L, k1, v1, T, lens, impl="tc1")),
            "mma_fwd": time_fn(lambda: A.attn_fwd(q, L, k0, v0, L, L, k1, v1, T, lens, impl="mma")),
            "tc_bwd": time_fn(lambda: A.attn_bwd(do, q, L, k0, v0, L, L, o, lse, k1, v1, T, lens, impl="tc")),
+           "tc2_bwd": time_fn(lambda: A.attn_bwd(do, q, L, k0, v0, L, L, o, lse, k1, v1, T, lens, impl="tc2")),
            "tc1_bwd": time_fn(lambda: A.attn_bwd(do, q, L, k0, v0, L, L, o, lse, k1, v1, T, lens, impl="tc1")),
            "mma_bwd": time_fn(lambda: A.attn_bwd(do, q, L, k0, v0, L, L, o, lse, k1, v1, T, lens, impl="mma"))}
     Q = q.view(batch, L, H, 64).transpose(1, 2)

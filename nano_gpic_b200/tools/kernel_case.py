@@ -15,7 +15,9 @@ def main():
     ap.add_argument("--d", type=int, default=1024)
     ap.add_argument("--t", type=int, default=128, help="caption length (attention cases)")
     ap.add_argument("--reps", type=int, default=3)
-    ap.add_argument("--impl", default=None, help="attention implementation (tc, tc1, mma)")
+    ap.add_argument("--impl", default=None, help="attention implementation (tc, tc2, tc1, mma)")
+    ap.add_argument("--prof", action="store_true", help="attention backward: print the per-role cycle breakdown of the "
+                                                         "profiled kernel instantiation (csrc/attn_tc.cu)")
     ap.add_argument("--time", action="store_true", help="also print the mean time per call (CUDA events, after the "
                                                           "--reps warm-up calls, 20 timed calls)")
     a = ap.parse_args()
@@ -71,6 +73,22 @@ def main():
     torch.cuda.synchronize()
     status.check()
     print(f"{a.case} ok", flush=True)
+    if a.prof:
+        from nano_gpic_b200._ext import ext
+        cnt = torch.zeros(16, dtype=torch.int64, device="cuda")
+        ext().attn_prof_set(cnt)
+        fn()
+        torch.cuda.synchronize()
+        ext().attn_prof_set(None)
+        c = cnt.tolist()
+        names = ["compute: wait S", "compute: load+exp", "compute: wait products", "compute: store P/dS",
+                 "compute: wait dK/dV", "compute: dK/dV out", "compute: wait dQ", "compute: dQ out",
+                 "compute: total", "mma: wait Q/dO", "mma: wait K/V", "mma: wait S free", "mma: wait P/dS",
+                 "mma: wait epilogue", "mma: total", "tma: waits"]
+        tot_c, tot_m = max(c[8], 1), max(c[14], 1)
+        for i, (n, v) in enumerate(zip(names, c)):
+            base = tot_c if i <= 8 else tot_m if i <= 14 else tot_m
+            print(f"  {n:26s} {v:16d}  {100.0 * v / base:6.1f} %", flush=True)
     if a.time:
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()

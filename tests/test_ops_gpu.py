@@ -140,7 +140,10 @@ def test_attention_tc_forward(case):
         k1 = v1 = None
     o, lse = A.attn_fwd(q, Lq, k0, v0, L0, n0, k1, v1, L1, n1, impl="tc")
     o1, lse1 = A.attn_fwd(q, Lq, k0, v0, L0, n0, k1, v1, L1, n1, impl="tc1")
-    _close(o, o1, rtol=1e-2, atol=1e-2, what="o: two-tile vs one-tile kernel")
+    _close(o, o1, rtol=1e-2, atol=1e-2, what="o: version 3 vs one-tile kernel")
+    o2, lse2 = A.attn_fwd(q, Lq, k0, v0, L0, n0, k1, v1, L1, n1, impl="tc2")
+    _close(o, o2, rtol=1e-2, atol=1e-2, what="o: version 3 vs version 2")
+    _close(lse, lse2, rtol=1e-4, atol=1e-4, what="lse: version 3 vs version 2")
     om, lsem = A.attn_fwd(q, Lq, k0, v0, L0, n0, k1, v1, L1, n1, impl="mma")
     oc, lsec = A.attn_fwd(*_cpu(q), Lq, *_cpu(k0, v0), L0, n0 if isinstance(n0, int) else n0.cpu(),
                           *_cpu(k1, v1), L1, n1.cpu() if n1 is not None else None)
@@ -179,6 +182,7 @@ def test_attention_tc_backward(case):
     o, lse = A.attn_fwd(q, Lq, k0, v0, L0, n0, k1, v1, L1, n1)
     do = torch.randn_like(o)
     g1 = A.attn_bwd(do, q, Lq, k0, v0, L0, n0, o, lse, k1, v1, L1, n1, impl="tc1")
+    g2 = A.attn_bwd(do, q, Lq, k0, v0, L0, n0, o, lse, k1, v1, L1, n1, impl="tc2")
     dqkv = torch.full_like(qkv, 7.0)  # strided destinations, like the fused qkv gradient
     dkv = torch.full((B * L1, 2 * C), 7.0, device="cuda", dtype=torch.bfloat16) if L1 else None
     g = A.attn_bwd(do, q, Lq, k0, v0, L0, n0, o, lse, k1, v1, L1, n1, dq=dqkv[:, :C], dk0=dqkv[:, C:2 * C],
@@ -187,11 +191,12 @@ def test_attention_tc_backward(case):
     n0c = n0 if isinstance(n0, int) else n0.cpu()
     gc = A.attn_bwd(*_cpu(do, q), Lq, *_cpu(k0, v0), L0, n0c, *_cpu(o, lse, k1, v1), L1,
                     n1.cpu() if n1 is not None else None)
-    for name, a, m, c, a1 in zip(["dq", "dk0", "dv0", "dk1", "dv1"], g, gm, gc, g1):
+    for name, a, m, c, a1, a2 in zip(["dq", "dk0", "dv0", "dk1", "dv1"], g, gm, gc, g1, g2):
         if a is None:
             continue
         _close(a, c, what=name + " vs fp32")
         _close(a, m, what=name + " vs mma")
-        _close(a, a1, rtol=1e-2, atol=1e-2, what=name + " persistent vs one CTA per key tile")
+        _close(a, a1, rtol=1e-2, atol=1e-2, what=name + " version 3 vs one CTA per key tile")
+        _close(a, a2, rtol=1e-2, atol=1e-2, what=name + " version 3 vs version 2")
     from nano_gpic_b200.ops import status
     assert status.read() == 0
