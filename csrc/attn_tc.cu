@@ -969,12 +969,12 @@ __global__ void __launch_bounds__(at3::THREADS, 1)
 // ====================================================================================================== torch glue
 // Cycle counters for the profiled instantiations (kBwdProf* slots of the backward), or null: set by attn_prof_set
 // with a device uint64 tensor of at least 16 entries (a diagnostic; the normal instantiations record nothing).
-static unsigned long long* g_attn_prof = nullptr;
+static unsigned long long* g_attn_prof = nullptr;  // at least 20 counters
 
 void attn_prof_set(const c10::optional<at::Tensor>& counters) {
   if (counters.has_value() && counters->defined()) {
-    TORCH_CHECK(counters->is_cuda() && counters->scalar_type() == at::kLong && counters->numel() >= 16,
-                "attn_prof_set: a CUDA int64 tensor of at least 16 counters");
+    TORCH_CHECK(counters->is_cuda() && counters->scalar_type() == at::kLong && counters->numel() >= 20,
+                "attn_prof_set: a CUDA int64 tensor of at least 20 counters");
     g_attn_prof = reinterpret_cast<unsigned long long*>(counters->data_ptr());
   } else {
     g_attn_prof = nullptr;
@@ -1737,7 +1737,8 @@ struct AttnTcBwd3Params {
 enum : int {
   kBwdProfWaitSt = 0, kBwdProfExp, kBwdProfWaitMma, kBwdProfStore, kBwdProfWaitDkv, kBwdProfEpiDkv, kBwdProfWaitDq,
   kBwdProfEpiDq, kBwdProfCompute, kBwdProfMmaWaitQd, kBwdProfMmaWaitKv, kBwdProfMmaWaitSfree, kBwdProfMmaWaitPs,
-  kBwdProfMmaWaitEpi, kBwdProfMma, kBwdProfTmaWait, kBwdProfSlots
+  kBwdProfMmaWaitEpi, kBwdProfMma, kBwdProfTmaWait, kBwdProfWaitQd, kBwdProfItem, kBwdProfMmaIssueS,
+  kBwdProfMmaIssueProd, kBwdProfSlots
 };
 
 struct Bwd3Tile {
@@ -1883,6 +1884,7 @@ __global__ void __launch_bounds__(ab3::THREADS, 1)
           NG_PROF_T0(ts);
           if (g > 0 && !mbar_wait(s_free, (g - 1) & 1, abort_flag, p.err, kErrWaitAccEmpty)) return false;
           NG_PROF_ADD(kBwdProfMmaWaitSfree, ts);
+          NG_PROF_T0(tis);
           tc_fence_after();
           const uint32_t aK = smem_u32(smem + OFF_KV + (slot & 1) * 2 * T16), aV = aK + T16;
           const uint32_t aQ = smem_u32(smem + OFF_QD + i * T16), aDO = smem_u32(smem + OFF_QD + (2 + i) * T16);
@@ -1896,6 +1898,7 @@ __global__ void __launch_bounds__(ab3::THREADS, 1)
             umma_f16(tmem + C_DP, dV + k * 2, dO + k * 2, id_s, k != 0 ? 1u : 0u);
           }
           umma_commit(st_full);
+          NG_PROF_ADD(kBwdProfMmaIssueS, tis);
           return true;
         };
         auto issue_prod = [&](int it) -> bool {
@@ -1913,6 +1916,7 @@ __global__ void __launch_bounds__(ab3::THREADS, 1)
           if (it == 0 && ndq > 0 && !mbar_wait(dq_empty, (ndq - 1) & 1, abort_flag, p.err, kErrWaitAccEmpty))
             return false;
           NG_PROF_ADD(kBwdProfMmaWaitEpi, te);
+          NG_PROF_T0(tip);
           tc_fence_after();
           const uint32_t aK = smem_u32(smem + OFF_KV + (slot & 1) * 2 * T16);
           const uint32_t aQ = smem_u32(smem + OFF_QD + i * T16), aDO = smem_u32(smem + OFF_QD + (2 + i) * T16);
@@ -1933,6 +1937,7 @@ __global__ void __launch_bounds__(ab3::THREADS, 1)
             umma_commit(dkv_full);
             umma_commit(&kv_empty[slot & 1]);
           }
+          NG_PROF_ADD(kBwdProfMmaIssueProd, tip);
           return true;
         };
         ok = issue_s(0);
@@ -1958,12 +1963,54 @@ __global__ void __launch_bounds__(ab3::THREADS, 1)
     uint32_t gq = 0, nkt = 0, ndq = 0;
     int ii = 0;
     bool ok = true;
+    // dK / dV of a key tile that is not the item's last live tile are read in the next live tile's first iteration,
+    // after its exponentials (the wait for the tile's last products then overlaps them): the destination rows of the
+    // pending tile, or null
+    bf16 *pend_dk = nullptr, *pend_dv = nullptr;
+    bool pend = false;
+    // reads dK / dV of the finished key tile (once its last products completed), frees them, stores them
+    auto flush_dkv = [&](bf16* dk_row, bf16* dv_row) -> bool {
+      if (!__all_sync(0xffffffffu, mbar_wait(dkv_full, nkt & 1, abort_flag, p.err, kErrWaitAccFull))) return false;
+      tc_fence_after();
+      uint32_t rv[16], rk[16];
+      tmem_ld16(trow + C_DV + cg * 16, rv);
+      tmem_ld16(trow + C_DK + cg * 16, rk);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dkv_empty);
+      ++nkt;
+      if (dk_row != nullptr) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          reinterpret_cast<uint4*>(dv_row)[k] =
+              make_uint4(pack_bf16(__uint_as_float(rv[8 * k]), __uint_as_float(rv[8 * k + 1])),
+                         pack_bf16(__uint_as_float(rv[8 * k + 2]), __uint_as_float(rv[8 * k + 3])),
+                         pack_bf16(__uint_as_float(rv[8 * k + 4]), __uint_as_float(rv[8 * k + 5])),
+                         pack_bf16(__uint_as_float(rv[8 * k + 6]), __uint_as_float(rv[8 * k + 7])));
+          reinterpret_cast<uint4*>(dk_row)[k] =
+              make_uint4(pack_bf16(__uint_as_float(rk[8 * k]) * p.scale, __uint_as_float(rk[8 * k + 1]) * p.scale),
+                         pack_bf16(__uint_as_float(rk[8 * k + 2]) * p.scale, __uint_as_float(rk[8 * k + 3]) * p.scale),
+                         pack_bf16(__uint_as_float(rk[8 * k + 4]) * p.scale, __uint_as_float(rk[8 * k + 5]) * p.scale),
+                         pack_bf16(__uint_as_float(rk[8 * k + 6]) * p.scale, __uint_as_float(rk[8 * k + 7]) * p.scale));
+        }
+      }
+      return true;
+    };
     NG_PROF_T0(tall);
     for (int item = blockIdx.x; ok && item < p.items && !*abort_flag; item += gridDim.x, ++ii) {
       const int b = item / p.H, h = item - b * p.H;
-      int nlive = 0;
-      for (int j = 0; j < nt; ++j) nlive += bwd3_tile(p, b, j).live ? 1 : 0;
+      NG_PROF_T0(ti);
+      int nlive = 0, last_live = -1;
+      for (int j = 0; j < nt; ++j)
+        if (bwd3_tile(p, b, j).live) {
+          ++nlive;
+          last_live = j;
+        }
+      NG_PROF_ADD(kBwdProfItem, ti);
+      NG_PROF_T0(tqd);
       if (nlive > 0 && !__all_sync(0xffffffffu, mbar_wait(qd_full, ii & 1, abort_flag, p.err, kErrWaitFull))) break;
+      NG_PROF_ADD(kBwdProfWaitQd, tqd);
       for (int j = 0; ok && j < nt; ++j) {
         const Bwd3Tile t = bwd3_tile(p, b, j);
         const int s_row = t.kt0 + r;
@@ -2058,45 +2105,33 @@ __global__ void __launch_bounds__(ab3::THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(ps_full);
           NG_PROF_ADD(kBwdProfStore, t3);
+          if (pend) {  // the previous key tile's dK / dV (its products completed before mma_done above)
+            NG_PROF_T0(t5);
+            pend = false;
+            if (!flush_dkv(pend_dk, pend_dv)) {
+              ok = false;
+              break;
+            }
+            NG_PROF_ADD(kBwdProfEpiDkv, t5);
+          }
         }
         if (!ok) break;
-        // dV, dK of key tile j: 16 d columns of this column group, key rows of its quarter
+        // dV, dK of key tile j (16 d columns of this column group, key rows of its quarter): now for the item's last
+        // live tile, else in the next live tile's first iteration
+        bf16 *dk_row = nullptr, *dv_row = nullptr;
+        if (s_row < t.Lsrc) dkv_rows(dk_row, dv_row);
+        if (j != last_live) {
+          pend = true;
+          pend_dk = dk_row;
+          pend_dv = dv_row;
+          continue;
+        }
         NG_PROF_T0(t4);
-        if (!__all_sync(0xffffffffu, mbar_wait(dkv_full, nkt & 1, abort_flag, p.err, kErrWaitAccFull))) {
+        if (!flush_dkv(dk_row, dv_row)) {
           ok = false;
           break;
         }
         NG_PROF_ADD(kBwdProfWaitDkv, t4);
-        NG_PROF_T0(t5);
-        tc_fence_after();
-        {
-          uint32_t rv[16], rk[16];
-          tmem_ld16(trow + C_DV + cg * 16, rv);
-          tmem_ld16(trow + C_DK + cg * 16, rk);
-          tmem_wait_ld();
-          if (s_row < t.Lsrc) {
-            bf16 *dk_row, *dv_row;
-            dkv_rows(dk_row, dv_row);
-#pragma unroll
-            for (int k = 0; k < 2; ++k) {
-              reinterpret_cast<uint4*>(dv_row)[k] =
-                  make_uint4(pack_bf16(__uint_as_float(rv[8 * k]), __uint_as_float(rv[8 * k + 1])),
-                             pack_bf16(__uint_as_float(rv[8 * k + 2]), __uint_as_float(rv[8 * k + 3])),
-                             pack_bf16(__uint_as_float(rv[8 * k + 4]), __uint_as_float(rv[8 * k + 5])),
-                             pack_bf16(__uint_as_float(rv[8 * k + 6]), __uint_as_float(rv[8 * k + 7])));
-              reinterpret_cast<uint4*>(dk_row)[k] =
-                  make_uint4(pack_bf16(__uint_as_float(rk[8 * k]) * p.scale, __uint_as_float(rk[8 * k + 1]) * p.scale),
-                             pack_bf16(__uint_as_float(rk[8 * k + 2]) * p.scale, __uint_as_float(rk[8 * k + 3]) * p.scale),
-                             pack_bf16(__uint_as_float(rk[8 * k + 4]) * p.scale, __uint_as_float(rk[8 * k + 5]) * p.scale),
-                             pack_bf16(__uint_as_float(rk[8 * k + 6]) * p.scale, __uint_as_float(rk[8 * k + 7]) * p.scale));
-            }
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(dkv_empty);
-        NG_PROF_ADD(kBwdProfEpiDkv, t5);
-        ++nkt;
       }
       if (!ok) break;
       // dQ of the item: column group cg takes query tile cg / 2, d columns [32 (cg % 2), +32), query rows of its

@@ -75,7 +75,7 @@ def main():
     print(f"{a.case} ok", flush=True)
     if a.prof:
         from nano_gpic_b200._ext import ext
-        cnt = torch.zeros(16, dtype=torch.int64, device="cuda")
+        cnt = torch.zeros(20, dtype=torch.int64, device="cuda")
         ext().attn_prof_set(cnt)
         fn()
         torch.cuda.synchronize()
@@ -84,10 +84,11 @@ def main():
         names = ["compute: wait S", "compute: load+exp", "compute: wait products", "compute: store P/dS",
                  "compute: wait dK/dV", "compute: dK/dV out", "compute: wait dQ", "compute: dQ out",
                  "compute: total", "mma: wait Q/dO", "mma: wait K/V", "mma: wait S free", "mma: wait P/dS",
-                 "mma: wait epilogue", "mma: total", "tma: waits"]
+                 "mma: wait epilogue", "mma: total", "tma: waits", "compute: wait Q/dO", "compute: item setup",
+                 "mma: issue S", "mma: issue products"]
         tot_c, tot_m = max(c[8], 1), max(c[14], 1)
         for i, (n, v) in enumerate(zip(names, c)):
-            base = tot_c if i <= 8 else tot_m if i <= 14 else tot_m
+            base = tot_m if 9 <= i <= 15 or i >= 18 else tot_c
             print(f"  {n:26s} {v:16d}  {100.0 * v / base:6.1f} %", flush=True)
     if a.time:
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
