@@ -3,8 +3,9 @@
 # jobs/train_ladder.sh interface). Records the launch, runs the GPU-health gate in the background (main.py waits for
 # its verdict and exits 98 on a failure), resumes from the newest last*.ckpt of the run directory with the same shard
 # seed, builds the callback list (ms-step every STEPS/4, last.ckpt every LADDER_LAST_EVERY, warm-up, host tuning,
-# shard clock, save-on-term, None refcount, first-step marker), launches one process per GPU with torchrun and checks
-# that ms-step=<STEPS>.ckpt exists at the end (exit 99 otherwise).
+# shard clock, save-on-term, None refcount, first-step marker), launches one process per GPU with torchrun under the
+# launch guard (watchdog, retries, leftover cleanup) and checks that ms-step=<STEPS>.ckpt exists at the end (exit 99
+# otherwise).
 set -o pipefail
 HERE=$(cd "$(dirname "$(readlink -f "$0")")/.." && pwd)
 source $HERE/jobs/env.sh
@@ -37,11 +38,15 @@ if [ -n "$LASTCK" ]; then
   done
 fi
 [ -s $SEEDF ] || date +%s > $SEEDF
-export GPIC_SHARD_SEED=$(cat $SEEDF) GPIC_SHARD_LOG_DIR=$RUN GPIC_FIRST_STEP_FILE=$RUN/first_step.txt
+export GPIC_SHARD_SEED=$(cat $SEEDF) GPIC_SHARD_LOG_DIR=$RUN
 CB='[{"class_path":"nano_gpic_b200.train.callbacks.CheckpointHook","init_args":{"filename":"ms-{step:06d}","save_last":false,"save_top_k":-1,"every_n_train_steps":'$MS'}},{"class_path":"nano_gpic_b200.train.callbacks.CheckpointHook","init_args":{"filename":"resume-{step:06d}","save_last":true,"save_top_k":0,"every_n_train_steps":'$LAST'}},{"class_path":"nano_gpic_b200.train.callbacks.Warmup"},{"class_path":"nano_gpic_b200.train.callbacks.HostTuning"},{"class_path":"nano_gpic_b200.train.callbacks.ShardClock"},{"class_path":"nano_gpic_b200.train.callbacks.SaveOnTermCallback"},{"class_path":"nano_gpic_b200.train.callbacks.NoneRefcount","init_args":{"every":1000}},{"class_path":"nano_gpic_b200.train.callbacks.FirstStepMarker"}]'
 NGPU=${GPUS:-$(nvidia-smi -L 2>/dev/null | wc -l)}; [ "$NGPU" -ge 1 ] || NGPU=1
 cd $HERE
-timeout -k 60 ${GPIC_LAUNCH_TIMEOUT:-1000000} torchrun --standalone --local-addr 127.0.0.1 --nproc-per-node $NGPU main.py fit \
+# the launch guard (nano_gpic_b200/train/launch_guard.py): first-step watchdog (GPIC_LAUNCH_START_TIMEOUT_S, 1500 s of
+# no first step and no warm-up progress -> TERM, KILL, status 125), retries before the first step
+# (GPIC_LAUNCH_RETRIES, 2), and no process of the launch left behind (GPIC_LAUNCH_ID)
+timeout -k 60 ${GPIC_LAUNCH_TIMEOUT:-1000000} python -m nano_gpic_b200.train.launch_guard --run $RUN -- \
+  torchrun --standalone --local-addr 127.0.0.1 --nproc-per-node $NGPU main.py fit \
   --config configs/lite_ladder.yaml \
   --model.denoiser.init_args.hidden_size $D --model.denoiser.init_args.num_groups $((D / 64)) \
   --model.denoiser.init_args.num_blocks $NB --model.denoiser.init_args.num_text_blocks $NT \

@@ -102,6 +102,14 @@ class ShardClock(Callback):
 
 
 # --------------------------------------------------------------------------------------------------- warm-up
+def _progress(ctx):
+    """Rank 0 touches <GPIC_FIRST_STEP_FILE>.progress: start-up work is still advancing (launch_guard.py)."""
+    path = os.environ.get("GPIC_FIRST_STEP_FILE")
+    if path and ctx.rank == 0:
+        with open(path + ".progress", "a"):
+            os.utime(path + ".progress", None)
+
+
 class Warmup(Callback):
     """Before the first step, the real forward + backward on dummy batches at caption lengths T (64, 128, 320, 192 by
     default) on every rank, then the gradients are zeroed and the weights are untouched: kernels' tensor maps,
@@ -127,6 +135,7 @@ class Warmup(Callback):
             y = torch.randn(B, T, D, generator=g).to(dev, torch.bfloat16)
             m = torch.ones(B, T, dtype=torch.bool, device=dev)
             tr.obj.train_step(model, x, y, m, grad_scale=1.0 / x.numel())
+            _progress(ctx)  # the launch watchdog restarts its clock at each finished warm-up length
         if tr.flat is not None:
             tr.flat.zero_grad()
         if dev.type == "cuda":
