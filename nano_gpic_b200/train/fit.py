@@ -9,7 +9,9 @@ src/lightning_data_gpic.py:51-147) on every rank of a torchrun launch:
     callbacks (trainer.callbacks), run directory <default_root_dir>/exp_<tags.exp>, the resolved config written there
     resume from ckpt_path ("last" = the newest last*.ckpt of the run directory)
     the loop: accumulate_grad_batches micro-batches of data.train_batch_size per optimizer step, until max_steps
-    or a SIGTERM stop; logs every trainer.log_every_n_steps steps to metrics.jsonl (the only host syncs).
+    or a SIGTERM stop; logs every trainer.log_every_n_steps steps (loss, lr, images/s, per-caption-type losses) to
+    metrics.jsonl and, when the trainer's logger node names a W&B logger, to an offline W&B run (train/metrics.py);
+    log steps are the only host synchronisations.
 predict: sampling with model.diffusion_sampler over data.pred_dataset prompts, images written by SaveImagesHook.
 
 GPIC_SYNTHETIC=1 (or data.synthetic: true) trains on synthetic batches of the configured shape.
@@ -54,6 +56,7 @@ class FitContext:
         self.rank, self.world, self.device, self.cfg = rank, world, device, cfg
         self.max_steps, self.micro_batch, self.writer, self.callbacks = max_steps, micro_batch, writer, callbacks
         self.stop = False
+        self.sinks = None  # MetricSinks (metrics.jsonl, W&B when configured)
 
     def save(self, name, full, dirpath=None, wait=False):
         """Collective: every rank calls it (zero mode gathers the sharded state); rank 0 writes."""
@@ -75,10 +78,10 @@ class FitContext:
         return path
 
     def log(self, values, step):
-        if self.rank != 0:
-            return
-        with open(os.path.join(self.run_dir, "metrics.jsonl"), "a") as f:
-            f.write(json.dumps({"step": step, **values}) + "\n")
+        if self.sinks is None:
+            from .metrics import MetricSinks
+            self.sinks = MetricSinks(self.run_dir, self.rank)
+        self.sinks.log(values, step)
 
 
 def _seed_everything(seed):
@@ -158,6 +161,8 @@ def fit(cfg):
     writer = AsyncWriter() if rank == 0 and os.environ.get("GPIC_MFU_ASYNC_CKPT", "1") != "0" else None
     mb = int((cfg.get("data") or {}).get("train_batch_size", 32))
     ctx = FitContext(trainer, ema, rdir, rank, world, dev, cfg, max_steps, mb, writer, callbacks)
+    from .metrics import MetricSinks, caption_type_losses
+    ctx.sinks = MetricSinks(rdir, rank, logger_node=tcfg.get("logger"), config=cfg)
     for c in callbacks:
         c.setup(ctx)
 
@@ -185,9 +190,10 @@ def fit(cfg):
     try:
         while trainer.global_step < max_steps and not ctx.stop:
             step = trainer.global_step
-            micros = []
+            micros, types = [], []
             for _ in range(accum):
                 img, caps, meta = next(it)
+                types += list(meta.get("caption_type") or [])
                 if isinstance(img, ResizeBatch):  # the bicubic crop passes of the batch, on the device
                     img = img.run(dev)
                 if cond is not None:
@@ -213,6 +219,10 @@ def fit(cfg):
                 dt = time.perf_counter() - t_log
                 imgs = n_log * accum * mb * world
                 vals = {"loss": float(loss), "lr": opt.param_groups[0]["lr"], "images_per_s": imgs / max(dt, 1e-9)}
+                if rebal is None and trainer.last_per_sample is not None:
+                    # collective (every rank, every log step); samples whose type is unknown count for no type
+                    n = trainer.last_per_sample.numel()
+                    vals.update(caption_type_losses(trainer.last_per_sample, types if len(types) == n else [""] * n))
                 ctx.log(vals, trainer.global_step)
                 if rank == 0:
                     print(f"[step {trainer.global_step}] " + " ".join(f"{k}={v:.5g}" for k, v in vals.items()),
@@ -223,6 +233,8 @@ def fit(cfg):
     finally:
         if writer is not None:
             writer.close()
+        if ctx.sinks is not None:
+            ctx.sinks.close()
         if dist.is_initialized():
             dist.barrier()
             dist.destroy_process_group()

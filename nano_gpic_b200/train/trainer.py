@@ -59,6 +59,7 @@ class Trainer:
         self.global_step = 0
         self.copy_stream = None
         self.last_grad_norm = None  # device scalar: the pre-clip global norm of the last step
+        self.last_per_sample = None  # device [images of the step]: per-sample losses of the last step
         self.encode = None  # optional autoencoder encode applied to the float images (PixelAE with scale/shift)
 
     # --------------------------------------------------------------------------------------------- construction
@@ -180,7 +181,8 @@ class Trainer:
             self.model.weights_changed()
         _nvtx_pop()
         self.global_step += 1
-        return torch.cat(losses).mean()
+        self.last_per_sample = torch.cat(losses)  # per-sample losses of the step, micro-batch order (device)
+        return self.last_per_sample.mean()
 
     @torch.no_grad()
     def clip_grad(self):

@@ -59,3 +59,41 @@ def test_accumulation_equals_one_big_batch():
         grads.append(tr.flat.grad.clone())
     rel = (grads[0] - grads[1]).norm() / grads[0].norm()
     assert rel < 2e-2, rel
+
+
+def test_caption_type_losses_and_sinks(tmp_path, monkeypatch):
+    """Per-caption-type losses are the per-type means of the step's per-sample losses (0 for an absent type), and the
+    sinks write metrics.jsonl and, with a W&B logger configured, log the same values to a (stand-in) wandb run in
+    offline mode."""
+    import json
+    import sys
+    import types as pytypes
+    from nano_gpic_b200.train.metrics import MetricSinks, caption_type_losses
+    per = torch.tensor([1.0, 2.0, 4.0, 8.0, 16.0])
+    out = caption_type_losses(per, ["short", "tag", "short", "long", "medium"])
+    assert out == {"train/loss_tag": 2.0, "train/loss_short": 2.5, "train/loss_medium": 16.0, "train/loss_long": 8.0}
+    assert caption_type_losses(per, [""] * 5)["train/loss_tag"] == 0.0
+    calls = []
+
+    class _Run:
+        def log(self, values, step):
+            calls.append(("log", step, values))
+
+        def finish(self):
+            calls.append(("finish",))
+
+    fake = pytypes.ModuleType("wandb")
+    fake.init = lambda **kw: calls.append(("init", kw)) or _Run()
+    monkeypatch.setitem(sys.modules, "wandb", fake)
+    monkeypatch.delenv("WANDB_MODE", raising=False)
+    node = {"class_path": "lightning.pytorch.loggers.WandbLogger",
+            "init_args": {"name": "ladder", "project": "gpic-speed", "offline": False, "resume": "allow"}}
+    sinks = MetricSinks(str(tmp_path), 0, logger_node=node, config={"a": 1})
+    monkeypatch.setenv("WANDB_MODE", "offline")
+    sinks.log({"loss": 0.5, **out}, 10)
+    sinks.close()
+    assert calls[0][0] == "init" and calls[0][1]["project"] == "gpic-speed" and calls[0][1]["dir"] == str(tmp_path)
+    assert calls[1] == ("log", 10, {"loss": 0.5, **out}) and calls[2] == ("finish",)
+    rec = json.loads((tmp_path / "metrics.jsonl").read_text())
+    assert rec["step"] == 10 and rec["train/loss_long"] == 8.0
+    assert MetricSinks(str(tmp_path), 1, logger_node=node).wandb is None  # only rank 0 writes
