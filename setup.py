@@ -21,8 +21,6 @@ NVCC_FLAGS = [
     "-Xptxas=-v" if os.environ.get("NG_PTXAS_VERBOSE") == "1" else "-Xptxas=-O3",
     "-DNDEBUG",
 ]
-if os.environ.get("NG_BOUNDS_CHECK") == "1":
-    NVCC_FLAGS.append("-DNANO_BOUNDS_CHECK")
 
 
 def sources():
