@@ -1,6 +1,8 @@
-"""Muon's per-unit elementwise work as one launch each (csrc/optim.cu): the stacked Nesterov inputs of a shape's units
-and `W <- W * decay + coef * O` over every unit (the reference's Muon-add lever, baselines/PixelGen/src/optim/
-muon_add.py:9-35, plus the weight decay that the reference applies with a separate _foreach_mul_).
+"""The optimizer's elementwise work as one launch each (csrc/optim.cu): the stacked Nesterov inputs of a shape's units,
+`W <- W * decay + coef * O` over every Muon unit (the reference's Muon-add lever, baselines/PixelGen/src/optim/
+muon_add.py:9-35, plus the weight decay that the reference applies with a separate _foreach_mul_), and AdamW over every
+vector parameter (the reference's FusedAdamWEMA lever, baselines/PixelGen/src/utils/fused_adamw_ema.py:39-113); both
+apply the EMA of the weights in the same pass when one is attached.
 
 The kernels read device pointer tables (int64 rows) built here each call. Operands that are not contiguous, not
 16-byte aligned, or whose size is not a multiple of 4 take the PyTorch path, as do CPU tensors.
@@ -35,14 +37,49 @@ def _f32_bits(x):
     return struct.unpack("<i", struct.pack("<f", float(x)))[0]
 
 
-def apply_updates(items, decay):
-    """For each (param view fp32, update bf16 of the same shape, coef): param <- param * decay + coef * update."""
-    fast = [it for it in items if _ok(it[0], torch.float32) and _ok(it[1], torch.bfloat16)]
-    slow = [it for it in items if not (_ok(it[0], torch.float32) and _ok(it[1], torch.bfloat16))]
+def apply_updates(items, decay, ema_w=0.0):
+    """For each (param view fp32, update bf16 of the same shape, coef[, ema view fp32 or None]):
+    param <- param * decay + coef * update, then ema <- lerp(ema, param, ema_w) where an EMA view is given."""
+    def fits(it):
+        return _ok(it[0], torch.float32) and _ok(it[1], torch.bfloat16) and (
+            len(it) < 4 or it[3] is None or _ok(it[3], torch.float32))
+    fast = [it for it in items if fits(it)]
+    slow = [it for it in items if not fits(it)]
     if fast:
-        rows = [[p.data_ptr(), o.data_ptr(), p.numel(), _f32_bits(c)] for p, o, c in fast]
-        ext().muon_apply(_table(rows, fast[0][0].device), float(decay), max(p.numel() for p, _, _ in fast))
-    for p, o, c in slow:
+        with_ema = any(len(it) > 3 and it[3] is not None for it in fast)
+        rows = [[it[0].data_ptr(), it[1].data_ptr(), it[0].numel(), _f32_bits(it[2])] +
+                ([it[3].data_ptr() if len(it) > 3 and it[3] is not None else 0] if with_ema else []) for it in fast]
+        ext().muon_apply(_table(rows, fast[0][0].device), float(decay), max(it[0].numel() for it in fast),
+                         float(ema_w))
+    for it in slow:
+        p, o, c = it[:3]
         if decay != 1.0:
             p.mul_(decay)
         p.add_(o, alpha=c)
+        if len(it) > 3 and it[3] is not None:
+            it[3].lerp_(p, ema_w)
+
+
+def adamw_update(params, grads, m1, m2, emas, lr, wd, b1, b2, eps, bc1, bc2, ema_w=0.0):
+    """AdamW with decoupled weight decay on lists of fp32 tensors (torch.optim.AdamW's formula: p *= 1 - lr wd;
+    m = lerp(m, g, 1 - b1); v = b2 v + (1 - b2) g^2; p -= (lr / bc1) m / (sqrt(v) / sqrt(bc2) + eps)), bias
+    corrections bc1 = 1 - b1^t, bc2 = 1 - b2^t given; then ema = lerp(ema, p, ema_w) where emas[i] is not None.
+    One launch for all of them on CUDA (csrc/optim.cu adamw_apply); the same arithmetic in PyTorch otherwise."""
+    if not params:
+        return
+    emas = list(emas) if emas is not None else [None] * len(params)
+    tensors = [t for group in (params, grads, m1, m2) for t in group] + [e for e in emas if e is not None]
+    if all(_ok(t, torch.float32) for t in tensors):
+        rows = [[p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), e.data_ptr() if e is not None else 0,
+                 p.numel()] for p, g, m, v, e in zip(params, grads, m1, m2, emas)]
+        ext().adamw_apply(_table(rows, params[0].device), [float(lr), float(wd), float(b1), float(b2), float(eps),
+                                                           float(bc1), float(bc2), float(ema_w)],
+                          max(p.numel() for p in params))
+        return
+    for p, g, m, v, e in zip(params, grads, m1, m2, emas):
+        p.mul_(1 - lr * wd)
+        m.lerp_(g, 1 - b1)
+        v.mul_(b2).addcmul_(g, g, value=1 - b2)
+        p.addcdiv_(m, v.sqrt().div_(bc2 ** 0.5).add_(eps), value=-lr / bc1)
+        if e is not None:
+            e.lerp_(p, ema_w)

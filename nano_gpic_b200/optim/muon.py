@@ -109,6 +109,18 @@ class MuonAdamW(torch.optim.Optimizer):
         # scalars for it.
         self.defer = None
         self.deferred = None
+        # an attached EMA (train.ema.SimpleEMA.attach): the update kernels also move the EMA of every parameter they
+        # update, so no separate pass over the weights is needed
+        self.ema = None
+        self.applies_ema = True
+        self._adam_t = {}  # AdamW step count per group index, on the host (bias corrections of the table kernel)
+
+    def load_state_dict(self, state_dict):
+        super().load_state_dict(state_dict)
+        self._adam_t = {}  # re-read from the loaded step tensors
+
+    def _ema_of(self, p):
+        return self.ema.view(p) if self.ema is not None else None
 
     @staticmethod
     def update_coef(group, shape):
@@ -181,9 +193,10 @@ class MuonAdamW(torch.optim.Optimizer):
             self.deferred = dict(self.deferred or {}, lr_m=lr, wd_m=wd or 0.0)
             return
         # weight decay and W += coef O for every unit in one launch (units partition each matrix's rows)
-        items = [(params[i][r0:r1], o, -lr * self.update_coef(group, shape))
+        items = [(params[i][r0:r1], o, -lr * self.update_coef(group, shape),
+                  None if self.ema is None else self._ema_of(params[i])[r0:r1])
                  for shape, us, O in outs for (i, r0, r1), o in zip(us, O)]
-        OPT.apply_updates(items, 1 - lr * wd if wd else 1.0)
+        OPT.apply_updates(items, 1 - lr * wd if wd else 1.0, self.ema.weight if self.ema is not None else 0.0)
 
     @torch.no_grad()
     def _muon_step(self, group):
@@ -226,9 +239,10 @@ class MuonAdamW(torch.optim.Optimizer):
             else:
                 o0 = u["owner"] * plan["shard"] + u["off"]
                 src = full[o0:o0 + math.prod(u["shape"])].view(u["shape"])
-            items.append((params[u["p"]][u["r0"]:u["r1"]], src, -lr * self.update_coef(group, u["shape"])))
+            ema = None if self.ema is None else self._ema_of(params[u["p"]])[u["r0"]:u["r1"]]
+            items.append((params[u["p"]][u["r0"]:u["r1"]], src, -lr * self.update_coef(group, u["shape"]), ema))
         # weight decay and W += coef O for every unit in one launch (units partition each matrix's rows)
-        OPT.apply_updates(items, 1 - lr * wd if wd else 1.0)
+        OPT.apply_updates(items, 1 - lr * wd if wd else 1.0, self.ema.weight if self.ema is not None else 0.0)
 
     @staticmethod
     def _all_gather(shard, plan):
@@ -288,6 +302,17 @@ class MuonAdamW(torch.optim.Optimizer):
             return
         b1, b2 = group["betas"]
         fused = self.fused_adamw and params[0].is_cuda
+        if fused or self.ema is not None:
+            # one launch for every parameter of the group (csrc/optim.cu adamw_apply), with the attached EMA; the
+            # step tensors stay current for checkpoints, the bias corrections come from a host-side count
+            torch._foreach_add_(steps, 1.0)
+            gi = next(i for i, g in enumerate(self.param_groups) if g is group)
+            t = self._adam_t[gi] + 1 if gi in self._adam_t else int(float(steps[0]))
+            self._adam_t[gi] = t
+            OPT.adamw_update(params, grads, m1, m2, [self._ema_of(p) for p in params], group["lr"],
+                             group["weight_decay"], b1, b2, group["eps"], 1 - b1 ** t, 1 - b2 ** t,
+                             self.ema.weight if self.ema is not None else 0.0)
+            return
         _adam_fn(params, grads, m1, m2, [], steps, foreach=None if fused else True, capturable=False,
                  differentiable=False, fused=fused or None, grad_scale=None, found_inf=None, has_complex=False,
                  decoupled_weight_decay=True, amsgrad=False, beta1=b1, beta2=b2, lr=group["lr"],

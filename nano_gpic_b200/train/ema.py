@@ -20,12 +20,37 @@ class SimpleEMA:
         self.buf = None if self.off else flat.data.clone()
         self._stream = None
         self.previous_step = 0
+        self.fused = False  # True once attach() handed the update to the optimizer's kernels
+        self._index = None
+
+    @property
+    def weight(self):
+        return 1.0 - self.decay
+
+    def view(self, p):
+        """The EMA tensor of parameter p (a view of the flat EMA buffer)."""
+        if self._index is None:
+            self._index = {id(q): i for i, q in enumerate(self.flat.params)}
+        return self.flat.view(self.buf, self._index[id(p)])
+
+    def attach(self, opt):
+        """Let the optimizer's update kernels apply the EMA in the same pass as the weight update (the role of the
+        reference's FusedAdamWEMA with an EMA, baselines/PixelGen/src/utils/fused_adamw_ema.py:39-113): the same
+        lerp, one pass over the weights fewer. Only for an EMA updated every step; returns whether it attached."""
+        if self.off or self.every_n_steps != 1 or not self.buf.is_cuda or not getattr(opt, "applies_ema", False):
+            return False
+        opt.ema = self
+        self.fused = True
+        return True
 
     def step(self, global_step):
-        """Call after the optimizer step; updates once per new step."""
+        """Call after the optimizer step; updates once per new step (nothing to do when attached to the optimizer,
+        whose kernels updated it)."""
         if self.off or global_step == self.previous_step:
             return
         self.previous_step = global_step
+        if self.fused:
+            return
         if global_step % self.every_n_steps:
             return
         if self.buf.is_cuda:

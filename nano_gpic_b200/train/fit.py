@@ -148,6 +148,8 @@ def fit(cfg):
         dp.broadcast_params(0)
     ema_spec = instantiate(m["ema_tracker"]) if is_spec(m.get("ema_tracker")) else EMASpec()
     ema = ema_spec.build(flat, ranges=dp.own_ranges() if dp is not None else None)
+    if dp is None or dp.p2p is None:  # the update kernels apply the EMA in the same pass (peer memory: its own kernel)
+        ema.attach(opt)
 
     rdir = run_dir(cfg)
     if rank == 0:

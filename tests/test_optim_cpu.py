@@ -63,3 +63,20 @@ def test_warmup_flat_cooldown_matches_reference():
                 s.step()
             lrs.append(seq)
         assert lrs[0] == lrs[1]
+
+
+def test_adamw_update_fallback_matches_torch_adamw():
+    """The PyTorch form of the table kernel (CPU) follows torch.optim.AdamW (decoupled weight decay)."""
+    import torch
+    from nano_gpic_b200.ops import optim as OPT
+    torch.manual_seed(0)
+    p = torch.randn(33)  # not a multiple of 4: the PyTorch path
+    q = torch.nn.Parameter(p.clone())
+    opt = torch.optim.AdamW([q], lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    m, v = torch.zeros_like(p), torch.zeros_like(p)
+    for t in range(1, 5):
+        g = torch.randn(33)
+        OPT.adamw_update([p], [g], [m], [v], None, 1e-2, 0.1, 0.9, 0.95, 1e-8, 1 - 0.9 ** t, 1 - 0.95 ** t)
+        q.grad = g.clone()
+        opt.step()
+    torch.testing.assert_close(p, q.detach(), rtol=1e-5, atol=1e-6)
