@@ -395,6 +395,7 @@ def main():
         ms, e2e_ms, launches, clocks, _ = run_ours(a, rank, world, dev)
     ms = max_over_ranks(ms, dev)
     e2e_ms = max_over_ranks(e2e_ms, dev) if e2e_ms is not None else None
+    peak_gb = max_over_ranks(torch.cuda.max_memory_allocated(dev) / 2 ** 30, dev) if dev.type == "cuda" else None
     pk, pk_src = peaks()
     value = a.global_batch / (ms / 1000.0)
     flops_img = train_flops_per_image(s, T)
@@ -421,7 +422,8 @@ def main():
                "e2e": {"value": round(a.global_batch / (e2e_ms / 1000.0), 1) if e2e_ms else None, "unit": "images/s",
                        "h2d_bytes_per_step": B * (256 * 256 * 3 + T * 2048 * 2 + T),
                        "d2h_bytes_per_step": 4} if e2e_ms else None,
-               "gpu_launches": launches}
+               "gpu_launches": launches,
+               "peak_mem_gib": round(peak_gb, 1) if peak_gb is not None else None}
         # how the data parallelism is carried out, apart from `parallelism` (which names the work: N data-parallel
         # ranks over one global batch, the same for both arms)
         if a.impl == "reference":
