@@ -10,14 +10,15 @@ void gemm_torch(const at::Tensor& A, bool a_mn, int64_t lda, int64_t a_bs, const
                 const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& res, int64_t ldr,
                 int64_t res_bs, const c10::optional<at::Tensor>& gate, int64_t ldg, int64_t rows_per_group,
                 const c10::optional<at::Tensor>& aux, int64_t ld_aux, int64_t half_n, double alpha, double beta,
-                bool accumulate);
+                bool accumulate, const c10::optional<at::Tensor>& seg);
 void rms_mod_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& shift,
                  const c10::optional<at::Tensor>& scale, const at::Tensor& h, const at::Tensor& rstd, int64_t rpg,
-                 double eps);
+                 double eps, const c10::optional<at::Tensor>& seg);
 void rms_mod_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& rstd, const at::Tensor& w,
                  const c10::optional<at::Tensor>& scale, const c10::optional<at::Tensor>& dres, const at::Tensor& dx,
                  const c10::optional<at::Tensor>& dw, const c10::optional<at::Tensor>& dshift,
-                 const c10::optional<at::Tensor>& dscale, int64_t rpg);
+                 const c10::optional<at::Tensor>& dscale, int64_t rpg, const c10::optional<at::Tensor>& cu,
+                 int64_t max_rows);
 void rms_mod_fwd_mx(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& shift,
                     const c10::optional<at::Tensor>& scale, const at::Tensor& h, const at::Tensor& rstd,
                     const at::Tensor& q, const at::Tensor& sf, int64_t rpg, double eps);
@@ -39,7 +40,9 @@ void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k0,
               const at::Tensor& dk0, const at::Tensor& dv0, const c10::optional<at::Tensor>& dk1,
               const c10::optional<at::Tensor>& dv1, int64_t Lq, int64_t L0, int64_t L1, double scale);
 void gate_bwd(const at::Tensor& dout, const at::Tensor& y, const at::Tensor& gate, const at::Tensor& dy,
-              const c10::optional<at::Tensor>& dgate, const c10::optional<at::Tensor>& dbias, int64_t rpg);
+              const c10::optional<at::Tensor>& dgate, const c10::optional<at::Tensor>& dbias, int64_t rpg,
+              const c10::optional<at::Tensor>& cu, int64_t max_rows);
+void gather_rows(const at::Tensor& src, const at::Tensor& idx, const at::Tensor& out);
 void fm_prep(const at::Tensor& x, const at::Tensor& noise, const at::Tensor& t, const at::Tensor& xt_tok, int64_t p);
 void fm_loss(const at::Tensor& pred, const at::Tensor& x, const at::Tensor& noise, const at::Tensor& t,
              const c10::optional<at::Tensor>& dpred, const at::Tensor& per_sample, int64_t p, double t_eps,
@@ -130,6 +133,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("dk0"), py::arg("dv0"), py::arg("dk1"), py::arg("dv1"), py::arg("Lq"), py::arg("L0"), py::arg("L1"),
         py::arg("scale"), py::arg("version") = 2);
   m.def("gate_bwd", &ng::gate_bwd);
+  m.def("gather_rows", &ng::gather_rows, "out[r] = src[idx[r]] (bf16 rows), zeros where idx[r] < 0");
   m.def("fm_prep", &ng::fm_prep);
   m.def("fm_loss", &ng::fm_loss);
   m.def("patchify", &ng::patchify);

@@ -5,6 +5,7 @@
 //   fm_loss       per-sample sum of (out - v)^2 with out = (pred - x_t)/d, v = (x - x_t)/d, d = max(1 - t, t_eps),
 //                 and the gradient w.r.t. the bf16 prediction tokens in the same pass
 //   patchify / unpatchify, add_rows (bf16(a + table[row % period]))
+//   gather_rows   packed caption rows moved between the packed and the padded [B, Tp] layouts
 // Reference: the gated residuals of JiT_T2I.py:201-210, JiTTrainer._impl_trainstep
 // (baselines/PixelGen/src/diffusion/flow_matching/training_JiT.py:36-64) and patchify (JiT_T2I.py:42-52).
 #include <ATen/cuda/CUDAContext.h>
@@ -47,11 +48,14 @@ constexpr int GB_ROWS = 32;  // rows per CTA: 1024 CTAs at 128 x 256 rows (2.3 w
 __global__ void __launch_bounds__(256) gate_bwd_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ y,
                                                        const bf16* __restrict__ gate, int64_t ldg,
                                                        bf16* __restrict__ dy, float* __restrict__ part, int M, int C,
-                                                       int rpg) {
+                                                       int rpg, const int* __restrict__ cu) {
   extern __shared__ float red[];  // [RG - 1][2][C]
   const int g = blockIdx.y, chunk = blockIdx.x;
-  const int r0 = g * rpg + chunk * GB_ROWS;
-  const int r1 = min(min(g * rpg + rpg, r0 + GB_ROWS), M);
+  // rows of group g: [g rpg, (g + 1) rpg), or [cu[g], cu[g + 1]) for packed rows (a chunk past the end: zero partials)
+  const int gb = cu != nullptr ? cu[g] : g * rpg;
+  const int ge = cu != nullptr ? cu[g + 1] : min(g * rpg + rpg, M);
+  const int r0 = gb + chunk * GB_ROWS;
+  const int r1 = min(ge, r0 + GB_ROWS);
   const int nv = C >> 3;
   const int RG = max(1, (int)blockDim.x / nv);
   const int cid = g * gridDim.x + chunk;
@@ -276,14 +280,24 @@ __global__ void add_rows_kernel(const bf16* __restrict__ a, const TT* __restrict
 
 // ====================================================================================================== torch glue
 void gate_bwd(const at::Tensor& dout, const at::Tensor& y, const at::Tensor& gate, const at::Tensor& dy,
-              const c10::optional<at::Tensor>& dgate, const c10::optional<at::Tensor>& dbias, int64_t rpg) {
+              const c10::optional<at::Tensor>& dgate, const c10::optional<at::Tensor>& dbias, int64_t rpg,
+              const c10::optional<at::Tensor>& cu, int64_t max_rows) {
   TORCH_CHECK(dout.is_contiguous() && y.is_contiguous() && dy.is_contiguous() && gate.stride(1) == 1,
               "gate_bwd: layouts");
   const at::cuda::CUDAGuard guard(dout.device());
   const int M = dout.size(0), C = dout.size(1);
   TORCH_CHECK(C % 8 == 0, "gate_bwd: C % 8");
-  const int G = (M + (int)rpg - 1) / (int)rpg;
-  const int chunks = ((int)rpg + GB_ROWS - 1) / GB_ROWS;
+  const bool packed = cu.has_value() && cu->defined();
+  const int* cup = nullptr;
+  if (packed) {
+    TORCH_CHECK(cu->scalar_type() == at::kInt && cu->is_contiguous() && cu->numel() >= 2 && cu->is_cuda() &&
+                    max_rows > 0,
+                "gate_bwd: cu must be a [G + 1] int32 CUDA tensor of row offsets, with max_rows > 0");
+    cup = cu->data_ptr<int>();
+  }
+  const int G = packed ? (int)cu->numel() - 1 : (M + (int)rpg - 1) / (int)rpg;
+  TORCH_CHECK(G <= 65535, "gate_bwd: at most 65535 groups");
+  const int chunks = ((packed ? (int)max_rows : (int)rpg) + GB_ROWS - 1) / GB_ROWS;
   auto s = at::cuda::getCurrentCUDAStream();
   at::Tensor part = at::empty({(int64_t)G * chunks * 2 * C}, dout.options().dtype(at::kFloat));
   const int RG = std::max(1, 256 / (C / 8));
@@ -291,7 +305,7 @@ void gate_bwd(const at::Tensor& dout, const at::Tensor& y, const at::Tensor& gat
   gate_bwd_kernel<<<dim3(chunks, G), 256, smem, s>>>(
       reinterpret_cast<const bf16*>(dout.data_ptr()), reinterpret_cast<const bf16*>(y.data_ptr()),
       reinterpret_cast<const bf16*>(gate.data_ptr()), gate.stride(0), reinterpret_cast<bf16*>(dy.data_ptr()),
-      part.data_ptr<float>(), M, C, (int)rpg);
+      part.data_ptr<float>(), M, C, (int)rpg, cup);
   NG_LAUNCH_CHECK();
   float* dg = (dgate.has_value() && dgate->defined()) ? dgate->data_ptr<float>() : nullptr;
   float* db = (dbias.has_value() && dbias->defined()) ? dbias->data_ptr<float>() : nullptr;
@@ -377,6 +391,43 @@ void add_rows(const at::Tensor& a, const at::Tensor& table, const at::Tensor& ou
     add_rows_kernel<bf16><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
         reinterpret_cast<const bf16*>(a.data_ptr()), reinterpret_cast<const bf16*>(table.data_ptr()),
         reinterpret_cast<bf16*>(out.data_ptr()), rows, C, (int)period);
+  NG_LAUNCH_CHECK();
+}
+
+// --------------------------------------------------------------------------------------------- packed caption rows
+// gather_rows: out[r] = src[idx[r]] for bf16 rows of C values (16-byte vectors), zeros where idx[r] < 0. Moves packed
+// caption rows into the padded [B, Tp] layout the attention reads and back (JiT_T2I.py:54-65 of the reference).
+__global__ void gather_rows_kernel(const bf16* __restrict__ src, int64_t lds, const int* __restrict__ idx,
+                                   bf16* __restrict__ out, int64_t ldo, int64_t rows, int nv) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * nv) return;
+  const int64_t r = i / nv;
+  const int v = (int)(i - r * nv);
+  const int s = idx[r];
+  uint4 val = make_uint4(0u, 0u, 0u, 0u);
+  if (s >= 0) val = reinterpret_cast<const uint4*>(src + (int64_t)s * lds)[v];
+  reinterpret_cast<uint4*>(out + r * ldo)[v] = val;
+}
+
+void gather_rows(const at::Tensor& src, const at::Tensor& idx, const at::Tensor& out) {
+  TORCH_CHECK(src.dim() == 2 && out.dim() == 2 && src.size(1) == out.size(1) && src.stride(1) == 1 &&
+                  out.stride(1) == 1 && src.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16,
+              "gather_rows: 2-D bf16 rows with unit column stride");
+  TORCH_CHECK(idx.scalar_type() == at::kInt && idx.is_contiguous() && idx.numel() == out.size(0),
+              "gather_rows: idx [rows of out] int32");
+  const int C = src.size(1);
+  TORCH_CHECK(C % 8 == 0 && src.stride(0) % 8 == 0 && out.stride(0) % 8 == 0 &&
+                  reinterpret_cast<uintptr_t>(src.data_ptr()) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0,
+              "gather_rows: 16-byte aligned rows");
+  const at::cuda::CUDAGuard guard(src.device());
+  const int64_t rows = out.size(0);
+  const int nv = C / 8;
+  const int64_t n = rows * nv;
+  if (n == 0) return;
+  gather_rows_kernel<<<(unsigned)((n + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const bf16*>(src.data_ptr()), src.stride(0), idx.data_ptr<int>(),
+      reinterpret_cast<bf16*>(out.data_ptr()), out.stride(0), rows, nv);
   NG_LAUNCH_CHECK();
 }
 

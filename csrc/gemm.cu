@@ -87,6 +87,7 @@ struct EpiParams {
   const __nv_bfloat16* gate;
   int64_t ldg;
   int rows_per_group;
+  const int* seg;
   const __nv_bfloat16* aux;
   int64_t ld_aux;
   float alpha, beta;
@@ -599,7 +600,8 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
         float gv[32], bv[32];
         if (live && (EPI == EPI_GATED || EPI == EPI_BF16)) load_bias(p.bias, bv, col, p.N);
         if (live && EPI == EPI_GATED) {
-          const int grow = min(row, p.M - 1) / p.rows_per_group;
+          const int crow = min(row, p.M - 1);
+          const int grow = p.seg != nullptr ? p.seg[crow] : crow / p.rows_per_group;
           load_row_bf16(p.gate + (int64_t)grow * p.ldg + col, gv, col, p.N);
         }
         const uint8_t* ibuf = ibase + (L % (R > 0 ? R : 1)) * Cfg::IN_SLOT;
@@ -999,6 +1001,7 @@ void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   p.gate = g.gate;
   p.ldg = g.ldg;
   p.rows_per_group = g.rows_per_group > 0 ? g.rows_per_group : 1;
+  p.seg = g.seg;
   p.aux = g.aux;
   p.ld_aux = g.ld_aux;
   p.alpha = g.alpha;
@@ -1102,8 +1105,12 @@ void gemm_torch(const at::Tensor& A, bool a_mn, int64_t lda, int64_t a_bs, const
                 const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& res, int64_t ldr,
                 int64_t res_bs, const c10::optional<at::Tensor>& gate, int64_t ldg, int64_t rows_per_group,
                 const c10::optional<at::Tensor>& aux, int64_t ld_aux, int64_t half_n, double alpha, double beta,
-                bool accumulate) {
+                bool accumulate, const c10::optional<at::Tensor>& seg) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && out.is_cuda(), "gemm: CUDA tensors expected");
+  if (seg.has_value() && seg->defined())
+    TORCH_CHECK(seg->is_cuda() && seg->scalar_type() == at::kInt && seg->is_contiguous() && seg->numel() == M &&
+                    epi == EPI_GATED,
+                "gemm: seg must be an [M] int32 CUDA tensor, for the gated epilogue");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm: bf16 operands expected");
   if (bias.has_value() && bias->defined()) TORCH_CHECK(bias->scalar_type() == at::kFloat, "gemm: fp32 bias expected");
   const at::cuda::CUDAGuard guard(A.device());
@@ -1139,6 +1146,7 @@ void gemm_torch(const at::Tensor& A, bool a_mn, int64_t lda, int64_t a_bs, const
   g.gate = static_cast<const __nv_bfloat16*>(ptr_or_null(gate));
   g.ldg = ldg;
   g.rows_per_group = (int)rows_per_group;
+  g.seg = static_cast<const int*>(ptr_or_null(seg));
   g.aux = static_cast<const __nv_bfloat16*>(ptr_or_null(aux));
   g.ld_aux = ld_aux;
   g.half_n = (int)half_n;

@@ -39,6 +39,7 @@ struct GemmArgs {
   const __nv_bfloat16* gate = nullptr;
   int64_t ldg = 0;
   int rows_per_group = 1;
+  const int* seg = nullptr;  // optional [M] int32: the gate row of each output row (packed captions); else row / rpg
   const __nv_bfloat16* aux = nullptr;
   int64_t ld_aux = 0;
   int half_n = 0;

@@ -59,7 +59,8 @@ __global__ void __launch_bounds__(256) rms_mod_fwd_kernel(const bf16* __restrict
                                                           const bf16* __restrict__ scale, int64_t ld_sc,
                                                           bf16* __restrict__ h, float* __restrict__ rstd, int M, int C,
                                                           int rpg, float eps, uint8_t* __restrict__ q = nullptr,
-                                                          uint8_t* __restrict__ sf = nullptr) {
+                                                          uint8_t* __restrict__ sf = nullptr,
+                                                          const int* __restrict__ seg = nullptr) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 8 + warp;
   if (row >= M) return;
@@ -81,7 +82,7 @@ __global__ void __launch_bounds__(256) rms_mod_fwd_kernel(const bf16* __restrict
   ss = warp_sum(ss);
   const float r = rsqrtf(ss / (float)C + eps);
   if (lane == 0) rstd[row] = r;
-  const int g = row / rpg;
+  const int g = seg != nullptr ? seg[row] : row / rpg;  // packed rows: the row's sample from the segment table
   uint4* hr = reinterpret_cast<uint4*>(h + (int64_t)row * C);
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
@@ -137,11 +138,16 @@ __global__ void __launch_bounds__(256) rms_mod_bwd_kernel(const bf16* __restrict
                                                           const float* __restrict__ rstd, const float* __restrict__ w,
                                                           const bf16* __restrict__ scale, int64_t ld_sc,
                                                           const bf16* __restrict__ dres, bf16* __restrict__ dx,
-                                                          float* __restrict__ part, int M, int C, int rpg) {
+                                                          float* __restrict__ part, int M, int C, int rpg,
+                                                          const int* __restrict__ cu = nullptr) {
   __shared__ float s_c[BWD_ROWS];
   const int g = blockIdx.y, chunk = blockIdx.x;
-  const int r0 = g * rpg + chunk * BWD_ROWS;
-  const int r1 = min(min(g * rpg + rpg, r0 + BWD_ROWS), M);
+  // rows of group g: [g rpg, (g + 1) rpg), or [cu[g], cu[g + 1]) for packed rows; a chunk past its group's end writes
+  // zero partials
+  const int gb = cu != nullptr ? cu[g] : g * rpg;
+  const int ge = cu != nullptr ? cu[g + 1] : min(g * rpg + rpg, M);
+  const int r0 = gb + chunk * BWD_ROWS;
+  const int r1 = min(ge, r0 + BWD_ROWS);
   const int nrows = r1 - r0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nv = C >> 3;
@@ -232,13 +238,16 @@ __global__ void __launch_bounds__(256, VPL <= 4 ? 2 : 1) rms_mod_bwd_kernel2(con
                                                            const float* __restrict__ rstd, const float* __restrict__ w,
                                                            const bf16* __restrict__ scale, int64_t ld_sc,
                                                            const bf16* __restrict__ dres, bf16* __restrict__ dx,
-                                                           float* __restrict__ part, int M, int rpg) {
+                                                           float* __restrict__ part, int M, int rpg,
+                                                           const int* __restrict__ cu = nullptr) {
   constexpr int C = 256 * VPL, NV = C / 8;
   constexpr int G2 = 256 / NV;  // row groups in phase 2
   __shared__ float red[G2 > 1 ? (G2 - 1) * 3 * C : 1];
   const int g = blockIdx.y, chunk = blockIdx.x;
-  const int r0 = g * rpg + chunk * BWD_ROWS;
-  const int r1 = min(min(g * rpg + rpg, r0 + BWD_ROWS), M);
+  const int gb = cu != nullptr ? cu[g] : g * rpg;  // as in rms_mod_bwd_kernel
+  const int ge = cu != nullptr ? cu[g + 1] : min(g * rpg + rpg, M);
+  const int r0 = gb + chunk * BWD_ROWS;
+  const int r1 = min(ge, r0 + BWD_ROWS);
   const int nrows = r1 - r0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const bf16* sc_row = MOD ? scale + (int64_t)g * ld_sc : nullptr;
@@ -508,18 +517,25 @@ static void check_rows(const at::Tensor& x) {
 
 void rms_mod_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& shift,
                  const c10::optional<at::Tensor>& scale, const at::Tensor& h, const at::Tensor& rstd, int64_t rpg,
-                 double eps) {
+                 double eps, const c10::optional<at::Tensor>& seg) {
   check_rows(x);
   TORCH_CHECK(w.scalar_type() == at::kFloat && w.is_contiguous(), "fp32 weight expected");
   const at::cuda::CUDAGuard guard(x.device());
   const int M = x.size(0), C = x.size(1);
   auto s = at::cuda::getCurrentCUDAStream();
   const bool mod = scale.has_value() && scale->defined();
+  const int* segp = nullptr;
+  if (seg.has_value() && seg->defined()) {
+    TORCH_CHECK(mod && seg->scalar_type() == at::kInt && seg->is_contiguous() && seg->numel() == M && seg->is_cuda(),
+                "rms_mod_fwd: seg must be a [M] int32 CUDA tensor (modulated rows only)");
+    segp = seg->data_ptr<int>();
+  }
   dim3 grid((M + 7) / 8);
   if (mod)
     rms_mod_fwd_kernel<true><<<grid, 256, 0, s>>>(
         reinterpret_cast<const bf16*>(x.data_ptr()), w.data_ptr<float>(), bptr(shift), ld_of(shift), bptr(scale),
-        ld_of(scale), reinterpret_cast<bf16*>(h.data_ptr()), rstd.data_ptr<float>(), M, C, (int)rpg, (float)eps);
+        ld_of(scale), reinterpret_cast<bf16*>(h.data_ptr()), rstd.data_ptr<float>(), M, C, (int)rpg, (float)eps,
+        nullptr, nullptr, segp);
   else
     rms_mod_fwd_kernel<false><<<grid, 256, 0, s>>>(reinterpret_cast<const bf16*>(x.data_ptr()), w.data_ptr<float>(),
                                                    nullptr, 0, nullptr, 0, reinterpret_cast<bf16*>(h.data_ptr()),
@@ -560,15 +576,26 @@ void rms_mod_fwd_mx(const at::Tensor& x, const at::Tensor& w, const c10::optiona
 void rms_mod_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& rstd, const at::Tensor& w,
                  const c10::optional<at::Tensor>& scale, const c10::optional<at::Tensor>& dres, const at::Tensor& dx,
                  const c10::optional<at::Tensor>& dw, const c10::optional<at::Tensor>& dshift,
-                 const c10::optional<at::Tensor>& dscale, int64_t rpg) {
+                 const c10::optional<at::Tensor>& dscale, int64_t rpg, const c10::optional<at::Tensor>& cu,
+                 int64_t max_rows) {
   check_rows(x);
   check_rows(dh);
   const at::cuda::CUDAGuard guard(x.device());
   const int M = x.size(0), C = x.size(1);
   const bool mod = scale.has_value() && scale->defined();
-  const int G = mod ? (M + (int)rpg - 1) / (int)rpg : 1;
+  // packed rows: group g is rows [cu[g], cu[g + 1]), every group at most max_rows long
+  const bool packed = cu.has_value() && cu->defined();
+  const int* cup = nullptr;
+  if (packed) {
+    TORCH_CHECK(mod && cu->scalar_type() == at::kInt && cu->is_contiguous() && cu->numel() >= 2 && cu->is_cuda() &&
+                    max_rows > 0,
+                "rms_mod_bwd: cu must be a [G + 1] int32 CUDA tensor of row offsets, with max_rows > 0");
+    cup = cu->data_ptr<int>();
+  }
+  const int G = packed ? (int)cu->numel() - 1 : mod ? (M + (int)rpg - 1) / (int)rpg : 1;
+  TORCH_CHECK(G <= 65535, "rms_mod_bwd: at most 65535 groups");
   const int rows_per_group = mod ? (int)rpg : M;
-  const int chunks = (rows_per_group + BWD_ROWS - 1) / BWD_ROWS;
+  const int chunks = ((packed ? (int)max_rows : rows_per_group) + BWD_ROWS - 1) / BWD_ROWS;
   auto s = at::cuda::getCurrentCUDAStream();
   at::Tensor part = at::empty({(int64_t)G * chunks * 3 * C}, x.options().dtype(at::kFloat));
   dim3 grid(chunks, G);
@@ -580,7 +607,7 @@ void rms_mod_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& rs
     rms_mod_bwd_kernel2<true, V><<<grid, 256, 0, s>>>(                                                              \
         reinterpret_cast<const bf16*>(dh.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),                   \
         rstd.data_ptr<float>(), w.data_ptr<float>(), scp, ldsc, bptr(dres), reinterpret_cast<bf16*>(dx.data_ptr()), \
-        part.data_ptr<float>(), M, rows_per_group);                                                                  \
+        part.data_ptr<float>(), M, rows_per_group, cup);                                                             \
   else                                                                                                               \
     rms_mod_bwd_kernel2<false, V><<<grid, 256, 0, s>>>(                                                             \
         reinterpret_cast<const bf16*>(dh.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),                   \
@@ -600,7 +627,7 @@ void rms_mod_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& rs
     rms_mod_bwd_kernel<true><<<grid, 256, 0, s>>>(
         reinterpret_cast<const bf16*>(dh.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),
         rstd.data_ptr<float>(), w.data_ptr<float>(), bptr(scale), ld_of(scale), bptr(dres),
-        reinterpret_cast<bf16*>(dx.data_ptr()), part.data_ptr<float>(), M, C, rows_per_group);
+        reinterpret_cast<bf16*>(dx.data_ptr()), part.data_ptr<float>(), M, C, rows_per_group, cup);
   else
     rms_mod_bwd_kernel<false><<<grid, 256, 0, s>>>(
         reinterpret_cast<const bf16*>(dh.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),

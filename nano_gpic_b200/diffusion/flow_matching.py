@@ -84,18 +84,22 @@ class JiTTrainer:
         fm = w * (out - v_t) ** 2
         return dict(fm_loss=fm.mean(), loss=fm.mean(), loss_per_sample=fm.mean(dim=(1, 2, 3)))
 
-    def train_step(self, net, x, y, y_mask=None, t=None, noise=None, grad_scale=None, backward=True):
+    def train_step(self, net, x, y, y_mask=None, t=None, noise=None, grad_scale=None, backward=True, y_pack=None):
         """Forward + backward of the objective through the fused kernels. grad_scale multiplies the gradient of the
         sum of squared errors (default 1 / numel(x): the batch mean); with gradient accumulation over k micro-batches
-        pass 1 / (k numel(x)). Returns loss_per_sample [B] (fp32, on the device, no host sync)."""
+        pass 1 / (k numel(x)). y_pack: packed captions (y [S, D] then; parallel.rebalance.pack_captions). Returns
+        loss_per_sample [B] (fp32, on the device, no host sync)."""
         from ..ops import elementwise as E
+        if y_pack is not None and self.null_condition_p > 0:
+            raise ValueError("packed captions have no caption dropout (as in the reference: training.py:17-18)")
         B = x.shape[0]
         t = self.sample_t(B, x.device) if t is None else t
         noise = torch.randn_like(x) if noise is None else noise
         p = net.patch_size
         tok = E.fm_prep(x, noise, t, p)
         with torch.set_grad_enabled(backward):
-            pred = net.forward_tokens(tok, t, y, y_mask)
+            pred = net.forward_tokens(tok, t, y, y_mask, y_pack) if y_pack is not None else \
+                net.forward_tokens(tok, t, y, y_mask)
         per, g = E.fm_loss(pred.detach(), x, noise, t, p, self.t_eps, grad_scale, need_grad=backward)
         if backward:
             pred.backward(g)

@@ -14,7 +14,8 @@ Compute weights are bf16 shadows of the fp32 master weights (refreshed after eve
 
 Inputs: x [B, 3, H, W], t [B], y [B, T, txt_embed_dim] caption features, y_mask [B, T] bool (left-aligned, True = a
 real token) or None (all T tokens real). The caption-length handling is the reference's masked path (option B): padded
-caption keys are masked out of every attention.
+caption keys are masked out of every attention. Or packed captions (the reference's lever E): y [S, txt_embed_dim]
+with y_pack; the text blocks and the caption projections then run on the S packed rows (`Packing`).
 """
 import math
 import os
@@ -154,7 +155,8 @@ class BottleneckEmbed(nn.Module):
 
 
 class TimestepEmbedder(nn.Module):
-    """mlp = Linear(256, C), SiLU, Linear(C, C) (reference layers/time_embed.py:5-29, max_period 10)."""
+    """mlp = Linear(256, C), SiLU, Linear(C, C) (reference layers/time_embed.py:5-29, max_period 10); both Linears on
+    the tcgen05 GEMM with the bias in the epilogue (`_TimeEmbedFn`), weight gradients into the fp32 .grad buffers."""
 
     def __init__(self, hidden, freq_dim=256):
         super().__init__()
@@ -162,10 +164,9 @@ class TimestepEmbedder(nn.Module):
         self.mlp = nn.Sequential(nn.Linear(freq_dim, hidden, bias=True), nn.SiLU(), nn.Linear(hidden, hidden, bias=True))
 
     def forward(self, t):
-        f = timestep_freq(t.view(-1), self.freq_dim)
+        f = timestep_freq(t.view(-1), self.freq_dim).to(BF16)
         l0, l2 = self.mlp[0], self.mlp[2]
-        h = F.linear(f.to(BF16), l0.weight.to(BF16), l0.bias.to(BF16))
-        return F.linear(F.silu(h), l2.weight.to(BF16), l2.bias.to(BF16))
+        return _TimeEmbedFn.apply(f, l0.weight, l0, l2)
 
 
 class CaptionEmbed(nn.Module):
@@ -193,28 +194,79 @@ def _stage_hook(hook):
         hook[0]._bwd_hook(hook[1])
 
 
+class Packing:
+    """Packed captions (the reference's y_pack, JiT_T2I.py:54-65): the caption tokens of the batch back to back,
+    S rows (the real tokens, then dummy rows up to a bucketed count). Built once per forward from y_pack:
+      segs  Segments: row -> its sample's modulation row (dummy rows -> a zero row B), sample b owns rows
+            [cu[b], cu[b + 1]), at most Tp of them
+      pidx  [S] int32: the row's place b * Tp + pos in the padded [B, Tp] layout, -1 for a dummy row
+      inv   [B * Tp] int32: the packed row of each padded place, -1 for padding
+      lens  [B] int32 caption lengths, Tp the padded width (>= the longest caption)
+    The text blocks and the caption key/value projections run on the S packed rows; only the attention reads the
+    padded layout (gathered in one pass per tensor), as the reference's default text attention does."""
+
+    def __init__(self, y_pack, S, device):
+        kmask = y_pack["kmask"]
+        B, Tp = kmask.shape
+        self.B, self.Tp, self.S = B, Tp, S
+        self.lens = y_pack["lens"].to(device=device, dtype=torch.int32)
+        cu = y_pack["cu"].to(device=device, dtype=torch.int32).contiguous()
+        p = y_pack["pidx"].to(device=device, dtype=torch.int64)
+        real = p < B * Tp
+        self.pidx = torch.where(real, p, torch.full_like(p, -1)).to(torch.int32).contiguous()
+        seg = torch.where(real, torch.div(p, Tp, rounding_mode="floor"), torch.full_like(p, B))
+        self.segs = E.Segments(seg.to(torch.int32).contiguous(), cu, Tp)
+        inv = torch.full((B * Tp + 1,), -1, dtype=torch.int64, device=device)
+        inv.scatter_(0, torch.where(real, p, torch.full_like(p, B * Tp)), torch.arange(S, device=device))
+        inv[B * Tp] = -1
+        self.inv = inv[:B * Tp].to(torch.int32).contiguous()
+        self.pos = y_pack["pos"].to(device=device, dtype=torch.int32).contiguous()
+
+    def to_padded(self, t):
+        return E.gather_rows(t, self.inv)
+
+    def to_packed(self, t, out=None):
+        return E.gather_rows(t, self.pidx, out)
+
+
+def _with_zero_row(mod):
+    """mod [B, 6C] with a zero row appended: the modulation of the dummy rows of packed captions."""
+    return torch.cat([mod, mod.new_zeros(1, mod.shape[1])])
+
+
 class _TextBlockFn(torch.autograd.Function):
     @staticmethod
-    def _run(y, mod, blk, lens, T):
-        """The block's forward: (output, the activations its backward reads)."""
+    def _run(y, mod, blk, lens, T, pack=None):
+        """The block's forward: (output, the activations its backward reads). pack: a Packing (y holds packed rows)
+        or None (T rows per sample)."""
         C = y.shape[1]
         a = blk.attn
         n1, n2 = blk.norm1, blk.norm2
-        h1, r1 = NR.rms_mod_fwd(y, f32(n1.weight), mod[:, 0:C], mod[:, C:2 * C], T, n1.variance_epsilon)
+        grp = T if pack is None else pack.segs
+        h1, r1 = NR.rms_mod_fwd(y, f32(n1.weight), mod[:, 0:C], mod[:, C:2 * C], grp, n1.variance_epsilon)
         qkv = G.linear(h1, w16(a.qkv))
         q, rq = QK.qk_norm_fwd(qkv[:, 0:C], f32(a.q_norm.weight), eps=a.q_norm.variance_epsilon)
         k, rk = QK.qk_norm_fwd(qkv[:, C:2 * C], f32(a.k_norm.weight), eps=a.k_norm.variance_epsilon)
-        o, lse = A.attn_fwd(q, T, k, qkv[:, 2 * C:], T, lens)
-        y2, ya = G.linear_gated_residual(o, w16(a.proj), f32(a.proj.bias), y, mod[:, 2 * C:3 * C], T)
-        h2, r2 = NR.rms_mod_fwd(y2, f32(n2.weight), mod[:, 3 * C:4 * C], mod[:, 4 * C:5 * C], T, n2.variance_epsilon)
+        if pack is None:
+            o, lse = A.attn_fwd(q, T, k, qkv[:, 2 * C:], T, lens)
+            padded = ()
+        else:  # the attention on the padded layout, its output back to the packed rows (dummy rows read zeros)
+            qp, kp, vp = pack.to_padded(q), pack.to_padded(k), pack.to_padded(qkv[:, 2 * C:])
+            op, lse = A.attn_fwd(qp, pack.Tp, kp, vp, pack.Tp, lens)
+            o = pack.to_packed(op)
+            padded = (qp, kp, vp, op)
+        y2, ya = G.linear_gated_residual(o, w16(a.proj), f32(a.proj.bias), y, mod[:, 2 * C:3 * C], grp)
+        h2, r2 = NR.rms_mod_fwd(y2, f32(n2.weight), mod[:, 3 * C:4 * C], mod[:, 4 * C:5 * C], grp, n2.variance_epsilon)
         act, pre = G.swiglu_linear(h2, w16(blk.mlp.w12))
-        y3, ym = G.linear_gated_residual(act, w16(blk.mlp.w3), None, y2, mod[:, 5 * C:6 * C], T)
-        return y3, (h1, r1, qkv, q, rq, k, rk, o, lse, y2, ya, h2, r2, act, pre, ym)
+        y3, ym = G.linear_gated_residual(act, w16(blk.mlp.w3), None, y2, mod[:, 5 * C:6 * C], grp)
+        return y3, (h1, r1, qkv, q, rq, k, rk, o, lse, y2, ya, h2, r2, act, pre, ym) + padded
 
     @staticmethod
-    def forward(ctx, y, mod, anchor, blk, lens, T, hook=None):
-        y3, acts = _TextBlockFn._run(y, mod, blk, lens, T)
-        ctx.blk, ctx.T, ctx.hook = blk, T, hook
+    def forward(ctx, y, mod, anchor, blk, lens, T, hook=None, pack=None):
+        if pack is not None:
+            mod = _with_zero_row(mod)
+        y3, acts = _TextBlockFn._run(y, mod, blk, lens, T, pack)
+        ctx.blk, ctx.T, ctx.hook, ctx.pack = blk, T, hook, pack
         ctx.recompute = getattr(blk, "_recompute", False)
         ctx.save_for_backward(y, mod, lens, *(() if ctx.recompute else acts))
         return y3
@@ -222,44 +274,55 @@ class _TextBlockFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy3):
         y, mod, lens, *acts = ctx.saved_tensors
-        blk, T = ctx.blk, ctx.T
+        blk, T, pack = ctx.blk, ctx.T, ctx.pack
         _stage_hook(ctx.hook)
         if ctx.recompute:  # activation checkpointing: rerun the forward from the saved inputs
-            acts = _TextBlockFn._run(y, mod, blk, lens, T)[1]
-        (h1, r1, qkv, q, rq, k, rk, o, lse, y2, ya, h2, r2, act, pre, ym) = acts
+            acts = _TextBlockFn._run(y, mod, blk, lens, T, pack)[1]
+        (h1, r1, qkv, q, rq, k, rk, o, lse, y2, ya, h2, r2, act, pre, ym) = acts[:16]
+        grp = T if pack is None else pack.segs
         a = blk.attn
         C = y.shape[1]
         dy3 = dy3.contiguous()
         dmod = torch.empty(mod.shape, device=mod.device, dtype=torch.float32)
         # mlp branch: y3 = y2 + g2 * w3(act)
-        dym = E.gate_bwd(dy3, ym, mod[:, 5 * C:6 * C], T, dgate=dmod[:, 5 * C:6 * C])
+        dym = E.gate_bwd(dy3, ym, mod[:, 5 * C:6 * C], grp, dgate=dmod[:, 5 * C:6 * C])
         dpre = G.swiglu_dgrad(dym, w16(blk.mlp.w3), pre)
         _wgrad(dym, act, blk.mlp.w3.weight)
         dh2 = G.linear_dgrad(dpre, w16(blk.mlp.w12))
         _wgrad(dpre, h2, blk.mlp.w12.weight)
-        dy2 = NR.rms_mod_bwd(dh2, y2, r2, f32(blk.norm2.weight), mod[:, 4 * C:5 * C], T, dres=dy3,
+        dy2 = NR.rms_mod_bwd(dh2, y2, r2, f32(blk.norm2.weight), mod[:, 4 * C:5 * C], grp, dres=dy3,
                              dw_acc=grad_of(blk.norm2.weight), dshift=dmod[:, 3 * C:4 * C],
                              dscale=dmod[:, 4 * C:5 * C])
         # attention branch: y2 = y + g1 * proj(o)
-        dya = E.gate_bwd(dy2, ya, mod[:, 2 * C:3 * C], T, dgate=dmod[:, 2 * C:3 * C], dbias=grad_of(a.proj.bias))
+        dya = E.gate_bwd(dy2, ya, mod[:, 2 * C:3 * C], grp, dgate=dmod[:, 2 * C:3 * C], dbias=grad_of(a.proj.bias))
         do = G.linear_dgrad(dya, w16(a.proj))
         _wgrad(dya, o, a.proj.weight)
         dqkv = torch.empty_like(qkv)
-        dq, dk, _, _, _ = A.attn_bwd(do, q, T, k, qkv[:, 2 * C:], T, lens, o, lse, dv0=dqkv[:, 2 * C:])
+        if pack is None:
+            dq, dk, _, _, _ = A.attn_bwd(do, q, T, k, qkv[:, 2 * C:], T, lens, o, lse, dv0=dqkv[:, 2 * C:])
+        else:
+            qp, kp, vp, op = acts[16:]
+            dvp = torch.empty_like(vp)
+            dqp, dkp, _, _, _ = A.attn_bwd(pack.to_padded(do), qp, pack.Tp, kp, vp, pack.Tp, lens, op, lse, dv0=dvp)
+            pack.to_packed(dvp, out=dqkv[:, 2 * C:])
+            dq, dk = pack.to_packed(dqp), pack.to_packed(dkp)
         QK.qk_norm_bwd(dq, qkv[:, 0:C], rq, f32(a.q_norm.weight), dsrc=dqkv[:, 0:C], dw_acc=grad_of(a.q_norm.weight))
         QK.qk_norm_bwd(dk, qkv[:, C:2 * C], rk, f32(a.k_norm.weight), dsrc=dqkv[:, C:2 * C],
                        dw_acc=grad_of(a.k_norm.weight))
         dh1 = G.linear_dgrad(dqkv, w16(a.qkv))
         _wgrad(dqkv, h1, a.qkv.weight)
-        dy = NR.rms_mod_bwd(dh1, y, r1, f32(blk.norm1.weight), mod[:, C:2 * C], T, dres=dy2,
+        dy = NR.rms_mod_bwd(dh1, y, r1, f32(blk.norm1.weight), mod[:, C:2 * C], grp, dres=dy2,
                             dw_acc=grad_of(blk.norm1.weight), dshift=dmod[:, 0:C], dscale=dmod[:, C:2 * C])
-        return dy, dmod.to(BF16), None, None, None, None, None
+        if pack is not None:
+            dmod = dmod[:pack.B]  # the dummy rows' zero modulation row is no input
+        return dy, dmod.to(BF16), None, None, None, None, None, None
 
 
 class _ImageBlockFn(torch.autograd.Function):
     @staticmethod
-    def _run(x, yt, mod, blk, lens, L, T, cos, sin):
-        """The block's forward: (output, the activations its backward reads)."""
+    def _run(x, yt, mod, blk, lens, L, T, cos, sin, pack=None):
+        """The block's forward: (output, the activations its backward reads). pack: a Packing (yt holds packed caption
+        rows) or None (T rows per sample)."""
         C = x.shape[1]
         a = blk.attn
         n1, n2 = blk.norm1, blk.norm2
@@ -276,7 +339,13 @@ class _ImageBlockFn(torch.autograd.Function):
         q, rq = QK.qk_norm_fwd(qkv[:, 0:C], f32(a.q_norm.weight), cos, sin, L, a.q_norm.variance_epsilon)
         kx, rkx = QK.qk_norm_fwd(qkv[:, C:2 * C], f32(a.k_norm.weight), cos, sin, L, a.k_norm.variance_epsilon)
         ky, rky = QK.qk_norm_fwd(kvy[:, 0:C], f32(a.k_norm.weight), eps=a.k_norm.variance_epsilon)
-        o, lse = A.attn_fwd(q, L, kx, qkv[:, 2 * C:], L, L, ky, kvy[:, C:], T, lens)
+        if pack is None:
+            o, lse = A.attn_fwd(q, L, kx, qkv[:, 2 * C:], L, L, ky, kvy[:, C:], T, lens)
+            padded = ()
+        else:  # packed caption keys/values placed in the padded [B, Tp] layout the attention reads
+            kyp, vyp = pack.to_padded(ky), pack.to_padded(kvy[:, C:])
+            o, lse = A.attn_fwd(q, L, kx, qkv[:, 2 * C:], L, L, kyp, vyp, pack.Tp, lens)
+            padded = (kyp, vyp)
         if mxw is None:
             x2, ya = G.linear_gated_residual(o, w16(a.proj), f32(a.proj.bias), x, mod[:, 2 * C:3 * C], L)
         else:
@@ -291,12 +360,12 @@ class _ImageBlockFn(torch.autograd.Function):
                                             n2.variance_epsilon)
             act, pre, actq = MXO.swiglu_linear(h2q, mxw["w12"], quant_act=True)  # act's MX copy from the epilogue
             x3, ym = MXO.linear_gated_residual(actq, mxw["w3"], None, x2, mod[:, 5 * C:6 * C], L)
-        return x3, (h1, r1, qkv, kvy, q, rq, kx, rkx, ky, rky, o, lse, x2, ya, h2, r2, act, pre, ym)
+        return x3, (h1, r1, qkv, kvy, q, rq, kx, rkx, ky, rky, o, lse, x2, ya, h2, r2, act, pre, ym) + padded
 
     @staticmethod
-    def forward(ctx, x, yt, mod, anchor, blk, lens, L, T, cos, sin, hook=None):
-        x3, acts = _ImageBlockFn._run(x, yt, mod, blk, lens, L, T, cos, sin)
-        ctx.blk, ctx.L, ctx.T, ctx.hook = blk, L, T, hook
+    def forward(ctx, x, yt, mod, anchor, blk, lens, L, T, cos, sin, hook=None, pack=None):
+        x3, acts = _ImageBlockFn._run(x, yt, mod, blk, lens, L, T, cos, sin, pack)
+        ctx.blk, ctx.L, ctx.T, ctx.hook, ctx.pack = blk, L, T, hook, pack
         ctx.recompute = getattr(blk, "_recompute", False)
         ctx.save_for_backward(x, yt, mod, lens, cos, sin, *(() if ctx.recompute else acts))
         return x3
@@ -304,11 +373,11 @@ class _ImageBlockFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dx3):
         x, yt, mod, lens, cos, sin, *acts = ctx.saved_tensors
-        blk, L, T = ctx.blk, ctx.L, ctx.T
+        blk, L, T, pack = ctx.blk, ctx.L, ctx.T, ctx.pack
         _stage_hook(ctx.hook)
         if ctx.recompute:  # activation checkpointing: rerun the forward from the saved inputs
-            acts = _ImageBlockFn._run(x, yt, mod, blk, lens, L, T, cos, sin)[1]
-        (h1, r1, qkv, kvy, q, rq, kx, rkx, ky, rky, o, lse, x2, ya, h2, r2, act, pre, ym) = acts
+            acts = _ImageBlockFn._run(x, yt, mod, blk, lens, L, T, cos, sin, pack)[1]
+        (h1, r1, qkv, kvy, q, rq, kx, rkx, ky, rky, o, lse, x2, ya, h2, r2, act, pre, ym) = acts[:19]
         a = blk.attn
         C = x.shape[1]
         dx3 = dx3.contiguous()
@@ -326,8 +395,16 @@ class _ImageBlockFn(torch.autograd.Function):
         _wgrad(dya, o, a.proj.weight)
         dqkv = torch.empty_like(qkv)
         dkvy = torch.empty_like(kvy)
-        dq, dkx, _, dky, _ = A.attn_bwd(do, q, L, kx, qkv[:, 2 * C:], L, L, o, lse, ky, kvy[:, C:], T, lens,
-                                        dv0=dqkv[:, 2 * C:], dv1=dkvy[:, C:])
+        if pack is None:
+            dq, dkx, _, dky, _ = A.attn_bwd(do, q, L, kx, qkv[:, 2 * C:], L, L, o, lse, ky, kvy[:, C:], T, lens,
+                                            dv0=dqkv[:, 2 * C:], dv1=dkvy[:, C:])
+        else:
+            kyp, vyp = acts[19:]
+            dvyp = torch.empty_like(vyp)
+            dq, dkx, _, dkyp, _ = A.attn_bwd(do, q, L, kx, qkv[:, 2 * C:], L, L, o, lse, kyp, vyp, pack.Tp, lens,
+                                             dv0=dqkv[:, 2 * C:], dv1=dvyp)
+            pack.to_packed(dvyp, out=dkvy[:, C:])
+            dky = pack.to_packed(dkyp)
         QK.qk_norm_bwd(dq, qkv[:, 0:C], rq, f32(a.q_norm.weight), cos, sin, L, dsrc=dqkv[:, 0:C],
                        dw_acc=grad_of(a.q_norm.weight))
         dwk = grad_of(a.k_norm.weight)
@@ -339,18 +416,18 @@ class _ImageBlockFn(torch.autograd.Function):
         _wgrad(dkvy, yt, a.kv_y.weight)
         dx = NR.rms_mod_bwd(dh1, x, r1, f32(blk.norm1.weight), mod[:, C:2 * C], L, dres=dx2,
                             dw_acc=grad_of(blk.norm1.weight), dshift=dmod[:, 0:C], dscale=dmod[:, C:2 * C])
-        return dx, dyt, dmod.to(BF16), None, None, None, None, None, None, None, None
+        return dx, dyt, dmod.to(BF16), None, None, None, None, None, None, None, None, None
 
 
 class _ModFn(torch.autograd.Function):
-    """adaLN modulation mod = c W^T + b from the bf16 weight shadow (the reference's autocast Linear(C, 6C));
-    W and b gradients into the fp32 .grad buffers, dc = dmod W."""
+    """adaLN modulation mod = c W^T + b on the tcgen05 GEMM (bias in the epilogue) from the bf16 weight shadow (the
+    reference's autocast Linear(C, 6C)); W and b gradients into the fp32 .grad buffers, dc = dmod W."""
 
     @staticmethod
     def forward(ctx, c16, anchor, lin):
         ctx.lin = lin
         ctx.save_for_backward(c16)
-        return F.linear(c16, w16(lin), w16(lin.bias))
+        return G.linear(c16.contiguous(), w16(lin), f32(lin.bias))
 
     @staticmethod
     def backward(ctx, dmod):
@@ -360,6 +437,34 @@ class _ModFn(torch.autograd.Function):
         _wgrad(dmod, c16, lin.weight)
         _bias_grad(dmod, lin.bias)
         return G.linear_dgrad(dmod, w16(lin)), None, None
+
+
+class _TimeEmbedFn(torch.autograd.Function):
+    """t_emb = W2 silu(W1 f + b1) + b2 for the sinusoidal features f [B, 256] bf16: two GEMMs with bias epilogues,
+    bf16 activations as under the reference's autocast; the weight and bias gradients go into .grad, no gradient
+    flows to f (the timesteps are data)."""
+
+    @staticmethod
+    def forward(ctx, f, anchor, l0, l2):
+        h = G.linear(f, w16(l0), f32(l0.bias))
+        s = F.silu(h)
+        ctx.l0, ctx.l2 = l0, l2
+        ctx.save_for_backward(f, h, s)
+        return G.linear(s, w16(l2), f32(l2.bias))
+
+    @staticmethod
+    def backward(ctx, dt):
+        f, h, s = ctx.saved_tensors
+        l0, l2 = ctx.l0, ctx.l2
+        dt = dt.to(BF16).contiguous()
+        _wgrad(dt, s, l2.weight)
+        _bias_grad(dt, l2.bias)
+        ds = G.linear_dgrad(dt, w16(l2)).float()
+        sig = torch.sigmoid(h.float())
+        dh = (ds * sig * (1 + h.float() * (1 - sig))).to(BF16)
+        _wgrad(dh, f, l0.weight)
+        _bias_grad(dh, l0.bias)
+        return None, None, None, None
 
 
 class _LinearFn(torch.autograd.Function):
@@ -417,6 +522,28 @@ class _AddRowsFn(torch.autograd.Function):
         return d, None, None, None, None
 
 
+class _AddPosFn(torch.autograd.Function):
+    """Packed captions: bf16(a + table[pos[row]]) (the reference's y_pos_embedding[0].index_select(0, pos)); the
+    table's gradient sums each position over the real rows (dummy rows add nothing), through the padded layout, in a
+    fixed order."""
+
+    @staticmethod
+    def forward(ctx, a, anchor, table, pack, param):
+        ctx.pack, ctx.param = pack, param
+        return a + E.gather_rows(table, pack.pos)
+
+    @staticmethod
+    def backward(ctx, d):
+        pack, param = ctx.pack, ctx.param
+        d = d.contiguous()
+        if param is not None:
+            Cd = d.shape[-1]
+            P = pack.Tp
+            dp = pack.to_padded(d)  # [B * Tp, C], zeros where no token
+            E.colsum(dp.reshape(-1, P * Cd), grad_of(param).view(-1)[:P * Cd], accumulate=True)
+        return d, None, None, None, None
+
+
 class _LayerNormFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, eps):
@@ -466,7 +593,7 @@ class JiT_T2I(nn.Module):
                                                  for _ in range(num_text_blocks)])
         self.final_layer = FinalLayer(hidden_size, patch_dim)
         self.initialize_weights()
-        for p in self.t_embedder.parameters():  # read in fp32 by the forward: replicated under sharding
+        for p in self.t_embedder.parameters():  # small and read by every micro-batch first: replicated under sharding
             p._replicate = True
         self._rope = {}
         self._bwd_hook = None  # set by the data-parallel layer around the last micro-batch's backward
@@ -538,25 +665,36 @@ class JiT_T2I(nn.Module):
             return torch.full((B,), T, dtype=torch.int32, device=y.device)
         return y_mask.sum(1, dtype=torch.int32)
 
-    def forward_tokens(self, x_tok, t, y, y_mask=None):
-        """x_tok: [B*N, patch_dim] bf16 patch tokens -> predicted clean-image tokens [B*N, patch_dim] bf16."""
-        B, T = y.shape[:2]
+    def forward_tokens(self, x_tok, t, y, y_mask=None, y_pack=None):
+        """x_tok: [B*N, patch_dim] bf16 patch tokens -> predicted clean-image tokens [B*N, patch_dim] bf16.
+        y: [B, T, txt_embed_dim] with y_mask, or packed [S, txt_embed_dim] with y_pack (the reference's lever E
+        format: lens, cu, pidx, kmask, pos; JiT_T2I.py:54-65,478-496 there)."""
         N, C = self.num_patches, self.hidden_size
-        lens = self._caption_lens(y, y_mask)
         cos, sin = self.rope(x_tok.device)
         # condition: c = silu(t_embedder(t))  [B, C]
         c = F.silu(self.t_embedder(t.view(-1)))
-        # caption tokens: RMSNorm(Linear(y)) + y_pos_embedding[:T]
-        yt = y.reshape(B * T, -1).to(BF16)
+        # caption tokens: RMSNorm(Linear(y)) + y_pos_embedding[position]
+        pack = None
+        if y_pack is not None:
+            pack = Packing(y_pack, y.shape[0], x_tok.device)
+            T, lens = pack.Tp, pack.lens
+            yt = y.to(BF16).contiguous()
+        else:
+            B, T = y.shape[:2]
+            lens = self._caption_lens(y, y_mask)
+            yt = y.reshape(B * T, -1).to(BF16)
         yt = _LinearFn.apply(yt, self.y_embedder.proj.weight, self.y_embedder.proj, False)
         yt = _RMSFn.apply(yt, self.y_embedder.norm.weight, self.y_embedder.norm)
-        yt = _AddRowsFn.apply(yt, self.y_pos_embedding, w16(self.y_pos_embedding)[0, :T], T, self.y_pos_embedding)
+        if pack is None:
+            yt = _AddRowsFn.apply(yt, self.y_pos_embedding, w16(self.y_pos_embedding)[0, :T], T, self.y_pos_embedding)
+        else:
+            yt = _AddPosFn.apply(yt, self.y_pos_embedding, w16(self.y_pos_embedding)[0], pack, self.y_pos_embedding)
         nb, nt = len(self.blocks), len(self.text_refine_blocks)
         c = c.to(BF16)
         for j, blk in enumerate(self.text_refine_blocks):
             lin = blk.adaLN_modulation.lin
             mod = _ModFn.apply(c, lin.weight, lin)
-            yt = _TextBlockFn.apply(yt, mod, blk.norm1.weight, blk, lens, T, (self, 1 + nb + (nt - 1 - j)))
+            yt = _TextBlockFn.apply(yt, mod, blk.norm1.weight, blk, lens, T, (self, 1 + nb + (nt - 1 - j)), pack)
         # image tokens: Linear(Linear(patch)) + pos_embed
         h = _LinearFn.apply(x_tok, self.x_embedder.proj1.weight, self.x_embedder.proj1, False)
         h = _LinearFn.apply(h, self.x_embedder.proj2.weight, self.x_embedder.proj2, True)
@@ -564,15 +702,15 @@ class JiT_T2I(nn.Module):
         for i, blk in enumerate(self.blocks):
             lin = blk.adaLN_modulation.lin
             mod = _ModFn.apply(c, lin.weight, lin)
-            x = _ImageBlockFn.apply(x, yt, mod, blk.norm1.weight, blk, lens, N, T, cos, sin, (self, nb - i))
+            x = _ImageBlockFn.apply(x, yt, mod, blk.norm1.weight, blk, lens, N, T, cos, sin, (self, nb - i), pack)
         x = _LayerNormFn.apply(x, 1e-6)
         return _LinearFn.apply(x, self.final_layer.linear.weight, self.final_layer.linear, True)
 
     def forward(self, x, t, y, return_layer=None, y_mask=None, y_pack=None):
-        """x [B, C, H, W] -> predicted clean image [B, C, H, W] (fp32). Same call as the reference's forward;
-        return_layer and y_pack are not supported (the reference's ladder path does not use them)."""
-        assert return_layer is None and y_pack is None, "return_layer / y_pack are not supported"
+        """x [B, C, H, W] -> predicted clean image [B, C, H, W] (fp32). Same call as the reference's forward, packed
+        captions (y_pack) included; return_layer is not supported (the reference's ladder path does not use it)."""
+        assert return_layer is None, "return_layer is not supported"
         B, Cin, H, W = x.shape
         tok = E.patchify(x.float(), self.patch_size)
-        out = self.forward_tokens(tok, t, y, y_mask)
+        out = self.forward_tokens(tok, t, y, y_mask, y_pack)
         return _UnpatchifyFn.apply(out, (B, Cin, H, W), self.patch_size)

@@ -9,23 +9,81 @@ import torch
 from .._ext import ext
 
 
+class Segments:
+    """Packed rows grouped by sample (the reference's packed captions, JiT_T2I.py:54-65): row r takes the modulation
+    row seg[r] ([S] int32; rows after the last sample point at a zero row); sample g owns rows [cu[g], cu[g + 1])
+    ([G + 1] int32), at most max_rows of them. Ops that take `rows_per_group` accept a Segments in its place: forward
+    kernels read seg, backward reductions read cu, and rows after cu[G] get zero gradients."""
+
+    def __init__(self, seg, cu, max_rows):
+        self.seg, self.cu, self.max_rows = seg, cu, int(max_rows)
+        self.groups = cu.numel() - 1
+
+    def expand(self, t):
+        """t [G (+ 1), C] -> [S, C]: each row's group row (PyTorch; the CPU paths)."""
+        return t.index_select(0, self.seg.long())
+
+    def sum_rows(self, v):
+        """[S, C] -> [G, C]: per-group sums of the rows each group owns (PyTorch; the CPU paths)."""
+        owned = self.seg.long() < self.groups
+        out = torch.zeros(self.groups, v.shape[1], dtype=v.dtype, device=v.device)
+        return out.index_add_(0, self.seg.long()[owned], v[owned])
+
+    def owned(self, M, device):
+        """[M] bool: rows that belong to a group."""
+        return self.seg.long().to(device) < self.groups
+
+
+def _rows(rows_per_group, t, M):
+    """t [G, C] expanded to one row per token for the PyTorch paths."""
+    if isinstance(rows_per_group, Segments):
+        return rows_per_group.expand(t)
+    return t.repeat_interleave(rows_per_group, 0)[:M]
+
+
 def gate_bwd(dout, y, gate, rows_per_group, dgate=None, dbias=None):
-    """Backward of out = res + gate[row // rows_per_group] * y (res's gradient is dout itself).
+    """Backward of out = res + gate[row // rows_per_group] * y (res's gradient is dout itself); rows_per_group may be
+    a Segments (packed rows).
     Returns dy = bf16(gate * dout); writes d_gate [G, C] into `dgate` (fp32 view) and adds d_bias (the column sums of
     the rounded dy) into `dbias` [C] fp32 when given."""
     M, C = dout.shape
+    seg = rows_per_group if isinstance(rows_per_group, Segments) else None
     if not dout.is_cuda:
-        G = gate.shape[0]
-        g = gate.float().repeat_interleave(rows_per_group, 0)[:M]
+        g = _rows(rows_per_group, gate.float(), M)
         dy = (g * dout.float()).to(torch.bfloat16)
+        if seg is not None:
+            dy = dy * seg.owned(M, dy.device)[:, None].to(dy.dtype)
         if dgate is not None:
-            dgate.copy_((dout.float() * y.float()).view(G, rows_per_group, C).sum(1))
+            prod = dout.float() * y.float()
+            if seg is not None:
+                dgate[:seg.groups].copy_(seg.sum_rows(prod))
+            else:
+                dgate.copy_(prod.view(gate.shape[0], rows_per_group, C).sum(1))
         if dbias is not None:
             dbias.add_(dy.float().sum(0))
         return dy
+    if seg is not None:
+        dy = torch.zeros_like(dout)  # rows of no sample keep a zero gradient
+        ext().gate_bwd(dout, y, gate, dy, dgate, dbias, 1, seg.cu, seg.max_rows)
+        return dy
     dy = torch.empty_like(dout)
-    ext().gate_bwd(dout, y, gate, dy, dgate, dbias, rows_per_group)
+    ext().gate_bwd(dout, y, gate, dy, dgate, dbias, rows_per_group, None, 0)
     return dy
+
+
+def gather_rows(src, idx, out=None):
+    """out[r] = src[idx[r]] for bf16 rows (zeros where idx[r] < 0): src [R, C] (row stride free), idx [M] int32 ->
+    [M, C]. Moves caption rows between the packed layout and the padded [B, Tp] layout."""
+    M, C = idx.numel(), src.shape[1]
+    if out is None:
+        out = torch.empty(M, C, dtype=src.dtype, device=src.device)
+    if not src.is_cuda:
+        i = idx.long()
+        vals = src.index_select(0, i.clamp(min=0))
+        out.copy_(vals * (i >= 0)[:, None].to(vals.dtype))
+        return out
+    ext().gather_rows(src, idx, out)
+    return out
 
 
 def _patch_index(B, Cin, H, W, p, device):

@@ -11,6 +11,7 @@ JiT_T2I.py:201-210.
 import torch
 
 from .._ext import ext
+from .elementwise import Segments, _rows
 
 EPI_BF16, EPI_F32, EPI_AXPBY, EPI_GATED, EPI_SWIGLU, EPI_SWIGLU_BWD = range(6)
 
@@ -25,11 +26,11 @@ def _bs(t):
 
 
 def _call(A, a_mn, B, b_mn, out, epi, M, N, K, batch=1, b_rows=0, out2=None, bias=None, res=None, gate=None,
-          rows_per_group=1, aux=None, half_n=0, alpha=1.0, beta=0.0, accumulate=False):
+          rows_per_group=1, aux=None, half_n=0, alpha=1.0, beta=0.0, accumulate=False, seg=None):
     ext().gemm(A, a_mn, _ld(A), _bs(A), B, b_mn, _ld(B), _bs(B), b_rows, out, _ld(out), _bs(out), epi, M, N, K, batch,
                out2, _ld(out2) if out2 is not None else 0, bias, res, _ld(res) if res is not None else 0,
                _bs(res) if res is not None else 0, gate, _ld(gate) if gate is not None else 0, rows_per_group, aux,
-               _ld(aux) if aux is not None else 0, half_n, float(alpha), float(beta), bool(accumulate))
+               _ld(aux) if aux is not None else 0, half_n, float(alpha), float(beta), bool(accumulate), seg)
     return out
 
 
@@ -91,20 +92,22 @@ def linear_wgrad_bf16(dy, x):
 # ------------------------------------------------------------------------------------------------- fused epilogues
 def linear_gated_residual(x, w, bias, res, gate, rows_per_group):
     """y = bf16(x @ w^T + bias); out = bf16(res + gate[row // rows_per_group] * y). Returns (out, y).
-    gate: [G, N] bf16 with a row stride of its own (e.g. a column slice of the adaLN output)."""
+    gate: [G, N] bf16 with a row stride of its own (e.g. a column slice of the adaLN output). rows_per_group may be a
+    Segments (packed rows: the gate row of each row from its segment table)."""
     M, K = x.shape
     N = w.shape[0]
+    seg = rows_per_group if isinstance(rows_per_group, Segments) else None
     if not x.is_cuda:
         y = x.float() @ w.float().t()
         if bias is not None:
             y = y + bias.float()
         y = y.to(torch.bfloat16)
-        g = gate.float().repeat_interleave(rows_per_group, 0)[:M]
+        g = _rows(rows_per_group, gate.float(), M)
         return (res.float() + g * y.float()).to(torch.bfloat16), y
     out = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
     y = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
     _call(x, False, w, False, out, EPI_GATED, M, N, K, out2=y, bias=bias, res=res, gate=gate,
-          rows_per_group=rows_per_group)
+          rows_per_group=1 if seg is not None else rows_per_group, seg=seg.seg if seg is not None else None)
     return out, y
 
 

@@ -14,6 +14,7 @@ norm of the reference's lever K (baselines/PixelGen/src/models/layers/fused_norm
 import torch
 
 from .._ext import ext
+from .elementwise import Segments, _rows
 
 
 def rms_mod_fwd(x, w, shift=None, scale=None, rows_per_group=1, eps=1e-6):
@@ -25,13 +26,16 @@ def rms_mod_fwd(x, w, shift=None, scale=None, rows_per_group=1, eps=1e-6):
         rstd = torch.rsqrt(xf.pow(2).mean(-1) + eps)
         u = w.float() * xf * rstd[:, None]
         if scale is not None:
-            sc = scale.float().repeat_interleave(rows_per_group, 0)[:M]
-            sh = shift.float().repeat_interleave(rows_per_group, 0)[:M]
+            sc = _rows(rows_per_group, scale.float(), M)
+            sh = _rows(rows_per_group, shift.float(), M)
             u = u * (1 + sc) + sh
         return u.to(torch.bfloat16), rstd
     h = torch.empty_like(x)
     rstd = torch.empty(M, device=x.device, dtype=torch.float32)
-    ext().rms_mod_fwd(x, w, shift, scale, h, rstd, rows_per_group, eps)
+    if isinstance(rows_per_group, Segments):
+        ext().rms_mod_fwd(x, w, shift, scale, h, rstd, 1, eps, rows_per_group.seg)
+    else:
+        ext().rms_mod_fwd(x, w, shift, scale, h, rstd, rows_per_group, eps, None)
     return h, rstd
 
 
@@ -57,20 +61,30 @@ def rms_mod_fwd_mx(x, w, shift=None, scale=None, rows_per_group=1, eps=1e-6):
 
 def rms_mod_bwd(dh, x, rstd, w, scale=None, rows_per_group=1, dres=None, dw_acc=None, dshift=None, dscale=None):
     """Backward of rms_mod_fwd. Returns dx [M, C] bf16 (plus dres when given).
-    dw_acc [C] fp32: d_w is added into it. dshift/dscale [G, C] fp32 views: overwritten (None: not computed)."""
+    dw_acc [C] fp32: d_w is added into it. dshift/dscale [G, C] fp32 views: overwritten (None: not computed).
+    rows_per_group may be a Segments (packed rows): rows of no sample then get dx = 0 and add nothing to d_w."""
     M, C = x.shape
+    seg = rows_per_group if isinstance(rows_per_group, Segments) else None
     if not x.is_cuda:
         xf, dhf = x.float(), dh.float()
+        if seg is not None:
+            dhf = dhf * seg.owned(M, dhf.device)[:, None].float()
         xn = xf * rstd[:, None]
         u = w.float() * xn
         if scale is not None:
             G = scale.shape[0]
-            sc = scale.float().repeat_interleave(rows_per_group, 0)[:M]
+            sc = _rows(rows_per_group, scale.float(), M)
             du = dhf * (1 + sc)
             if dshift is not None:
-                dshift.copy_(dhf.view(G, rows_per_group, C).sum(1))
+                if seg is not None:
+                    dshift[:seg.groups].copy_(seg.sum_rows(dhf))
+                else:
+                    dshift.copy_(dhf.view(G, rows_per_group, C).sum(1))
             if dscale is not None:
-                dscale.copy_((dhf * u).view(G, rows_per_group, C).sum(1))
+                if seg is not None:
+                    dscale[:seg.groups].copy_(seg.sum_rows(dhf * u))
+                else:
+                    dscale.copy_((dhf * u).view(G, rows_per_group, C).sum(1))
         else:
             du = dhf
         if dw_acc is not None:
@@ -79,9 +93,15 @@ def rms_mod_bwd(dh, x, rstd, w, scale=None, rows_per_group=1, dres=None, dw_acc=
         dx = rstd[:, None] * (dxn - xn * (dxn * xn).mean(-1, keepdim=True))
         if dres is not None:
             dx = dx + dres.float()
+        if seg is not None:
+            dx = dx * seg.owned(M, dx.device)[:, None].float()
         return dx.to(torch.bfloat16)
+    if seg is not None:
+        dx = torch.zeros_like(x)  # rows of no sample keep a zero gradient
+        ext().rms_mod_bwd(dh, x, rstd, w, scale, dres, dx, dw_acc, dshift, dscale, 1, seg.cu, seg.max_rows)
+        return dx
     dx = torch.empty_like(x)
-    ext().rms_mod_bwd(dh, x, rstd, w, scale, dres, dx, dw_acc, dshift, dscale, rows_per_group)
+    ext().rms_mod_bwd(dh, x, rstd, w, scale, dres, dx, dw_acc, dshift, dscale, rows_per_group, None, 0)
     return dx
 
 

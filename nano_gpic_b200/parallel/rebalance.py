@@ -91,3 +91,41 @@ class Rebalancer:
         Tn = min(Tn, Tmax)
         new_mask = (torch.arange(Tn)[None, :] < new_lens[:, None]).to(mask.device)
         return img_out, cap_out[:, :Tn].contiguous(), new_mask
+
+
+PACK_BUCKET = 128
+
+
+def pack_captions(captions, mask, lens=None, bucket=PACK_BUCKET):
+    """Packed captions in the reference's y_pack format (baselines/PixelGen/src/utils/rebalance.py:39-44 and
+    JiT_T2I.py:54-65): the real caption tokens of the batch back to back, their count rounded up to a multiple of
+    `bucket` with zero dummy rows (so the caption GEMMs see few distinct row counts).
+
+    captions [B, T, D], mask [B, T] bool left-aligned; lens: the host list of caption lengths when the caller has it
+    (else one read of the mask). Returns (y [S, D], y_pack) with y_pack = {lens [B] int32, cu [B + 1] int32, pidx [S]
+    int64 (b * T + pos; B * T for a dummy row), kmask [B, T] bool, onehot [S, B] bool, real [S] bool, pos [S] int64,
+    max_T}, all on the captions' device."""
+    B, T, D = captions.shape
+    dev = captions.device
+    if lens is None:
+        lens = [int(v) for v in mask.sum(1).tolist()]
+    s_real = sum(lens)
+    S = max(bucket, -(-s_real // bucket) * bucket)
+    rows = torch.cat([torch.arange(n, dtype=torch.int64) + b * T for b, n in enumerate(lens)] +
+                     [torch.full((S - s_real,), B * T, dtype=torch.int64)])
+    owner = torch.cat([torch.full((n,), b, dtype=torch.int64) for b, n in enumerate(lens)] +
+                      [torch.full((S - s_real,), -1, dtype=torch.int64)])
+    real = torch.arange(S) < s_real
+    pos = torch.where(real, rows % T, torch.zeros_like(rows))
+    onehot = torch.zeros(S, B, dtype=torch.bool)
+    onehot[torch.arange(s_real), owner[:s_real]] = True
+    lens_t = torch.tensor(lens, dtype=torch.int32)
+    cu = torch.zeros(B + 1, dtype=torch.int32)
+    cu[1:] = torch.cumsum(lens_t, 0)
+    flat = captions.reshape(B * T, D)
+    y = torch.zeros(S, D, dtype=captions.dtype, device=dev)
+    y[:s_real] = flat.index_select(0, rows[:s_real].to(dev))
+    y_pack = {"lens": lens_t.to(dev), "cu": cu.to(dev), "pidx": rows.to(dev),
+              "kmask": (torch.arange(T)[None] < lens_t[:, None]).to(dev), "onehot": onehot.to(dev),
+              "real": real.to(dev), "pos": pos.to(dev), "max_T": T}
+    return y, y_pack

@@ -43,8 +43,12 @@ def _nvtx_pop():
 
 
 class Trainer:
-    def __init__(self, model, optimizer, scheduler=None, objective=None, accum=1, clip=1.0, flat=None, dp=None):
+    def __init__(self, model, optimizer, scheduler=None, objective=None, accum=1, clip=1.0, flat=None, dp=None,
+                 pack=None):
         self.model = model
+        # packed captions (the reference's lever E, GPIC_MFU_PACK=1; off by default there too): every micro-batch's
+        # caption tokens back to back, so the text blocks skip the padding
+        self.pack = (os.environ.get("GPIC_MFU_PACK") == "1") if pack is None else bool(pack)
         self.opt = optimizer
         self.sched = scheduler
         self.obj = objective or JiTTrainer()
@@ -147,6 +151,9 @@ class Trainer:
             self.flat.zero_grad()
         n = len(micros)
         losses = []
+        # caption lengths on the host for packing, read from the loader's host masks before the copies
+        host_lens = [(mc[2].sum(1).tolist() if mc[2] is not None and mc[2].device.type == "cpu" else None)
+                     for mc in micros] if self.pack else [None] * n
         staged = self._stage(micros[0], dev)
         for i in range(n):
             (x, y, m, ti, ni), ready = staged
@@ -160,10 +167,18 @@ class Trainer:
             if self.encode is not None:
                 x = self.encode(x)
             y = y.to(torch.bfloat16)
+            y_pack = None
+            if self.pack:
+                from ..parallel.rebalance import pack_captions
+                if m is None:
+                    m = torch.ones(y.shape[:2], dtype=torch.bool, device=y.device)
+                y, y_pack = pack_captions(y, m, host_lens[i])
+                m = None
             # mean over this rank's images and over ranks (the collectives sum)
             _nvtx_push(f"micro {i} fwd+bwd")
             per = self.obj.train_step(self.model, x, y, m, t=ti, noise=ni,
-                                      grad_scale=1.0 / (x.numel() * n * self.world))
+                                      grad_scale=1.0 / (x.numel() * n * self.world),
+                                      **({"y_pack": y_pack} if y_pack is not None else {}))
             _nvtx_pop()
             losses.append(per)
         _nvtx_push("optimizer")

@@ -63,7 +63,8 @@ def test_noalloc_matches_allocating_entry_point_twice():
         dx_ref = torch.empty_like(x)
         dw_ref = torch.full((C,), 0.25, device="cuda")
         dmod_ref = torch.zeros(G, 6 * C, device="cuda")
-        ext().rms_mod_bwd(dh, x, rstd, w, scale, dres, dx_ref, dw_ref, dmod_ref[:, :C], dmod_ref[:, C:2 * C], rpg)
+        ext().rms_mod_bwd(dh, x, rstd, w, scale, dres, dx_ref, dw_ref, dmod_ref[:, :C], dmod_ref[:, C:2 * C], rpg,
+                          None, 0)
         # the no-allocation entry point, same inputs, outputs pre-filled with garbage where they are overwritten
         dx = torch.full_like(x, 7.0)
         dw = torch.full((C,), 0.25, device="cuda")
@@ -94,7 +95,7 @@ def test_noalloc_plain_rmsnorm_and_optional_outputs():
         M, C = 1000 + 37 * rep, 512
         dh, x, _, w, _, rstd = _case(M, C, M, 10 + rep)
         dx_ref, dw_ref = torch.empty_like(x), torch.zeros(C, device="cuda")
-        ext().rms_mod_bwd(dh, x, rstd, w, None, None, dx_ref, dw_ref, None, None, 1)
+        ext().rms_mod_bwd(dh, x, rstd, w, None, None, dx_ref, dw_ref, None, None, 1, None, 0)
         dx, dw = torch.full_like(x, 5.0), torch.zeros(C, device="cuda")
         rc = f(_ptr(dh), _ptr(x), _ptr(rstd), _ptr(w), None, 0, None, _ptr(dx), _ptr(dw), None, 0, None, 0, M, C, 0,
                stream.cuda_stream)
@@ -107,7 +108,8 @@ def test_noalloc_plain_rmsnorm_and_optional_outputs():
         G = M // rpg
         scale = mod[:, C:2 * C]
         dx_ref, dmod_ref = torch.empty_like(x), torch.zeros(G, 6 * C, device="cuda")
-        ext().rms_mod_bwd(dh, x, rstd, w, scale, dres, dx_ref, None, dmod_ref[:, :C], dmod_ref[:, C:2 * C], rpg)
+        ext().rms_mod_bwd(dh, x, rstd, w, scale, dres, dx_ref, None, dmod_ref[:, :C], dmod_ref[:, C:2 * C], rpg,
+                          None, 0)
         dx, dmod = torch.full_like(x, 5.0), torch.full((G, 6 * C), 9.0, device="cuda")
         rc = f(_ptr(dh), _ptr(x), _ptr(rstd), _ptr(w), _ptr(scale), scale.stride(0), _ptr(dres), _ptr(dx), None,
                _ptr(dmod[:, :C]), dmod.stride(0), _ptr(dmod[:, C:2 * C]), dmod.stride(0), M, C, rpg,
