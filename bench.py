@@ -363,8 +363,9 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--recompute", default="none", choices=["none", "image", "all"],
                     help="activation checkpointing of the image (and text) blocks")
-    ap.add_argument("--fp8", default="none", choices=["none", "mx"],
-                    help="mx: the image blocks' forward GEMMs in MXFP8 (the d12-FP8 config); default bf16")
+    ap.add_argument("--fp8", default="none", choices=["none", "mx", "mx2"],
+                    help="mx: the image blocks' forward GEMMs in MXFP8 (the d12-FP8 config); mx2: also the MLP dgrads "
+                         "(the reference's phase 2); default bf16")
     ap.add_argument("--transport", default="nccl", choices=["nccl", "p2p"],
                     help="zero mode: NCCL collectives or this framework's peer-memory kernels")
     ap.add_argument("--dp", default="zero", choices=["ddp", "zero"],
@@ -407,7 +408,9 @@ def main():
                "higher_is_better": True, "scaling": "strong",
                "vs_baseline": round(value / PUBLISHED[a.size], 4) if a.size in PUBLISHED else None,
                "dtype": "bf16" if a.fp8 == "none" or a.impl == "reference" else
-                        "bf16 + MXFP8 forward GEMMs (image-block qkv_x/proj/w12/w3)", "data": "synthetic (uint8 images uniform, N(0,1) caption features, random-length "
+                        ("bf16 + MXFP8 forward GEMMs (image-block qkv_x/proj/w12/w3)" if a.fp8 == "mx" else
+                         "bf16 + MXFP8 forward GEMMs (image-block qkv_x/proj/w12/w3) + MXFP8 MLP dgrads (w3, w12)"),
+               "data": "synthetic (uint8 images uniform, N(0,1) caption features, random-length "
                                          "masks; random-init weights)",
                "mfu": round(mfu, 4), "mfu_peak": f"{pk / 1e12:.1f} TFLOP/s bf16 ({pk_src})",
                "model_tflops_per_gpu": round(value * flops_img / world / 1e12, 1),

@@ -63,7 +63,8 @@ void gemm_mx_torch(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor&
                    const at::Tensor& out, int64_t epi, int64_t N, const c10::optional<at::Tensor>& out2,
                    const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& res,
                    const c10::optional<at::Tensor>& gate, int64_t rows_per_group, int64_t half_n,
-                   const c10::optional<at::Tensor>& act_q, const c10::optional<at::Tensor>& act_sf);
+                   const c10::optional<at::Tensor>& act_q, const c10::optional<at::Tensor>& act_sf,
+                   const c10::optional<at::Tensor>& aux);
 at::Tensor p2p_alloc(int64_t nbytes, int64_t device);
 at::Tensor p2p_export(const at::Tensor& t);
 int64_t p2p_import(const at::Tensor& handle, int64_t device);

@@ -58,7 +58,7 @@ struct EpiCfg {
   static constexpr int STAGE_BYTES = PAIR ? gemm_cfg::A_BYTES + gemm_cfg::B_BYTES / 2 : gemm_cfg::STAGE_BYTES;
   // SwiGLU backward reads two input tiles per chunk: with pairs it keeps two chunks of inputs in flight (one stage
   // fewer in the mainloop ring)
-  static constexpr int STAGES = MX ? (PAIR ? (EPI == EPI_GATED ? 4 : 5) : 3)
+  static constexpr int STAGES = MX ? (PAIR ? ((EPI == EPI_GATED || EPI == EPI_SWIGLU_BWD) ? 4 : 5) : 3)
                                    : PAIR ? (EPI == EPI_SWIGLU_BWD ? 4 : (HEAVY ? 5 : 6)) : (HEAVY ? 3 : 4);
   static constexpr int SF_BYTES = MX ? STAGES * gemm_cfg::MX_SF_STAGE : 0;
   // one output slot holds every 32x32 output tile of a chunk (bf16 2 KiB, fp32 4 KiB)
@@ -67,7 +67,8 @@ struct EpiCfg {
                                                                                                   : 2048;
   static constexpr int OUT_SLOTS = (EPI == EPI_BF16) ? 2 : 1;
   static constexpr int IN_SLOT = EPI == EPI_SWIGLU_BWD ? 4096 : (EPI == EPI_GATED || EPI == EPI_AXPBY) ? 2048 : 0;
-  static constexpr int IN_RING = IN_SLOT == 0 ? 0 : ((EPI == EPI_GATED || (PAIR && EPI == EPI_SWIGLU_BWD)) ? 2 : 1);
+  static constexpr int IN_RING =
+      IN_SLOT == 0 ? 0 : ((EPI == EPI_GATED || (PAIR && !MX && EPI == EPI_SWIGLU_BWD)) ? 2 : 1);
   static constexpr int WARP_BYTES = (OUT_SLOTS * OUT_SLOT + IN_RING * IN_SLOT + 1023) / 1024 * 1024;
   static constexpr int EPI_BYTES = 8 * WARP_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_BYTES + SF_BYTES + 1024 /*align slack*/ + 512 /*barriers*/;
@@ -702,6 +703,38 @@ __global__ void __launch_bounds__(gemm_cfg::THREADS, 1)
             }
             st_tile_bf16(obuf, lane, v);
             st_tile_bf16(obuf + 2048, lane, d2);
+            if constexpr (MX) {
+              // the MXFP8 copy of d(pre) = [d1 | d2] for the next MX dgrad (w12's): this lane's 32 columns of d1 and
+              // of d2 are one scale block each, quantized from the bf16 values the tiles hold
+              if (p.act_q != nullptr && row < p.M) {
+                const int kb = 2 * p.half_n / 128;
+#pragma unroll
+                for (int half = 0; half < 2; ++half) {
+                  float* h = half == 0 ? v : d2;
+                  float am = 0.f;
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) {
+                    h[j] = round_bf16(h[j]);
+                    am = fmaxf(am, fabsf(h[j]));
+                  }
+                  const int e = mx_scale_exp(am);
+                  const float inv = ldexpf(1.f, -e);
+                  const int c = half * p.half_n + col;
+                  uint4* dq = reinterpret_cast<uint4*>(p.act_q + (int64_t)row * 2 * p.half_n + c);
+#pragma unroll
+                  for (int j = 0; j < 2; ++j) {
+                    uint4 o;
+                    o.x = e4m3x4(h[16 * j] * inv, h[16 * j + 1] * inv, h[16 * j + 2] * inv, h[16 * j + 3] * inv);
+                    o.y = e4m3x4(h[16 * j + 4] * inv, h[16 * j + 5] * inv, h[16 * j + 6] * inv, h[16 * j + 7] * inv);
+                    o.z = e4m3x4(h[16 * j + 8] * inv, h[16 * j + 9] * inv, h[16 * j + 10] * inv, h[16 * j + 11] * inv);
+                    o.w = e4m3x4(h[16 * j + 12] * inv, h[16 * j + 13] * inv, h[16 * j + 14] * inv,
+                                 h[16 * j + 15] * inv);
+                    dq[j] = o;
+                  }
+                  p.act_sf[mx_sf_offset(row, c / 32, kb)] = (uint8_t)(e + 127);
+                }
+              }
+            }
           }
           fence_proxy_async_smem();
         }
@@ -968,7 +1001,10 @@ void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     // e4m3 operands, K-major, boxes of 128 bytes x 128 rows (the bf16 tile's bytes)
     TORCH_CHECK(!g.a_mn && !g.b_mn && g.batch == 1 && g.k_splits <= 1 && g.K % MX_BK == 0,
                 "MXFP8 GEMM: K-major A and B, one batch, K a multiple of 128");
-    TORCH_CHECK(g.epi == EPI_BF16 || g.epi == EPI_GATED || g.epi == EPI_SWIGLU, "MXFP8 GEMM: unsupported epilogue");
+    TORCH_CHECK(g.epi == EPI_BF16 || g.epi == EPI_GATED || g.epi == EPI_SWIGLU || g.epi == EPI_SWIGLU_BWD,
+                "MXFP8 GEMM: unsupported epilogue");
+    TORCH_CHECK(g.epi != EPI_SWIGLU_BWD || (g.half_n == g.N && g.N % 128 == 0 && g.aux != nullptr),
+                "MXFP8 SwiGLU backward: N = half width, a multiple of 128, and the saved pre-activation");
     TORCH_CHECK(g.sfa != nullptr && g.sfb != nullptr && (reinterpret_cast<uintptr_t>(g.sfa) & 15) == 0 &&
                     (reinterpret_cast<uintptr_t>(g.sfb) & 15) == 0,
                 "MXFP8 GEMM: 16-byte aligned scale factors expected");
@@ -1048,12 +1084,14 @@ void gemm_launch(const GemmArgs& g, cudaStream_t stream) {
     switch (g.epi) {
       case EPI_BF16: launch_t<0, 0, EPI_BF16, true, true>(ta, tb, em, p, tiles, stream); break;
       case EPI_GATED: launch_t<0, 0, EPI_GATED, true, true>(ta, tb, em, p, tiles, stream); break;
+      case EPI_SWIGLU_BWD: launch_t<0, 0, EPI_SWIGLU_BWD, true, true>(ta, tb, em, p, tiles, stream); break;
       default: launch_t<0, 0, EPI_SWIGLU, true, true>(ta, tb, em, p, tiles, stream); break;
     }
   } else if (g.mx) {
     switch (g.epi) {
       case EPI_BF16: launch_t<0, 0, EPI_BF16, false, true>(ta, tb, em, p, tiles, stream); break;
       case EPI_GATED: launch_t<0, 0, EPI_GATED, false, true>(ta, tb, em, p, tiles, stream); break;
+      case EPI_SWIGLU_BWD: launch_t<0, 0, EPI_SWIGLU_BWD, false, true>(ta, tb, em, p, tiles, stream); break;
       default: launch_t<0, 0, EPI_SWIGLU, false, true>(ta, tb, em, p, tiles, stream); break;
     }
   } else if (pair)
@@ -1155,14 +1193,25 @@ void gemm_torch(const at::Tensor& A, bool a_mn, int64_t lda, int64_t a_bs, const
   g.accumulate = accumulate ? 1 : 0;
   g.err = status_word();
   auto stream = at::cuda::getCurrentCUDAStream();
-  // Weight gradients with few output tiles (e.g. a 1024 x 1024 dW is 32 tiles for 148 SMs) but a long reduction
-  // (all tokens): split K over CTAs, each split writes an fp32 slice, then one ordered reduction adds the slices.
-  // (counted in CTAs: a CTA pair's 256-row tile occupies two)
-  const int64_t tiles = gemm_use_pair(M) ? 2 * ((M + 255) / 256) * ((N + 255) / 256)
-                                         : ((M + 127) / 128) * ((N + 255) / 256);
+  // Weight gradients have few output tiles (a 3072 x 1024 dW is 48 CTA-pair tiles for 74 pair slots: one wave at
+  // 65 %) but a long reduction (all tokens): split K, each split writes an fp32 slice, then one ordered reduction adds
+  // the slices (deterministic). The split count minimises a wave model: waves(tiles x s) x k-blocks per split, plus
+  // the reduction's traffic ((s + 2) slices of M x N fp32) in the same time unit.
+  const bool pair_t = gemm_use_pair(M);
+  const int64_t tiles = pair_t ? ((M + 255) / 256) * ((N + 255) / 256) : ((M + 127) / 128) * ((N + 255) / 256);
+  const int64_t slots = pair_t ? num_sms() / 2 : num_sms();
   const int64_t nkb = (K + 63) / 64;
-  if (epi == EPI_F32 && batch == 1 && tiles * 2 <= num_sms() && nkb >= 16 && ldo == N) {
-    int splits = (int)std::min<int64_t>(num_sms() / tiles, nkb / 8);
+  if (epi == EPI_F32 && batch == 1 && nkb >= 16 && ldo == N) {
+    // one k-block of one tile ~ 0.35 us; the reduction streams (s + 2) M N 4 bytes at ~6 TB/s
+    auto cost = [&](int64_t sp) {
+      const int64_t kps_ = (nkb + sp - 1) / sp;
+      const double waves = (double)((tiles * sp + slots - 1) / slots);
+      const double red = sp > 1 ? (double)(sp + 2) * M * N * 4 / 6.0e6 / 0.35 : 0.0;
+      return waves * (double)kps_ + red;
+    };
+    int splits = 1;
+    for (int64_t sp = 2; sp <= std::min<int64_t>(16, nkb / 8); ++sp)
+      if (cost(sp) < 0.93 * cost(splits)) splits = (int)sp;
     const int kps = (int)((nkb + splits - 1) / splits);
     splits = (int)((nkb + kps - 1) / kps);
     if (splits > 1) {

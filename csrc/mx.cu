@@ -106,12 +106,15 @@ static const void* opt_ptr(const c10::optional<at::Tensor>& t) {
 // out = epilogue(A_q B_q^T) with A_q [M, K], B_q [b_rows, K] e4m3 and their scale blocks (mx_quant's layout).
 // epi: EPI_BF16 (out = acc + bias), EPI_GATED (out2 = y = acc + bias; out = res + gate[row / rpg] * y), EPI_SWIGLU
 // (B rows [0, half_n) gate half, [half_n, 2 half_n) up half; out2 = pre, out = silu(x1) * x2; with act_q / act_sf
-// given, act is also written in MXFP8, byte-identical to mx_quant(out)).
+// given, act is also written in MXFP8, byte-identical to mx_quant(out)), EPI_SWIGLU_BWD (acc = d(act) [M, half_n],
+// aux = the saved pre-activation [M, 2 half_n]; out = d(pre) [M, 2 half_n]; with act_q / act_sf given, d(pre) is also
+// written in MXFP8 for the next dgrad).
 void gemm_mx_torch(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor& B, const at::Tensor& sfb,
                    const at::Tensor& out, int64_t epi, int64_t N, const c10::optional<at::Tensor>& out2,
                    const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& res,
                    const c10::optional<at::Tensor>& gate, int64_t rows_per_group, int64_t half_n,
-                   const c10::optional<at::Tensor>& act_q, const c10::optional<at::Tensor>& act_sf) {
+                   const c10::optional<at::Tensor>& act_q, const c10::optional<at::Tensor>& act_sf,
+                   const c10::optional<at::Tensor>& aux) {
   TORCH_CHECK(A.is_cuda() && B.is_cuda() && out.is_cuda(), "gemm_mx: CUDA tensors expected");
   TORCH_CHECK(A.scalar_type() == at::kByte && B.scalar_type() == at::kByte && sfa.scalar_type() == at::kByte &&
                   sfb.scalar_type() == at::kByte,
@@ -156,13 +159,22 @@ void gemm_mx_torch(const at::Tensor& A, const at::Tensor& sfa, const at::Tensor&
   }
   g.rows_per_group = (int)rows_per_group;
   g.half_n = (int)half_n;
+  if (aux.has_value() && aux->defined()) {
+    TORCH_CHECK(epi == EPI_SWIGLU_BWD && aux->scalar_type() == at::kBFloat16 && aux->stride(1) == 1 &&
+                    aux->size(0) == M && aux->size(1) == 2 * half_n,
+                "gemm_mx: aux is the [M, 2 half_n] bf16 pre-activation of the SwiGLU backward");
+    g.aux = static_cast<const __nv_bfloat16*>(aux->data_ptr());
+    g.ld_aux = aux->stride(0);
+  }
   if (act_q.has_value() && act_q->defined()) {
-    TORCH_CHECK(epi == EPI_SWIGLU && half_n % 128 == 0, "gemm_mx: the MXFP8 act output is for the SwiGLU epilogue");
+    TORCH_CHECK((epi == EPI_SWIGLU || epi == EPI_SWIGLU_BWD) && half_n % 128 == 0,
+                "gemm_mx: the MXFP8 copy of the output is for the SwiGLU epilogues");
+    const int64_t qcols = epi == EPI_SWIGLU ? half_n : 2 * half_n;
     TORCH_CHECK(act_sf.has_value() && act_sf->defined(), "gemm_mx: act scale blocks missing");
-    TORCH_CHECK(act_q->scalar_type() == at::kByte && act_q->is_contiguous() && act_q->numel() == M * half_n,
-                "gemm_mx: act_q must be [M, half_n] uint8");
+    TORCH_CHECK(act_q->scalar_type() == at::kByte && act_q->is_contiguous() && act_q->numel() == M * qcols,
+                "gemm_mx: act_q must be [M, half_n] (SwiGLU) or [M, 2 half_n] (SwiGLU backward) uint8");
     TORCH_CHECK(act_sf->scalar_type() == at::kByte && act_sf->is_contiguous() &&
-                    act_sf->numel() >= mx_rows_pad(M) * (half_n / 32),
+                    act_sf->numel() >= mx_rows_pad(M) * (qcols / 32),
                 "gemm_mx: act scale blocks too small");
     g.act_q = act_q->data_ptr();
     g.act_sf = act_sf->data_ptr();

@@ -62,14 +62,19 @@ def _wgrad(dy, x, p):
 
 
 def _mx_weights(blk):
-    """MXFP8 copies of an image block's forward GEMM weights (qkv_x, proj, w12, w3), made from the bf16 compute weights
-    once per weight version (JiT_T2I.weights_changed() after every optimizer step or load)."""
+    """MXFP8 copies of an image block's forward GEMM weights (qkv_x, proj, w12, w3) and, with the MLP backward in FP8
+    (fp8 "mx2"), of the transposed MLP weights its dgrads read (w3t [H, C], w12t [C, 2H]); made from the bf16 compute
+    weights once per weight version (JiT_T2I.weights_changed() after every optimizer step or load)."""
     ver = getattr(blk, "_wver", 0)
     c = getattr(blk, "_mxw", None)
     if c is None or c[0] != ver:
         a = blk.attn
-        c = (ver, {"qkv_x": MXO.quant(w16(a.qkv_x)), "proj": MXO.quant(w16(a.proj)),
-                   "w12": MXO.quant(w16(blk.mlp.w12)), "w3": MXO.quant(w16(blk.mlp.w3))})
+        d = {"qkv_x": MXO.quant(w16(a.qkv_x)), "proj": MXO.quant(w16(a.proj)),
+             "w12": MXO.quant(w16(blk.mlp.w12)), "w3": MXO.quant(w16(blk.mlp.w3))}
+        if getattr(blk, "_fp8_bwd", False):
+            d["w3t"] = MXO.quant(w16(blk.mlp.w3).t().contiguous())
+            d["w12t"] = MXO.quant(w16(blk.mlp.w12).t().contiguous())
+        c = (ver, d)
         blk._mxw = c
     return c[1]
 
@@ -383,9 +388,17 @@ class _ImageBlockFn(torch.autograd.Function):
         dx3 = dx3.contiguous()
         dmod = torch.empty(mod.shape, device=mod.device, dtype=torch.float32)
         dym = E.gate_bwd(dx3, ym, mod[:, 5 * C:6 * C], L, dgate=dmod[:, 5 * C:6 * C])
-        dpre = G.swiglu_dgrad(dym, w16(blk.mlp.w3), pre)
+        if getattr(blk, "_fp8_bwd", False):
+            # the MLP's dgrads in MXFP8 (the reference's phase 2, fp8_native.py:236-266): dy's MX copy, the w3 dgrad
+            # with the SwiGLU backward in its epilogue writing d(pre) in bf16 (w12's weight gradient) and in MXFP8
+            # (w12's dgrad); weight gradients stay bf16
+            mxw = _mx_weights(blk)
+            dpre, dpreq = MXO.swiglu_dgrad(MXO.quant(dym), mxw["w3t"], pre, quant_out=True)
+            dh2 = MXO.linear(dpreq, mxw["w12t"])
+        else:
+            dpre = G.swiglu_dgrad(dym, w16(blk.mlp.w3), pre)
+            dh2 = G.linear_dgrad(dpre, w16(blk.mlp.w12))
         _wgrad(dym, act, blk.mlp.w3.weight)
-        dh2 = G.linear_dgrad(dpre, w16(blk.mlp.w12))
         _wgrad(dpre, h2, blk.mlp.w12.weight)
         dx2 = NR.rms_mod_bwd(dh2, x2, r2, f32(blk.norm2.weight), mod[:, 4 * C:5 * C], L, dres=dx3,
                              dw_acc=grad_of(blk.norm2.weight), dshift=dmod[:, 3 * C:4 * C],
@@ -598,7 +611,8 @@ class JiT_T2I(nn.Module):
         self._rope = {}
         self._bwd_hook = None  # set by the data-parallel layer around the last micro-batch's backward
         if fp8 is None and os.environ.get("GPIC_MFU_FP8", "") not in ("", "0", "off"):
-            fp8 = "mx"  # the reference's switch (GPIC_MFU_FP8=native) selects this package's MXFP8 GEMMs
+            # the reference's switch (GPIC_MFU_FP8=native / native2) selects this package's MXFP8 GEMMs
+            fp8 = "mx2" if os.environ["GPIC_MFU_FP8"] == "native2" else "mx"
         self.set_fp8(fp8)
         self.set_recompute(recompute)
 
@@ -616,11 +630,15 @@ class JiT_T2I(nn.Module):
 
     # ------------------------------------------------------------------------------------------------- fp8
     def set_fp8(self, mode):
-        """None: bf16 GEMMs everywhere. "mx": the image blocks' qkv_x / proj / w12 / w3 forward GEMMs in MXFP8."""
-        assert mode in (None, "mx"), f"fp8 mode {mode!r}: None or 'mx'"
+        """None: bf16 GEMMs everywhere. "mx": the image blocks' qkv_x / proj / w12 / w3 forward GEMMs in MXFP8 (the
+        reference's GPIC_MFU_FP8=native, phase 1). "mx2": also the MLP's two dgrads (w3, w12) in MXFP8 (native2, its
+        phase 2)."""
+        assert mode in (None, "mx", "mx2"), f"fp8 mode {mode!r}: None, 'mx' or 'mx2'"
         self.fp8 = mode
         for blk in self.blocks:
-            blk._fp8 = mode == "mx"
+            blk._fp8 = mode in ("mx", "mx2")
+            blk._fp8_bwd = mode == "mx2"
+            blk._mxw = None
         self.weights_changed()
 
     def weights_changed(self):

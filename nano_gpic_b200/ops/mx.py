@@ -79,7 +79,7 @@ def linear(xq, wq, bias=None):
         return G.linear(xq.dequant(), wq.dequant(), bias)
     M, N = xq.shape[0], wq.shape[0]
     out = torch.empty(M, N, device=xq.q.device, dtype=torch.bfloat16)
-    ext().gemm_mx(xq.q, xq.sf, wq.q, wq.sf, out, G.EPI_BF16, N, None, bias, None, None, 1, 0, None, None)
+    ext().gemm_mx(xq.q, xq.sf, wq.q, wq.sf, out, G.EPI_BF16, N, None, bias, None, None, 1, 0, None, None, None)
     return out
 
 
@@ -90,7 +90,8 @@ def linear_gated_residual(xq, wq, bias, res, gate, rows_per_group):
     M, N = xq.shape[0], wq.shape[0]
     out = torch.empty(M, N, device=xq.q.device, dtype=torch.bfloat16)
     y = torch.empty(M, N, device=xq.q.device, dtype=torch.bfloat16)
-    ext().gemm_mx(xq.q, xq.sf, wq.q, wq.sf, out, G.EPI_GATED, N, y, bias, res, gate, rows_per_group, 0, None, None)
+    ext().gemm_mx(xq.q, xq.sf, wq.q, wq.sf, out, G.EPI_GATED, N, y, bias, res, gate, rows_per_group, 0, None, None,
+                  None)
     return out, y
 
 
@@ -116,5 +117,22 @@ def swiglu_linear(xq, w12q, quant_act=False):
     pre = torch.empty(M, H2, device=xq.q.device, dtype=torch.bfloat16)
     aq = empty_like_rows(M, H, xq.q.device) if quant_act else None
     ext().gemm_mx(xq.q, xq.sf, w12q.q, w12q.sf, act, G.EPI_SWIGLU, H2, pre, None, None, None, 1, H,
-                  aq.q if aq is not None else None, aq.sf if aq is not None else None)
+                  aq.q if aq is not None else None, aq.sf if aq is not None else None, None)
     return (act, pre, aq) if quant_act else (act, pre)
+
+
+def swiglu_dgrad(dyq, w3tq, pre, quant_out=False):
+    """Backward of act = silu(pre[:, :H]) * pre[:, H:] through y = act W3^T, in MXFP8 (the reference's phase-2 FP8
+    MLP backward, fp8_native.py:236-266): d(act) = dy W3 from dy's MX copy and W3^T's ([H, C]), and the SwiGLU
+    backward in the GEMM's epilogue. Returns d(pre) [M, 2H] bf16, or with quant_out (dpre, dpre's MX copy written by
+    the same epilogue, equal to quant(dpre))."""
+    if not dyq.q.is_cuda:
+        dpre = G.swiglu_dgrad(dyq.dequant().to(torch.bfloat16), w3tq.dequant().t().contiguous().to(torch.bfloat16),
+                              pre)
+        return (dpre, quant(dpre)) if quant_out else dpre
+    M, H = dyq.shape[0], w3tq.shape[0]
+    dpre = torch.empty(M, 2 * H, device=dyq.q.device, dtype=torch.bfloat16)
+    dq = empty_like_rows(M, 2 * H, dyq.q.device) if quant_out else None
+    ext().gemm_mx(dyq.q, dyq.sf, w3tq.q, w3tq.sf, dpre, G.EPI_SWIGLU_BWD, H, None, None, None, None, 1, H,
+                  dq.q if dq is not None else None, dq.sf if dq is not None else None, pre)
+    return (dpre, dq) if quant_out else dpre

@@ -97,7 +97,7 @@ def main(argv=None):
     ap.add_argument("--micro-batch", type=int, default=128)
     ap.add_argument("--caption-len", type=int, default=128)
     ap.add_argument("--heldout", type=int, default=64, help="held-out images")
-    ap.add_argument("--fp8", default="none", choices=["none", "mx"], help="our arm's GEMM precision")
+    ap.add_argument("--fp8", default="none", choices=["none", "mx", "mx2"], help="our arm's GEMM precision")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--lr-warmup", type=int, default=None,
                     help="warmup steps of both schedules (default: the ladder's, 1%% of the full run)")

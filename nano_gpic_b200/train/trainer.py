@@ -73,7 +73,7 @@ class Trainer:
                    transport="nccl", fp8=None, recompute=None):
         """dp: "ddp" (all-reduce, as the reference's DDP sizes) or "zero" (reduce-scatter to owners, sharded
         optimizer state; the role of the reference's FSDP2 sizes). transport (zero mode): "nccl" or "p2p" (this
-        package's peer-memory kernels). fp8: None (bf16) or "mx" (MXFP8 forward GEMMs in the image blocks). recompute:
+        package's peer-memory kernels). fp8: None (bf16), "mx" (MXFP8 forward GEMMs in the image blocks) or "mx2" (also the MLP dgrads). recompute:
         None, "image" or "all" (activation checkpointing of those blocks)."""
         s = SIZES[size]
         torch.manual_seed(seed)

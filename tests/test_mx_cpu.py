@@ -49,11 +49,15 @@ def test_model_fp8_cpu_runs_and_is_close():
         for prm in net.parameters():
             prm.add_(torch.randn_like(prm) * 0.02)
     outs = []
-    for mode in (None, "mx"):
+    grads = []
+    for mode in (None, "mx", "mx2"):
         net.set_fp8(mode)
         net.zero_grad(set_to_none=True)
         o = net(x, t, y, y_mask=m)
         o.float().square().mean().backward()
         outs.append(o.float().detach())
+        grads.append(net.blocks[0].mlp.w12.weight.grad.clone())
     assert net.blocks[0].mlp.w3.weight.grad is not None
     assert (outs[1] - outs[0]).norm() / outs[0].norm() < 0.05
+    assert torch.equal(outs[2], outs[1])  # mx2 changes the backward only
+    assert (grads[2] - grads[0]).norm() / grads[0].norm() < 0.1

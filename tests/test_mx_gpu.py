@@ -148,3 +148,48 @@ def test_mx_swiglu_act_output_equals_separate_quant(M, H, K):
     ref = mx.quant(act)
     assert torch.equal(aq.q, ref.q)
     assert torch.equal(aq.sf, ref.sf)
+
+
+@pytest.mark.parametrize("M,H,C", [(4096, 4096, 1024), (300, 384, 256)])
+def test_mx_swiglu_dgrad(M, H, C):
+    """The MLP backward in MXFP8 (fp8 "mx2"): d(pre) from dy's and W3^T's MX copies with the SwiGLU backward in the
+    epilogue, against the bf16 formula on the dequantized operands; its MX copy equals quantizing d(pre) separately."""
+    from nano_gpic_b200.ops import gemm as G
+    from nano_gpic_b200.ops import mx
+    dyq = mx.quant(_input(M, C, 5))
+    w3 = (torch.randn(C, H, device="cuda") * 0.05).to(torch.bfloat16)
+    w3tq = mx.quant(w3.t().contiguous())
+    pre = (torch.randn(M, 2 * H, device="cuda") * 2).to(torch.bfloat16)
+    dpre, dq = mx.swiglu_dgrad(dyq, w3tq, pre, quant_out=True)
+    ref = G.swiglu_dgrad(dyq.dequant().to(torch.bfloat16).cpu(), w3tq.dequant().t().contiguous().to(torch.bfloat16).cpu(),
+                         pre.cpu())
+    _close(dpre.cpu(), ref, rtol=2e-2, atol=1e-3)
+    assert torch.equal(mx.swiglu_dgrad(dyq, w3tq, pre), dpre)
+    sep = mx.quant(dpre)
+    assert torch.equal(dq.q, sep.q) and torch.equal(dq.sf, sep.sf)
+
+
+def test_model_fp8_backward_close_to_bf16():
+    """fp8 "mx2" (the MLP dgrads in MXFP8 too): loss-gradient direction stays close to bf16."""
+    from nano_gpic_b200.models.jit_t2i import JiT_T2I
+    torch.manual_seed(0)
+    net = JiT_T2I(input_size=64, in_channels=3, num_groups=4, hidden_size=256, num_blocks=2, num_text_blocks=1,
+                  patch_size=16, txt_embed_dim=2048, txt_max_length=32).cuda()
+    B = 4
+    x = torch.randn(B, 3, 64, 64, device="cuda")
+    t = torch.rand(B, device="cuda")
+    y = torch.randn(B, 32, 2048, device="cuda").to(torch.bfloat16)
+    m = torch.ones(B, 32, dtype=torch.bool, device="cuda")
+    with torch.no_grad():
+        for prm in net.parameters():
+            prm.add_(torch.randn_like(prm) * 0.02)
+    grads = []
+    for mode in (None, "mx2"):
+        net.set_fp8(mode)
+        net.zero_grad(set_to_none=True)
+        o = net(x, t, y, y_mask=m)
+        o.float().square().mean().backward()
+        grads.append({n: p.grad.clone() for n, p in net.named_parameters() if p.grad is not None})
+    for n in ("blocks.0.norm1.weight", "blocks.0.attn.qkv_x.weight", "blocks.1.mlp.w12.weight", "x_embedder.proj2.weight"):
+        rel = (grads[1][n] - grads[0][n]).norm() / grads[0][n].norm()
+        assert rel < 0.1, (n, rel)
