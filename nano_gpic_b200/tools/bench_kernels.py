@@ -2,7 +2,7 @@
 torch.matmul, SDPA, torch elementwise), timed with CUDA events after warm-up, inputs larger than L2 where the shape
 allows, reported as TFLOP/s or GB/s and as a fraction of MEASURED_PEAKS.json.
 
-    python -m nano_gpic_b200.tools.bench_kernels [--only gemm,fused,attn,mx] [--d 1024] [--batch 128] [--json out.json]
+    python -m nano_gpic_b200.tools.bench_kernels [--only gemm,fused,attn,mx,sample] [--d 1024] [--batch 128] [--json out.json]
 """
 import argparse
 import json
@@ -173,6 +173,37 @@ def bench_mx(d, batch, rows):
         print(json.dumps(row), flush=True)
 
 
+def bench_sample(d, batch, rows, steps=50, pred_batch=8):
+    """Euler sampling (the predict path) at a small batch with classifier-free guidance: the denoiser's forward run
+    eagerly and replayed from a CUDA graph (runtime/graphs.py). Reports images/s and ms per sampling step."""
+    from nano_gpic_b200.config.ladder import SIZES
+    from nano_gpic_b200.diffusion.sampling import EulerSamplerJiT
+    from nano_gpic_b200.models.jit_t2i import JiT_T2I
+    from nano_gpic_b200.runtime.graphs import GraphedCall
+    size = next((k for k, v in SIZES.items() if v.width == d), "d12")
+    s = SIZES[size]
+    torch.manual_seed(0)
+    net = JiT_T2I(input_size=256, in_channels=3, num_groups=d // 64, hidden_size=d, num_blocks=s.image_layers,
+                  num_text_blocks=s.text_layers, patch_size=16, txt_embed_dim=2048, txt_max_length=320,
+                  bottleneck_dim=128).cuda().eval()
+    B, T = pred_batch, 128
+    x = torch.randn(B, 3, 256, 256, device="cuda")
+    y = torch.randn(B, T, 2048, device="cuda").bfloat16()
+    m = torch.arange(T, device="cuda")[None] < torch.randint(16, T + 1, (B, 1), device="cuda")
+    null = torch.zeros_like(m)
+    null[:, 0] = True
+    sampler = EulerSamplerJiT(num_steps=steps, guidance=2.0)
+    row = {"kernel": "sample", "model": size, "batch": B, "steps": steps, "cfg": 2.0}
+    for name, call in (("eager", lambda a, b_, c, e: net(a, b_, c, y_mask=e)),
+                       ("graph", GraphedCall(lambda a, b_, c, e: net(a, b_, c, y_mask=e)))):
+        f = lambda a, b_, c: call(a, b_, c, torch.cat([null, m]) if c.shape[0] == 2 * B else m)
+        t = time_fn(lambda: sampler(f, x, y, torch.zeros_like(y)), iters=3, warmup=1)
+        row[name + "_img_s"] = round(B / t, 2)
+        row[name + "_ms_per_step"] = round(t / steps * 1e3, 3)
+    rows.append(row)
+    print(json.dumps(row), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="gemm")
@@ -190,6 +221,8 @@ def main():
         bench_attn(a.d, a.batch, rows)
     if "mx" in only:
         bench_mx(a.d, a.batch, rows)
+    if "sample" in only:
+        bench_sample(a.d, a.batch, rows)
     if a.json:
         with open(a.json, "w") as f:
             json.dump(rows, f, indent=1)

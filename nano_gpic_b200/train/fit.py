@@ -270,6 +270,11 @@ def predict(cfg):
     hook = SaveImagesHook(save_dir=os.environ.get("GPIC_PRED_DIR", "predict"))
     ctx = FitContext(None, None, rdir, rank, world, dev, cfg, 0, bs, None, [])
     images, metas = [], []
+    # the denoiser's forward replayed from a CUDA graph per batch shape (sampling at small batches is launch-bound);
+    # GPIC_PRED_GRAPHS=0 runs it eagerly
+    from ..runtime.graphs import GraphedCall
+    den_call = (GraphedCall(lambda x, t, yy, mm: den(x, t, yy, y_mask=mm))
+                if os.environ.get("GPIC_PRED_GRAPHS", "1") != "0" else (lambda x, t, yy, mm: den(x, t, yy, y_mask=mm)))
     for s in range(0, len(idx), bs):
         items = [ds[i] for i in idx[s:s + bs]]
         noise = torch.stack([it[0] for it in items]).to(dev)
@@ -283,7 +288,7 @@ def predict(cfg):
 
         def net(x, t, yy):
             mm = torch.cat([null_mask, mask]) if cfg_on and yy.shape[0] == 2 * mask.shape[0] else mask
-            return den(x, t, yy, y_mask=mm)
+            return den_call(x, t, yy, mm)
 
         x = sampler(net, noise, y, uncond)
         if vae is not None:
