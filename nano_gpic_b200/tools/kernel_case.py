@@ -1,7 +1,8 @@
 """Runs one kernel on one shape a few times: the target of ncu captures (small cases that end by themselves).
 
     python -m nano_gpic_b200.tools.kernel_case --case swiglu_fwd --m 8192 --d 1024 [--reps 3]
-cases: linear_fwd, linear_dgrad, linear_wgrad, swiglu_fwd, swiglu_bwd, gated, attn_fwd, attn_bwd, rms_bwd, gate_bwd
+cases: linear_fwd, linear_dgrad, linear_wgrad, swiglu_fwd, swiglu_bwd, gated, attn_fwd, attn_bwd, rms_bwd, gate_bwd,
+       qk_fwd, qk_bwd (per-head q norm + RoPE of the image rows)
 """
 import argparse
 
@@ -61,6 +62,18 @@ def main():
         fn = lambda: NR.rms_mod_bwd(dh, x, rstd, w, mod[:, d:2 * d], 256, dres=dh, dw_acc=dw,
                                     dshift=dsh[:, :d], dscale=dsh[:, d:])
         dsh = torch.empty(M // 256, 2 * d, device="cuda")
+    elif a.case in ("qk_fwd", "qk_bwd"):
+        from nano_gpic_b200.models.layers import rope_tables
+        from nano_gpic_b200.ops import qk as QK
+        L = 256
+        cos, sin = rope_tables(64, 16, 16, device="cuda")
+        qkv, dq = r(M, 3 * d), r(M, d)
+        w = torch.ones(64, device="cuda")
+        q, rq = QK.qk_norm_fwd(qkv[:, :d], w, cos, sin, L)
+        dsrc = torch.empty(M, d, device="cuda", dtype=torch.bfloat16)
+        dw = torch.zeros(64, device="cuda")
+        fn = (lambda: QK.qk_norm_fwd(qkv[:, :d], w, cos, sin, L)) if a.case == "qk_fwd" else \
+            (lambda: QK.qk_norm_bwd(dq, qkv[:, :d], rq, w, cos, sin, L, dsrc=dsrc, dw_acc=dw))
     elif a.case == "gate_bwd":
         from nano_gpic_b200.ops import elementwise as E
         dout, y, mod = r(M, d), r(M, d), r(M // 256, 6 * d)
