@@ -43,6 +43,7 @@ void gate_bwd(const at::Tensor& dout, const at::Tensor& y, const at::Tensor& gat
               const c10::optional<at::Tensor>& dgate, const c10::optional<at::Tensor>& dbias, int64_t rpg,
               const c10::optional<at::Tensor>& cu, int64_t max_rows);
 void gather_rows(const at::Tensor& src, const at::Tensor& idx, const at::Tensor& out);
+void u8_to_unit(const at::Tensor& img, const at::Tensor& out);
 void fm_prep(const at::Tensor& x, const at::Tensor& noise, const at::Tensor& t, const at::Tensor& xt_tok, int64_t p);
 void fm_loss(const at::Tensor& pred, const at::Tensor& x, const at::Tensor& noise, const at::Tensor& t,
              const c10::optional<at::Tensor>& dpred, const at::Tensor& per_sample, int64_t p, double t_eps,
@@ -54,7 +55,7 @@ void attn_fwd_tc(const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0
                  const at::Tensor& lse, int64_t Lq, int64_t L0, int64_t L1, double scale, int64_t version);
 void gemm_set_pair(int64_t on);
 std::vector<at::Tensor> mx_quant(const at::Tensor& x);
-void muon_gather(const at::Tensor& tab, double beta, bool nesterov, int64_t max_numel);
+void muon_gather(const at::Tensor& tab, double beta, bool nesterov, int64_t max_numel, double mom, bool out_bf16);
 void muon_apply(const at::Tensor& tab, double decay, int64_t max_numel, double ema_w);
 void adamw_apply(const at::Tensor& tab, std::vector<double> scalars, int64_t max_numel);
 void resize_passes(const at::Tensor& src, const at::Tensor& tab, const at::Tensor& desc, const at::Tensor& tmp,
@@ -135,6 +136,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("version") = 2);
   m.def("gate_bwd", &ng::gate_bwd);
   m.def("gather_rows", &ng::gather_rows, "out[r] = src[idx[r]] (bf16 rows), zeros where idx[r] < 0");
+  m.def("u8_to_unit", &ng::u8_to_unit, "uint8 [B, H, W, 3] -> fp32 [B, 3, H, W] in [-1, 1] (ToTensor + Normalize 0.5)");
   m.def("fm_prep", &ng::fm_prep);
   m.def("fm_loss", &ng::fm_loss);
   m.def("patchify", &ng::patchify);

@@ -13,6 +13,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "finish.cuh"
 #include "reduce.h"
 #include "status.h"
 
@@ -48,7 +49,7 @@ constexpr int GB_ROWS = 32;  // rows per CTA: 1024 CTAs at 128 x 256 rows (2.3 w
 __global__ void __launch_bounds__(256) gate_bwd_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ y,
                                                        const bf16* __restrict__ gate, int64_t ldg,
                                                        bf16* __restrict__ dy, float* __restrict__ part, int M, int C,
-                                                       int rpg, const int* __restrict__ cu) {
+                                                       int rpg, const int* __restrict__ cu, FinishArgs fa) {
   extern __shared__ float red[];  // [RG - 1][2][C]
   const int g = blockIdx.y, chunk = blockIdx.x;
   // rows of group g: [g rpg, (g + 1) rpg), or [cu[g], cu[g + 1]) for packed rows (a chunk past the end: zero partials)
@@ -132,23 +133,55 @@ __global__ void __launch_bounds__(256) gate_bwd_kernel(const bf16* __restrict__ 
       }
     }
   }
+  // the group's last CTA writes d_gate[g] and the group's d_bias row: fixed order, no group-sum launch
+  finish_partials<2>(part, 2 * C, C, gridDim.x, g, fa);
 }
 
-__global__ void gate_bwd_reduce(const float* __restrict__ part, int G, int chunks, int C, float* dgate, int64_t ld_dg,
-                                float* dbias) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= C) return;
-  float tb = 0.f;
-  for (int g = 0; g < G; ++g) {
-    float a = 0.f;
-    for (int k = 0; k < chunks; ++k) {
-      const float* pp = part + (int64_t)(g * chunks + k) * 2 * C;
-      a += pp[c];
-      tb += pp[C + c];
-    }
-    if (dgate != nullptr) dgate[(int64_t)g * ld_dg + c] = a;
+// ---------------------------------------------------------------------------------------------- image input
+// uint8 HWC images [B, H, W, 3] -> fp32 CHW in [-1, 1] with the reference's formula (ToTensor, then Normalize(0.5,
+// 0.5): (u / 255 - 0.5) / 0.5), rounded as PyTorch evaluates it on the device: a division by a scalar is a
+// multiplication by the scalar's fp32 reciprocal, each operation rounded on its own (no fused multiply-add), and the
+// division by 0.5 is the exact multiplication by 2. A thread per 8 pixels of a row: three 8-byte loads, two 16-byte
+// stores per channel. W % 8 == 0.
+__global__ void u8_to_unit_kernel(const uint8_t* __restrict__ img, float* __restrict__ out, int64_t rows, int H,
+                                  int W) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int w8 = W / 8;
+  if (i >= rows * w8) return;
+  const int64_t bh = i / w8;
+  const int x0 = (int)(i - bh * w8) * 8;
+  const int64_t b = bh / H;
+  const int h = (int)(bh - b * H);
+  const uint2* src = reinterpret_cast<const uint2*>(img + (bh * W + x0) * 3);
+  uint8_t px[24];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) *reinterpret_cast<uint2*>(px + 8 * k) = src[k];
+#pragma unroll
+  for (int c = 0; c < 3; ++c) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __fsub_rn(__fmul_rn((float)px[3 * j + c], 1.0f / 255.0f), 0.5f) * 2.0f;
+    float4* dst = reinterpret_cast<float4*>(out + ((b * 3 + c) * H + h) * (int64_t)W + x0);
+    dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+    dst[1] = make_float4(v[4], v[5], v[6], v[7]);
   }
-  if (dbias != nullptr) dbias[c] += tb;
+}
+
+void u8_to_unit(const at::Tensor& img, const at::Tensor& out) {
+  TORCH_CHECK(img.is_cuda() && img.scalar_type() == at::kByte && img.is_contiguous() && img.dim() == 4 &&
+                  img.size(3) == 3 && img.size(2) % 8 == 0,
+              "u8_to_unit: contiguous uint8 [B, H, W, 3] with W % 8 == 0");
+  TORCH_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous() && out.size(0) == img.size(0) &&
+                  out.size(1) == 3 && out.size(2) == img.size(1) && out.size(3) == img.size(2),
+              "u8_to_unit: fp32 [B, 3, H, W] output");
+  const at::cuda::CUDAGuard guard(img.device());
+  const int64_t rows = img.size(0) * img.size(1);
+  const int H = img.size(1), W = img.size(2);
+  const int64_t n = rows * (W / 8);
+  if (n == 0) return;
+  u8_to_unit_kernel<<<(unsigned)((n + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      img.data_ptr<uint8_t>(), out.data_ptr<float>(), rows, H, W);
+  NG_LAUNCH_CHECK();
 }
 
 // ---------------------------------------------------------------------------------------------- flow matching
@@ -299,19 +332,23 @@ void gate_bwd(const at::Tensor& dout, const at::Tensor& y, const at::Tensor& gat
   TORCH_CHECK(G <= 65535, "gate_bwd: at most 65535 groups");
   const int chunks = ((packed ? (int)max_rows : (int)rpg) + GB_ROWS - 1) / GB_ROWS;
   auto s = at::cuda::getCurrentCUDAStream();
-  at::Tensor part = at::empty({(int64_t)G * chunks * 2 * C}, dout.options().dtype(at::kFloat));
+  // chunk partials, then the group rows of the d_bias sums
+  at::Tensor part = at::empty({(int64_t)G * chunks * 2 * C + (int64_t)G * C}, dout.options().dtype(at::kFloat));
   const int RG = std::max(1, 256 / (C / 8));
   const size_t smem = RG > 1 ? (size_t)(RG - 1) * 2 * C * sizeof(float) : 0;
+  FinishArgs fa{};
+  fa.gout[0] = (dgate.has_value() && dgate->defined()) ? dgate->data_ptr<float>() : nullptr;
+  fa.gld[0] = fa.gout[0] != nullptr ? dgate->stride(0) : 0;
+  fa.scratch = part.data_ptr<float>() + (int64_t)G * chunks * 2 * C;
+  fa.cnt = finish_counters(s, G);
   gate_bwd_kernel<<<dim3(chunks, G), 256, smem, s>>>(
       reinterpret_cast<const bf16*>(dout.data_ptr()), reinterpret_cast<const bf16*>(y.data_ptr()),
       reinterpret_cast<const bf16*>(gate.data_ptr()), gate.stride(0), reinterpret_cast<bf16*>(dy.data_ptr()),
-      part.data_ptr<float>(), M, C, (int)rpg, cup);
+      part.data_ptr<float>(), M, C, (int)rpg, cup, fa);
   NG_LAUNCH_CHECK();
-  float* dg = (dgate.has_value() && dgate->defined()) ? dgate->data_ptr<float>() : nullptr;
-  float* db = (dbias.has_value() && dbias->defined()) ? dbias->data_ptr<float>() : nullptr;
-  const float* pp = part.data_ptr<float>();
-  group_sum_launch(pp, G, chunks, C, 2 * C, dg, dg ? dgate->stride(0) : 0, s);
-  if (db != nullptr) colsum_launch(pp + C, false, (int64_t)G * chunks, C, 2 * C, db, true, s);
+  // d_bias: the column sums of the G group rows the kernel left in the scratch
+  if (dbias.has_value() && dbias->defined())
+    colsum_launch(fa.scratch, false, G, C, C, dbias->data_ptr<float>(), true, s);
 }
 
 void fm_prep(const at::Tensor& x, const at::Tensor& noise, const at::Tensor& t, const at::Tensor& xt_tok, int64_t p) {

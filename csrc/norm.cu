@@ -11,6 +11,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "finish.cuh"
 #include "reduce.h"
 #include "status.h"
 
@@ -139,7 +140,8 @@ __global__ void __launch_bounds__(256) rms_mod_bwd_kernel(const bf16* __restrict
                                                           const bf16* __restrict__ scale, int64_t ld_sc,
                                                           const bf16* __restrict__ dres, bf16* __restrict__ dx,
                                                           float* __restrict__ part, int M, int C, int rpg,
-                                                          const int* __restrict__ cu = nullptr) {
+                                                          const int* __restrict__ cu = nullptr,
+                                                          FinishArgs fa = FinishArgs{}) {
   __shared__ float s_c[BWD_ROWS];
   const int g = blockIdx.y, chunk = blockIdx.x;
   // rows of group g: [g rpg, (g + 1) rpg), or [cu[g], cu[g + 1]) for packed rows; a chunk past its group's end writes
@@ -179,54 +181,56 @@ __global__ void __launch_bounds__(256) rms_mod_bwd_kernel(const bf16* __restrict
   __syncthreads();
   // ---- phase 2: a thread per 8 columns walks the chunk's rows
   const int v = threadIdx.x;
-  if (v >= nv) return;
-  const int c0 = v * 8;
-  float wf[8], sc[8];
-  load_w8(w, c0, wf);
-  if (MOD) {
-    unpack8(*reinterpret_cast<const uint4*>(scale + (int64_t)g * ld_sc + c0), sc);
-  } else {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) sc[j] = 0.f;
-  }
-  float psh[8], psc[8], pw[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) psh[j] = psc[j] = pw[j] = 0.f;
-  for (int rr = 0; rr < nrows; ++rr) {
-    const int row = r0 + rr;
-    const float r = rstd[row];
-    const float cm = s_c[rr];
-    float d[8], xf[8], o[8];
-    unpack8(*reinterpret_cast<const uint4*>(dh + (int64_t)row * C + c0), d);
-    unpack8(*reinterpret_cast<const uint4*>(x + (int64_t)row * C + c0), xf);
-    float rs[8];
-    if (dres != nullptr) {
-      unpack8(*reinterpret_cast<const uint4*>(dres + (int64_t)row * C + c0), rs);
+  if (v < nv) {
+    const int c0 = v * 8;
+    float wf[8], sc[8];
+    load_w8(w, c0, wf);
+    if (MOD) {
+      unpack8(*reinterpret_cast<const uint4*>(scale + (int64_t)g * ld_sc + c0), sc);
     } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) rs[j] = 0.f;
+      for (int j = 0; j < 8; ++j) sc[j] = 0.f;
     }
+    float psh[8], psc[8], pw[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) psh[j] = psc[j] = pw[j] = 0.f;
+    for (int rr = 0; rr < nrows; ++rr) {
+      const int row = r0 + rr;
+      const float r = rstd[row];
+      const float cm = s_c[rr];
+      float d[8], xf[8], o[8];
+      unpack8(*reinterpret_cast<const uint4*>(dh + (int64_t)row * C + c0), d);
+      unpack8(*reinterpret_cast<const uint4*>(x + (int64_t)row * C + c0), xf);
+      float rs[8];
+      if (dres != nullptr) {
+        unpack8(*reinterpret_cast<const uint4*>(dres + (int64_t)row * C + c0), rs);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) rs[j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float xn = xf[j] * r;
+        const float u = wf[j] * xn;
+        const float du = d[j] * (1.f + sc[j]);
+        psh[j] += d[j];
+        psc[j] += d[j] * u;
+        pw[j] += du * xn;
+        const float dxn = du * wf[j];
+        o[j] = r * (dxn - xn * cm) + rs[j];
+      }
+      *reinterpret_cast<uint4*>(dx + (int64_t)row * C + c0) = pack8(o);
+    }
+    const int cid = g * gridDim.x + chunk;
+    float* pp = part + (int64_t)cid * 3 * C;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float xn = xf[j] * r;
-      const float u = wf[j] * xn;
-      const float du = d[j] * (1.f + sc[j]);
-      psh[j] += d[j];
-      psc[j] += d[j] * u;
-      pw[j] += du * xn;
-      const float dxn = du * wf[j];
-      o[j] = r * (dxn - xn * cm) + rs[j];
+      pp[c0 + j] = psh[j];
+      pp[C + c0 + j] = psc[j];
+      pp[2 * C + c0 + j] = pw[j];
     }
-    *reinterpret_cast<uint4*>(dx + (int64_t)row * C + c0) = pack8(o);
   }
-  const int cid = g * gridDim.x + chunk;
-  float* pp = part + (int64_t)cid * 3 * C;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    pp[c0 + j] = psh[j];
-    pp[C + c0 + j] = psc[j];
-    pp[2 * C + c0 + j] = pw[j];
-  }
+  if (fa.cnt != nullptr) finish_partials<3>(part, 3 * C, C, gridDim.x, g, fa);
 }
 
 // Bandwidth-shaped variant for C = 256 * VPL (the ladder widths 768 .. 1792). Phase 1: a warp per row, lane l owning
@@ -239,7 +243,8 @@ __global__ void __launch_bounds__(256, VPL <= 4 ? 2 : 1) rms_mod_bwd_kernel2(con
                                                            const bf16* __restrict__ scale, int64_t ld_sc,
                                                            const bf16* __restrict__ dres, bf16* __restrict__ dx,
                                                            float* __restrict__ part, int M, int rpg,
-                                                           const int* __restrict__ cu = nullptr) {
+                                                           const int* __restrict__ cu = nullptr,
+                                                           FinishArgs fa = FinishArgs{}) {
   constexpr int C = 256 * VPL, NV = C / 8;
   constexpr int G2 = 256 / NV;  // row groups in phase 2
   __shared__ float red[G2 > 1 ? (G2 - 1) * 3 * C : 1];
@@ -336,6 +341,7 @@ __global__ void __launch_bounds__(256, VPL <= 4 ? 2 : 1) rms_mod_bwd_kernel2(con
       }
     }
   }
+  bool writer = active;
   if (G2 > 1) {
     if (active && grp > 0) {
       float* dst = red + (grp - 1) * 3 * C;
@@ -347,27 +353,31 @@ __global__ void __launch_bounds__(256, VPL <= 4 ? 2 : 1) rms_mod_bwd_kernel2(con
       }
     }
     __syncthreads();
-    if (grp != 0) return;
-    for (int q = 0; q < G2 - 1; ++q) {
-      const float* src = red + q * 3 * C;
+    writer = grp == 0;
+    if (writer) {
+      for (int q = 0; q < G2 - 1; ++q) {
+        const float* src = red + q * 3 * C;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        psh[j] += src[c0 + j];
-        psc[j] += src[C + c0 + j];
-        pw[j] += src[2 * C + c0 + j];
+        for (int j = 0; j < 8; ++j) {
+          psh[j] += src[c0 + j];
+          psc[j] += src[C + c0 + j];
+          pw[j] += src[2 * C + c0 + j];
+        }
       }
     }
-  } else if (!active) {
-    return;
   }
-  const int cid = g * gridDim.x + chunk;
-  float* pp = part + (int64_t)cid * 3 * C;
+  if (writer) {
+    const int cid = g * gridDim.x + chunk;
+    float* pp = part + (int64_t)cid * 3 * C;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    pp[c0 + j] = psh[j];
-    pp[C + c0 + j] = psc[j];
-    pp[2 * C + c0 + j] = pw[j];
+    for (int j = 0; j < 8; ++j) {
+      pp[c0 + j] = psh[j];
+      pp[C + c0 + j] = psc[j];
+      pp[2 * C + c0 + j] = pw[j];
+    }
   }
+  // the group's last CTA adds the group's chunks in a fixed order: no group-sum launches
+  if (fa.cnt != nullptr) finish_partials<3>(part, 3 * C, C, gridDim.x, g, fa);
 }
 
 // Reduction of the chunk partials for the no-allocation entry point, in two launches that allocate nothing.
@@ -597,8 +607,17 @@ void rms_mod_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& rs
   const int rows_per_group = mod ? (int)rpg : M;
   const int chunks = ((packed ? (int)max_rows : rows_per_group) + BWD_ROWS - 1) / BWD_ROWS;
   auto s = at::cuda::getCurrentCUDAStream();
-  at::Tensor part = at::empty({(int64_t)G * chunks * 3 * C}, x.options().dtype(at::kFloat));
+  // chunk partials, then the group rows of the d_w sums (the kernel's last CTA per group writes d_shift, d_scale and
+  // the group's d_w row: no group-sum launches)
+  at::Tensor part = at::empty({(int64_t)G * chunks * 3 * C + (int64_t)G * C}, x.options().dtype(at::kFloat));
   dim3 grid(chunks, G);
+  FinishArgs fa{};
+  fa.gout[0] = (mod && dshift.has_value() && dshift->defined()) ? dshift->data_ptr<float>() : nullptr;
+  fa.gout[1] = (mod && dscale.has_value() && dscale->defined()) ? dscale->data_ptr<float>() : nullptr;
+  fa.gld[0] = fa.gout[0] != nullptr ? ld_of(dshift) : 0;
+  fa.gld[1] = fa.gout[1] != nullptr ? ld_of(dscale) : 0;
+  fa.scratch = part.data_ptr<float>() + (int64_t)G * chunks * 3 * C;
+  fa.cnt = finish_counters(s, G);
   const bf16* scp = mod ? bptr(scale) : nullptr;
   const int64_t ldsc = mod ? ld_of(scale) : 0;
   bool done = true;
@@ -607,12 +626,12 @@ void rms_mod_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& rs
     rms_mod_bwd_kernel2<true, V><<<grid, 256, 0, s>>>(                                                              \
         reinterpret_cast<const bf16*>(dh.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),                   \
         rstd.data_ptr<float>(), w.data_ptr<float>(), scp, ldsc, bptr(dres), reinterpret_cast<bf16*>(dx.data_ptr()), \
-        part.data_ptr<float>(), M, rows_per_group, cup);                                                             \
+        part.data_ptr<float>(), M, rows_per_group, cup, fa);                                                         \
   else                                                                                                               \
     rms_mod_bwd_kernel2<false, V><<<grid, 256, 0, s>>>(                                                             \
         reinterpret_cast<const bf16*>(dh.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),                   \
         rstd.data_ptr<float>(), w.data_ptr<float>(), nullptr, 0, bptr(dres), reinterpret_cast<bf16*>(dx.data_ptr()), \
-        part.data_ptr<float>(), M, rows_per_group);
+        part.data_ptr<float>(), M, rows_per_group, nullptr, fa);
   switch (C) {
     case 768: NG_RMS_BWD2(3) break;
     case 1024: NG_RMS_BWD2(4) break;
@@ -627,22 +646,15 @@ void rms_mod_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& rs
     rms_mod_bwd_kernel<true><<<grid, 256, 0, s>>>(
         reinterpret_cast<const bf16*>(dh.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),
         rstd.data_ptr<float>(), w.data_ptr<float>(), bptr(scale), ld_of(scale), bptr(dres),
-        reinterpret_cast<bf16*>(dx.data_ptr()), part.data_ptr<float>(), M, C, rows_per_group, cup);
+        reinterpret_cast<bf16*>(dx.data_ptr()), part.data_ptr<float>(), M, C, rows_per_group, cup, fa);
   else
     rms_mod_bwd_kernel<false><<<grid, 256, 0, s>>>(
         reinterpret_cast<const bf16*>(dh.data_ptr()), reinterpret_cast<const bf16*>(x.data_ptr()),
         rstd.data_ptr<float>(), w.data_ptr<float>(), nullptr, 0, bptr(dres), reinterpret_cast<bf16*>(dx.data_ptr()),
-        part.data_ptr<float>(), M, C, rows_per_group);
+        part.data_ptr<float>(), M, C, rows_per_group, nullptr, fa);
   NG_LAUNCH_CHECK();
-  float* dsh = (dshift.has_value() && dshift->defined()) ? dshift->data_ptr<float>() : nullptr;
-  float* dsc = (dscale.has_value() && dscale->defined()) ? dscale->data_ptr<float>() : nullptr;
-  float* dwp = (dw.has_value() && dw->defined()) ? dw->data_ptr<float>() : nullptr;
-  const float* pp = part.data_ptr<float>();
-  if (mod) {
-    group_sum_launch(pp, G, chunks, C, 3 * C, dsh, ld_of(dshift), s);
-    group_sum_launch(pp + C, G, chunks, C, 3 * C, dsc, ld_of(dscale), s);
-  }
-  if (dwp != nullptr) colsum_launch(pp + 2 * C, false, (int64_t)G * chunks, C, 3 * C, dwp, true, s);
+  // d_w: the column sums of the G group rows the kernel left in the scratch
+  if (dw.has_value() && dw->defined()) colsum_launch(fa.scratch, false, G, C, C, dw->data_ptr<float>(), true, s);
 }
 
 void layernorm_fwd(const at::Tensor& x, const at::Tensor& h, const at::Tensor& mu, const at::Tensor& rstd, double eps) {

@@ -6,8 +6,9 @@
 // two SwiGLU halves, w3 and the six adaLN parts of every block); issued one by one, their lerps, copies and adds are
 // ~660 tiny launches per step that leave the GPU waiting on the host.
 //
-// muon_gather: rows [dst fp32*, grad fp32*, momentum fp32*, numel]: dst = nesterov ? lerp(grad, momentum, beta)
-//              : momentum, with torch.lerp's formula (the end-anchored form for weights >= 0.5).
+// muon_gather: rows [dst*, grad fp32*, momentum fp32*, numel]: optionally momentum = lerp(momentum, grad, 1 - beta)
+//              first (written back), then dst = nesterov ? lerp(grad, momentum, beta) : momentum, with torch.lerp's
+//              formula (the end-anchored form for weights >= 0.5); dst fp32 or bf16.
 // muon_apply:  rows [param fp32*, update bf16*, numel, coef (fp32 bits)(, ema fp32*)]: param = param * decay + coef *
 //              update (then the EMA's lerp toward it when the row has an EMA buffer).
 // numel is a multiple of 4 and every pointer is 16-byte aligned (row slices of contiguous matrices); the host checks.
@@ -26,20 +27,35 @@ __device__ __forceinline__ float lerp_torch(float a, float b, float w) {
   return fabsf(w) < 0.5f ? a + w * (b - a) : b - (b - a) * (1.0f - w);
 }
 
-__global__ void muon_gather_kernel(const int64_t* __restrict__ tab, float beta, int nesterov) {
+// mom >= 0: the momentum update m = lerp(m, grad, mom) (torch._foreach_lerp_'s formula) happens in the same pass and
+// m is written back; out_bf16: dst holds bf16 (the Newton-Schulz input's precision: the same rounding as a later
+// .to(bfloat16)).
+__global__ void muon_gather_kernel(const int64_t* __restrict__ tab, float beta, int nesterov, float mom,
+                                   int out_bf16) {
   const int64_t* r = tab + (int64_t)blockIdx.y * 4;
-  float4* dst = reinterpret_cast<float4*>(r[0]);
   const float4* g = reinterpret_cast<const float4*>(r[1]);
-  const float4* m = reinterpret_cast<const float4*>(r[2]);
+  float4* m = reinterpret_cast<float4*>(r[2]);
   const int64_t n4 = r[3] / 4;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
-    const float4 mv = m[i];
-    if (nesterov) {
-      const float4 gv = g[i];
-      dst[i] = make_float4(lerp_torch(gv.x, mv.x, beta), lerp_torch(gv.y, mv.y, beta), lerp_torch(gv.z, mv.z, beta),
-                           lerp_torch(gv.w, mv.w, beta));
+    float4 mv = m[i];
+    const float4 gv = (nesterov || mom >= 0.f) ? g[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+    if (mom >= 0.f) {
+      mv = make_float4(lerp_torch(mv.x, gv.x, mom), lerp_torch(mv.y, gv.y, mom), lerp_torch(mv.z, gv.z, mom),
+                       lerp_torch(mv.w, gv.w, mom));
+      m[i] = mv;
+    }
+    const float4 o = nesterov ? make_float4(lerp_torch(gv.x, mv.x, beta), lerp_torch(gv.y, mv.y, beta),
+                                            lerp_torch(gv.z, mv.z, beta), lerp_torch(gv.w, mv.w, beta))
+                              : mv;
+    if (out_bf16) {
+      uint2 pk;
+      pk.x = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(o.x)) |
+             ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(o.y)) << 16);
+      pk.y = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(o.z)) |
+             ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(o.w)) << 16);
+      reinterpret_cast<uint2*>(r[0])[i] = pk;
     } else {
-      dst[i] = mv;
+      reinterpret_cast<float4*>(r[0])[i] = o;
     }
   }
 }
@@ -126,11 +142,11 @@ static dim3 table_grid(const at::Tensor& tab, int64_t max_numel, int64_t width =
   return dim3((unsigned)std::max<int64_t>(blocks, 1), (unsigned)tab.size(0));
 }
 
-void muon_gather(const at::Tensor& tab, double beta, bool nesterov, int64_t max_numel) {
+void muon_gather(const at::Tensor& tab, double beta, bool nesterov, int64_t max_numel, double mom, bool out_bf16) {
   if (tab.size(0) == 0) return;
   const at::cuda::CUDAGuard guard(tab.device());
   muon_gather_kernel<<<table_grid(tab, max_numel), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      tab.data_ptr<int64_t>(), (float)beta, nesterov ? 1 : 0);
+      tab.data_ptr<int64_t>(), (float)beta, nesterov ? 1 : 0, (float)mom, out_bf16 ? 1 : 0);
   NG_LAUNCH_CHECK();
 }
 

@@ -6,8 +6,12 @@
 //   group_sum: out[g * ldo + c] = sum_{k < chunks} part[(g * chunks + k) * stride + c] (the chunk partials of one
 //           modulation group, e.g. one sample).
 #include <ATen/cuda/CUDAContext.h>
+#include <ATen/cuda/CUDAGraphsUtils.cuh>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
+
+#include <map>
+#include <mutex>
 
 #include "common.cuh"
 #include "reduce.h"
@@ -79,6 +83,28 @@ void group_sum_launch(const float* part, int G, int chunks, int C, int64_t strid
   if (out == nullptr || G <= 0) return;
   group_sum_kernel<<<dim3((C + 255) / 256, G), 256, 0, stream>>>(part, chunks, C, stride, out, ldo);
   NG_LAUNCH_CHECK();
+}
+
+int* finish_counters(cudaStream_t stream, int n) {
+  static std::mutex mu;
+  static std::map<std::pair<int, cudaStream_t>, std::pair<int*, int>> tables;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  auto& t = tables[{dev, stream}];
+  if (t.second < n) {
+    at::cuda::assertNotCapturing("finish_counters: allocating the ticket table");
+    int* p = nullptr;
+    const int cap = std::max(n, 4096);
+    TORCH_CHECK(cudaMalloc(&p, cap * sizeof(int)) == cudaSuccess, "finish_counters: cudaMalloc failed");
+    TORCH_CHECK(cudaMemsetAsync(p, 0, cap * sizeof(int), stream) == cudaSuccess, "finish_counters: memset failed");
+    if (t.first != nullptr) {
+      cudaStreamSynchronize(stream);  // the old table's last user on this stream has finished
+      cudaFree(t.first);
+    }
+    t = {p, cap};
+  }
+  return t.first;
 }
 
 // torch: out (+)= column sums of src [rows, C] (fp32 or bf16, unit column stride)

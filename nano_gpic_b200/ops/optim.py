@@ -23,13 +23,18 @@ def _ok(t, dtype):
     return t.is_cuda and t.dtype == dtype and t.is_contiguous() and t.numel() % 4 == 0 and t.data_ptr() % 16 == 0
 
 
-def stack_nesterov(grads, moms, beta, nesterov):
-    """torch.stack([g.lerp(m, beta) if nesterov else m for g, m in zip(grads, moms)]) (fp32, all of one shape)."""
+def stack_nesterov(grads, moms, beta, nesterov, update_momentum=False, dtype=torch.float32):
+    """torch.stack([g.lerp(m, beta) if nesterov else m for g, m in zip(grads, moms)]) in `dtype` (fp32 or bf16), all
+    of one shape. update_momentum: first m.lerp_(g, 1 - beta) for every pair (in the same pass on CUDA)."""
     if not all(_ok(g, torch.float32) and _ok(m, torch.float32) for g, m in zip(grads, moms)):
-        return torch.stack([g.lerp(m, beta) if nesterov else m for g, m in zip(grads, moms)])
-    out = torch.empty((len(grads),) + tuple(grads[0].shape), dtype=torch.float32, device=grads[0].device)
+        if update_momentum:
+            for g, m in zip(grads, moms):
+                m.lerp_(g, 1 - beta)
+        return torch.stack([g.lerp(m, beta) if nesterov else m for g, m in zip(grads, moms)]).to(dtype)
+    out = torch.empty((len(grads),) + tuple(grads[0].shape), dtype=dtype, device=grads[0].device)
     rows = [[out[j].data_ptr(), g.data_ptr(), m.data_ptr(), g.numel()] for j, (g, m) in enumerate(zip(grads, moms))]
-    ext().muon_gather(_table(rows, out.device), float(beta), bool(nesterov), grads[0].numel())
+    ext().muon_gather(_table(rows, out.device), float(beta), bool(nesterov), grads[0].numel(),
+                      float(1 - beta) if update_momentum else -1.0, dtype == torch.bfloat16)
     return out
 
 

@@ -170,7 +170,6 @@ class MuonAdamW(torch.optim.Optimizer):
             grads.append(p.grad)
             bufs.append(st["momentum_buffer"])
         beta, lr, wd = group["momentum"], group["lr"], group["weight_decay"]
-        torch._foreach_lerp_(bufs, grads, 1 - beta)
         by_shape = {}
         for i, p in enumerate(params):
             parts = p._muon_parts if group["split"] else 1
@@ -178,9 +177,11 @@ class MuonAdamW(torch.optim.Optimizer):
             for k in range(parts):
                 by_shape.setdefault((rows, p.shape[1]), []).append((i, k * rows, (k + 1) * rows))
         outs = []
+        # the units cover every row of every owned matrix once: the momentum update happens in the gather's pass,
+        # which writes the Newton-Schulz input straight in its precision
         for shape, us in by_shape.items():
             ins = OPT.stack_nesterov([grads[i][r0:r1] for i, r0, r1 in us], [bufs[i][r0:r1] for i, r0, r1 in us],
-                                     beta, group["nesterov"])
+                                     beta, group["nesterov"], update_momentum=True, dtype=self.ns_dtype)
             O = msign(ins, steps=group["ns_steps"], dtype=self.ns_dtype)
             outs.append((shape, us, O.contiguous() if O.is_cuda else O))
         if self.defer is not None:  # the fused kernel applies W <- W (1 - lr wd) - lr coef O
@@ -212,17 +213,19 @@ class MuonAdamW(torch.optim.Optimizer):
             grads.append(g)
             bufs.append(st["momentum_buffer"])
         beta, lr, wd = group["momentum"], group["lr"], group["weight_decay"]
-        torch._foreach_lerp_(bufs, grads, 1 - beta)
         if self._plan is None:
             self._plan = self._build_plan(group)
         plan = self._plan
         dev = params[0].device
         single = plan["world"] == 1
+        if not single:  # every rank keeps every momentum buffer; with one rank the gather's pass updates them
+            torch._foreach_lerp_(bufs, grads, 1 - beta)
         shard = None if single else torch.zeros(plan["shard"], dtype=self.ns_dtype, device=dev)
         local = {}  # one rank: each unit's update straight from the Newton-Schulz output
         for shape, us in plan["mine"].items():
             ins = OPT.stack_nesterov([grads[u["p"]][u["r0"]:u["r1"]] for u in us],
-                                     [bufs[u["p"]][u["r0"]:u["r1"]] for u in us], beta, group["nesterov"])
+                                     [bufs[u["p"]][u["r0"]:u["r1"]] for u in us], beta, group["nesterov"],
+                                     update_momentum=single, dtype=self.ns_dtype)
             O = msign(ins, steps=group["ns_steps"], dtype=self.ns_dtype)
             O = O.contiguous() if O.is_cuda else O
             for u, o in zip(us, O):

@@ -23,7 +23,13 @@ from ..optim.muon import MuonAdamW, tag_muon_params
 
 def uint8_to_float(img):
     """uint8 HWC [B, H, W, 3] -> fp32 CHW in [-1, 1]: ToTensor then Normalize(0.5, 0.5), as the reference's lever D
-    (baselines/PixelGen/src/data/dataset/gpic_dataset.py:869-881)."""
+    (baselines/PixelGen/src/data/dataset/gpic_dataset.py:869-881). On CUDA one pass of csrc/elementwise.cu's
+    u8_to_unit (the same fp32 arithmetic); the PyTorch form otherwise."""
+    if img.is_cuda and img.is_contiguous() and img.dim() == 4 and img.shape[3] == 3 and img.shape[2] % 8 == 0:
+        from .._ext import ext
+        out = torch.empty(img.shape[0], 3, img.shape[1], img.shape[2], device=img.device, dtype=torch.float32)
+        ext().u8_to_unit(img, out)
+        return out
     return (((img.permute(0, 3, 1, 2).float() / 255.0) - 0.5) / 0.5).contiguous()
 
 

@@ -200,3 +200,14 @@ def test_attention_tc_backward(case):
         _close(a, a2, rtol=1e-2, atol=1e-2, what=name + " version 3 vs version 2")
     from nano_gpic_b200.ops import status
     assert status.read() == 0
+
+
+def test_u8_to_unit_matches_torch_formula():
+    """uint8 HWC -> fp32 CHW in [-1, 1] in one kernel pass, bit-identical to ToTensor + Normalize(0.5, 0.5)."""
+    from nano_gpic_b200.train.trainer import uint8_to_float
+    img = torch.randint(0, 256, (3, 40, 64, 3), dtype=torch.uint8, device="cuda")
+    ref = (((img.permute(0, 3, 1, 2).float() / 255.0) - 0.5) / 0.5).contiguous()
+    got = uint8_to_float(img)
+    assert got.shape == ref.shape
+    if not torch.equal(got, ref):  # at most one rounding step apart where PyTorch rounds differently
+        assert (got - ref).abs().max().item() <= 2.0 ** -23, (got - ref).abs().max().item()

@@ -128,3 +128,21 @@ def test_attached_ema_matches_separate_lerp():
     for x, y in zip(pa, pb):
         torch.testing.assert_close(x, y, rtol=1e-3, atol=1e-4)
     torch.testing.assert_close(ea, eb, rtol=1e-3, atol=1e-4)
+
+
+def test_stack_nesterov_with_momentum_update_and_bf16_output():
+    """The fused gather: momentum m = lerp(m, g, 1 - beta) written back and the Nesterov input in bf16 in one pass,
+    equal to torch's lerp_ then lerp then .to(bfloat16)."""
+    from nano_gpic_b200.ops import optim as OPT
+    torch.manual_seed(4)
+    G = [torch.randn(512, 256, device="cuda") for _ in range(3)]
+    M = [torch.randn(512, 256, device="cuda") for _ in range(3)]
+    Mr = [m.clone() for m in M]
+    for nesterov in (True, False):
+        got = OPT.stack_nesterov(G, M, 0.95, nesterov, update_momentum=True, dtype=torch.bfloat16)
+        for m, g in zip(Mr, G):
+            m.lerp_(g, 1 - 0.95)
+        ref = torch.stack([g.lerp(m, 0.95) if nesterov else m for g, m in zip(G, Mr)]).to(torch.bfloat16)
+        assert torch.equal(got, ref)
+        for a, b in zip(M, Mr):
+            assert torch.equal(a, b)
