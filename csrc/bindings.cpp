@@ -56,6 +56,9 @@ void attn_fwd_tc(const at::Tensor& q, const at::Tensor& k0, const at::Tensor& v0
 void gemm_set_pair(int64_t on);
 std::vector<at::Tensor> mx_quant(const at::Tensor& x);
 void muon_gather(const at::Tensor& tab, double beta, bool nesterov, int64_t max_numel, double mom, bool out_bf16);
+void scale_by(const at::Tensor& buf, const at::Tensor& coef);
+void ns_normalize(const at::Tensor& x, bool transpose, const at::Tensor& out);
+void transpose_bf16(const at::Tensor& x, const at::Tensor& out);
 void muon_apply(const at::Tensor& tab, double decay, int64_t max_numel, double ema_w);
 void adamw_apply(const at::Tensor& tab, std::vector<double> scalars, int64_t max_numel);
 void resize_passes(const at::Tensor& src, const at::Tensor& tab, const at::Tensor& desc, const at::Tensor& tmp,
@@ -120,6 +123,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("muon_gather", &ng::muon_gather, "stacked Nesterov inputs of every Muon unit from a pointer table");
   m.def("muon_apply", &ng::muon_apply, "param = param * decay + coef * update for every Muon unit from a pointer table");
   m.def("adamw_apply", &ng::adamw_apply, "AdamW (+ EMA) of every row of a pointer table in one launch");
+  m.def("scale_by", &ng::scale_by, "buf *= coef (fp32, coef read on the device)");
+  m.def("ns_normalize", &ng::ns_normalize, "per matrix X / (||X|| + 1e-7) in bf16, optionally transposed");
+  m.def("transpose_bf16", &ng::transpose_bf16, "batched bf16 transpose [n, a, b] -> [n, b, a]");
   m.def("rms_mod_fwd_mx", &ng::rms_mod_fwd_mx, "RMSNorm + adaLN modulate forward that also writes h in MXFP8");
   m.def("mx_quant", &ng::mx_quant, "bf16 [rows, K] -> MXFP8 (e4m3 values, E8M0 scale blocks)");
   m.def("gemm_mx", &ng::gemm_mx_torch, "MXFP8 block-scaled tcgen05 GEMM with the bf16 / gated / SwiGLU epilogues");

@@ -13,6 +13,7 @@
 //              update (then the EMA's lerp toward it when the row has an EMA buffer).
 // numel is a multiple of 4 and every pointer is 16-byte aligned (row slices of contiguous matrices); the host checks.
 #include <ATen/cuda/CUDAContext.h>
+#include <algorithm>
 #include <cmath>
 #include <vector>
 #include <c10/cuda/CUDAGuard.h>
@@ -177,6 +178,207 @@ void adamw_apply(const at::Tensor& tab, std::vector<double> scalars, int64_t max
   sc.ema_w = (float)scalars[7];
   adamw_apply_kernel<<<table_grid(tab, max_numel, 6), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       tab.data_ptr<int64_t>(), sc);
+  NG_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------------------- clip and Newton-Schulz
+// scale_by: buf *= *coef (the clip coefficient, read on the device: no host sync), float4 vectors; n % 4 == 0.
+__global__ void scale_by_kernel(float4* __restrict__ buf, int64_t n4, const float* __restrict__ coef) {
+  const float c = *coef;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 v = buf[i];
+    v.x *= c;
+    v.y *= c;
+    v.z *= c;
+    v.w *= c;
+    buf[i] = v;
+  }
+}
+
+void scale_by(const at::Tensor& buf, const at::Tensor& coef) {
+  TORCH_CHECK(buf.is_cuda() && buf.scalar_type() == at::kFloat && buf.is_contiguous() && buf.numel() % 4 == 0 &&
+                  (reinterpret_cast<uintptr_t>(buf.data_ptr()) & 15) == 0,
+              "scale_by: contiguous, 16-byte aligned fp32 buffer of a multiple of 4 values");
+  TORCH_CHECK(coef.is_cuda() && coef.scalar_type() == at::kFloat && coef.numel() == 1, "scale_by: one fp32 coef");
+  const int64_t n4 = buf.numel() / 4;
+  if (n4 == 0) return;
+  const at::cuda::CUDAGuard guard(buf.device());
+  int sms = 0;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, buf.get_device());
+  const int64_t blocks = std::min<int64_t>((n4 + 255) / 256, 8 * (int64_t)sms);
+  scale_by_kernel<<<(unsigned)blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<float4*>(buf.data_ptr()), n4, coef.data_ptr<float>());
+  NG_LAUNCH_CHECK();
+}
+
+// Newton-Schulz input: per matrix of a batch [n, a, b] bf16, X / (||X||_F + 1e-7) as PyTorch evaluates it on bf16
+// tensors (the norm rounded to bf16, then + 1e-7 in bf16, then an IEEE division rounded to bf16), optionally written
+// transposed ([n, b, a]: tall matrices iterate on X^T). Two kernels: per-CTA sums of squares of row chunks, then the
+// scale (+ transpose) pass, in which one warp of every CTA adds its matrix's partials in a fixed order (deterministic).
+constexpr int NS_ROWS = 16;  // rows per CTA of the sum-of-squares pass
+
+__device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+__global__ void ns_sumsq_kernel(const __nv_bfloat16* __restrict__ x, int a, int b, float* __restrict__ part) {
+  __shared__ float red[8];
+  const int item = blockIdx.y, chunk = blockIdx.x;
+  const int r0 = chunk * NS_ROWS, r1 = min(a, r0 + NS_ROWS);
+  const __nv_bfloat16* base = x + (int64_t)item * a * b;
+  float acc = 0.f;
+  const int nv = b / 8;  // 16-byte vectors per row
+  for (int r = r0; r < r1; ++r)
+    for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+      const uint4 u = reinterpret_cast<const uint4*>(base + (int64_t)r * b)[v];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float lo = __uint_as_float(w[k] << 16), hi = __uint_as_float(w[k] & 0xffff0000u);
+        acc += lo * lo + hi * hi;
+      }
+    }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int k = 0; k < (int)(blockDim.x >> 5); ++k) t += red[k];
+    part[(int64_t)item * gridDim.x + chunk] = t;
+  }
+}
+
+// The divisor of one matrix from its chunk partials, summed by one warp in a fixed order (lane-strided, then a
+// butterfly): the same value in every CTA of the matrix. Call with all 32 lanes of a warp.
+__device__ __forceinline__ float ns_den(const float* __restrict__ p, int chunks) {
+  const int lane = threadIdx.x & 31;
+  float ss = 0.f;
+  for (int k = lane; k < chunks; k += 32) ss += p[k];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  return bf16_round(bf16_round(sqrtf(ss)) + 1e-7f);
+}
+
+// untransposed: 8 values per thread (16-byte vectors), a CTA per (row block, matrix)
+__global__ void ns_scale_vec_kernel(const __nv_bfloat16* __restrict__ x, int64_t per_item, const float* __restrict__ part,
+                                    int chunks, __nv_bfloat16* __restrict__ out) {
+  __shared__ float s_den;
+  const int item = blockIdx.y;
+  if (threadIdx.x < 32) {
+    const float d = ns_den(part + (int64_t)item * chunks, chunks);
+    if (threadIdx.x == 0) s_den = d;
+  }
+  __syncthreads();
+  const float den = s_den;
+  const uint4* in = reinterpret_cast<const uint4*>(x + (int64_t)item * per_item);
+  uint4* o = reinterpret_cast<uint4*>(out + (int64_t)item * per_item);
+  const int64_t nv = per_item / 8;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+    uint4 u = in[i];
+    uint32_t* w = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float lo = __fdiv_rn(__uint_as_float(w[k] << 16), den);
+      const float hi = __fdiv_rn(__uint_as_float(w[k] & 0xffff0000u), den);
+      w[k] = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(lo)) |
+             ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(hi)) << 16);
+    }
+    o[i] = u;
+  }
+}
+
+// transposed: 32 x 32 tiles (8 warps, 4 rows each): out[item] = in[item]^T / den[item]
+__global__ void ns_scale_kernel(const __nv_bfloat16* __restrict__ x, int a, int b, const float* __restrict__ part,
+                                int chunks, int transpose, __nv_bfloat16* __restrict__ out) {
+  __shared__ float tile[32][33];
+  __shared__ float s_den;
+  const int item = blockIdx.z;
+  if (threadIdx.y == 0) s_den = ns_den(part + (int64_t)item * chunks, chunks);
+  __syncthreads();
+  const float den = s_den;
+  const __nv_bfloat16* in = x + (int64_t)item * a * b;
+  __nv_bfloat16* o = out + (int64_t)item * a * b;
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int r = r0 + k, c = c0 + threadIdx.x;
+    float v = 0.f;
+    if (r < a && c < b) v = __fdiv_rn(__bfloat162float(in[(int64_t)r * b + c]), den);
+    tile[k][threadIdx.x] = v;
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    if (transpose) {  // out [b, a]: row c0 + k, column r0 + x
+      const int r = c0 + k, c = r0 + threadIdx.x;
+      if (r < b && c < a) o[(int64_t)r * a + c] = __float2bfloat16_rn(tile[threadIdx.x][k]);
+    } else {
+      const int r = r0 + k, c = c0 + threadIdx.x;
+      if (r < a && c < b) o[(int64_t)r * b + c] = __float2bfloat16_rn(tile[k][threadIdx.x]);
+    }
+  }
+}
+
+// batched transpose of bf16 matrices [n, a, b] -> [n, b, a] (the Newton-Schulz output of tall matrices)
+__global__ void transpose_bf16_kernel(const __nv_bfloat16* __restrict__ x, int a, int b,
+                                      __nv_bfloat16* __restrict__ out) {
+  __shared__ __nv_bfloat16 tile[32][34];
+  const int item = blockIdx.z;
+  const __nv_bfloat16* in = x + (int64_t)item * a * b;
+  __nv_bfloat16* o = out + (int64_t)item * a * b;
+  const int c0 = blockIdx.x * 32, r0 = blockIdx.y * 32;
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int r = r0 + k, c = c0 + threadIdx.x;
+    if (r < a && c < b) tile[k][threadIdx.x] = in[(int64_t)r * b + c];
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int r = c0 + k, c = r0 + threadIdx.x;
+    if (r < b && c < a) o[(int64_t)r * a + c] = tile[threadIdx.x][k];
+  }
+}
+
+static void check_batch(const at::Tensor& x, const char* what) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous() && x.dim() == 3 &&
+                  x.size(1) <= 65535 * 32 && x.size(2) <= 65535 * 32 && x.size(0) <= 65535,
+              what, ": contiguous bf16 [n, a, b] CUDA batch expected");
+}
+
+void ns_normalize(const at::Tensor& x, bool transpose, const at::Tensor& out) {
+  check_batch(x, "ns_normalize");
+  TORCH_CHECK(x.size(2) % 8 == 0, "ns_normalize: b % 8 == 0");
+  TORCH_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16 && out.numel() == x.numel(),
+              "ns_normalize: bf16 output of the same size");
+  const int n = x.size(0), a = x.size(1), b = x.size(2);
+  if (x.numel() == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  auto s = at::cuda::getCurrentCUDAStream();
+  const int chunks = (a + NS_ROWS - 1) / NS_ROWS;
+  at::Tensor part = at::empty({(int64_t)n * chunks}, x.options().dtype(at::kFloat));
+  ns_sumsq_kernel<<<dim3(chunks, n), 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), a, b,
+                                                  part.data_ptr<float>());
+  NG_LAUNCH_CHECK();
+  if (transpose) {
+    ns_scale_kernel<<<dim3((b + 31) / 32, (a + 31) / 32, n), dim3(32, 8), 0, s>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), a, b, part.data_ptr<float>(), chunks, 1,
+        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+  } else {
+    const int64_t per = (int64_t)a * b;
+    const int64_t bx = std::min<int64_t>((per / 8 + 255) / 256, 64);
+    ns_scale_vec_kernel<<<dim3((unsigned)bx, n), 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                                                               per, part.data_ptr<float>(), chunks,
+                                                               reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+  }
+  NG_LAUNCH_CHECK();
+}
+
+void transpose_bf16(const at::Tensor& x, const at::Tensor& out) {
+  check_batch(x, "transpose_bf16");
+  TORCH_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16 && out.numel() == x.numel(),
+              "transpose_bf16: bf16 output of the same size");
+  const int n = x.size(0), a = x.size(1), b = x.size(2);
+  if (x.numel() == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  transpose_bf16_kernel<<<dim3((b + 31) / 32, (a + 31) / 32, n), dim3(32, 8), 0,
+                          at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), a,
+                                                              b, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
   NG_LAUNCH_CHECK();
 }
 

@@ -88,3 +88,34 @@ def adamw_update(params, grads, m1, m2, emas, lr, wd, b1, b2, eps, bc1, bc2, ema
         p.addcdiv_(m, v.sqrt().div_(bc2 ** 0.5).add_(eps), value=-lr / bc1)
         if e is not None:
             e.lerp_(p, ema_w)
+
+
+def scale_(buf, coef):
+    """buf *= coef in place, coef a one-element fp32 device tensor (the clip coefficient: no host read). One vectorized
+    pass on CUDA (csrc/optim.cu scale_by) for contiguous, 16-byte aligned buffers of 4k values; PyTorch otherwise."""
+    if (buf.is_cuda and buf.dtype == torch.float32 and buf.is_contiguous() and buf.numel() % 4 == 0
+            and buf.data_ptr() % 16 == 0 and coef.is_cuda and coef.dtype == torch.float32 and coef.numel() == 1):
+        ext().scale_by(buf, coef.reshape(1))
+        return buf
+    return buf.mul_(coef)
+
+
+def ns_normalize(X, transpose=False):
+    """Per matrix of X [n, a, b] (bf16): X / (||X||_F + 1e-7) with PyTorch's bf16 rounding, written as [n, b, a] when
+    transpose (the Newton-Schulz input of tall matrices). One sum-of-squares pass and one scale pass on CUDA."""
+    if not (X.is_cuda and X.dtype == torch.bfloat16 and X.dim() == 3 and X.is_contiguous() and X.shape[2] % 8 == 0):
+        Y = X.mT if transpose else X
+        return (Y / (Y.norm(dim=(-2, -1), keepdim=True) + 1e-7)).contiguous()
+    n, a, b = X.shape
+    out = torch.empty((n, b, a) if transpose else (n, a, b), dtype=X.dtype, device=X.device)
+    ext().ns_normalize(X, bool(transpose), out)
+    return out
+
+
+def transpose_bf16(X):
+    """[n, a, b] -> contiguous [n, b, a] (bf16, one tiled pass on CUDA)."""
+    if not (X.is_cuda and X.dtype == torch.bfloat16 and X.dim() == 3 and X.is_contiguous()):
+        return X.mT.contiguous()
+    out = torch.empty((X.shape[0], X.shape[2], X.shape[1]), dtype=X.dtype, device=X.device)
+    ext().transpose_bf16(X, out)
+    return out

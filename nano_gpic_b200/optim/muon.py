@@ -50,20 +50,25 @@ def msign(Gm, steps=5, dtype=torch.bfloat16, fused=True):
     the tcgen05 GEMM with fused alpha/beta epilogues; other dtypes/devices use torch (the fp32 path is the exact
     reference for tests)."""
     a, b, c = NS_COEFFS
-    X = Gm.to(dtype)
     tall = Gm.size(-2) > Gm.size(-1)
-    if tall:
-        X = X.mT
-    X = X / (X.norm(dim=(-2, -1), keepdim=True) + 1e-7)
-    if X.is_cuda and dtype == torch.bfloat16 and fused:
-        squeeze = X.dim() == 2
+    if Gm.is_cuda and dtype == torch.bfloat16 and fused:
+        # the normalisation (and, for tall matrices, the transpose) in two passes of this package's kernels, the
+        # iteration on the tcgen05 GEMM, the transpose back in one tiled pass: no PyTorch elementwise passes
+        squeeze = Gm.dim() == 2
+        X = Gm.to(dtype)
         X = (X.unsqueeze(0) if squeeze else X).contiguous()
+        X = OPT.ns_normalize(X, transpose=tall)
         for _ in range(steps):
             A = G.bmm_axpby(X, X, False)                       # X X^T
             B = G.bmm_axpby(A, A, False, alpha=c, beta=b, C=A)  # b A + c A A  (A symmetric)
             X = G.bmm_axpby(B, X, True, alpha=1.0, beta=a, C=X)  # a X + B X
-        X = X[0] if squeeze else X
-        return X.mT if tall else X
+        if tall:
+            X = OPT.transpose_bf16(X)
+        return X[0] if squeeze else X
+    X = Gm.to(dtype)
+    if tall:
+        X = X.mT
+    X = X / (X.norm(dim=(-2, -1), keepdim=True) + 1e-7)
     for _ in range(steps):
         A = X @ X.mT
         B = b * A + c * (A @ A)

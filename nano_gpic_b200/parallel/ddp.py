@@ -33,6 +33,7 @@ bucket made only of finished stages is reduced at once on a side CUDA stream, un
 import torch
 import torch.distributed as dist
 
+from ..ops.optim import scale_
 from .flat import FlatParams, _round
 
 
@@ -421,7 +422,7 @@ class DataParallel:
     @torch.no_grad()
     def scale_grads(self, coef):
         for s in self.own_slices(self.flat.grad):
-            s.mul_(coef)
+            scale_(s, coef)
 
     # ------------------------------------------------------------------------------------------- weights
     @torch.no_grad()

@@ -216,6 +216,7 @@ class Trainer:
             return norm
         if self.flat is not None:
             norm = self.flat.grad.norm()
-            self.flat.grad.mul_((self.clip / (norm + 1e-6)).clamp(max=1.0))
+            from ..ops.optim import scale_
+            scale_(self.flat.grad, (self.clip / (norm + 1e-6)).clamp(max=1.0))
             return norm
         return torch.nn.utils.clip_grad_norm_([p for p in self.model.parameters() if p.grad is not None], self.clip)

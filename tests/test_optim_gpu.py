@@ -146,3 +146,23 @@ def test_stack_nesterov_with_momentum_update_and_bf16_output():
         assert torch.equal(got, ref)
         for a, b in zip(M, Mr):
             assert torch.equal(a, b)
+
+
+def test_ns_normalize_transpose_and_scale_match_torch():
+    """The Newton-Schulz input kernels: X / (||X|| + 1e-7) per matrix in bf16 (optionally transposed) against the
+    PyTorch form, the batched transpose exactly, and the clip's in-place scale by a device scalar."""
+    from nano_gpic_b200.ops import optim as OPT
+    torch.manual_seed(5)
+    for n, a, b in ((3, 512, 128), (2, 200, 72), (4, 128, 384)):
+        X = (torch.randn(n, a, b, device="cuda") * 3).bfloat16()
+        for tr in (False, True):
+            Y = X.mT if tr else X
+            ref = (Y / (Y.norm(dim=(-2, -1), keepdim=True) + 1e-7)).contiguous()
+            got = OPT.ns_normalize(X, transpose=tr)
+            assert got.shape == ref.shape and got.is_contiguous()
+            torch.testing.assert_close(got.float(), ref.float(), rtol=1e-2, atol=1e-4)
+        assert torch.equal(OPT.transpose_bf16(X), X.mT.contiguous())
+    buf = torch.randn(1 << 20, device="cuda")
+    ref = buf * 0.37
+    OPT.scale_(buf, torch.tensor(0.37, device="cuda"))
+    assert torch.equal(buf, ref)
