@@ -9,7 +9,9 @@ One optimizer step = 1024 images over all ranks (1024 / N per rank, split into m
 untimed warm-up steps, then exactly K steps bracketed by a barrier + cuda synchronize on both sides, timed with CUDA
 events on the launching stream; the reported time is the max over ranks. Every step's inputs (about 1.3 GB per rank)
 exceed the 126 MB L2. `e2e` repeats the measurement through the public Trainer.train_step API with each step's inputs
-copied from pinned host memory and the loss read back to the host. `--impl reference` runs the unmodified reference
+copied from pinned host memory and every step's loss read back to the host (one step behind, while the next step
+runs; the last read closes the timed region), for both arms; ours also starts each step's first host -> device copy
+under the previous step (Trainer.prefetch). `--impl reference` runs the unmodified reference
 (baseline/_ref: its JiT_T2I, JiTTrainer, MuonAdamW, WarmupFlatCooldown, bf16 autocast, SDPA attention because its FA3
 binary is Hopper-only) on the same data, with the data parallelism its final ladder uses for the size: whole-model
 torch.compile + DDP below width 1280, FSDP2 per block + ShardMuonAdamW + NoSync accumulation from width 1280 (d14+)
@@ -116,6 +118,28 @@ def sync_all():
     torch.cuda.synchronize()
 
 
+def timed_e2e(step_fn, K):
+    """Like timed() for the end-to-end run: step_fn(i) runs step i from host inputs and returns its loss (a device
+    scalar); every step's loss is read back to the host, one step behind (while the next step runs, as a training loop
+    that logs asynchronously does), and the last step's read is inside the timed region."""
+    sync_all()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    prev, vals = None, []
+    for i in range(K):
+        loss = step_fn(i)
+        if prev is not None:
+            vals.append(prev.item())
+        prev = loss
+    vals.append(prev.item())
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / K
+    sync_all()
+    assert len(vals) == K
+    return ms
+
+
 def timed(step_fn, K):
     sync_all()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -159,12 +183,11 @@ def run_ours(a, rank, world, dev):
     status.check()
     e2e_ms = None
     if not a.no_e2e:
-        losses = []
-
         def e2e_step(i):
             loss = tr.train_step(*host_batches[i % 2])
-            losses.append(loss.item())   # the step's result read back to the host
-        e2e_ms = timed(e2e_step, a.steps)
+            tr.prefetch(*host_batches[(i + 1) % 2])  # the next step's first copies run under this step
+            return loss
+        e2e_ms = timed_e2e(e2e_step, a.steps)
     return ms, e2e_ms, launches, clock_rec, tr
 
 
@@ -345,7 +368,7 @@ def run_reference(a, rank, world, dev):
     clock_rec = clocks.stop() if clocks else None
     e2e_ms = None
     if not a.no_e2e:
-        e2e_ms = timed(lambda i: step(*host_batches[i % 2]).item(), a.steps)
+        e2e_ms = timed_e2e(lambda i: step(*host_batches[i % 2]), a.steps)
     return (ms, e2e_ms, None, clock_rec, None), None
 
 

@@ -134,10 +134,7 @@ class Trainer:
                 t.record_stream(cur)  # freed only after the compute stream's uses
         return out, ready
 
-    def train_step(self, images, captions, caption_mask=None, t=None, noise=None):
-        """One optimizer step over this rank's batch, split into `accum` micro-batches.
-        images: uint8 [B, H, W, 3] or float [B, 3, H, W] in [-1, 1] (host pinned or device);
-        captions [B, T, D] (bf16); caption_mask [B, T] bool or None. Returns the batch-mean loss (device scalar)."""
+    def _split(self, images, captions, caption_mask=None, t=None, noise=None):
         B = images.shape[0]
         assert B % self.accum == 0
         mb = B // self.accum
@@ -146,7 +143,25 @@ class Trainer:
             sl = slice(i * mb, (i + 1) * mb)
             micros.append((images[sl], captions[sl], caption_mask[sl] if caption_mask is not None else None,
                            t[sl] if t is not None else None, noise[sl] if noise is not None else None))
-        return self.train_micro(micros)
+        return micros
+
+    @staticmethod
+    def _key(mbatch):
+        return tuple((x.data_ptr(), tuple(x.shape), x.dtype) if x is not None else None for x in mbatch)
+
+    def train_step(self, images, captions, caption_mask=None, t=None, noise=None):
+        """One optimizer step over this rank's batch, split into `accum` micro-batches.
+        images: uint8 [B, H, W, 3] or float [B, 3, H, W] in [-1, 1] (host pinned or device);
+        captions [B, T, D] (bf16); caption_mask [B, T] bool or None. Returns the batch-mean loss (device scalar)."""
+        return self.train_micro(self._split(images, captions, caption_mask, t, noise))
+
+    def prefetch(self, images, captions, caption_mask=None, t=None, noise=None):
+        """Starts the host -> device copies of a later step's first micro-batch now (same arguments as train_step),
+        on the copy stream: called right after train_step, they overlap the step the GPU is still running, so the next
+        train_step with these tensors does not wait for its first copy. Host tensors only (device ones need no copy)."""
+        first = self._split(images, captions, caption_mask, t, noise)[0]
+        dev = self.flat.data.device if self.flat is not None else next(self.model.parameters()).device
+        self._prefetched = (self._key(first), self._stage(first, dev))
 
     def train_micro(self, micros):
         """One optimizer step over a list of micro-batches (images, captions, mask[, t, noise]); the micro-batches may
@@ -160,7 +175,9 @@ class Trainer:
         # caption lengths on the host for packing, read from the loader's host masks before the copies
         host_lens = [(mc[2].sum(1).tolist() if mc[2] is not None and mc[2].device.type == "cpu" else None)
                      for mc in micros] if self.pack else [None] * n
-        staged = self._stage(micros[0], dev)
+        pre = getattr(self, "_prefetched", None)
+        self._prefetched = None
+        staged = pre[1] if pre is not None and pre[0] == self._key(micros[0]) else self._stage(micros[0], dev)
         for i in range(n):
             (x, y, m, ti, ni), ready = staged
             if ready is not None:  # this micro-batch's copies, enqueued one micro-batch earlier

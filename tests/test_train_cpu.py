@@ -97,3 +97,29 @@ def test_caption_type_losses_and_sinks(tmp_path, monkeypatch):
     rec = json.loads((tmp_path / "metrics.jsonl").read_text())
     assert rec["step"] == 10 and rec["train/loss_long"] == 8.0
     assert MetricSinks(str(tmp_path), 1, logger_node=node).wandb is None  # only rank 0 writes
+
+
+def test_prefetch_gives_the_same_steps():
+    """Trainer.prefetch (the next step's first micro-batch staged ahead) changes nothing in the steps it feeds, and a
+    prefetch of other tensors is ignored."""
+    img, cap, mask = _batch()
+    img2, cap2, mask2 = _batch(seed=5)
+    t = torch.full((4,), 0.3)
+    noise = torch.randn(4, 3, 64, 64, generator=torch.Generator().manual_seed(7))
+    runs = []
+    for use in (False, True):
+        tr = _trainer()
+        out = []
+        for k in range(3):
+            a = (img, cap, mask) if k % 2 == 0 else (img2, cap2, mask2)
+            out.append(float(tr.train_step(*a, t=t, noise=noise)))
+            if use:
+                nxt = (img2, cap2, mask2) if k % 2 == 0 else (img, cap, mask)
+                tr.prefetch(*nxt, t=t, noise=noise)
+        if use:
+            tr.prefetch(*_batch(seed=9), t=t, noise=noise)  # not the next step's tensors: ignored
+            out.append(float(tr.train_step(img2, cap2, mask2, t=t, noise=noise)))
+        else:
+            out.append(float(tr.train_step(img2, cap2, mask2, t=t, noise=noise)))
+        runs.append(out)
+    assert runs[0] == runs[1], runs
