@@ -2205,32 +2205,47 @@ __global__ void dq_store_kernel(const float* __restrict__ acc, bf16* __restrict_
 void attn_delta(const bf16* dout, int64_t lddo, const bf16* o, int64_t ldo, float* delta, int rows, int Lq, int H,
                 cudaStream_t s);
 
-// ld[b, h, q] = (lse * log2(e), sum_d dO * O) for q < Lq; (+inf, 0) for Lq <= q < Lqp (padding rows then give P = 0)
-__global__ void attn_ld_kernel(const bf16* __restrict__ dout, int64_t lddo, const bf16* __restrict__ o, int64_t ldo,
-                               const float* __restrict__ lse, float2* __restrict__ ld, int B, int H, int Lq, int Lqp) {
+// ld[b, h, q] = (lse * log2(e), sum_d dO * O) for q < Lq; (+inf, 0) for Lq <= q < Lqp (padding rows then give P = 0).
+// Eight lanes per (row, head): each lane reads one 16-byte vector of dO and of O, so a warp reads 512 contiguous bytes
+// of a row (four heads) per load, and the eight partial dots meet in three shuffles. Threads past the B * Lq * H * 8
+// lanes fill the padding rows q >= Lq.
+__global__ void attn_ld8_kernel(const bf16* __restrict__ dout, int64_t lddo, const bf16* __restrict__ o, int64_t ldo,
+                                const float* __restrict__ lse, float2* __restrict__ ld, int B, int H, int Lq, int Lqp) {
   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= (int64_t)B * H * Lqp) return;
-  const int q = (int)(t % Lqp);
-  const int64_t bh = t / Lqp;
-  const int b = (int)(bh / H), h = (int)(bh - (int64_t)b * H);
-  if (q >= Lq) {
-    ld[t] = make_float2(INFINITY, 0.f);
-    return;
-  }
-  const int64_t row = (int64_t)b * Lq + q;
-  const uint4* a = reinterpret_cast<const uint4*>(dout + row * lddo + h * 64);
-  const uint4* c = reinterpret_cast<const uint4*>(o + row * ldo + h * 64);
+  const int64_t lanes = (int64_t)B * Lq * H * 8;
+  // every lane of the warp reaches the shuffles (a warp may hold both dot lanes and padding or idle lanes; groups of
+  // eight never mix, since `lanes` is a multiple of 8)
+  const bool dot = t < lanes;
+  const int64_t unit = t >> 3;
+  const int e = (int)(t & 7);
+  const int64_t row = dot ? unit / H : 0;  // b * Lq + q
+  const int h = dot ? (int)(unit - row * H) : 0;
   float acc = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint4 x = a[i], y = c[i];
+  if (dot) {
+    const uint4 x = reinterpret_cast<const uint4*>(dout + row * lddo + h * 64)[e];
+    const uint4 y = reinterpret_cast<const uint4*>(o + row * ldo + h * 64)[e];
     const uint32_t xs[4] = {x.x, x.y, x.z, x.w}, ys[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
     for (int k = 0; k < 4; ++k)
       acc += __uint_as_float(xs[k] << 16) * __uint_as_float(ys[k] << 16) +
              __uint_as_float(xs[k] & 0xffff0000u) * __uint_as_float(ys[k] & 0xffff0000u);
   }
-  ld[t] = make_float2(lse[bh * Lq + q] * atc::kLog2e, acc);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+  if (dot) {
+    if (e == 0) {
+      const int b = (int)(row / Lq), q = (int)(row - (int64_t)b * Lq);
+      const int64_t bh = (int64_t)b * H + h;
+      ld[bh * Lqp + q] = make_float2(lse[bh * Lq + q] * atc::kLog2e, acc);
+    }
+    return;
+  }
+  const int64_t u = t - lanes;  // padding rows
+  const int pad = Lqp - Lq;
+  if (pad <= 0 || u >= (int64_t)B * H * pad) return;
+  const int64_t bh = u / pad;
+  ld[bh * Lqp + Lq + (int)(u - bh * pad)] = make_float2(INFINITY, 0.f);
 }
 
 // Same contract as attn_bwd (csrc/attention.cu): delta = rowsum(dO * O), then the tcgen05 kernel, whose dQ partials
@@ -2285,8 +2300,8 @@ void attn_bwd_tc(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& 
   } else {
     const int64_t Lqp = (int64_t)p.nq * atb::BQ;
     ldt = at::empty({B, (int64_t)p.H, Lqp, 2}, q.options().dtype(at::kFloat));
-    const int64_t n = B * p.H * Lqp;
-    attn_ld_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
+    const int64_t n = B * Lq * p.H * 8 + B * p.H * (Lqp - Lq);
+    attn_ld8_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(
         reinterpret_cast<const bf16*>(dout.data_ptr()), dout.stride(0), reinterpret_cast<const bf16*>(o.data_ptr()),
         o.stride(0), lse.data_ptr<float>(), reinterpret_cast<float2*>(ldt.data_ptr()), (int)B, p.H, (int)Lq, (int)Lqp);
     NG_LAUNCH_CHECK();
