@@ -340,15 +340,21 @@ void gate_bwd(const at::Tensor& dout, const at::Tensor& y, const at::Tensor& gat
   fa.gout[0] = (dgate.has_value() && dgate->defined()) ? dgate->data_ptr<float>() : nullptr;
   fa.gld[0] = fa.gout[0] != nullptr ? dgate->stride(0) : 0;
   fa.scratch = part.data_ptr<float>() + (int64_t)G * chunks * 2 * C;
-  fa.cnt = finish_counters(s, G);
+  const bool in_kernel = chunks <= kFinishMaxChunks;  // as in rms_mod_bwd: no long serial tail
+  fa.cnt = in_kernel ? finish_counters(s, G) : nullptr;
   gate_bwd_kernel<<<dim3(chunks, G), 256, smem, s>>>(
       reinterpret_cast<const bf16*>(dout.data_ptr()), reinterpret_cast<const bf16*>(y.data_ptr()),
       reinterpret_cast<const bf16*>(gate.data_ptr()), gate.stride(0), reinterpret_cast<bf16*>(dy.data_ptr()),
       part.data_ptr<float>(), M, C, (int)rpg, cup, fa);
   NG_LAUNCH_CHECK();
-  // d_bias: the column sums of the G group rows the kernel left in the scratch
-  if (dbias.has_value() && dbias->defined())
-    colsum_launch(fa.scratch, false, G, C, C, dbias->data_ptr<float>(), true, s);
+  float* db = (dbias.has_value() && dbias->defined()) ? dbias->data_ptr<float>() : nullptr;
+  if (in_kernel) {  // d_bias: the column sums of the G group rows the kernel left in the scratch
+    if (db != nullptr) colsum_launch(fa.scratch, false, G, C, C, db, true, s);
+    return;
+  }
+  const float* pp = part.data_ptr<float>();
+  group_sum_launch(pp, G, chunks, C, 2 * C, fa.gout[0], fa.gld[0], s);
+  if (db != nullptr) colsum_launch(pp + C, false, (int64_t)G * chunks, C, 2 * C, db, true, s);
 }
 
 void fm_prep(const at::Tensor& x, const at::Tensor& noise, const at::Tensor& t, const at::Tensor& xt_tok, int64_t p) {

@@ -13,6 +13,9 @@
 
 namespace ng {
 
+// Above this many chunks per group the host reduces the partials (two-stage, many CTAs) instead.
+constexpr int kFinishMaxChunks = 16;
+
 // Outputs of a finish: up to two per-group fields (null: not wanted), the scratch rows of the last field's group sums
 // ([G, C] fp32), and the ticket table (null: no finish in the kernel).
 struct FinishArgs {

@@ -617,7 +617,10 @@ void rms_mod_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& rs
   fa.gld[0] = fa.gout[0] != nullptr ? ld_of(dshift) : 0;
   fa.gld[1] = fa.gout[1] != nullptr ? ld_of(dscale) : 0;
   fa.scratch = part.data_ptr<float>() + (int64_t)G * chunks * 3 * C;
-  fa.cnt = finish_counters(s, G);
+  // a group of many chunks (the plain norm over all rows) would make its last CTA a long serial tail: then the host's
+  // two-stage reductions take the partials instead
+  const bool in_kernel = chunks <= kFinishMaxChunks;
+  fa.cnt = in_kernel ? finish_counters(s, G) : nullptr;
   const bf16* scp = mod ? bptr(scale) : nullptr;
   const int64_t ldsc = mod ? ld_of(scale) : 0;
   bool done = true;
@@ -653,8 +656,17 @@ void rms_mod_bwd(const at::Tensor& dh, const at::Tensor& x, const at::Tensor& rs
         rstd.data_ptr<float>(), w.data_ptr<float>(), nullptr, 0, bptr(dres), reinterpret_cast<bf16*>(dx.data_ptr()),
         part.data_ptr<float>(), M, C, rows_per_group, nullptr, fa);
   NG_LAUNCH_CHECK();
-  // d_w: the column sums of the G group rows the kernel left in the scratch
-  if (dw.has_value() && dw->defined()) colsum_launch(fa.scratch, false, G, C, C, dw->data_ptr<float>(), true, s);
+  float* dwp = (dw.has_value() && dw->defined()) ? dw->data_ptr<float>() : nullptr;
+  if (in_kernel) {  // d_w: the column sums of the G group rows the kernel left in the scratch
+    if (dwp != nullptr) colsum_launch(fa.scratch, false, G, C, C, dwp, true, s);
+    return;
+  }
+  const float* pp = part.data_ptr<float>();
+  if (mod) {
+    group_sum_launch(pp, G, chunks, C, 3 * C, fa.gout[0], fa.gld[0], s);
+    group_sum_launch(pp + C, G, chunks, C, 3 * C, fa.gout[1], fa.gld[1], s);
+  }
+  if (dwp != nullptr) colsum_launch(pp + 2 * C, false, (int64_t)G * chunks, C, 3 * C, dwp, true, s);
 }
 
 void layernorm_fwd(const at::Tensor& x, const at::Tensor& h, const at::Tensor& mu, const at::Tensor& rstd, double eps) {
