@@ -325,19 +325,35 @@ __global__ void __launch_bounds__(256, VPL <= 4 ? 2 : 1) rms_mod_bwd_kernel2(con
 #pragma unroll
       for (int j = 0; j < 8; ++j) sc[j] = 0.f;
     }
-#pragma unroll 2
-    for (int rr = grp; rr < nrows; rr += G2) {
-      const int64_t row = r0 + rr;
-      const float r = rstd[row];
-      float d[8], xf[8];
-      unpack8(*reinterpret_cast<const uint4*>(dh + row * C + c0), d);
-      unpack8(*reinterpret_cast<const uint4*>(x + row * C + c0), xf);
+    // the loads of four rows are issued before their math (the chunk's rows come back from L2: latency, not
+    // bandwidth, bounds this loop); the rows are still added in the order rr, rr + G2, ...
+    for (int rr = grp; rr < nrows; rr += 4 * G2) {
+      uint4 dv[4], xv[4];
+      float rv[4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float xn = xf[j] * r;
-        psh[j] += d[j];
-        psc[j] += d[j] * wf[j] * xn;
-        pw[j] += d[j] * (1.f + sc[j]) * xn;
+      for (int u = 0; u < 4; ++u) {
+        const int q = rr + u * G2;
+        if (q < nrows) {
+          const int64_t row = r0 + q;
+          rv[u] = rstd[row];
+          dv[u] = *reinterpret_cast<const uint4*>(dh + row * C + c0);
+          xv[u] = *reinterpret_cast<const uint4*>(x + row * C + c0);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (rr + u * G2 < nrows) {
+          float d[8], xf[8];
+          unpack8(dv[u], d);
+          unpack8(xv[u], xf);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float xn = xf[j] * rv[u];
+            psh[j] += d[j];
+            psc[j] += d[j] * wf[j] * xn;
+            pw[j] += d[j] * (1.f + sc[j]) * xn;
+          }
+        }
       }
     }
   }
