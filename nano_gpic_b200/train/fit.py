@@ -189,27 +189,34 @@ def fit(cfg):
     rebal_mode = int(get_dotted(cfg, "trainer.rebalance", os.environ.get("GPIC_MFU_REBALANCE", "0")) or 0)
     rebal = Rebalancer() if rebal_mode and dist.is_initialized() and dist.get_world_size() > 1 else None
     t_log, n_log = time.perf_counter(), 0
+    def fetch_micro():
+        img, caps, meta = next(it)
+        mtypes = list(meta.get("caption_type") or [])
+        if isinstance(img, ResizeBatch):  # the bicubic crop passes of the batch, on the device
+            img = img.run(dev)
+        if cond is not None:
+            y, uncond = cond(caps, meta)
+            mask = meta.get("y_mask")
+            if obj is not None and obj.null_condition_p > 0:
+                y, mask = obj.caption_dropout(y.to(dev), mask, uncond.to(dev))
+        else:
+            y, mask = meta["text_emb"], meta["text_mask"]
+        if rebal is not None and mask is not None:
+            if rebal_mode == 1 or img.is_cuda:  # lever E: exchange on the device (NCCL)
+                img, y, mask = img.to(dev), y.to(dev), mask.to(dev)
+            img, y, mask = rebal(img, y, mask)  # host tensors (lever E2): exchange over gloo
+        return (img, y, mask), mtypes
+
+    ahead = None  # the next step's first micro-batch, fetched (and its copies started) during the previous step
     try:
         while trainer.global_step < max_steps and not ctx.stop:
             step = trainer.global_step
             micros, types = [], []
-            for _ in range(accum):
-                img, caps, meta = next(it)
-                types += list(meta.get("caption_type") or [])
-                if isinstance(img, ResizeBatch):  # the bicubic crop passes of the batch, on the device
-                    img = img.run(dev)
-                if cond is not None:
-                    y, uncond = cond(caps, meta)
-                    mask = meta.get("y_mask")
-                    if obj is not None and obj.null_condition_p > 0:
-                        y, mask = obj.caption_dropout(y.to(dev), mask, uncond.to(dev))
-                else:
-                    y, mask = meta["text_emb"], meta["text_mask"]
-                if rebal is not None and mask is not None:
-                    if rebal_mode == 1 or img.is_cuda:  # lever E: exchange on the device (NCCL)
-                        img, y, mask = img.to(dev), y.to(dev), mask.to(dev)
-                    img, y, mask = rebal(img, y, mask)  # host tensors (lever E2): exchange over gloo
-                micros.append((img, y, mask))
+            for k in range(accum):
+                mbatch, mtypes = ahead if (k == 0 and ahead is not None) else fetch_micro()
+                types += mtypes
+                micros.append(mbatch)
+            ahead = None
             for c in callbacks:
                 c.on_step_start(ctx, step)
             loss = trainer.train_micro(micros)
@@ -230,6 +237,11 @@ def fit(cfg):
                     print(f"[step {trainer.global_step}] " + " ".join(f"{k}={v:.5g}" for k, v in vals.items()),
                           flush=True)
                 t_log, n_log = time.perf_counter(), 0
+            # after the step's callbacks (checkpoints record the data position first): the next step's first
+            # micro-batch, whose host -> device copies then run under this step's queued work
+            if trainer.global_step < max_steps and not ctx.stop:
+                ahead = fetch_micro()
+                trainer.prefetch_micro(ahead[0])
         for c in callbacks:
             c.on_train_end(ctx)
     finally:

@@ -155,6 +155,12 @@ class Trainer:
         captions [B, T, D] (bf16); caption_mask [B, T] bool or None. Returns the batch-mean loss (device scalar)."""
         return self.train_micro(self._split(images, captions, caption_mask, t, noise))
 
+    def prefetch_micro(self, mbatch):
+        """prefetch() for a list-of-micro-batches caller (train_micro): stages one micro-batch (images, captions,
+        mask[, t, noise]) now; the next train_micro whose first micro-batch is these tensors uses the staged copy."""
+        dev = self.flat.data.device if self.flat is not None else next(self.model.parameters()).device
+        self._prefetched = (self._key(tuple(mbatch)), self._stage(tuple(mbatch), dev))
+
     def prefetch(self, images, captions, caption_mask=None, t=None, noise=None):
         """Starts the host -> device copies of a later step's first micro-batch now (same arguments as train_step),
         on the copy stream: called right after train_step, they overlap the step the GPU is still running, so the next
@@ -177,7 +183,7 @@ class Trainer:
                      for mc in micros] if self.pack else [None] * n
         pre = getattr(self, "_prefetched", None)
         self._prefetched = None
-        staged = pre[1] if pre is not None and pre[0] == self._key(micros[0]) else self._stage(micros[0], dev)
+        staged = pre[1] if pre is not None and pre[0] == self._key(tuple(micros[0])) else self._stage(micros[0], dev)
         for i in range(n):
             (x, y, m, ti, ni), ready = staged
             if ready is not None:  # this micro-batch's copies, enqueued one micro-batch earlier
