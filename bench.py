@@ -31,7 +31,7 @@ import torch
 import torch.distributed as dist
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-PUBLISHED = {"d12": 7817.0, "d18": 2183.0, "d10": 12724.0}  # images/s per 8xH100 box
+PUBLISHED = {"d12": 7817.0, "d18": 2183.0, "d10": 12724.0}  # the reference's published images/s per 8 x H100 box
 
 
 # ------------------------------------------------------------------------------------------------------- helpers
@@ -352,7 +352,7 @@ def reference_fsdp_step_fn(a, rank, world, dev):
 def run_reference(a, rank, world, dev):
     pg = os.path.join(ROOT, "baseline", "_ref", "baselines", "PixelGen")
     if not os.path.isdir(os.path.join(pg, "src")):
-        return None, "baseline/_ref is missing: copy the reference tree there (see DESIGN.md)"
+        return None, "baseline/_ref is missing: copy the reference source tree there (cp -r; it is not a pip package)"
     fsdp = reference_uses_fsdp(a.size, world)
     step = (reference_fsdp_step_fn if fsdp else reference_step_fn)(a, rank, world, dev)
     B = a.global_batch // world
