@@ -1,7 +1,7 @@
 // Per-head RMSNorm of q/k with the 2D RoPE fused in, forward and backward (head dim 64), for sm_100a.
-// Four lanes per (row, head) (qk_norm_fwd4_kernel / qk_norm_bwd4_kernel, used by the glue): each lane keeps 16 of the
-// head's 64 values, the head's sums take two shuffles. The one-thread-per-head kernels below them are kept as the
-// simplest statement of the math.
+// Forward: four lanes per (row, head) (qk_norm_fwd4_kernel): each lane keeps 16 of the head's 64 values, the head's
+// sums take two shuffles. Backward: eight lanes per (row, head), two units in flight (qk_norm_bwd8_kernel). The
+// one-thread-per-head kernels that come first are kept as the simplest statement of the math.
 // Reference: q_norm/k_norm + apply_rotary_emb_real (baselines/PixelGen/src/models/transformer/JiT_T2I.py:141-166,
 // baselines/PixelGen/src/models/layers/rope.py:53-69), the Triton lever K2 (fused_qk.py:55-200).
 #include <ATen/cuda/CUDAContext.h>
@@ -235,95 +235,9 @@ __global__ void __launch_bounds__(256) qk_norm_fwd4_kernel(const bf16* __restric
   }
 }
 
-// d(src) and the per-block partials of dw (part[block][64], summed in a fixed order afterwards)
-template <bool ROPE>
-__global__ void __launch_bounds__(256) qk_norm_bwd4_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ src,
-                                                           int64_t ld_src, const float* __restrict__ rstd,
-                                                           const float* __restrict__ w, const float* __restrict__ cosT,
-                                                           const float* __restrict__ sinT, bf16* __restrict__ dsrc,
-                                                           int64_t ld_dsrc, float* __restrict__ part, int rows, int H,
-                                                           int L) {
-  __shared__ float s_part[8][64];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, q = lane & 3;
-  float dw[2][8];
-  float wf[2][8];
-#pragma unroll
-  for (int k = 0; k < 2; ++k) {
-    ldf8(w + 8 * q + 32 * k, wf[k]);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) dw[k][i] = 0.f;
-  }
-  const int64_t units = (int64_t)rows * H;
-  // every quad runs the same number of iterations (its shuffles need all four lanes)
-  for (int64_t base = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 2; base - (threadIdx.x >> 2) < units;
-       base += ((int64_t)gridDim.x * blockDim.x) >> 2) {
-    const bool valid = base < units;
-    const int64_t u = valid ? base : 0;
-    const int row = (int)(u / H), h = (int)(u - (int64_t)row * H);
-    float d[2][8], x[2][8];
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      ld8(dout + (int64_t)row * H * 64 + h * 64 + 8 * q + 32 * k, d[k]);
-      ld8(src + row * ld_src + h * 64 + 8 * q + 32 * k, x[k]);
-    }
-    if (ROPE) {
-      const int pos = row % L;
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        float c[4], sn[4];
-        ldf4(cosT + pos * 32 + 4 * q + 16 * k, c);
-        ldf4(sinT + pos * 32 + 4 * q + 16 * k, sn);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float a = d[k][2 * j], b = d[k][2 * j + 1];
-          d[k][2 * j] = a * c[j] + b * sn[j];
-          d[k][2 * j + 1] = -a * sn[j] + b * c[j];
-        }
-      }
-    }
-    const float r = valid ? rstd[u] : 0.f;
-    float dot = 0.f;
-#pragma unroll
-    for (int k = 0; k < 2; ++k)
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float xh = x[k][i] * r;
-        dw[k][i] += valid ? d[k][i] * xh : 0.f;
-        d[k][i] *= wf[k][i];  // d(xhat)
-        dot += d[k][i] * xh;
-      }
-    dot = quad_sum(dot) * (1.f / 64.f);
-#pragma unroll
-    for (int k = 0; k < 2; ++k) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) x[k][i] = r * (d[k][i] - x[k][i] * r * dot);
-      if (valid) st8(dsrc + row * ld_dsrc + h * 64 + 8 * q + 32 * k, x[k]);
-    }
-  }
-  // dw: lanes with the same q hold the same 16 elements; reduce over the 8 quads of the warp, then over warps
-#pragma unroll
-  for (int k = 0; k < 2; ++k)
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float v = dw[k][i];
-      v += __shfl_xor_sync(0xffffffffu, v, 4);
-      v += __shfl_xor_sync(0xffffffffu, v, 8);
-      v += __shfl_xor_sync(0xffffffffu, v, 16);
-      if (lane < 4) s_part[warp][8 * q + 32 * k + i] = v;
-    }
-  __syncthreads();
-  if (threadIdx.x < 64) {
-    float a = 0.f;
-#pragma unroll
-    for (int k2 = 0; k2 < 8; ++k2) a += s_part[k2][threadIdx.x];
-    part[(int64_t)blockIdx.x * 64 + threadIdx.x] = a;
-  }
-}
-
 // Backward with eight lanes per (row, head), one 16-byte vector of dout and of src per lane, two units in flight per
-// lane (both units' loads are issued before either's math): fewer registers than the four-lane form (four CTAs per
-// SM instead of two) and twice the bytes in flight per thread, for the DRAM-bound image q/k backward. Same math and
-// the same dw partial layout as qk_norm_bwd4_kernel.
+// lane (both units' loads are issued before either's math): few registers (four CTAs per SM) and many bytes in flight
+// per thread, for the DRAM-bound image q/k backward; a dw partial row per block, summed in a fixed order afterwards.
 template <bool ROPE>
 __global__ void __launch_bounds__(256, 4) qk_norm_bwd8_kernel(const bf16* __restrict__ dout, const bf16* __restrict__ src,
                                                               int64_t ld_src, const float* __restrict__ rstd,
